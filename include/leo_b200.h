@@ -1,0 +1,103 @@
+/*
+ * leo_b200: B200-native (sm_100a) per-byte training step over Leo's logical
+ * story workers, behind a C ABI with plain pointers and sizes.
+ *
+ * Every entry point returns 0 on success and -1 on failure, with the message
+ * available from leo_b200_last_error() (thread-local), mirroring LeoResult /
+ * LeoError (crates/leo-core/src/lib.rs:43-55).  Explicit GPU selection never
+ * falls back to a CPU path (crates/leo-core/src/backend.rs:803-822): without a
+ * Blackwell device leo_b200_open fails.
+ *
+ * Types: include/leo_b200_types.h; kernel configuration layout: the generated
+ * include/leo_cuda_abi.h (from cuda_abi.def, crates/leo-core/build.rs:97-121).
+ */
+#ifndef LEO_B200_H
+#define LEO_B200_H
+
+#include "leo_b200_types.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct LeoB200Device LeoB200Device;
+
+/* Last error message of the calling thread (LeoError::message). */
+const char* leo_b200_last_error(void);
+
+/* LEO_CUDA_ABI_VERSION of the generated header; must equal the host's
+   CUDA_ABI_VERSION (crates/leo-core/src/semantics.rs:12). */
+uint32_t leo_b200_abi_version(void);
+
+/* Config::validate (crates/leo-core/src/config.rs:250-519) plus this
+   backend's device limits. */
+int leo_b200_config_validate(const LeoB200Config* config);
+
+/* Model::initialize (crates/leo-core/src/model.rs:79-158) into caller-owned
+   arrays sized from the config; `topology` is a LeoB200Topology. */
+int leo_b200_model_initialize(const LeoB200Config* config, int topology, LeoB200HostModel* model);
+
+/* Model::validate (crates/leo-core/src/model.rs:223-396). */
+int leo_b200_model_validate(const LeoB200HostModel* model);
+
+/* training_state_hash (crates/leo-cli/src/main.rs:1187-1202) of a host model. */
+int leo_b200_training_state_hash(const LeoB200HostModel* model, uint8_t out[32]);
+
+/* Opens a backend on CUDA device `device` with `model` as the canonical
+   model and room for `max_lanes` story lanes.  Replaces GpuRuntime::new /
+   CudaRuntime creation (crates/leo-core/src/backend.rs:547-580,
+   crates/leo-core/src/cuda.rs:1138-1207). */
+int leo_b200_open(int device, const LeoB200HostModel* model, uint32_t max_lanes, LeoB200Device** out);
+void leo_b200_close(LeoB200Device* device);
+
+/* Replaces the canonical model and every resident lane
+   (RuntimeBackend::model_mut + synchronize, backend.rs:355-357). */
+int leo_b200_upload_canonical(LeoB200Device* device, const LeoB200HostModel* model);
+
+/* RuntimeBackend::synchronize_model + model (backend.rs:355-356): copies the
+   canonical model into caller-owned arrays (checkpoint layout). */
+int leo_b200_download_model(LeoB200Device* device, LeoB200HostModel* model);
+
+/* The canonical runtime's tick (Runtime::current_tick, runtime.rs:117); it
+   advances with single-story and replay steps. */
+uint64_t leo_b200_canonical_tick(LeoB200Device* device);
+int leo_b200_set_canonical_tick(LeoB200Device* device, uint64_t tick);
+
+/* One logical story batch: RuntimeBackend::training_story_batch
+   (backend.rs:457-463) followed by the batch-end mean merge
+   (parallel.rs:694-798) and serial canonical replay
+   (crates/leo-cli/src/training.rs:1539-1727).  Stories are
+   bytes[offsets[i] .. offsets[i+1]].  `summaries` (optional) receives one
+   DeviceStorySummary per story, `losses` (optional) the initial-pass loss of
+   every target of every story in story order (sum of len+1 floats). */
+int leo_b200_train_story_batch(LeoB200Device* device, const uint8_t* bytes, const uint64_t* offsets,
+                               uint32_t stories, int permission, LeoB200BatchReport* report,
+                               LeoB200StorySummary* summaries, float* losses);
+
+/* The same batch in three calls, so a caller can inspect lanes between steps:
+   begin (lane reset + schedules), steps (advance `count` ticks), finish
+   (remaining ticks, merge, replay, lane sync). */
+int leo_b200_batch_begin(LeoB200Device* device, const uint8_t* bytes, const uint64_t* offsets, uint32_t stories,
+                         int permission);
+int leo_b200_batch_steps(LeoB200Device* device, uint32_t count, uint32_t* steps_done);
+int leo_b200_batch_finish(LeoB200Device* device, LeoB200BatchReport* report, LeoB200StorySummary* summaries,
+                          float* losses);
+
+/* training_state_hash of the canonical device model. */
+int leo_b200_state_digest(LeoB200Device* device, uint8_t out[32]);
+
+/* Inspection for parity tests: a lane's learned parameters (lane ==
+   UINT32_MAX: the canonical model) and its transient arrays by the reference
+   runtime's field names (runtime.rs:112-186). */
+int leo_b200_lane_model(LeoB200Device* device, uint32_t lane, LeoB200HostModel* model);
+int leo_b200_lane_array(LeoB200Device* device, uint32_t lane, const char* name, void* out, size_t capacity,
+                        size_t* written);
+
+/* Device memory held by the backend, in bytes. */
+size_t leo_b200_device_bytes(LeoB200Device* device);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LEO_B200_H */

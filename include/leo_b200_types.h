@@ -1,0 +1,173 @@
+/*
+ * Plain-C data types shared by the leo_b200 C ABI.
+ *
+ * These types carry Leo's persistent model and configuration across the
+ * boundary as plain pointers and sizes, with no torch or CUDA types.  The
+ * kernel-side configuration is the generated `struct LeoConfig` from
+ * cuda_abi.def (crates/leo-core/cuda_abi.def:4-44, emitted by
+ * crates/leo-core/build.rs:97-121); the fields that file does not carry but
+ * that the reference host reads from `Config` are in LeoB200HostConfig.
+ *
+ * This header is C++-only when included together with leo_cuda_abi.h,
+ * because that generated header uses a C++ static_assert on a bare type name.
+ */
+#ifndef LEO_B200_TYPES_H
+#define LEO_B200_TYPES_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+/* The generated ABI header (byte-identical to the reference build's output)
+   has no include guard of its own. */
+#ifndef LEO_CUDA_ABI_INCLUDED
+#define LEO_CUDA_ABI_INCLUDED
+#include "leo_cuda_abi.h"
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LEO_B200_BYTE_SYMBOLS 256u
+#define LEO_B200_BEGIN_DOCUMENT 256u   /* crates/leo-core/src/symbols.rs:4 */
+#define LEO_B200_END_DOCUMENT 257u     /* crates/leo-core/src/symbols.rs:5 */
+#define LEO_B200_SYMBOL_COUNT 258u     /* crates/leo-core/src/symbols.rs:6 */
+#define LEO_B200_OUTPUT_CLASSES 257u   /* crates/leo-core/src/symbols.rs:7 */
+#define LEO_B200_END_OUTPUT_INDEX 256u /* crates/leo-core/src/symbols.rs:8 */
+
+/* Permission, crates/leo-core/src/permission.rs:5-11. */
+enum LeoB200Permission {
+    LEO_B200_FROZEN = 0,
+    LEO_B200_PROVISIONAL = 1,
+    LEO_B200_TRAINING = 2,
+    LEO_B200_VERIFIED = 3
+};
+
+/* Model topology builders for synthetic models. */
+enum LeoB200Topology {
+    /* crates/leo-core/src/model.rs:79-158 exactly (local/long-range fan-out). */
+    LEO_B200_TOPOLOGY_REFERENCE = 0,
+    /* Fan-out lists with targets drawn uniformly without replacement and
+       weights |N(0, 1/sqrt(S))| signed by source type. */
+    LEO_B200_TOPOLOGY_UNIFORM = 1,
+    /* As UNIFORM, but targets drawn from Zipf(s = 1.1) over a fixed random
+       permutation of the neurons (power-law in-degree skew). */
+    LEO_B200_TOPOLOGY_ZIPF = 2
+};
+
+/* Config fields the reference host reads from crates/leo-core/src/config.rs
+   but cuda_abi.def does not carry. */
+typedef struct LeoB200HostConfig {
+    uint64_t seed;                  /* config.rs:23  model.seed */
+    float excitatory_fraction;      /* config.rs:28  model.excitatory_fraction */
+    float provisional_strength;     /* config.rs:88  learning.provisional_strength */
+    float training_strength;        /* config.rs:89  learning.training_strength */
+    float verified_strength;        /* config.rs:90  learning.verified_strength */
+    uint32_t plasticity_window;     /* config.rs:94  learning.plasticity_window */
+    float end_document_weight;      /* config.rs:96  learning.end_document_weight */
+    float context_dropout_rate;     /* config.rs:109 context.dropout_rate */
+    float replay_fraction;          /* config.rs:116 replay.fraction */
+    uint32_t replay_segment_bytes;  /* config.rs:118 replay.segment_bytes */
+    uint32_t reserved0;
+} LeoB200HostConfig;
+
+typedef struct LeoB200Config {
+    struct LeoConfig abi;           /* 160 bytes, generated from cuda_abi.def */
+    LeoB200HostConfig host;         /* 48 bytes */
+} LeoB200Config;
+
+/* TrainingStatistics, crates/leo-core/src/metrics.rs:3-15. */
+typedef struct LeoB200Statistics {
+    uint64_t processed_bytes;
+    uint64_t processed_stories;
+    double training_loss_sum;
+    uint64_t training_targets;
+    uint64_t active_neurons_sum;
+    uint64_t active_neurons_peak;
+    uint64_t synaptic_events;
+    uint64_t numerical_rejections;
+    uint64_t persistent_ticks;
+} LeoB200Statistics;
+
+/*
+ * A persistent model (crates/leo-core/src/model.rs:65-76) as caller-owned
+ * arrays.  Sizes follow from the config: N = neuron_count,
+ * S = synapses_per_neuron, F = input_fanout, D = context_embedding_dim,
+ * C = context_max_order * context_slots_per_order.  The output matrix uses the
+ * checkpoint's output-major layout [257][N] (model.rs:48).
+ */
+typedef struct LeoB200HostModel {
+    LeoB200Config config;
+    uint64_t generation;
+    uint64_t parameter_revision;
+    LeoB200Statistics statistics;
+    float* threshold;               /* [N] */
+    float* excitability;            /* [N] */
+    uint8_t* neuron_type;           /* [N] 0 excitatory, 1 inhibitory */
+    uint32_t* recurrent_target;     /* [N*S] fan-out slots per source */
+    uint8_t* recurrent_branch;      /* [N*S] */
+    uint8_t* recurrent_delay;       /* [N*S] 1, 2, 4 or 8 */
+    float* recurrent_weight;        /* [N*S] */
+    uint32_t* input_target;         /* [258*F] */
+    uint8_t* input_branch;          /* [258*F] */
+    float* input_weight;            /* [258*F] */
+    float* output_weight;           /* [257*N] output-major */
+    float* output_bias;             /* [257] */
+    uint64_t* context_keys;         /* [C] */
+    float* context_embeddings;      /* [C*D] */
+    uint32_t* context_observations; /* [C] */
+    float* context_output_weight;   /* [257*D] output-major */
+} LeoB200HostModel;
+
+/* StepMetrics, crates/leo-core/src/metrics.rs:39-66 (subset with fixed-width
+   fields; `loss` is NaN when the step had no target). */
+typedef struct LeoB200StepMetrics {
+    float loss;
+    uint32_t predicted_symbol;
+    uint32_t active_neurons;
+    uint32_t emitted_events;
+    uint32_t suprathreshold_neurons;
+    uint32_t block_selected_neurons;
+    uint32_t global_cap_clipped_neurons;
+    float population_inhibition;
+    uint32_t context_cells;
+    uint32_t context_probes;
+    uint32_t context_applied;
+    float context_loss_gain;
+    uint64_t output_madds;
+    uint64_t eligible_recurrent_synapses;
+    uint64_t eligible_input_synapses;
+    float mean_abs_eligibility;
+    uint32_t reserved0;
+} LeoB200StepMetrics;
+
+/* DeviceStorySummary, crates/leo-core/src/backend.rs:320-328. */
+typedef struct LeoB200StorySummary {
+    double training_loss_sum;
+    uint64_t training_targets;
+    uint64_t active_neurons_sum;
+    uint64_t active_neurons_peak;
+    uint64_t synaptic_events;
+    uint64_t context_applied_steps;
+} LeoB200StorySummary;
+
+/* MergeMetrics, crates/leo-core/src/parallel.rs:305-310, plus replay counts
+   from BatchTrainingReport (crates/leo-cli/src/training.rs). */
+typedef struct LeoB200BatchReport {
+    uint64_t workers;
+    uint64_t fixed_parameter_updates;
+    uint64_t context_keys;
+    uint64_t stories;
+    uint64_t input_bytes;
+    uint64_t targets;
+    double mean_loss;
+    uint64_t replay_segments;
+    uint64_t replay_steps;
+    uint64_t replay_prefix_steps;
+} LeoB200BatchReport;
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LEO_B200_TYPES_H */

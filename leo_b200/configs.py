@@ -1,0 +1,172 @@
+"""Leo configurations used by the tests and the benchmark.
+
+Field names and defaults follow ``crates/leo-core/src/config.rs:8-156``; the
+base values are ``configs/probe.toml`` of the reference.  The numbered
+configurations restate the benchmark table (probe-sized CPU case, 65,536-unit
+single GPU, 262,144-unit Zipf single GPU, 128 workers over several GPUs):
+
+* ``baseline1``: probe.toml with ``synapses_per_neuron = 32``,
+  ``input_fanout = 32``, ``eligibility_decay = 0.9``; 4 workers, 64 stories of
+  256-1024 bytes, story seed 0.
+* ``baseline2``: N = 65,536 (128 blocks x 512), S = 64, F = 64, keep 8,
+  ``max_active_global = 1024``, ``target_activity = 0.01``, trace decay 0.9,
+  32 workers, stories of 256-1024 bytes.
+* ``baseline3``: N = 262,144 (256 blocks x 1024), S = 128 with Zipf(1.1)
+  target skew, keep 4, ``max_active_global = 1024``,
+  ``target_activity = 0.0039``, 64 workers, stories of 512-2048 bytes.
+* ``baseline4``: ``baseline3`` with 128 workers sharded across GPUs.
+
+Every synthetic configuration uses fan-out synapse lists with uniformly drawn
+(or Zipf-drawn) targets and weights ``|N(0, 1/sqrt(S))|`` signed by source
+type, because the reference's sign rules (``model.rs:362-379``) forbid
+negative excitatory weights.  The input projection, output projection,
+thresholds and neuron types come from the reference initializer
+(``model.rs:79-158``).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import asdict, dataclass, replace
+
+from .ctypes_types import (
+    LeoB200Config,
+    TOPOLOGY_REFERENCE,
+    TOPOLOGY_UNIFORM,
+    TOPOLOGY_ZIPF,
+)
+
+
+@dataclass(frozen=True)
+class Config:
+    # [model]
+    seed: int = 1337
+    neuron_count: int = 4096
+    block_count: int = 128
+    neurons_per_block: int = 32
+    branches_per_neuron: int = 4
+    excitatory_fraction: float = 0.8
+    synapses_per_neuron: int = 16
+    input_fanout: int = 32
+    max_active_per_block: int = 2
+    max_active_global: int = 192
+    # [dynamics]
+    branch_decay: float = 0.85
+    membrane_decay: float = 0.90
+    fatigue_decay: float = 0.97
+    fatigue_gain: float = 0.02
+    refractory_ticks: int = 1
+    target_activity: float = 0.01
+    threshold_homeostasis_rate: float = 0.0001
+    population_inhibition_rate: float = 0.05
+    population_inhibition_max: float = 2.0
+    adaptation_fast_decay: float = 0.95
+    adaptation_medium_decay: float = 0.99
+    adaptation_slow_decay: float = 0.999
+    adaptation_fast_gain: float = 0.005
+    adaptation_medium_gain: float = 0.001
+    adaptation_slow_gain: float = 0.0002
+    membrane_reset_fraction: float = 0.10
+    # [learning]
+    output_learning_rate: float = 0.002
+    recurrent_learning_rate: float = 0.0005
+    inhibitory_learning_rate: float = 0.00002
+    eligibility_decay: float = 0.95
+    eligibility_epsilon: float = 0.00001
+    surrogate_width: float = 0.25
+    surrogate_gain: float = 0.10
+    max_update: float = 0.01
+    weight_min: float = -1.0
+    weight_max: float = 1.0
+    provisional_strength: float = 0.20
+    training_strength: float = 1.0
+    verified_strength: float = 1.0
+    plasticity_window: int = 1
+    end_document_weight: float = 4.0
+    # [context]
+    context_embedding_dim: int = 16
+    context_max_order: int = 6
+    context_slots_per_order: int = 4096
+    context_probe_limit: int = 4
+    context_learning_rate: float = 0.02
+    context_confidence_observations: int = 8
+    context_dropout_rate: float = 0.5
+    # [replay]
+    replay_fraction: float = 0.30
+    replay_segment_bytes: int = 32
+
+    def to_c(self) -> LeoB200Config:
+        c = LeoB200Config()
+        a = c.abi
+        d = asdict(self)
+        for name, _ in a._fields_:
+            setattr(a, name, d[name])
+        h = c.host
+        h.seed = self.seed
+        h.excitatory_fraction = self.excitatory_fraction
+        h.provisional_strength = self.provisional_strength
+        h.training_strength = self.training_strength
+        h.verified_strength = self.verified_strength
+        h.plasticity_window = self.plasticity_window
+        h.end_document_weight = self.end_document_weight
+        h.context_dropout_rate = self.context_dropout_rate
+        h.replay_fraction = self.replay_fraction
+        h.replay_segment_bytes = self.replay_segment_bytes
+        return c
+
+    @property
+    def context_slots(self) -> int:
+        return self.context_max_order * self.context_slots_per_order
+
+
+@dataclass(frozen=True)
+class Workload:
+    """A configuration plus the synthetic story stream that exercises it."""
+
+    name: str
+    config: Config
+    topology: int
+    workers: int
+    stories: int
+    min_story_bytes: int
+    max_story_bytes: int
+    story_seed: int = 0
+
+
+PROBE = Config()
+
+TEST = Config(
+    neuron_count=128, block_count=8, neurons_per_block=16, synapses_per_neuron=8, input_fanout=8,
+    max_active_per_block=2, max_active_global=8, target_activity=0.04, inhibitory_learning_rate=0.00005,
+    context_embedding_dim=8, context_max_order=4, context_slots_per_order=128, context_learning_rate=0.08,
+    context_confidence_observations=2, context_dropout_rate=0.0, replay_segment_bytes=8,
+)
+
+BASELINE1 = replace(PROBE, synapses_per_neuron=32, input_fanout=32, eligibility_decay=0.9)
+
+BASELINE2 = replace(
+    PROBE, neuron_count=65536, block_count=128, neurons_per_block=512, synapses_per_neuron=64, input_fanout=64,
+    max_active_per_block=8, max_active_global=1024, target_activity=0.01, eligibility_decay=0.9,
+)
+
+BASELINE3 = replace(
+    PROBE, neuron_count=262144, block_count=256, neurons_per_block=1024, synapses_per_neuron=128,
+    input_fanout=64, max_active_per_block=4, max_active_global=1024, target_activity=0.0039,
+)
+
+WORKLOADS = {
+    "test": Workload("test", TEST, TOPOLOGY_REFERENCE, 4, 16, 8, 48),
+    "probe": Workload("probe", PROBE, TOPOLOGY_REFERENCE, 4, 64, 256, 1024),
+    "baseline1": Workload("baseline1", BASELINE1, TOPOLOGY_UNIFORM, 4, 64, 256, 1024),
+    "baseline2": Workload("baseline2", BASELINE2, TOPOLOGY_UNIFORM, 32, 10_000, 256, 1024),
+    "baseline3": Workload("baseline3", BASELINE3, TOPOLOGY_ZIPF, 64, 50_000, 512, 2048),
+    "baseline4": Workload("baseline4", BASELINE3, TOPOLOGY_ZIPF, 128, 50_000, 512, 2048),
+}
+
+
+def c_config(config: Config) -> LeoB200Config:
+    return config.to_c()
+
+
+__all__ = ["Config", "Workload", "WORKLOADS", "PROBE", "TEST", "BASELINE1", "BASELINE2", "BASELINE3", "c_config"]
+_ = C  # re-exported types keep ctypes imported for callers

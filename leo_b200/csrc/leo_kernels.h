@@ -1,0 +1,53 @@
+// Host-side launchers for the sm_100a kernels (implemented in the .cu files).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "leo_device.cuh"
+
+// One per-byte step (all phases) for every lane whose schedule covers step s.
+void leo_launch_step(const LaneState* lanes, int lane_count, uint32_t s, const KernelConsts& kc, int grid,
+                     cudaStream_t stream);
+size_t leo_select_smem_bytes(const KernelConsts& kc);
+
+// Batch-end sparse merge of one fixed f32 tensor (threshold, recurrent, input,
+// output rows, bias, context output): see leo_merge_kernels.cu.
+struct MergeTensor {
+    float** lane_values;          // device array [lanes] of lane tensor pointers
+    float* base;                  // canonical tensor
+    uint32_t** lane_lists;        // device array [lanes] of changed-index lists (rows for output)
+    uint32_t* lane_counts;        // device array [lanes] of list lengths
+    uint8_t** lane_marks;         // device array [lanes] of changed marks (cleared by the merge)
+    uint32_t row;                 // 1 for element tensors, LEO_OUTPUT_STRIDE for output rows
+    uint32_t row_len;             // 1, or 257 valid entries per output row
+    uint32_t length;              // elements (rows for output)
+    uint32_t kind;                // projection rule, see LeoProjection
+};
+
+enum LeoProjection : uint32_t {
+    LEO_PROJECT_THRESHOLD = 0,   // clamp [0.05, 2]
+    LEO_PROJECT_RECURRENT = 1,   // clamp [wmin, wmax], sign by source type
+    LEO_PROJECT_INPUT = 2,       // clamp [0, wmax]
+    LEO_PROJECT_WEIGHT = 3,      // clamp [wmin, wmax]
+    LEO_PROJECT_NONE = 4         // bias: no clamp
+};
+
+struct MergeScratch {
+    uint8_t* union_mark;          // [length] cleared after use
+    uint32_t* union_list;         // [length]
+    uint32_t* union_count;        // [1]
+    uint32_t* updates;            // [1] indices whose merged delta was applied
+    uint32_t* error_flag;         // [1]
+};
+
+// `lanes` stories contribute deltas (the first entries of the pointer tables);
+// all `sync_lanes` resident lanes receive the merged canonical values.
+void leo_launch_merge_tensor(const MergeTensor& t, const MergeScratch& m, int lanes, int sync_lanes, float wmin,
+                             float wmax, const uint8_t* neuron_type, uint32_t synapses_per_neuron, int grid,
+                             cudaStream_t stream);
+
+// Writes base[list[i] * row + o] (o < row_len) into every lane tensor.
+void leo_launch_scatter_rows(float** lane_values, int lanes, const float* base, const uint32_t* list, uint32_t count,
+                             uint32_t row, uint32_t row_len, int grid, cudaStream_t stream);

@@ -1,0 +1,1373 @@
+// Host runtime behind the leo_b200 C ABI: device buffers, canonical model,
+// story lanes, the per-byte step loop, the batch-end merge and serial replay.
+//
+// This replaces the reference's CUDA host runtime (crates/leo-core/src/cuda.rs,
+// train_story_batch_shared_device :8407-9355) behind the same backend
+// contract (RuntimeBackend::training_story_batch, backend.rs:457-463).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/leo_b200.h"
+#include "leo_device.cuh"
+#include "leo_host.h"
+#include "leo_kernels.h"
+#include "libm_tables.inc"
+
+namespace {
+
+thread_local std::string g_error;
+
+struct LeoFailure : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+
+void check_cuda(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw LeoFailure(std::string(what) + ": " + cudaGetErrorString(e));
+}
+#define CUDA_CHECK(x) check_cuda((x), #x)
+
+struct DevMem {
+    void* p = nullptr;
+    DevMem() = default;
+    DevMem(const DevMem&) = delete;
+    DevMem& operator=(const DevMem&) = delete;
+    ~DevMem() {
+        if (p) cudaFree(p);
+    }
+};
+
+struct MemPool {
+    std::vector<std::unique_ptr<DevMem>> blocks;
+    size_t bytes = 0;
+    template <typename T>
+    T* alloc(size_t count, int fill = 0) {
+        auto m = std::make_unique<DevMem>();
+        size_t b = std::max<size_t>(count * sizeof(T), 16);
+        CUDA_CHECK(cudaMalloc(&m->p, b));
+        CUDA_CHECK(cudaMemset(m->p, fill, b));
+        bytes += b;
+        T* out = (T*)m->p;
+        blocks.push_back(std::move(m));
+        return out;
+    }
+};
+
+using leo_host::ModelSizes;
+
+struct Lane {
+    MemPool mem;
+    LaneState st{};
+    size_t schedule_capacity = 0;
+    uint32_t* schedule = nullptr;
+    float* step_loss = nullptr;
+};
+
+struct ContextRow {
+    unsigned long long key;
+    uint32_t obs;
+    uint32_t pad;
+};
+
+}  // namespace
+
+struct LeoB200Device {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    LeoB200Config cfg{};
+    ModelSizes z{};
+    KernelConsts kc{};
+    int grid = 0;
+    MemPool mem;  // topology, canonical, tables, scratch
+    LaneParams canon{};
+    // Host mirrors of the canonical model's metadata and context tables.
+    std::vector<uint8_t> neuron_type;
+    std::vector<unsigned long long> ctx_keys;
+    std::vector<uint32_t> ctx_obs;
+    std::vector<float> ctx_emb;
+    uint64_t generation = 0, revision = 0, canonical_tick = 0;
+    LeoB200Statistics stats{};
+    std::vector<std::unique_ptr<Lane>> lanes;
+    std::unique_ptr<Lane> replay;
+    LaneState* d_lanes = nullptr;  // device copy of the story lanes' LaneState
+    LaneState* d_replay = nullptr;
+    uint32_t lane_capacity = 0;
+    // merge scratch
+    MergeScratch scratch{};
+    size_t scratch_len = 0;
+    float** d_lane_ptrs = nullptr;       // [max_lanes]
+    uint32_t** d_lane_lists = nullptr;   // [max_lanes]
+    uint32_t* d_lane_counts = nullptr;   // [max_lanes]
+    uint8_t** d_lane_marks = nullptr;    // [max_lanes]
+    // in-flight batch
+    bool batch_open = false;
+    uint32_t batch_lanes = 0;
+    uint32_t batch_steps = 0;
+    uint32_t steps_done = 0;
+    int batch_permission = LEO_B200_TRAINING;
+    bool single_story = false;
+    std::vector<std::vector<uint8_t>> batch_stories;
+    std::vector<LaneScalars> host_scalars;
+    float last_ms = 0.0f;
+};
+
+namespace {
+
+int fail(const std::exception& e) {
+    g_error = e.what();
+    return -1;
+}
+
+uint32_t schedule_word(uint32_t symbol, int target, int permission) {
+    return symbol | ((uint32_t)(target + 1) << 9) | ((uint32_t)permission << 19);
+}
+
+KernelConsts make_consts(LeoB200Device& dev) {
+    KernelConsts kc{};
+    kc.cfg = dev.cfg.abi;
+    kc.strength[LEO_B200_FROZEN] = 0.0f;
+    kc.strength[LEO_B200_PROVISIONAL] = dev.cfg.host.provisional_strength;
+    kc.strength[LEO_B200_TRAINING] = dev.cfg.host.training_strength;
+    kc.strength[LEO_B200_VERIFIED] = dev.cfg.host.verified_strength;
+    kc.end_document_weight = dev.cfg.host.end_document_weight;
+    kc.plasticity_window = dev.cfg.host.plasticity_window;
+    kc.dropout_rate = dev.cfg.host.context_dropout_rate;
+    kc.seed = dev.cfg.host.seed;
+    kc.track_changes = 1;
+    return kc;
+}
+
+void allocate_lane_transient(LeoB200Device& dev, Lane& lane) {
+    const ModelSizes& z = dev.z;
+    MemPool& m = lane.mem;
+    LaneState& st = lane.st;
+    uint32_t maxa = dev.cfg.abi.max_active_global, B = dev.cfg.abi.block_count, npb = dev.cfg.abi.neurons_per_block;
+    st.sc = m.alloc<LaneScalars>(1);
+    st.hot = m.alloc<NeuronHot>(z.n);
+    st.cold = m.alloc<NeuronCold>(z.n);
+    st.branches = m.alloc<float4>(z.n);
+    st.touch_epoch = m.alloc<uint32_t>(z.n);
+    st.touched = m.alloc<uint32_t>(z.n);
+    st.block_cand = m.alloc<unsigned long long>((size_t)B * npb);
+    st.block_cand_count = m.alloc<uint32_t>(B);
+    st.block_cutoff = m.alloc<float>(B);
+    st.ring_src = m.alloc<uint32_t>((size_t)LEO_RING * maxa);
+    st.ring_act = m.alloc<float>((size_t)LEO_RING * maxa);
+    st.ring_val = m.alloc<float>((size_t)LEO_RING * maxa * z.s);
+    st.ev_head = m.alloc<uint32_t>(z.n * 4, 0xff);
+    st.ev_next = m.alloc<uint32_t>(dev.kc.event_capacity);
+    st.ev_val = m.alloc<float>(dev.kc.event_capacity);
+    for (int i = 0; i < 2; ++i) {
+        st.elig[i] = m.alloc<uint4>(z.synapses);
+        st.in_elig[i] = m.alloc<uint4>(z.inputs);
+    }
+    st.traces = m.alloc<Trace>(z.synapses);
+    st.in_traces = m.alloc<Trace>(z.inputs);
+    st.dst_list = m.alloc<uint32_t>(z.n);
+    st.dst_epoch = m.alloc<uint32_t>(z.n);
+    st.signal = m.alloc<float>(z.n);
+    st.errors = m.alloc<float>(LEO_OUTPUT_STRIDE);
+    st.probs = m.alloc<float>(LEO_OUTPUT_STRIDE);
+    st.thr_mark = m.alloc<uint8_t>((z.n + 3) & ~(size_t)3);
+    st.thr_list = m.alloc<uint32_t>(z.n);
+    st.rec_mark = m.alloc<uint8_t>((z.synapses + 3) & ~(size_t)3);
+    st.rec_list = m.alloc<uint32_t>(z.synapses);
+    st.in_mark = m.alloc<uint8_t>((z.inputs + 3) & ~(size_t)3);
+    st.in_list = m.alloc<uint32_t>(z.inputs);
+    st.out_mark = m.alloc<uint8_t>((z.n + 3) & ~(size_t)3);
+    st.out_list = m.alloc<uint32_t>(z.n);
+    st.ctx_mark = m.alloc<uint8_t>((z.ctx + 3) & ~(size_t)3);
+    st.ctx_list = m.alloc<uint32_t>(z.ctx);
+}
+
+void allocate_lane_params(LeoB200Device& dev, Lane& lane) {
+    const ModelSizes& z = dev.z;
+    MemPool& m = lane.mem;
+    LaneParams& p = lane.st.p;
+    p.threshold = m.alloc<float>(z.n);
+    p.rec_weight = m.alloc<float>(z.synapses);
+    p.in_weight = m.alloc<float>(z.inputs);
+    p.out_weight = m.alloc<float>(z.n * LEO_OUTPUT_STRIDE);
+    p.out_bias = m.alloc<float>(LEO_OUTPUT_STRIDE);
+    p.ctx_keys = m.alloc<unsigned long long>(z.ctx);
+    p.ctx_obs = m.alloc<uint32_t>(z.ctx);
+    p.ctx_emb = m.alloc<float>(z.ctx_emb);
+    p.ctx_out = m.alloc<float>(z.ctx_out);
+}
+
+void copy_params(LeoB200Device& dev, const LaneParams& dst, const LaneParams& src) {
+    const ModelSizes& z = dev.z;
+    cudaStream_t s = dev.stream;
+    CUDA_CHECK(cudaMemcpyAsync(dst.threshold, src.threshold, z.n * 4, cudaMemcpyDeviceToDevice, s));
+    CUDA_CHECK(cudaMemcpyAsync(dst.rec_weight, src.rec_weight, z.synapses * 4, cudaMemcpyDeviceToDevice, s));
+    CUDA_CHECK(cudaMemcpyAsync(dst.in_weight, src.in_weight, z.inputs * 4, cudaMemcpyDeviceToDevice, s));
+    CUDA_CHECK(cudaMemcpyAsync(dst.out_weight, src.out_weight, z.n * LEO_OUTPUT_STRIDE * 4, cudaMemcpyDeviceToDevice, s));
+    CUDA_CHECK(cudaMemcpyAsync(dst.out_bias, src.out_bias, LEO_OUTPUT_STRIDE * 4, cudaMemcpyDeviceToDevice, s));
+    CUDA_CHECK(cudaMemcpyAsync(dst.ctx_keys, src.ctx_keys, z.ctx * 8, cudaMemcpyDeviceToDevice, s));
+    CUDA_CHECK(cudaMemcpyAsync(dst.ctx_obs, src.ctx_obs, z.ctx * 4, cudaMemcpyDeviceToDevice, s));
+    CUDA_CHECK(cudaMemcpyAsync(dst.ctx_emb, src.ctx_emb, z.ctx_emb * 4, cudaMemcpyDeviceToDevice, s));
+    CUDA_CHECK(cudaMemcpyAsync(dst.ctx_out, src.ctx_out, z.ctx_out * 4, cudaMemcpyDeviceToDevice, s));
+}
+
+// Transient reset of one lane (runtime.rs:375-435) for a document starting
+// at absolute tick `base_tick`, with per-lane statistics starting from the
+// canonical values (parallel.rs:1115-1137 subtracts them back out).
+void reset_lane(LeoB200Device& dev, Lane& lane, unsigned long long base_tick, uint32_t steps) {
+    const ModelSizes& z = dev.z;
+    cudaStream_t s = dev.stream;
+    LaneState& st = lane.st;
+    CUDA_CHECK(cudaMemsetAsync(st.hot, 0, z.n * sizeof(NeuronHot), s));
+    CUDA_CHECK(cudaMemsetAsync(st.cold, 0, z.n * sizeof(NeuronCold), s));
+    CUDA_CHECK(cudaMemsetAsync(st.branches, 0, z.n * sizeof(float4), s));
+    CUDA_CHECK(cudaMemsetAsync(st.touch_epoch, 0, z.n * 4, s));
+    CUDA_CHECK(cudaMemsetAsync(st.dst_epoch, 0, z.n * 4, s));
+    CUDA_CHECK(cudaMemsetAsync(st.ev_head, 0xff, z.n * 16, s));
+    CUDA_CHECK(cudaMemsetAsync(st.block_cand_count, 0, dev.cfg.abi.block_count * 4, s));
+    CUDA_CHECK(cudaMemsetAsync(st.traces, 0, z.synapses * sizeof(Trace), s));
+    CUDA_CHECK(cudaMemsetAsync(st.in_traces, 0, z.inputs * sizeof(Trace), s));
+    LaneScalars sc{};
+    sc.base_tick = base_tick;
+    sc.steps = steps;
+    sc.loss_sum = dev.stats.training_loss_sum;
+    sc.active_peak = dev.stats.active_neurons_peak;
+    CUDA_CHECK(cudaMemcpyAsync(st.sc, &sc, sizeof(sc), cudaMemcpyHostToDevice, s));
+}
+
+void ensure_schedule(Lane& lane, size_t steps) {
+    if (lane.schedule_capacity >= steps) return;
+    size_t cap = std::max<size_t>(steps, 4096);
+    lane.schedule = lane.mem.alloc<uint32_t>(cap);
+    lane.step_loss = lane.mem.alloc<float>(cap);
+    lane.schedule_capacity = cap;
+    lane.st.schedule = lane.schedule;
+    lane.st.step_loss = lane.step_loss;
+}
+
+void ensure_lanes(LeoB200Device& dev, uint32_t count) {
+    if (count > dev.lane_capacity) throw LeoFailure("story batch exceeds the lanes reserved at open");
+    while (dev.lanes.size() < count) {
+        auto lane = std::make_unique<Lane>();
+        allocate_lane_params(dev, *lane);
+        allocate_lane_transient(dev, *lane);
+        copy_params(dev, lane->st.p, dev.canon);
+        dev.lanes.push_back(std::move(lane));
+    }
+}
+
+// Uploads every resident lane's LaneState; a batch of L stories uses the first L.
+void upload_lane_table(LeoB200Device& dev) {
+    uint32_t count = (uint32_t)dev.lanes.size();
+    std::vector<LaneState> table(count);
+    for (uint32_t i = 0; i < count; ++i) table[i] = dev.lanes[i]->st;
+    if (count)
+        CUDA_CHECK(cudaMemcpyAsync(dev.d_lanes, table.data(), count * sizeof(LaneState), cudaMemcpyHostToDevice, dev.stream));
+    CUDA_CHECK(cudaMemcpyAsync(dev.d_replay, &dev.replay->st, sizeof(LaneState), cudaMemcpyHostToDevice, dev.stream));
+}
+
+// ---------------------------------------------------------------- model I/O
+void upload_model(LeoB200Device& dev, const LeoB200HostModel& m) {
+    const ModelSizes& z = dev.z;
+    std::vector<uint32_t> rec_word(z.synapses), in_word(z.inputs);
+    for (size_t i = 0; i < z.synapses; ++i)
+        rec_word[i] = m.recurrent_target[i] | ((uint32_t)m.recurrent_branch[i] << 24) | ((uint32_t)m.recurrent_delay[i] << 26);
+    for (size_t i = 0; i < z.inputs; ++i) in_word[i] = m.input_target[i] | ((uint32_t)m.input_branch[i] << 24);
+    CUDA_CHECK(cudaMemcpy((void*)dev.kc.topo.rec_word, rec_word.data(), z.synapses * 4, cudaMemcpyHostToDevice));
+    CUDA_CHECK(cudaMemcpy((void*)dev.kc.topo.in_word, in_word.data(), z.inputs * 4, cudaMemcpyHostToDevice));
+    CUDA_CHECK(cudaMemcpy((void*)dev.kc.topo.neuron_type, m.neuron_type, z.n, cudaMemcpyHostToDevice));
+    CUDA_CHECK(cudaMemcpy((void*)dev.kc.topo.excitability, m.excitability, z.n * 4, cudaMemcpyHostToDevice));
+    dev.neuron_type.assign(m.neuron_type, m.neuron_type + z.n);
+    LaneParams& p = dev.canon;
+    CUDA_CHECK(cudaMemcpy(p.threshold, m.threshold, z.n * 4, cudaMemcpyHostToDevice));
+    CUDA_CHECK(cudaMemcpy(p.rec_weight, m.recurrent_weight, z.synapses * 4, cudaMemcpyHostToDevice));
+    CUDA_CHECK(cudaMemcpy(p.in_weight, m.input_weight, z.inputs * 4, cudaMemcpyHostToDevice));
+    std::vector<float> rows(z.n * LEO_OUTPUT_STRIDE, 0.0f);
+    for (size_t o = 0; o < LEO_OUTPUT_CLASSES; ++o)
+        for (size_t n = 0; n < z.n; ++n) rows[n * LEO_OUTPUT_STRIDE + o] = m.output_weight[o * z.n + n];
+    CUDA_CHECK(cudaMemcpy(p.out_weight, rows.data(), rows.size() * 4, cudaMemcpyHostToDevice));
+    std::vector<float> bias(LEO_OUTPUT_STRIDE, 0.0f);
+    std::memcpy(bias.data(), m.output_bias, LEO_OUTPUT_CLASSES * 4);
+    CUDA_CHECK(cudaMemcpy(p.out_bias, bias.data(), LEO_OUTPUT_STRIDE * 4, cudaMemcpyHostToDevice));
+    CUDA_CHECK(cudaMemcpy(p.ctx_keys, m.context_keys, z.ctx * 8, cudaMemcpyHostToDevice));
+    CUDA_CHECK(cudaMemcpy(p.ctx_obs, m.context_observations, z.ctx * 4, cudaMemcpyHostToDevice));
+    CUDA_CHECK(cudaMemcpy(p.ctx_emb, m.context_embeddings, z.ctx_emb * 4, cudaMemcpyHostToDevice));
+    CUDA_CHECK(cudaMemcpy(p.ctx_out, m.context_output_weight, z.ctx_out * 4, cudaMemcpyHostToDevice));
+    dev.ctx_keys.assign(m.context_keys, m.context_keys + z.ctx);
+    dev.ctx_obs.assign(m.context_observations, m.context_observations + z.ctx);
+    dev.ctx_emb.assign(m.context_embeddings, m.context_embeddings + z.ctx_emb);
+    dev.generation = m.generation;
+    dev.revision = m.parameter_revision;
+    dev.stats = m.statistics;
+    for (auto& lane : dev.lanes) copy_params(dev, lane->st.p, dev.canon);
+    CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+}
+
+void download_params(LeoB200Device& dev, const LaneParams& p, LeoB200HostModel& m) {
+    const ModelSizes& z = dev.z;
+    CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+    CUDA_CHECK(cudaMemcpy(m.threshold, p.threshold, z.n * 4, cudaMemcpyDeviceToHost));
+    CUDA_CHECK(cudaMemcpy(m.recurrent_weight, p.rec_weight, z.synapses * 4, cudaMemcpyDeviceToHost));
+    CUDA_CHECK(cudaMemcpy(m.input_weight, p.in_weight, z.inputs * 4, cudaMemcpyDeviceToHost));
+    std::vector<float> rows(z.n * LEO_OUTPUT_STRIDE);
+    CUDA_CHECK(cudaMemcpy(rows.data(), p.out_weight, rows.size() * 4, cudaMemcpyDeviceToHost));
+    for (size_t o = 0; o < LEO_OUTPUT_CLASSES; ++o)
+        for (size_t n = 0; n < z.n; ++n) m.output_weight[o * z.n + n] = rows[n * LEO_OUTPUT_STRIDE + o];
+    CUDA_CHECK(cudaMemcpy(m.output_bias, p.out_bias, LEO_OUTPUT_CLASSES * 4, cudaMemcpyDeviceToHost));
+    CUDA_CHECK(cudaMemcpy(m.context_keys, p.ctx_keys, z.ctx * 8, cudaMemcpyDeviceToHost));
+    CUDA_CHECK(cudaMemcpy(m.context_observations, p.ctx_obs, z.ctx * 4, cudaMemcpyDeviceToHost));
+    CUDA_CHECK(cudaMemcpy(m.context_embeddings, p.ctx_emb, z.ctx_emb * 4, cudaMemcpyDeviceToHost));
+    CUDA_CHECK(cudaMemcpy(m.context_output_weight, p.ctx_out, z.ctx_out * 4, cudaMemcpyDeviceToHost));
+    // Topology is immutable on the device; it is returned from the host copy.
+    std::vector<uint32_t> rec_word(z.synapses), in_word(z.inputs);
+    CUDA_CHECK(cudaMemcpy(rec_word.data(), dev.kc.topo.rec_word, z.synapses * 4, cudaMemcpyDeviceToHost));
+    CUDA_CHECK(cudaMemcpy(in_word.data(), dev.kc.topo.in_word, z.inputs * 4, cudaMemcpyDeviceToHost));
+    for (size_t i = 0; i < z.synapses; ++i) {
+        m.recurrent_target[i] = rec_word[i] & LEO_TARGET_MASK;
+        m.recurrent_branch[i] = (uint8_t)LEO_WORD_BRANCH(rec_word[i]);
+        m.recurrent_delay[i] = (uint8_t)LEO_WORD_DELAY(rec_word[i]);
+    }
+    for (size_t i = 0; i < z.inputs; ++i) {
+        m.input_target[i] = in_word[i] & LEO_TARGET_MASK;
+        m.input_branch[i] = (uint8_t)LEO_WORD_BRANCH(in_word[i]);
+    }
+    std::memcpy(m.neuron_type, dev.neuron_type.data(), z.n);
+    CUDA_CHECK(cudaMemcpy(m.excitability, dev.kc.topo.excitability, z.n * 4, cudaMemcpyDeviceToHost));
+    m.config = dev.cfg;
+}
+
+// ---------------------------------------------------------------- stepping
+void run_steps(LeoB200Device& dev, const LaneState* d_lanes, int lane_count, uint32_t begin, uint32_t end) {
+    for (uint32_t s = begin; s < end; ++s) leo_launch_step(d_lanes, lane_count, s, dev.kc, dev.grid, dev.stream);
+    CUDA_CHECK(cudaGetLastError());
+}
+
+void read_scalars(LeoB200Device& dev, Lane& lane, LaneScalars& out) {
+    CUDA_CHECK(cudaMemcpyAsync(&out, lane.st.sc, sizeof(LaneScalars), cudaMemcpyDeviceToHost, dev.stream));
+    CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+}
+
+void check_error_flag(const LaneScalars& sc) {
+    if (sc.error_flag & (LEO_ERR_NONFINITE_RECURRENT)) throw LeoFailure("non-finite recurrent update rejected");
+    if (sc.error_flag & LEO_ERR_NONFINITE_INPUT) throw LeoFailure("non-finite input update rejected");
+    if (sc.error_flag & LEO_ERR_NONFINITE_INHIBITORY) throw LeoFailure("non-finite inhibitory update rejected");
+    if (sc.error_flag & LEO_ERR_NONFINITE_BIAS) throw LeoFailure("output bias became non-finite");
+    if (sc.error_flag & LEO_ERR_NONFINITE_CONTEXT) throw LeoFailure("non-finite context update rejected");
+    if (sc.error_flag) throw LeoFailure("device step reported an error");
+}
+
+// ---------------------------------------------------------------- context merge (host, parallel.rs:1024-1113)
+__global__ void gather_context_rows_kernel(const uint32_t* __restrict__ slots, uint32_t count,
+                                           const unsigned long long* __restrict__ keys, const uint32_t* __restrict__ obs,
+                                           const float* __restrict__ emb, uint32_t d, ContextRow* rows, float* out_emb) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) {
+        uint32_t slot = slots[i];
+        rows[i].key = keys[slot];
+        rows[i].obs = obs[slot];
+        for (uint32_t k = 0; k < d; ++k) out_emb[(size_t)i * d + k] = emb[(size_t)slot * d + k];
+    }
+}
+
+__global__ void scatter_context_rows_kernel(const uint32_t* __restrict__ slots, uint32_t count,
+                                            const unsigned long long* __restrict__ src_keys,
+                                            const uint32_t* __restrict__ src_obs, const float* __restrict__ src_emb,
+                                            uint32_t d, const LaneState* lanes, int lane_count) {
+    uint32_t total = count * (d + 1);
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        uint32_t r = i / (d + 1), k = i - r * (d + 1);
+        uint32_t slot = slots[r];
+        for (int l = 0; l < lane_count; ++l) {
+            const LaneParams& p = lanes[l].p;
+            if (k == d) {
+                p.ctx_keys[slot] = src_keys[slot];
+                p.ctx_obs[slot] = src_obs[slot];
+            } else {
+                p.ctx_emb[(size_t)slot * d + k] = src_emb[(size_t)slot * d + k];
+            }
+        }
+    }
+}
+
+__global__ void clear_marks_kernel(const uint32_t* __restrict__ list, uint32_t count, uint8_t* marks) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) marks[list[i]] = 0;
+}
+
+struct CtxDelta {
+    uint32_t order;
+    unsigned long long key;
+    std::vector<float> emb_delta;
+    uint32_t obs_inc;
+};
+
+long find_slot(const LeoB200Device& dev, uint32_t order, unsigned long long key) {
+    uint32_t spo = dev.cfg.abi.context_slots_per_order, base = (order - 1) * spo, start = (uint32_t)(key % spo);
+    for (uint32_t off = 0; off < dev.cfg.abi.context_probe_limit; ++off) {
+        uint32_t slot = base + (start + off) % spo;
+        if (dev.ctx_keys[slot] == key) return slot;
+    }
+    return -1;
+}
+
+// model.rs:173-221 on the host mirror; returns the slot and records it.
+uint32_t resolve_allocate(LeoB200Device& dev, uint32_t order, unsigned long long key, std::vector<uint32_t>& touched) {
+    uint32_t spo = dev.cfg.abi.context_slots_per_order, base = (order - 1) * spo, start = (uint32_t)(key % spo);
+    long empty = -1;
+    uint32_t weakest = base + start, weakest_obs = 0xffffffffu;
+    for (uint32_t off = 0; off < dev.cfg.abi.context_probe_limit; ++off) {
+        uint32_t slot = base + (start + off) % spo;
+        if (dev.ctx_keys[slot] == key) return slot;
+        if (dev.ctx_keys[slot] == 0 && empty < 0) empty = slot;
+        if (dev.ctx_obs[slot] < weakest_obs) {
+            weakest_obs = dev.ctx_obs[slot];
+            weakest = slot;
+        }
+    }
+    uint32_t slot = empty >= 0 ? (uint32_t)empty : weakest;
+    if (dev.ctx_keys[slot] != key) {
+        dev.ctx_keys[slot] = key;
+        dev.ctx_obs[slot] = 0;
+        size_t d = dev.z.d;
+        std::fill(dev.ctx_emb.begin() + slot * d, dev.ctx_emb.begin() + (slot + 1) * d, 0.0f);
+        touched.push_back(slot);
+    }
+    return slot;
+}
+
+// Reads each lane's changed context rows, merges them by (order, key) into the
+// host mirror exactly as apply_context_deltas does, uploads the changed
+// canonical rows and syncs every lane.  Returns the number of merged keys.
+size_t merge_context(LeoB200Device& dev, uint32_t lane_count, const std::vector<LaneScalars>& scal) {
+    const ModelSizes& z = dev.z;
+    uint32_t d = (uint32_t)z.d, spo = dev.cfg.abi.context_slots_per_order;
+    std::vector<std::vector<CtxDelta>> per_lane(lane_count);
+    std::vector<uint32_t> lane_slots_union;
+    for (uint32_t l = 0; l < lane_count; ++l) {
+        uint32_t count = scal[l].ctx_changed;
+        if (count == 0) continue;
+        Lane& lane = *dev.lanes[l];
+        std::vector<uint32_t> slots(count);
+        std::vector<ContextRow> rows(count);
+        std::vector<float> emb((size_t)count * d);
+        MemPool tmp;
+        ContextRow* d_rows = tmp.alloc<ContextRow>(count);
+        float* d_emb = tmp.alloc<float>((size_t)count * d);
+        gather_context_rows_kernel<<<std::max(1u, std::min(count / 128 + 1, 1024u)), 128, 0, dev.stream>>>(
+            lane.st.ctx_list, count, lane.st.p.ctx_keys, lane.st.p.ctx_obs, lane.st.p.ctx_emb, d, d_rows, d_emb);
+        CUDA_CHECK(cudaMemcpyAsync(slots.data(), lane.st.ctx_list, count * 4, cudaMemcpyDeviceToHost, dev.stream));
+        CUDA_CHECK(cudaMemcpyAsync(rows.data(), d_rows, count * sizeof(ContextRow), cudaMemcpyDeviceToHost, dev.stream));
+        CUDA_CHECK(cudaMemcpyAsync(emb.data(), d_emb, emb.size() * 4, cudaMemcpyDeviceToHost, dev.stream));
+        clear_marks_kernel<<<std::max(1u, std::min(count / 128 + 1, 1024u)), 128, 0, dev.stream>>>(lane.st.ctx_list, count,
+                                                                                                   lane.st.ctx_mark);
+        CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+        // context_deltas_for_slots (parallel.rs:929-973)
+        for (uint32_t i = 0; i < count; ++i) {
+            lane_slots_union.push_back(slots[i]);
+            unsigned long long key = rows[i].key;
+            if (key == 0) continue;
+            uint32_t order = slots[i] / spo + 1;
+            long bs = find_slot(dev, order, key);
+            uint32_t bobs = bs >= 0 ? dev.ctx_obs[bs] : 0;
+            CtxDelta cd{order, key, std::vector<float>(d), 0};
+            bool changed = false;
+            for (uint32_t k = 0; k < d; ++k) {
+                float before = bs >= 0 ? dev.ctx_emb[(size_t)bs * d + k] : 0.0f;
+                float delta = emb[(size_t)i * d + k] - before;
+                changed |= delta != 0.0f;
+                cd.emb_delta[k] = delta;
+            }
+            cd.obs_inc = rows[i].obs > bobs ? rows[i].obs - bobs : 0;
+            if (changed || cd.obs_inc > 0) per_lane[l].push_back(std::move(cd));
+        }
+        std::sort(per_lane[l].begin(), per_lane[l].end(), [](const CtxDelta& a, const CtxDelta& b) {
+            return a.order != b.order ? a.order < b.order : a.key < b.key;
+        });
+    }
+    // k-way merge by (order, key) in lane order (parallel.rs:1045-1089)
+    struct Merged {
+        uint32_t order;
+        unsigned long long key;
+        std::vector<double> sum;
+        uint64_t obs;
+    };
+    std::vector<Merged> merged;
+    std::vector<size_t> pos(lane_count, 0);
+    for (;;) {
+        bool any = false;
+        std::pair<uint32_t, unsigned long long> next{0, 0};
+        for (uint32_t l = 0; l < lane_count; ++l) {
+            if (pos[l] < per_lane[l].size()) {
+                auto k = std::make_pair(per_lane[l][pos[l]].order, per_lane[l][pos[l]].key);
+                if (!any || k < next) next = k;
+                any = true;
+            }
+        }
+        if (!any) break;
+        Merged m{next.first, next.second, std::vector<double>(d, 0.0), 0};
+        for (uint32_t l = 0; l < lane_count; ++l) {
+            if (pos[l] < per_lane[l].size() && per_lane[l][pos[l]].order == next.first && per_lane[l][pos[l]].key == next.second) {
+                const CtxDelta& u = per_lane[l][pos[l]];
+                for (uint32_t k = 0; k < d; ++k) {
+                    if (!std::isfinite(u.emb_delta[k])) throw LeoFailure("invalid keyed context worker delta");
+                    m.sum[k] += (double)u.emb_delta[k];
+                }
+                m.obs += u.obs_inc;
+                pos[l] += 1;
+            }
+        }
+        merged.push_back(std::move(m));
+    }
+    std::sort(merged.begin(), merged.end(), [](const Merged& a, const Merged& b) {
+        if (a.obs != b.obs) return a.obs > b.obs;
+        if (a.order != b.order) return a.order < b.order;
+        return a.key < b.key;
+    });
+    std::vector<uint32_t> canon_slots;
+    for (auto& u : merged) {
+        uint32_t slot = resolve_allocate(dev, u.order, u.key, canon_slots);
+        for (uint32_t k = 0; k < d; ++k) dev.ctx_emb[(size_t)slot * d + k] += (float)(u.sum[k] / (double)lane_count);
+        uint64_t add = std::min<uint64_t>(u.obs, 0xffffffffull);
+        dev.ctx_obs[slot] = (uint32_t)std::min<uint64_t>((uint64_t)dev.ctx_obs[slot] + add, 0xffffffffull);
+        canon_slots.push_back(slot);
+    }
+    // projection (parallel.rs:1226-1233) and validation (parallel.rs:1317-1334)
+    float lo = dev.cfg.abi.weight_min, hi = dev.cfg.abi.weight_max;
+    for (uint32_t l = 0; l < lane_count; ++l) {
+        for (auto& u : per_lane[l]) {
+            long slot = find_slot(dev, u.order, u.key);
+            if (slot < 0) continue;
+            for (uint32_t k = 0; k < d; ++k) {
+                float& v = dev.ctx_emb[(size_t)slot * d + k];
+                v = std::min(std::max(v, lo), hi);
+                if (!std::isfinite(v)) throw LeoFailure("merged context embedding violates canonical parameter bounds");
+            }
+        }
+    }
+    // upload changed canonical rows, then sync every lane's changed and canonical-changed slots
+    std::vector<uint32_t> sync = canon_slots;
+    sync.insert(sync.end(), lane_slots_union.begin(), lane_slots_union.end());
+    std::sort(sync.begin(), sync.end());
+    sync.erase(std::unique(sync.begin(), sync.end()), sync.end());
+    if (!sync.empty()) {
+        for (uint32_t slot : sync) {
+            CUDA_CHECK(cudaMemcpyAsync(dev.canon.ctx_keys + slot, &dev.ctx_keys[slot], 8, cudaMemcpyHostToDevice, dev.stream));
+            CUDA_CHECK(cudaMemcpyAsync(dev.canon.ctx_obs + slot, &dev.ctx_obs[slot], 4, cudaMemcpyHostToDevice, dev.stream));
+            CUDA_CHECK(cudaMemcpyAsync(dev.canon.ctx_emb + (size_t)slot * d, &dev.ctx_emb[(size_t)slot * d], d * 4,
+                                       cudaMemcpyHostToDevice, dev.stream));
+        }
+        MemPool tmp;
+        uint32_t* d_slots = tmp.alloc<uint32_t>(sync.size());
+        CUDA_CHECK(cudaMemcpyAsync(d_slots, sync.data(), sync.size() * 4, cudaMemcpyHostToDevice, dev.stream));
+        uint32_t total = (uint32_t)sync.size() * (d + 1);
+        scatter_context_rows_kernel<<<std::max(1u, std::min(total / 256 + 1, 4096u)), 256, 0, dev.stream>>>(
+            d_slots, (uint32_t)sync.size(), dev.canon.ctx_keys, dev.canon.ctx_obs, dev.canon.ctx_emb, d, dev.d_lanes,
+            (int)dev.lanes.size());
+        CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+    }
+    return merged.size();
+}
+
+// ---------------------------------------------------------------- fixed tensor merge
+struct TensorSpec {
+    float* LaneParams::*member;
+    uint32_t* LaneState::*list;
+    uint8_t* LaneState::*marks;
+    uint32_t LaneScalars::*count;
+    uint32_t row, row_len, length, kind;
+};
+
+size_t merge_fixed(LeoB200Device& dev, uint32_t lane_count, const std::vector<LaneScalars>& scal) {
+    const ModelSizes& z = dev.z;
+    const TensorSpec specs[] = {
+        {&LaneParams::threshold, &LaneState::thr_list, &LaneState::thr_mark, &LaneScalars::thr_changed, 1, 1,
+         (uint32_t)z.n, LEO_PROJECT_THRESHOLD},
+        {&LaneParams::rec_weight, &LaneState::rec_list, &LaneState::rec_mark, &LaneScalars::rec_changed, 1, 1,
+         (uint32_t)z.synapses, LEO_PROJECT_RECURRENT},
+        {&LaneParams::in_weight, &LaneState::in_list, &LaneState::in_mark, &LaneScalars::in_changed, 1, 1,
+         (uint32_t)z.inputs, LEO_PROJECT_INPUT},
+        {&LaneParams::out_weight, &LaneState::out_list, &LaneState::out_mark, &LaneScalars::out_changed,
+         LEO_OUTPUT_STRIDE, LEO_OUTPUT_CLASSES, (uint32_t)z.n, LEO_PROJECT_WEIGHT},
+        {&LaneParams::out_bias, nullptr, nullptr, nullptr, 1, 1, LEO_OUTPUT_CLASSES, LEO_PROJECT_NONE},
+        {&LaneParams::ctx_out, nullptr, nullptr, nullptr, 1, 1, (uint32_t)z.ctx_out, LEO_PROJECT_WEIGHT},
+    };
+    uint32_t zero = 0;
+    CUDA_CHECK(cudaMemcpyAsync(dev.scratch.updates, &zero, 4, cudaMemcpyHostToDevice, dev.stream));
+    const uint32_t resident = (uint32_t)dev.lanes.size();
+    for (const TensorSpec& t : specs) {
+        std::vector<float*> ptrs(resident);
+        std::vector<uint32_t*> lists(lane_count);
+        std::vector<uint32_t> counts(lane_count);
+        std::vector<uint8_t*> marks(lane_count);
+        for (uint32_t l = 0; l < resident; ++l) ptrs[l] = dev.lanes[l]->st.p.*t.member;
+        for (uint32_t l = 0; l < lane_count; ++l) {
+            LaneState& st = dev.lanes[l]->st;
+            lists[l] = t.list ? st.*t.list : nullptr;
+            counts[l] = t.count ? scal[l].*t.count : t.length;
+            marks[l] = t.marks ? st.*t.marks : nullptr;
+        }
+        CUDA_CHECK(cudaMemcpyAsync(dev.d_lane_ptrs, ptrs.data(), resident * sizeof(float*), cudaMemcpyHostToDevice, dev.stream));
+        CUDA_CHECK(cudaMemcpyAsync(dev.d_lane_lists, lists.data(), lane_count * sizeof(uint32_t*), cudaMemcpyHostToDevice, dev.stream));
+        CUDA_CHECK(cudaMemcpyAsync(dev.d_lane_counts, counts.data(), lane_count * 4, cudaMemcpyHostToDevice, dev.stream));
+        CUDA_CHECK(cudaMemcpyAsync(dev.d_lane_marks, marks.data(), lane_count * sizeof(uint8_t*), cudaMemcpyHostToDevice, dev.stream));
+        MergeTensor mt{};
+        mt.lane_values = dev.d_lane_ptrs;
+        mt.base = dev.canon.*t.member;
+        mt.lane_lists = t.list ? dev.d_lane_lists : nullptr;
+        mt.lane_counts = dev.d_lane_counts;
+        mt.lane_marks = t.marks ? dev.d_lane_marks : nullptr;
+        mt.row = t.row;
+        mt.row_len = t.row_len;
+        mt.length = t.length;
+        mt.kind = t.kind;
+        leo_launch_merge_tensor(mt, dev.scratch, (int)lane_count, (int)resident, dev.cfg.abi.weight_min, dev.cfg.abi.weight_max,
+                                dev.kc.topo.neuron_type, (uint32_t)z.s, dev.grid, dev.stream);
+        // Each launch sequence reuses the pointer tables: wait before rewriting them.
+        CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+    }
+    uint32_t updates = 0, err = 0;
+    CUDA_CHECK(cudaMemcpy(&updates, dev.scratch.updates, 4, cudaMemcpyDeviceToHost));
+    CUDA_CHECK(cudaMemcpy(&err, dev.scratch.error_flag, 4, cudaMemcpyDeviceToHost));
+    if (err) throw LeoFailure("merged parameter became non-finite");
+    return updates;
+}
+
+// ---------------------------------------------------------------- replay sync
+// Writes canonical values at the replay lane's changed indices into every
+// story lane (fused multi-target scatter) and clears the replay marks.
+void sync_replay_changes(LeoB200Device& dev, const LaneScalars& rs) {
+    const ModelSizes& z = dev.z;
+    const uint32_t lane_count = (uint32_t)dev.lanes.size();
+    upload_lane_table(dev);
+    Lane& rl = *dev.replay;
+    // Fixed tensors: reuse the merge kernels with the replay list as the only
+    // "lane": every lane value at those indices then equals the canonical.
+    struct Item {
+        float* LaneParams::*member;
+        uint32_t* list;
+        uint8_t* marks;
+        uint32_t count, row, row_len;
+    };
+    const Item items[] = {
+        {&LaneParams::threshold, rl.st.thr_list, rl.st.thr_mark, rs.thr_changed, 1, 1},
+        {&LaneParams::rec_weight, rl.st.rec_list, rl.st.rec_mark, rs.rec_changed, 1, 1},
+        {&LaneParams::in_weight, rl.st.in_list, rl.st.in_mark, rs.in_changed, 1, 1},
+        {&LaneParams::out_weight, rl.st.out_list, rl.st.out_mark, rs.out_changed, LEO_OUTPUT_STRIDE, LEO_OUTPUT_CLASSES},
+    };
+    for (const Item& it : items) {
+        if (it.count == 0) continue;
+        std::vector<float*> ptrs(lane_count);
+        for (uint32_t l = 0; l < lane_count; ++l) ptrs[l] = dev.lanes[l]->st.p.*it.member;
+        CUDA_CHECK(cudaMemcpyAsync(dev.d_lane_ptrs, ptrs.data(), lane_count * sizeof(float*), cudaMemcpyHostToDevice, dev.stream));
+        leo_launch_scatter_rows(dev.d_lane_ptrs, (int)lane_count, dev.canon.*it.member, it.list, it.count, it.row,
+                                it.row_len, dev.grid, dev.stream);
+        clear_marks_kernel<<<std::max(1u, std::min(it.count / 256 + 1, 4096u)), 256, 0, dev.stream>>>(it.list, it.count,
+                                                                                                      it.marks);
+        CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+    }
+    // Dense tensors: bias and context output weights.
+    for (uint32_t l = 0; l < lane_count; ++l) {
+        LaneParams& p = dev.lanes[l]->st.p;
+        if (rs.bias_dirty)
+            CUDA_CHECK(cudaMemcpyAsync(p.out_bias, dev.canon.out_bias, LEO_OUTPUT_STRIDE * 4, cudaMemcpyDeviceToDevice, dev.stream));
+        if (rs.ctx_out_dirty)
+            CUDA_CHECK(cudaMemcpyAsync(p.ctx_out, dev.canon.ctx_out, z.ctx_out * 4, cudaMemcpyDeviceToDevice, dev.stream));
+    }
+    // Context rows: refresh the host mirror and scatter the canonical rows.
+    if (rs.ctx_changed) {
+        std::vector<uint32_t> slots(rs.ctx_changed);
+        CUDA_CHECK(cudaMemcpy(slots.data(), rl.st.ctx_list, slots.size() * 4, cudaMemcpyDeviceToHost));
+        // Allocation without a learning step cannot happen on a training
+        // replay step, so the changed list covers every slot replay rewrote.
+        for (uint32_t slot : slots) {
+            CUDA_CHECK(cudaMemcpy(&dev.ctx_keys[slot], dev.canon.ctx_keys + slot, 8, cudaMemcpyDeviceToHost));
+            CUDA_CHECK(cudaMemcpy(&dev.ctx_obs[slot], dev.canon.ctx_obs + slot, 4, cudaMemcpyDeviceToHost));
+            CUDA_CHECK(cudaMemcpy(&dev.ctx_emb[(size_t)slot * z.d], dev.canon.ctx_emb + (size_t)slot * z.d, z.d * 4,
+                                  cudaMemcpyDeviceToHost));
+        }
+        uint32_t d = (uint32_t)z.d, total = (uint32_t)slots.size() * (d + 1);
+        if (lane_count > 0)
+            scatter_context_rows_kernel<<<std::max(1u, std::min(total / 256 + 1, 4096u)), 256, 0, dev.stream>>>(
+                rl.st.ctx_list, (uint32_t)slots.size(), dev.canon.ctx_keys, dev.canon.ctx_obs, dev.canon.ctx_emb, d,
+                dev.d_lanes, (int)lane_count);
+        clear_marks_kernel<<<std::max(1u, std::min((uint32_t)slots.size() / 256 + 1, 4096u)), 256, 0, dev.stream>>>(
+            rl.st.ctx_list, (uint32_t)slots.size(), rl.st.ctx_mark);
+        CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+    }
+}
+
+// ---------------------------------------------------------------- replay (training.rs:1782-1955)
+struct ReplayRange {
+    size_t start, end;
+};
+
+std::vector<ReplayRange> select_replay_ranges(const std::vector<float>& losses, float fraction, size_t segment) {
+    std::vector<ReplayRange> selected;
+    if (losses.empty() || !std::isfinite(fraction) || fraction <= 0.0f || segment == 0) return selected;
+    size_t budget = (size_t)std::max(std::ceil((double)losses.size() * (double)std::min(fraction, 1.0f)), 1.0);
+    std::vector<std::pair<size_t, float>> order;
+    for (size_t i = 0; i < losses.size(); ++i) order.push_back({i, losses[i]});
+    auto total_key = [](float f) {
+        int32_t b;
+        std::memcpy(&b, &f, 4);
+        return b ^ (int32_t)(((uint32_t)(b >> 31)) >> 1);
+    };
+    std::sort(order.begin(), order.end(), [&](const auto& l, const auto& r) {
+        int32_t a = total_key(l.second), b = total_key(r.second);
+        return a != b ? a > b : l.first < r.first;
+    });
+    size_t picked = 0;
+    for (auto& [position, loss] : order) {
+        if (picked >= budget) break;
+        if (!std::isfinite(loss) || loss <= 0.0f) continue;
+        size_t width = std::min(std::min(segment, budget - picked), losses.size());
+        size_t start = position >= width / 2 ? position - width / 2 : 0;
+        size_t end = std::min(start + width, losses.size());
+        start = end >= width ? end - width : 0;
+        bool overlap = false;
+        for (auto& e : selected)
+            if (e.start < end && start < e.end) overlap = true;
+        if (overlap) continue;
+        picked += end - start;
+        selected.push_back({start, end});
+    }
+    std::sort(selected.begin(), selected.end(), [](const ReplayRange& a, const ReplayRange& b) { return a.start < b.start; });
+    return selected;
+}
+
+// Runs one schedule on the replay lane (canonical parameters) from a fresh
+// transient state at the canonical tick, then folds its statistics into the
+// canonical statistics.
+void run_canonical_schedule(LeoB200Device& dev, const std::vector<uint32_t>& schedule, LaneScalars& out) {
+    Lane& rl = *dev.replay;
+    ensure_schedule(rl, schedule.size());
+    CUDA_CHECK(cudaMemcpyAsync(rl.schedule, schedule.data(), schedule.size() * 4, cudaMemcpyHostToDevice, dev.stream));
+    reset_lane(dev, rl, dev.canonical_tick, (uint32_t)schedule.size());
+    CUDA_CHECK(cudaMemcpyAsync(dev.d_replay, &rl.st, sizeof(LaneState), cudaMemcpyHostToDevice, dev.stream));
+    // keep the replay lane's changed marks across schedules: carry counts over
+    LaneScalars carry{};
+    CUDA_CHECK(cudaMemcpyAsync(&carry, rl.st.sc, sizeof(carry), cudaMemcpyDeviceToHost, dev.stream));
+    CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+    carry.thr_changed = out.thr_changed;
+    carry.rec_changed = out.rec_changed;
+    carry.in_changed = out.in_changed;
+    carry.out_changed = out.out_changed;
+    carry.ctx_changed = out.ctx_changed;
+    carry.bias_dirty = out.bias_dirty;
+    carry.ctx_out_dirty = out.ctx_out_dirty;
+    CUDA_CHECK(cudaMemcpyAsync(rl.st.sc, &carry, sizeof(carry), cudaMemcpyHostToDevice, dev.stream));
+    run_steps(dev, dev.d_replay, 1, 0, (uint32_t)schedule.size());
+    LaneScalars sc;
+    read_scalars(dev, rl, sc);
+    check_error_flag(sc);
+    dev.canonical_tick += schedule.size();
+    dev.revision += sc.revision_increment;
+    dev.stats.processed_bytes += sc.processed_bytes;
+    dev.stats.training_loss_sum = sc.loss_sum;
+    dev.stats.training_targets += sc.targets;
+    dev.stats.active_neurons_sum += sc.active_sum;
+    dev.stats.active_neurons_peak = std::max<uint64_t>(dev.stats.active_neurons_peak, sc.active_peak);
+    dev.stats.synaptic_events += sc.synaptic_events;
+    dev.stats.numerical_rejections += sc.numerical_rejections;
+    dev.stats.persistent_ticks += sc.persistent_ticks;
+    out = sc;
+}
+
+void replay_story(LeoB200Device& dev, const std::vector<uint8_t>& story, const std::vector<float>& losses,
+                  int permission, LaneScalars& changes, LeoB200BatchReport* report) {
+    auto ranges = select_replay_ranges(losses, dev.cfg.host.replay_fraction, dev.cfg.host.replay_segment_bytes);
+    size_t len = story.size();
+    for (const ReplayRange& range : ranges) {
+        if (len == 0 || range.start >= range.end || range.start > len) continue;
+        size_t end = std::min(range.end, len + 1);
+        std::vector<uint32_t> sched;
+        size_t next = range.start;
+        if (next > 0) {
+            sched.push_back(schedule_word(LEO_B200_BEGIN_DOCUMENT, -1, LEO_B200_FROZEN));
+            for (size_t i = 0; i + 1 < next; ++i) sched.push_back(schedule_word(story[i], -1, LEO_B200_FROZEN));
+            if (report) report->replay_prefix_steps += next;
+        }
+        if (next == 0) {
+            sched.push_back(schedule_word(LEO_B200_BEGIN_DOCUMENT, story[0], permission));
+            next = 1;
+            if (report) report->replay_steps += 1;
+        }
+        for (size_t p = next; p < end; ++p) {
+            int target = p < len ? story[p] : (int)LEO_B200_END_DOCUMENT;
+            sched.push_back(schedule_word(story[p - 1], target, permission));
+            if (report) report->replay_steps += 1;
+        }
+        run_canonical_schedule(dev, sched, changes);
+    }
+    if (report) report->replay_segments += ranges.size();
+}
+
+void story_schedule(const std::vector<uint8_t>& story, int permission, std::vector<uint32_t>& out) {
+    out.clear();
+    size_t len = story.size();
+    for (size_t s = 0; s <= len; ++s) {
+        uint32_t symbol = s == 0 ? LEO_B200_BEGIN_DOCUMENT : story[s - 1];
+        int target = s < len ? story[s] : (int)LEO_B200_END_DOCUMENT;
+        out.push_back(schedule_word(symbol, target, permission));
+    }
+}
+
+// ---------------------------------------------------------------- batch
+void batch_begin(LeoB200Device& dev, const uint8_t* bytes, const uint64_t* offsets, uint32_t stories, int permission) {
+    if (dev.batch_open) throw LeoFailure("a story batch is already in progress");
+    if (stories == 0) throw LeoFailure("training batch cannot be empty");
+    if (permission < 0 || permission > 3) throw LeoFailure("invalid permission");
+    dev.batch_stories.assign(stories, {});
+    for (uint32_t i = 0; i < stories; ++i)
+        dev.batch_stories[i].assign(bytes + offsets[i], bytes + offsets[i + 1]);
+    dev.batch_permission = permission;
+    dev.single_story = stories == 1;
+    dev.steps_done = 0;
+    dev.batch_steps = 0;
+    std::vector<uint32_t> sched;
+    if (dev.single_story) {
+        // training.rs:1548-1581: one story trains the canonical runtime directly.
+        story_schedule(dev.batch_stories[0], permission, sched);
+        Lane& rl = *dev.replay;
+        ensure_schedule(rl, sched.size());
+        CUDA_CHECK(cudaMemcpyAsync(rl.schedule, sched.data(), sched.size() * 4, cudaMemcpyHostToDevice, dev.stream));
+        reset_lane(dev, rl, dev.canonical_tick, (uint32_t)(dev.batch_stories[0].empty() ? 0 : sched.size()));
+        CUDA_CHECK(cudaMemcpyAsync(dev.d_replay, &rl.st, sizeof(LaneState), cudaMemcpyHostToDevice, dev.stream));
+        dev.batch_lanes = 0;
+        dev.batch_steps = dev.batch_stories[0].empty() ? 0 : (uint32_t)sched.size();
+    } else {
+        ensure_lanes(dev, stories);
+        for (uint32_t i = 0; i < stories; ++i) {
+            Lane& lane = *dev.lanes[i];
+            const auto& story = dev.batch_stories[i];
+            story_schedule(story, permission, sched);
+            uint32_t steps = story.empty() ? 0 : (uint32_t)sched.size();
+            ensure_schedule(lane, sched.size());
+            CUDA_CHECK(cudaMemcpyAsync(lane.schedule, sched.data(), sched.size() * 4, cudaMemcpyHostToDevice, dev.stream));
+            // Forked workers start a fresh runtime at tick 0 (backend.rs:486-488).
+            reset_lane(dev, lane, 0ull, steps);
+            dev.batch_steps = std::max(dev.batch_steps, steps);
+        }
+        dev.batch_lanes = stories;
+        upload_lane_table(dev);
+    }
+    CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+    dev.batch_open = true;
+}
+
+void batch_steps(LeoB200Device& dev, uint32_t count) {
+    if (!dev.batch_open) throw LeoFailure("no story batch in progress");
+    uint32_t end = std::min(dev.batch_steps, dev.steps_done + count);
+    if (dev.single_story)
+        run_steps(dev, dev.d_replay, 1, dev.steps_done, end);
+    else
+        run_steps(dev, dev.d_lanes, (int)dev.batch_lanes, dev.steps_done, end);
+    dev.steps_done = end;
+}
+
+void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySummary* summaries, float* losses_out) {
+    if (!dev.batch_open) throw LeoFailure("no story batch in progress");
+    batch_steps(dev, dev.batch_steps);
+    CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+    dev.batch_open = false;
+    LeoB200BatchReport rep{};
+    uint32_t stories = (uint32_t)dev.batch_stories.size();
+    rep.stories = stories;
+    std::vector<std::vector<float>> losses(stories);
+    LaneScalars replay_changes{};
+    if (dev.single_story) {
+        const auto& story = dev.batch_stories[0];
+        LaneScalars sc;
+        read_scalars(dev, *dev.replay, sc);
+        check_error_flag(sc);
+        if (!story.empty()) {
+            losses[0].resize(story.size() + 1);
+            CUDA_CHECK(cudaMemcpy(losses[0].data(), dev.replay->step_loss, losses[0].size() * 4, cudaMemcpyDeviceToHost));
+            dev.canonical_tick += story.size() + 1;
+            dev.revision += sc.revision_increment;
+            dev.stats.processed_bytes += sc.processed_bytes;
+            dev.stats.processed_stories += 1;
+            dev.stats.training_loss_sum = sc.loss_sum;
+            dev.stats.training_targets += sc.targets;
+            dev.stats.active_neurons_sum += sc.active_sum;
+            dev.stats.active_neurons_peak = std::max<uint64_t>(dev.stats.active_neurons_peak, sc.active_peak);
+            dev.stats.synaptic_events += sc.synaptic_events;
+            dev.stats.numerical_rejections += sc.numerical_rejections;
+            dev.stats.persistent_ticks += sc.persistent_ticks;
+            if (summaries) {
+                summaries[0].training_loss_sum = 0.0;
+                for (float v : losses[0]) summaries[0].training_loss_sum += (double)v;
+                summaries[0].training_targets = sc.targets;
+                summaries[0].active_neurons_sum = sc.active_sum;
+                summaries[0].active_neurons_peak = sc.active_peak;
+                summaries[0].synaptic_events = sc.synaptic_events;
+                summaries[0].context_applied_steps = sc.context_applied_steps;
+            }
+        }
+        replay_changes = sc;
+        rep.workers = 1;
+        rep.targets = losses[0].size();
+        rep.input_bytes = story.size();
+        double sum = 0.0;
+        for (float v : losses[0]) sum += (double)v;
+        rep.mean_loss = sum / (double)std::max<size_t>(losses[0].size(), 1);
+        replay_story(dev, story, losses[0], dev.batch_permission, replay_changes, &rep);
+        sync_replay_changes(dev, replay_changes);
+    } else {
+        uint32_t L = dev.batch_lanes;
+        std::vector<LaneScalars> scal(L);
+        for (uint32_t l = 0; l < L; ++l) {
+            read_scalars(dev, *dev.lanes[l], scal[l]);
+            check_error_flag(scal[l]);
+            const auto& story = dev.batch_stories[l];
+            if (!story.empty()) {
+                losses[l].resize(story.size() + 1);
+                CUDA_CHECK(cudaMemcpy(losses[l].data(), dev.lanes[l]->step_loss, losses[l].size() * 4, cudaMemcpyDeviceToHost));
+            }
+            rep.input_bytes += story.size();
+        }
+        // apply_mean_deltas (parallel.rs:715-798): fixed tensors on the device,
+        // keyed context on the host mirror, statistics and revision here.
+        double canon_loss = dev.stats.training_loss_sum;
+        rep.fixed_parameter_updates = merge_fixed(dev, L, scal);
+        rep.context_keys = merge_context(dev, L, scal);
+        for (uint32_t l = 0; l < L; ++l) {
+            const LaneScalars& sc = scal[l];
+            const auto& story = dev.batch_stories[l];
+            dev.stats.processed_bytes += sc.processed_bytes;
+            dev.stats.processed_stories += story.empty() ? 0 : 1;
+            dev.stats.training_loss_sum += sc.loss_sum - canon_loss;
+            dev.stats.training_targets += sc.targets;
+            dev.stats.active_neurons_sum += sc.active_sum;
+            dev.stats.active_neurons_peak = std::max<uint64_t>(dev.stats.active_neurons_peak, sc.active_peak);
+            dev.stats.synaptic_events += sc.synaptic_events;
+            dev.stats.numerical_rejections += sc.numerical_rejections;
+            dev.stats.persistent_ticks += sc.persistent_ticks;
+            dev.revision += sc.revision_increment;
+            if (summaries) {
+                summaries[l].training_loss_sum = 0.0;
+                for (float v : losses[l]) summaries[l].training_loss_sum += (double)v;
+                summaries[l].training_targets = sc.targets;
+                summaries[l].active_neurons_sum = sc.active_sum;
+                summaries[l].active_neurons_peak = sc.active_peak;
+                summaries[l].synaptic_events = sc.synaptic_events;
+                summaries[l].context_applied_steps = sc.context_applied_steps;
+            }
+        }
+        rep.workers = L;
+        double weighted = 0.0;
+        size_t targets = 0;
+        for (uint32_t l = 0; l < L; ++l) {
+            double sum = 0.0;
+            for (float v : losses[l]) sum += (double)v;
+            double mean = sum / (double)std::max<size_t>(losses[l].size(), 1);
+            weighted += mean * (double)losses[l].size();
+            targets += losses[l].size();
+        }
+        rep.targets = targets;
+        rep.mean_loss = weighted / (double)std::max<size_t>(targets, 1);
+        // Serial canonical replay (training.rs:1709-1711), then one sync of the
+        // replay's changed rows into every lane (training.rs:1644-1649).
+        for (uint32_t l = 0; l < L; ++l)
+            replay_story(dev, dev.batch_stories[l], losses[l], dev.batch_permission, replay_changes, &rep);
+        sync_replay_changes(dev, replay_changes);
+    }
+    if (losses_out) {
+        size_t k = 0;
+        for (auto& l : losses)
+            for (float v : l) losses_out[k++] = v;
+    }
+    if (report) *report = rep;
+}
+
+}  // namespace
+
+// ============================================================================ C ABI
+extern "C" {
+
+const char* leo_b200_last_error(void) { return g_error.c_str(); }
+uint32_t leo_b200_abi_version(void) { return LEO_CUDA_ABI_VERSION; }
+
+int leo_b200_config_validate(const LeoB200Config* cfg) {
+    const char* e = leo_host::validate_config(*cfg);
+    if (*e) {
+        g_error = e;
+        return -1;
+    }
+    return 0;
+}
+
+int leo_b200_model_initialize(const LeoB200Config* cfg, int topology, LeoB200HostModel* model) {
+    try {
+        const char* e = leo_host::validate_config(*cfg);
+        if (*e) throw LeoFailure(e);
+        if (topology < 0 || topology > 2) throw LeoFailure("unknown topology");
+        model->config = *cfg;
+        leo_host::initialize_model(*cfg, topology, *model);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_model_validate(const LeoB200HostModel* model) {
+    const char* e = leo_host::validate_model(*model);
+    if (*e) {
+        g_error = e;
+        return -1;
+    }
+    return 0;
+}
+
+int leo_b200_training_state_hash(const LeoB200HostModel* model, uint8_t out[32]) {
+    leo_host::training_state_hash(*model, out);
+    return 0;
+}
+
+int leo_b200_open(int device, const LeoB200HostModel* canonical, uint32_t max_lanes, LeoB200Device** out) {
+    try {
+        const char* e = leo_host::validate_model(*canonical);
+        if (*e) throw LeoFailure(e);
+        if (max_lanes == 0 || max_lanes > 1024) throw LeoFailure("max_lanes must be in 1..=1024");
+        auto dev = std::make_unique<LeoB200Device>();
+        dev->device = device;
+        CUDA_CHECK(cudaSetDevice(device));
+        cudaDeviceProp prop;
+        CUDA_CHECK(cudaGetDeviceProperties(&prop, device));
+        if (prop.major < 10) throw LeoFailure("leo_b200 requires an sm_100 (Blackwell) device");
+        CUDA_CHECK(cudaStreamCreateWithFlags(&dev->stream, cudaStreamNonBlocking));
+        dev->cfg = canonical->config;
+        dev->z = leo_host::sizes_of(dev->cfg);
+        dev->kc = make_consts(*dev);
+        const ModelSizes& z = dev->z;
+        DeviceTopology& t = dev->kc.topo;
+        t.n = (uint32_t)z.n;
+        t.s = (uint32_t)z.s;
+        t.f = (uint32_t)z.f;
+        t.d = (uint32_t)z.d;
+        t.k = dev->cfg.abi.context_max_order;
+        t.spo = dev->cfg.abi.context_slots_per_order;
+        t.ctx_slots = (uint32_t)z.ctx;
+        t.blocks = dev->cfg.abi.block_count;
+        t.npb = dev->cfg.abi.neurons_per_block;
+        t.keep = dev->cfg.abi.max_active_per_block;
+        t.max_active = dev->cfg.abi.max_active_global;
+        // A tick's winners are bounded by the block capacity as well as the global cap.
+        uint32_t winners = std::min<uint32_t>(t.blocks * t.keep, t.max_active);
+        t.max_active = std::max<uint32_t>(t.max_active, winners);
+        t.rec_word = dev->mem.alloc<uint32_t>(z.synapses);
+        t.in_word = dev->mem.alloc<uint32_t>(z.inputs);
+        t.neuron_type = dev->mem.alloc<uint8_t>(z.n);
+        t.excitability = dev->mem.alloc<float>(z.n);
+        dev->kc.event_capacity = 4u * t.max_active * t.s + t.f;
+        // libm exception tables (leo_math.cuh)
+        uint32_t* ek = dev->mem.alloc<uint32_t>(LEO_EXP_EXCEPTIONS);
+        uint32_t* ev = dev->mem.alloc<uint32_t>(LEO_EXP_EXCEPTIONS);
+        uint32_t* lk = dev->mem.alloc<uint32_t>(LEO_LOG_EXCEPTIONS);
+        uint32_t* lv = dev->mem.alloc<uint32_t>(LEO_LOG_EXCEPTIONS);
+        CUDA_CHECK(cudaMemcpy(ek, leo_exp_exception_keys, sizeof(leo_exp_exception_keys), cudaMemcpyHostToDevice));
+        CUDA_CHECK(cudaMemcpy(ev, leo_exp_exception_values, sizeof(leo_exp_exception_values), cudaMemcpyHostToDevice));
+        CUDA_CHECK(cudaMemcpy(lk, leo_log_exception_keys, sizeof(leo_log_exception_keys), cudaMemcpyHostToDevice));
+        CUDA_CHECK(cudaMemcpy(lv, leo_log_exception_values, sizeof(leo_log_exception_values), cudaMemcpyHostToDevice));
+        dev->kc.exp_keys = ek;
+        dev->kc.exp_values = ev;
+        dev->kc.log_keys = lk;
+        dev->kc.log_values = lv;
+        dev->kc.exp_count = LEO_EXP_EXCEPTIONS;
+        dev->kc.log_count = LEO_LOG_EXCEPTIONS;
+        // canonical parameters
+        LaneParams& p = dev->canon;
+        p.threshold = dev->mem.alloc<float>(z.n);
+        p.rec_weight = dev->mem.alloc<float>(z.synapses);
+        p.in_weight = dev->mem.alloc<float>(z.inputs);
+        p.out_weight = dev->mem.alloc<float>(z.n * LEO_OUTPUT_STRIDE);
+        p.out_bias = dev->mem.alloc<float>(LEO_OUTPUT_STRIDE);
+        p.ctx_keys = dev->mem.alloc<unsigned long long>(z.ctx);
+        p.ctx_obs = dev->mem.alloc<uint32_t>(z.ctx);
+        p.ctx_emb = dev->mem.alloc<float>(z.ctx_emb);
+        p.ctx_out = dev->mem.alloc<float>(z.ctx_out);
+        // merge scratch sized for the largest tensor
+        size_t longest = std::max({z.n, z.synapses, z.inputs, z.ctx_out, (size_t)LEO_OUTPUT_STRIDE});
+        dev->scratch.union_mark = dev->mem.alloc<uint8_t>((longest + 3) & ~(size_t)3);
+        dev->scratch.union_list = dev->mem.alloc<uint32_t>(longest);
+        dev->scratch.union_count = dev->mem.alloc<uint32_t>(1);
+        dev->scratch.updates = dev->mem.alloc<uint32_t>(1);
+        dev->scratch.error_flag = dev->mem.alloc<uint32_t>(1);
+        dev->lane_capacity = max_lanes;
+        dev->d_lane_ptrs = dev->mem.alloc<float*>(max_lanes);
+        dev->d_lane_lists = dev->mem.alloc<uint32_t*>(max_lanes);
+        dev->d_lane_counts = dev->mem.alloc<uint32_t>(max_lanes);
+        dev->d_lane_marks = dev->mem.alloc<uint8_t*>(max_lanes);
+        dev->d_lanes = dev->mem.alloc<LaneState>(max_lanes);
+        dev->d_replay = dev->mem.alloc<LaneState>(1);
+        // replay lane: canonical parameters, private transient state
+        dev->replay = std::make_unique<Lane>();
+        dev->replay->st.p = dev->canon;
+        allocate_lane_transient(*dev, *dev->replay);
+        dev->grid = prop.multiProcessorCount * 4;
+        size_t smem = leo_select_smem_bytes(dev->kc);
+        if (smem > 48 * 1024) throw LeoFailure("block winners exceed the select kernel's shared memory");
+        upload_model(*dev, *canonical);
+        *out = dev.release();
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+void leo_b200_close(LeoB200Device* dev) {
+    if (!dev) return;
+    cudaSetDevice(dev->device);
+    cudaStreamSynchronize(dev->stream);
+    cudaStream_t s = dev->stream;
+    delete dev;
+    cudaStreamDestroy(s);
+}
+
+int leo_b200_upload_canonical(LeoB200Device* dev, const LeoB200HostModel* model) {
+    try {
+        const char* e = leo_host::validate_model(*model);
+        if (*e) throw LeoFailure(e);
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        upload_model(*dev, *model);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_download_model(LeoB200Device* dev, LeoB200HostModel* model) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        download_params(*dev, dev->canon, *model);
+        model->generation = dev->generation;
+        model->parameter_revision = dev->revision;
+        model->statistics = dev->stats;
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+uint64_t leo_b200_canonical_tick(LeoB200Device* dev) { return dev->canonical_tick; }
+
+int leo_b200_set_canonical_tick(LeoB200Device* dev, uint64_t tick) {
+    dev->canonical_tick = tick;
+    return 0;
+}
+
+int leo_b200_batch_begin(LeoB200Device* dev, const uint8_t* bytes, const uint64_t* offsets, uint32_t stories,
+                         int permission) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        batch_begin(*dev, bytes, offsets, stories, permission);
+        return 0;
+    } catch (const std::exception& e) {
+        dev->batch_open = false;
+        return fail(e);
+    }
+}
+
+int leo_b200_batch_steps(LeoB200Device* dev, uint32_t count, uint32_t* steps_done) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        batch_steps(*dev, count);
+        CUDA_CHECK(cudaStreamSynchronize(dev->stream));
+        if (steps_done) *steps_done = dev->steps_done;
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_batch_finish(LeoB200Device* dev, LeoB200BatchReport* report, LeoB200StorySummary* summaries,
+                          float* losses) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        batch_finish(*dev, report, summaries, losses);
+        return 0;
+    } catch (const std::exception& e) {
+        dev->batch_open = false;
+        return fail(e);
+    }
+}
+
+int leo_b200_train_story_batch(LeoB200Device* dev, const uint8_t* bytes, const uint64_t* offsets, uint32_t stories,
+                               int permission, LeoB200BatchReport* report, LeoB200StorySummary* summaries,
+                               float* losses) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        batch_begin(*dev, bytes, offsets, stories, permission);
+        batch_finish(*dev, report, summaries, losses);
+        return 0;
+    } catch (const std::exception& e) {
+        dev->batch_open = false;
+        return fail(e);
+    }
+}
+
+int leo_b200_state_digest(LeoB200Device* dev, uint8_t out[32]) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        const ModelSizes& z = dev->z;
+        std::vector<float> thr(z.n), exc(z.n), rw(z.synapses), iw(z.inputs), ow(z.outputs), bias(LEO_B200_OUTPUT_CLASSES);
+        std::vector<float> emb(z.ctx_emb), cow(z.ctx_out);
+        std::vector<uint8_t> nt(z.n), rb(z.synapses), rd(z.synapses), ib(z.inputs);
+        std::vector<uint32_t> rt(z.synapses), it(z.inputs), obs(z.ctx);
+        std::vector<uint64_t> keys(z.ctx);
+        LeoB200HostModel m{};
+        m.threshold = thr.data(); m.excitability = exc.data(); m.neuron_type = nt.data();
+        m.recurrent_target = rt.data(); m.recurrent_branch = rb.data(); m.recurrent_delay = rd.data();
+        m.recurrent_weight = rw.data(); m.input_target = it.data(); m.input_branch = ib.data();
+        m.input_weight = iw.data(); m.output_weight = ow.data(); m.output_bias = bias.data();
+        m.context_keys = keys.data(); m.context_embeddings = emb.data(); m.context_observations = obs.data();
+        m.context_output_weight = cow.data();
+        download_params(*dev, dev->canon, m);
+        m.generation = dev->generation;
+        m.parameter_revision = dev->revision;
+        m.statistics = dev->stats;
+        leo_host::training_state_hash(m, out);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+// Debug/parity inspection: the learned parameters of one story lane (or the
+// canonical model when lane == UINT32_MAX) in the checkpoint layout.
+int leo_b200_lane_model(LeoB200Device* dev, uint32_t lane, LeoB200HostModel* model) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        if (lane != 0xffffffffu && lane >= dev->lanes.size()) throw LeoFailure("lane out of range");
+        const LaneParams& p = lane == 0xffffffffu ? dev->canon : dev->lanes[lane]->st.p;
+        download_params(*dev, p, *model);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+// Debug/parity inspection of one lane's transient state by name; `lane ==
+// UINT32_MAX` selects the canonical (replay / single-story) lane.  Arrays are
+// converted to the reference runtime's layout (runtime.rs:112-186).
+int leo_b200_lane_array(LeoB200Device* dev, uint32_t lane, const char* name, void* out, size_t capacity,
+                        size_t* written) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        CUDA_CHECK(cudaStreamSynchronize(dev->stream));
+        if (lane != 0xffffffffu && lane >= dev->lanes.size()) throw LeoFailure("lane out of range");
+        Lane& L = lane == 0xffffffffu ? *dev->replay : *dev->lanes[lane];
+        const ModelSizes& z = dev->z;
+        std::string k(name);
+        LaneScalars sc;
+        CUDA_CHECK(cudaMemcpy(&sc, L.st.sc, sizeof(sc), cudaMemcpyDeviceToHost));
+        auto emit = [&](const void* src, size_t bytes) {
+            if (bytes > capacity) throw LeoFailure("capacity too small for " + k);
+            std::memcpy(out, src, bytes);
+            *written = bytes;
+        };
+        if (k == "scalars") {
+            emit(&sc, sizeof(sc));
+            return 0;
+        }
+        std::vector<NeuronHot> hot;
+        std::vector<NeuronCold> cold;
+        auto load_neurons = [&]() {
+            hot.resize(z.n);
+            cold.resize(z.n);
+            CUDA_CHECK(cudaMemcpy(hot.data(), L.st.hot, z.n * sizeof(NeuronHot), cudaMemcpyDeviceToHost));
+            CUDA_CHECK(cudaMemcpy(cold.data(), L.st.cold, z.n * sizeof(NeuronCold), cudaMemcpyDeviceToHost));
+        };
+        std::vector<float> f;
+        std::vector<uint64_t> u;
+        if (k == "membrane" || k == "fatigue" || k == "adaptation_fast" || k == "adaptation_medium" ||
+            k == "adaptation_slow" || k == "activation" || k == "selection_surrogate" || k == "refractory_until" ||
+            k == "branch_last_tick" || k == "neuron_last_tick") {
+            load_neurons();
+            uint32_t tick = dev->steps_done;  // ticks are relative to the lane's reset
+            for (size_t n = 0; n < z.n; ++n) {
+                if (k == "membrane") f.push_back(cold[n].membrane);
+                else if (k == "fatigue") f.push_back(cold[n].fatigue);
+                else if (k == "adaptation_fast") f.push_back(cold[n].adaptation[0]);
+                else if (k == "adaptation_medium") f.push_back(cold[n].adaptation[1]);
+                else if (k == "adaptation_slow") f.push_back(cold[n].adaptation[2]);
+                else if (k == "activation") f.push_back(hot[n].activation);
+                else if (k == "selection_surrogate")
+                    f.push_back((hot[n].tag >> 2) == tick ? hot[n].surrogate : 0.0f);
+                else if (k == "refractory_until") u.push_back(sc.base_tick + hot[n].refractory_until);
+                else if (k == "branch_last_tick") u.push_back(sc.base_tick + cold[n].branch_tick);
+                else u.push_back(sc.base_tick + cold[n].neuron_tick);
+            }
+            (void)tick;
+        } else if (k == "branches") {
+            std::vector<float4> br(z.n);
+            CUDA_CHECK(cudaMemcpy(br.data(), L.st.branches, z.n * sizeof(float4), cudaMemcpyDeviceToHost));
+            for (auto& b : br) {
+                f.push_back(b.x);
+                f.push_back(b.y);
+                f.push_back(b.z);
+                f.push_back(b.w);
+            }
+        } else if (k.rfind("rec_", 0) == 0 || k.rfind("input_", 0) == 0) {
+            bool input = k.rfind("input_", 0) == 0;
+            size_t count = input ? z.inputs : z.synapses;
+            std::vector<Trace> tr(count);
+            CUDA_CHECK(cudaMemcpy(tr.data(), input ? L.st.in_traces : L.st.traces, count * sizeof(Trace), cudaMemcpyDeviceToHost));
+            std::string field = k.substr(input ? 6 : 4);
+            for (auto& t : tr) {
+                if (field == "branch_sensitivity") f.push_back(t.branch_sens);
+                else if (field == "membrane_sensitivity") f.push_back(t.membrane_sens);
+                else if (field == "fatigue_sensitivity") f.push_back(t.fatigue_sens);
+                else if (field == "adaptation_fast_sensitivity") f.push_back(t.adaptation_sens[0]);
+                else if (field == "adaptation_medium_sensitivity") f.push_back(t.adaptation_sens[1]);
+                else if (field == "adaptation_slow_sensitivity") f.push_back(t.adaptation_sens[2]);
+                else if (field == "eligibility") f.push_back(t.eligibility);
+                else if (field == "last_tick") u.push_back(sc.base_tick + (t.tick_mark >> 1));
+                else throw LeoFailure("unknown lane array: " + k);
+            }
+        } else if (k == "eligible_recurrent_slots" || k == "eligible_input_slots") {
+            bool input = k == "eligible_input_slots";
+            uint32_t count = input ? sc.in_elig_count[sc.elig_cur] : sc.elig_count[sc.elig_cur];
+            std::vector<uint4> e(count);
+            if (count)
+                CUDA_CHECK(cudaMemcpy(e.data(), input ? L.st.in_elig[sc.elig_cur] : L.st.elig[sc.elig_cur],
+                                      count * sizeof(uint4), cudaMemcpyDeviceToHost));
+            for (auto& x : e) u.push_back(x.x);
+        } else if (k == "active") {
+            uint32_t entry = (dev->steps_done + LEO_RING - 1) % LEO_RING;
+            uint32_t count = dev->steps_done ? sc.ring_count[entry] : 0;
+            std::vector<uint32_t> src(count);
+            if (count)
+                CUDA_CHECK(cudaMemcpy(src.data(), L.st.ring_src + (size_t)entry * dev->kc.topo.max_active, count * 4,
+                                      cudaMemcpyDeviceToHost));
+            for (auto x : src) u.push_back(x);
+        } else if (k == "probabilities" || k == "errors") {
+            f.resize(LEO_B200_OUTPUT_CLASSES);
+            CUDA_CHECK(cudaMemcpy(f.data(), k == "errors" ? L.st.errors : L.st.probs, f.size() * 4, cudaMemcpyDeviceToHost));
+        } else if (k == "step_loss") {
+            f.resize(dev->steps_done);
+            if (!f.empty()) CUDA_CHECK(cudaMemcpy(f.data(), L.step_loss, f.size() * 4, cudaMemcpyDeviceToHost));
+        } else if (k == "population_inhibition") {
+            f.push_back(sc.population_inhibition);
+        } else {
+            throw LeoFailure("unknown lane array: " + k);
+        }
+        if (!f.empty() || u.empty()) emit(f.data(), f.size() * 4);
+        else emit(u.data(), u.size() * 8);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+size_t leo_b200_device_bytes(LeoB200Device* dev) {
+    size_t total = dev->mem.bytes + dev->replay->mem.bytes;
+    for (auto& l : dev->lanes) total += l->mem.bytes;
+    return total;
+}
+
+}  // extern "C"

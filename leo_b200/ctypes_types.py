@@ -1,0 +1,133 @@
+"""ctypes mirrors of ``include/leo_b200_types.h`` and ``include/leo_cuda_abi.h``.
+
+The ``LeoConfig`` field list is read from ``cuda_abi.def`` itself, so the
+Python view cannot drift from the generated C header
+(``crates/leo-core/cuda_abi.def:4-44``).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+from .abi.generate import DEFAULT_SPEC, parse_spec
+
+_SPEC = parse_spec(DEFAULT_SPEC.read_text(encoding="utf-8"))
+
+
+class LeoConfig(C.Structure):
+    _fields_ = [(name, C.c_uint32 if ty == "u32" else C.c_float) for ty, name in _SPEC.config]
+
+
+assert C.sizeof(LeoConfig) == 4 * len(_SPEC.config) == 160
+
+
+class LeoB200HostConfig(C.Structure):
+    _fields_ = [
+        ("seed", C.c_uint64),
+        ("excitatory_fraction", C.c_float),
+        ("provisional_strength", C.c_float),
+        ("training_strength", C.c_float),
+        ("verified_strength", C.c_float),
+        ("plasticity_window", C.c_uint32),
+        ("end_document_weight", C.c_float),
+        ("context_dropout_rate", C.c_float),
+        ("replay_fraction", C.c_float),
+        ("replay_segment_bytes", C.c_uint32),
+        ("reserved0", C.c_uint32),
+    ]
+
+
+class LeoB200Config(C.Structure):
+    _fields_ = [("abi", LeoConfig), ("host", LeoB200HostConfig)]
+
+
+class LeoB200Statistics(C.Structure):
+    _fields_ = [
+        ("processed_bytes", C.c_uint64),
+        ("processed_stories", C.c_uint64),
+        ("training_loss_sum", C.c_double),
+        ("training_targets", C.c_uint64),
+        ("active_neurons_sum", C.c_uint64),
+        ("active_neurons_peak", C.c_uint64),
+        ("synaptic_events", C.c_uint64),
+        ("numerical_rejections", C.c_uint64),
+        ("persistent_ticks", C.c_uint64),
+    ]
+
+
+class LeoB200HostModel(C.Structure):
+    _fields_ = [
+        ("config", LeoB200Config),
+        ("generation", C.c_uint64),
+        ("parameter_revision", C.c_uint64),
+        ("statistics", LeoB200Statistics),
+        ("threshold", C.POINTER(C.c_float)),
+        ("excitability", C.POINTER(C.c_float)),
+        ("neuron_type", C.POINTER(C.c_uint8)),
+        ("recurrent_target", C.POINTER(C.c_uint32)),
+        ("recurrent_branch", C.POINTER(C.c_uint8)),
+        ("recurrent_delay", C.POINTER(C.c_uint8)),
+        ("recurrent_weight", C.POINTER(C.c_float)),
+        ("input_target", C.POINTER(C.c_uint32)),
+        ("input_branch", C.POINTER(C.c_uint8)),
+        ("input_weight", C.POINTER(C.c_float)),
+        ("output_weight", C.POINTER(C.c_float)),
+        ("output_bias", C.POINTER(C.c_float)),
+        ("context_keys", C.POINTER(C.c_uint64)),
+        ("context_embeddings", C.POINTER(C.c_float)),
+        ("context_observations", C.POINTER(C.c_uint32)),
+        ("context_output_weight", C.POINTER(C.c_float)),
+    ]
+
+
+class LeoB200StepMetrics(C.Structure):
+    _fields_ = [
+        ("loss", C.c_float),
+        ("predicted_symbol", C.c_uint32),
+        ("active_neurons", C.c_uint32),
+        ("emitted_events", C.c_uint32),
+        ("suprathreshold_neurons", C.c_uint32),
+        ("block_selected_neurons", C.c_uint32),
+        ("global_cap_clipped_neurons", C.c_uint32),
+        ("population_inhibition", C.c_float),
+        ("context_cells", C.c_uint32),
+        ("context_probes", C.c_uint32),
+        ("context_applied", C.c_uint32),
+        ("context_loss_gain", C.c_float),
+        ("output_madds", C.c_uint64),
+        ("eligible_recurrent_synapses", C.c_uint64),
+        ("eligible_input_synapses", C.c_uint64),
+        ("mean_abs_eligibility", C.c_float),
+        ("reserved0", C.c_uint32),
+    ]
+
+
+class LeoB200StorySummary(C.Structure):
+    _fields_ = [
+        ("training_loss_sum", C.c_double),
+        ("training_targets", C.c_uint64),
+        ("active_neurons_sum", C.c_uint64),
+        ("active_neurons_peak", C.c_uint64),
+        ("synaptic_events", C.c_uint64),
+        ("context_applied_steps", C.c_uint64),
+    ]
+
+
+class LeoB200BatchReport(C.Structure):
+    _fields_ = [
+        ("workers", C.c_uint64),
+        ("fixed_parameter_updates", C.c_uint64),
+        ("context_keys", C.c_uint64),
+        ("stories", C.c_uint64),
+        ("input_bytes", C.c_uint64),
+        ("targets", C.c_uint64),
+        ("mean_loss", C.c_double),
+        ("replay_segments", C.c_uint64),
+        ("replay_steps", C.c_uint64),
+        ("replay_prefix_steps", C.c_uint64),
+    ]
+
+
+FROZEN, PROVISIONAL, TRAINING, VERIFIED = 0, 1, 2, 3
+TOPOLOGY_REFERENCE, TOPOLOGY_UNIFORM, TOPOLOGY_ZIPF = 0, 1, 2
+BEGIN_DOCUMENT, END_DOCUMENT, SYMBOL_COUNT, OUTPUT_CLASSES = 256, 257, 258, 257

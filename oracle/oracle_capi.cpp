@@ -1,0 +1,427 @@
+// TEST INFRASTRUCTURE ONLY -- C entry points over the parity oracle, for the
+// pytest suite (ctypes) and bench.py's cpu_baseline leg.  Never linked into or
+// called by the product library.
+#include <cstring>
+#include <string>
+
+#include "../include/leo_b200_types.h"
+#include "leo_oracle.hpp"
+
+using namespace leo_oracle;
+
+namespace {
+thread_local std::string g_error;
+
+int fail(const std::exception& e) {
+    g_error = e.what();
+    return -1;
+}
+
+Config from_c(const LeoB200Config& c) {
+    Config o;
+    const LeoConfig& a = c.abi;
+    o.seed = c.host.seed;
+    o.neuron_count = a.neuron_count;
+    o.block_count = a.block_count;
+    o.neurons_per_block = a.neurons_per_block;
+    o.branches_per_neuron = a.branches_per_neuron;
+    o.excitatory_fraction = c.host.excitatory_fraction;
+    o.synapses_per_neuron = a.synapses_per_neuron;
+    o.input_fanout = a.input_fanout;
+    o.max_active_per_block = a.max_active_per_block;
+    o.max_active_global = a.max_active_global;
+    o.branch_decay = a.branch_decay;
+    o.membrane_decay = a.membrane_decay;
+    o.fatigue_decay = a.fatigue_decay;
+    o.fatigue_gain = a.fatigue_gain;
+    o.refractory_ticks = a.refractory_ticks;
+    o.target_activity = a.target_activity;
+    o.threshold_homeostasis_rate = a.threshold_homeostasis_rate;
+    o.population_inhibition_rate = a.population_inhibition_rate;
+    o.population_inhibition_max = a.population_inhibition_max;
+    o.adaptation_fast_decay = a.adaptation_fast_decay;
+    o.adaptation_medium_decay = a.adaptation_medium_decay;
+    o.adaptation_slow_decay = a.adaptation_slow_decay;
+    o.adaptation_fast_gain = a.adaptation_fast_gain;
+    o.adaptation_medium_gain = a.adaptation_medium_gain;
+    o.adaptation_slow_gain = a.adaptation_slow_gain;
+    o.membrane_reset_fraction = a.membrane_reset_fraction;
+    o.output_learning_rate = a.output_learning_rate;
+    o.recurrent_learning_rate = a.recurrent_learning_rate;
+    o.inhibitory_learning_rate = a.inhibitory_learning_rate;
+    o.eligibility_decay = a.eligibility_decay;
+    o.eligibility_epsilon = a.eligibility_epsilon;
+    o.surrogate_width = a.surrogate_width;
+    o.surrogate_gain = a.surrogate_gain;
+    o.max_update = a.max_update;
+    o.weight_min = a.weight_min;
+    o.weight_max = a.weight_max;
+    o.provisional_strength = c.host.provisional_strength;
+    o.training_strength = c.host.training_strength;
+    o.verified_strength = c.host.verified_strength;
+    o.plasticity_window = c.host.plasticity_window;
+    o.end_document_weight = c.host.end_document_weight;
+    o.max_order = a.context_max_order;
+    o.embedding_dim = a.context_embedding_dim;
+    o.slots_per_order = a.context_slots_per_order;
+    o.probe_limit = a.context_probe_limit;
+    o.context_learning_rate = a.context_learning_rate;
+    o.confidence_observations = a.context_confidence_observations;
+    o.dropout_rate = c.host.context_dropout_rate;
+    o.replay_fraction = c.host.replay_fraction;
+    o.segment_bytes = c.host.replay_segment_bytes;
+    return o;
+}
+
+template <typename T>
+void copy_in(std::vector<T>& dst, const T* src, size_t n) {
+    dst.assign(src, src + n);
+}
+
+void stats_to_c(const Statistics& s, LeoB200Statistics& o) {
+    o.processed_bytes = s.processed_bytes;
+    o.processed_stories = s.processed_stories;
+    o.training_loss_sum = s.training_loss_sum;
+    o.training_targets = s.training_targets;
+    o.active_neurons_sum = s.active_neurons_sum;
+    o.active_neurons_peak = s.active_neurons_peak;
+    o.synaptic_events = s.synaptic_events;
+    o.numerical_rejections = s.numerical_rejections;
+    o.persistent_ticks = s.persistent_ticks;
+}
+void stats_from_c(const LeoB200Statistics& o, Statistics& s) {
+    s.processed_bytes = o.processed_bytes;
+    s.processed_stories = o.processed_stories;
+    s.training_loss_sum = o.training_loss_sum;
+    s.training_targets = o.training_targets;
+    s.active_neurons_sum = o.active_neurons_sum;
+    s.active_neurons_peak = o.active_neurons_peak;
+    s.synaptic_events = o.synaptic_events;
+    s.numerical_rejections = o.numerical_rejections;
+    s.persistent_ticks = o.persistent_ticks;
+}
+}  // namespace
+
+extern "C" {
+
+const char* leo_oracle_last_error(void) { return g_error.c_str(); }
+
+int leo_oracle_config_validate(const LeoB200Config* c) {
+    try {
+        from_c(*c).validate();
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+void* leo_oracle_model_initialize(const LeoB200Config* c, int topology) {
+    try {
+        return new Model(Model::initialize(from_c(*c), topology));
+    } catch (const std::exception& e) {
+        fail(e);
+        return nullptr;
+    }
+}
+
+void* leo_oracle_model_from_host(const LeoB200HostModel* h) {
+    try {
+        Model* m = new Model();
+        m->config = from_c(h->config);
+        size_t n = m->config.neuron_count, s = m->config.synapses_per_neuron, f = m->config.input_fanout;
+        size_t d = m->config.embedding_dim, ctx = m->config.max_order * m->config.slots_per_order;
+        m->generation = h->generation;
+        m->parameter_revision = h->parameter_revision;
+        stats_from_c(h->statistics, m->statistics);
+        copy_in(m->threshold, h->threshold, n);
+        copy_in(m->excitability, h->excitability, n);
+        copy_in(m->neuron_type, h->neuron_type, n);
+        m->capacity_per_neuron = s;
+        copy_in(m->recurrent_target, h->recurrent_target, n * s);
+        copy_in(m->recurrent_branch, h->recurrent_branch, n * s);
+        copy_in(m->recurrent_delay, h->recurrent_delay, n * s);
+        copy_in(m->recurrent_weight, h->recurrent_weight, n * s);
+        m->input_fanout = f;
+        copy_in(m->input_targets, h->input_target, SYMBOL_COUNT * f);
+        copy_in(m->input_branches, h->input_branch, SYMBOL_COUNT * f);
+        copy_in(m->input_weights, h->input_weight, SYMBOL_COUNT * f);
+        copy_in(m->output_weights, h->output_weight, OUTPUT_CLASSES * n);
+        copy_in(m->output_bias, h->output_bias, OUTPUT_CLASSES);
+        copy_in(m->context_keys, h->context_keys, ctx);
+        copy_in(m->context_embeddings, h->context_embeddings, ctx * d);
+        copy_in(m->context_observations, h->context_observations, ctx);
+        copy_in(m->context_output_weights, h->context_output_weight, OUTPUT_CLASSES * d);
+        return m;
+    } catch (const std::exception& e) {
+        fail(e);
+        return nullptr;
+    }
+}
+
+void leo_oracle_model_free(void* m) { delete (Model*)m; }
+void* leo_oracle_model_clone(void* m) { return new Model(*(Model*)m); }
+
+// Points `out` at the model's own arrays (valid until the model changes size
+// or is freed) and copies the scalar fields.  `out->config` is left unchanged.
+int leo_oracle_model_view(void* mp, LeoB200HostModel* out) {
+    Model& m = *(Model*)mp;
+    out->generation = m.generation;
+    out->parameter_revision = m.parameter_revision;
+    stats_to_c(m.statistics, out->statistics);
+    out->threshold = m.threshold.data();
+    out->excitability = m.excitability.data();
+    out->neuron_type = m.neuron_type.data();
+    out->recurrent_target = m.recurrent_target.data();
+    out->recurrent_branch = m.recurrent_branch.data();
+    out->recurrent_delay = m.recurrent_delay.data();
+    out->recurrent_weight = m.recurrent_weight.data();
+    out->input_target = m.input_targets.data();
+    out->input_branch = m.input_branches.data();
+    out->input_weight = m.input_weights.data();
+    out->output_weight = m.output_weights.data();
+    out->output_bias = m.output_bias.data();
+    out->context_keys = m.context_keys.data();
+    out->context_embeddings = m.context_embeddings.data();
+    out->context_observations = m.context_observations.data();
+    out->context_output_weight = m.context_output_weights.data();
+    return 0;
+}
+
+int leo_oracle_model_set_scalars(void* mp, uint64_t generation, uint64_t revision, const LeoB200Statistics* s) {
+    Model& m = *(Model*)mp;
+    m.generation = generation;
+    m.parameter_revision = revision;
+    stats_from_c(*s, m.statistics);
+    return 0;
+}
+
+int leo_oracle_model_validate(void* mp) {
+    try {
+        ((Model*)mp)->validate();
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+void leo_oracle_training_state_hash(void* mp, uint8_t out[32]) { training_state_hash(*(Model*)mp, out); }
+void leo_oracle_model_state_hash(void* mp, uint8_t out[32]) { model_state_hash(*(Model*)mp, out); }
+void leo_oracle_sha256(const uint8_t* data, size_t len, uint8_t out[32]) { sha256(data, len, out); }
+
+int leo_oracle_resolve_context_slot(void* mp, size_t order, uint64_t key, int allocate, int64_t* slot,
+                                    uint64_t* probes) {
+    try {
+        long s;
+        size_t p;
+        ((Model*)mp)->resolve_context_slot(order, key, allocate != 0, &s, &p);
+        *slot = s;
+        *probes = p;
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+// ------------------------------------------------------------------ runtime
+void* leo_oracle_runtime_new(void* mp) {
+    try {
+        return new Runtime(*(Model*)mp);
+    } catch (const std::exception& e) {
+        fail(e);
+        return nullptr;
+    }
+}
+void leo_oracle_runtime_free(void* rt) { delete (Runtime*)rt; }
+void* leo_oracle_runtime_model(void* rt) { return &((Runtime*)rt)->model; }
+void leo_oracle_runtime_model_changed(void* rt) { ((Runtime*)rt)->model_changed(); }
+void leo_oracle_runtime_begin_document(void* rt) { ((Runtime*)rt)->begin_document(); }
+void leo_oracle_runtime_finish_document(void* rt) { ((Runtime*)rt)->finish_document(); }
+void leo_oracle_runtime_reset(void* rt) { ((Runtime*)rt)->reset_transient_state(); }
+void leo_oracle_runtime_enable_tracking(void* rt) { ((Runtime*)rt)->enable_parameter_tracking(); }
+uint64_t leo_oracle_runtime_tick(void* rt) { return ((Runtime*)rt)->current_tick; }
+void leo_oracle_runtime_set_tick(void* rt, uint64_t t) { ((Runtime*)rt)->current_tick = t; }
+
+int leo_oracle_runtime_step(void* rtp, uint32_t symbol, int64_t target, int permission, LeoB200StepMetrics* out) {
+    try {
+        Runtime& rt = *(Runtime*)rtp;
+        StepMetrics m = rt.step(symbol, (long)target, (Permission)permission);
+        if (out) {
+            std::memset(out, 0, sizeof(*out));
+            out->loss = m.has_loss ? m.loss : __builtin_nanf("");
+            out->predicted_symbol = m.predicted_symbol;
+            out->active_neurons = (uint32_t)m.active_neurons;
+            out->emitted_events = (uint32_t)m.emitted_events;
+            out->suprathreshold_neurons = (uint32_t)m.suprathreshold_neurons;
+            out->block_selected_neurons = (uint32_t)m.block_selected_neurons;
+            out->global_cap_clipped_neurons = (uint32_t)m.global_cap_clipped_neurons;
+            out->population_inhibition = m.population_inhibition;
+            out->context_cells = (uint32_t)m.context_cells;
+            out->context_probes = (uint32_t)m.context_probes;
+            out->context_applied = m.context_applied ? 1 : 0;
+            out->context_loss_gain = m.context_loss_gain;
+            out->output_madds = m.output_madds;
+            out->eligible_recurrent_synapses = m.eligible_recurrent_synapses;
+            out->eligible_input_synapses = m.eligible_input_synapses;
+            out->mean_abs_eligibility = m.mean_abs_eligibility;
+        }
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+// Exposes one internal runtime array by name (read-only use by tests).
+int leo_oracle_runtime_array(void* rtp, const char* name, void** ptr, size_t* elem_size, size_t* count) {
+    Runtime& r = *(Runtime*)rtp;
+    std::string k(name);
+#define EXPOSE(label, vec)                        \
+    if (k == label) {                             \
+        *ptr = (void*)(vec).data();               \
+        *elem_size = sizeof((vec)[0]);            \
+        *count = (vec).size();                    \
+        return 0;                                 \
+    }
+    EXPOSE("membrane", r.membrane)
+    EXPOSE("activation", r.activation)
+    EXPOSE("fatigue", r.fatigue)
+    EXPOSE("refractory_until", r.refractory_until)
+    EXPOSE("branches", r.branches)
+    EXPOSE("touched", r.touched)
+    EXPOSE("active", r.active)
+    EXPOSE("selection_surrogate", r.selection_surrogate)
+    EXPOSE("branch_last_tick", r.branch_last_tick)
+    EXPOSE("neuron_last_tick", r.neuron_last_tick)
+    EXPOSE("adaptation_fast", r.adaptation_state[0])
+    EXPOSE("adaptation_medium", r.adaptation_state[1])
+    EXPOSE("adaptation_slow", r.adaptation_state[2])
+    EXPOSE("rec_branch_sensitivity", r.rec_branch_sens)
+    EXPOSE("rec_membrane_sensitivity", r.rec_membrane_sens)
+    EXPOSE("rec_fatigue_sensitivity", r.rec_fatigue_sens)
+    EXPOSE("rec_adaptation_fast_sensitivity", r.rec_adapt_sens[0])
+    EXPOSE("rec_adaptation_medium_sensitivity", r.rec_adapt_sens[1])
+    EXPOSE("rec_adaptation_slow_sensitivity", r.rec_adapt_sens[2])
+    EXPOSE("rec_eligibility", r.eligibility)
+    EXPOSE("rec_last_tick", r.eligibility_last_tick)
+    EXPOSE("eligible_recurrent_slots", r.eligible_recurrent_slots)
+    EXPOSE("input_branch_sensitivity", r.in_branch_sens)
+    EXPOSE("input_membrane_sensitivity", r.in_membrane_sens)
+    EXPOSE("input_fatigue_sensitivity", r.in_fatigue_sens)
+    EXPOSE("input_adaptation_fast_sensitivity", r.in_adapt_sens[0])
+    EXPOSE("input_adaptation_medium_sensitivity", r.in_adapt_sens[1])
+    EXPOSE("input_adaptation_slow_sensitivity", r.in_adapt_sens[2])
+    EXPOSE("input_eligibility", r.input_eligibility)
+    EXPOSE("input_last_tick", r.input_eligibility_last_tick)
+    EXPOSE("eligible_input_slots", r.eligible_input_slots)
+    EXPOSE("logits", r.logits)
+    EXPOSE("probabilities", r.probabilities)
+    EXPOSE("errors", r.errors)
+    EXPOSE("learning_signal", r.learning_signal)
+    EXPOSE("learning_destinations", r.learning_destinations)
+    EXPOSE("block_selection_cutoff", r.block_selection_cutoff)
+    EXPOSE("context_history", r.context_history)
+    EXPOSE("active_context_slots", r.active_context_slots)
+    EXPOSE("active_context_scales", r.active_context_scales)
+    EXPOSE("context_latent", r.context_latent)
+    EXPOSE("changed_threshold", r.changed_threshold)
+    EXPOSE("changed_recurrent_weight", r.changed_recurrent_weight)
+    EXPOSE("changed_input_weight", r.changed_input_weight)
+    EXPOSE("changed_output_neurons", r.changed_output_neurons)
+    EXPOSE("changed_context_slots", r.changed_context_slots)
+#undef EXPOSE
+    if (k == "population_inhibition") {
+        *ptr = &r.population_inhibition;
+        *elem_size = 4;
+        *count = 1;
+        return 0;
+    }
+    if (k == "population_selection_cutoff") {
+        *ptr = &r.population_selection_cutoff;
+        *elem_size = 4;
+        *count = 1;
+        return 0;
+    }
+    g_error = "unknown runtime array: " + k;
+    return -1;
+}
+
+// Runs one logical story batch on the CPU backend (training.rs:1539-1727).
+// `rtp` is the canonical runtime; stories are bytes[offsets[i]..offsets[i+1]].
+// `out_losses` (optional) receives the initial-pass per-target losses of all
+// stories concatenated in story order; `out_ranges` (optional, pairs of u64)
+// receives each story's replay ranges and `out_range_counts` their counts.
+int leo_oracle_train_story_batch(void* rtp, const uint8_t* bytes, const uint64_t* offsets, size_t stories,
+                                 int permission, size_t threads, LeoB200BatchReport* out, float* out_losses,
+                                 uint64_t* out_ranges, uint64_t* out_range_counts) {
+    try {
+        Runtime& rt = *(Runtime*)rtp;
+        std::vector<std::vector<uint8_t>> batch(stories);
+        uint64_t input_bytes = 0;
+        for (size_t i = 0; i < stories; ++i) {
+            batch[i].assign(bytes + offsets[i], bytes + offsets[i + 1]);
+            input_bytes += batch[i].size();
+        }
+        BatchReport r = train_story_batch(rt, batch, (Permission)permission, threads);
+        if (out) {
+            std::memset(out, 0, sizeof(*out));
+            out->workers = r.merge.workers;
+            out->fixed_parameter_updates = r.merge.fixed_parameter_updates;
+            out->context_keys = r.merge.context_keys;
+            out->stories = r.stories;
+            out->input_bytes = input_bytes;
+            out->targets = r.targets;
+            out->mean_loss = r.mean_loss;
+            out->replay_segments = r.replay.segments;
+            out->replay_steps = r.replay.replay_steps;
+            out->replay_prefix_steps = r.replay.prefix_steps;
+        }
+        if (out_losses) {
+            size_t k = 0;
+            for (auto& l : r.losses_by_story)
+                for (float v : l) out_losses[k++] = v;
+        }
+        if (out_ranges && out_range_counts) {
+            size_t k = 0;
+            for (size_t i = 0; i < r.replay_ranges.size(); ++i) {
+                out_range_counts[i] = r.replay_ranges[i].size();
+                for (auto& range : r.replay_ranges[i]) {
+                    out_ranges[2 * k] = range.start;
+                    out_ranges[2 * k + 1] = range.end;
+                    ++k;
+                }
+            }
+        }
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+// Merge helpers for unit tests of the delta algebra (parallel.rs).
+int leo_oracle_mean_of_models(void* master, void* const* trained, size_t count, int sum_instead) {
+    try {
+        Model& m = *(Model*)master;
+        std::vector<SparseModelDelta> deltas;
+        for (size_t i = 0; i < count; ++i) deltas.push_back(SparseModelDelta::between(m, *(Model*)trained[i]));
+        if (sum_instead)
+            apply_sum_deltas(m, deltas);
+        else
+            apply_mean_deltas(m, deltas);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_oracle_select_replay_ranges(const float* losses, size_t n, float fraction, size_t segment, uint64_t* out,
+                                    size_t cap, size_t* count) {
+    std::vector<float> l(losses, losses + n);
+    auto r = select_replay_ranges(l, fraction, segment);
+    *count = r.size();
+    for (size_t i = 0; i < r.size() && i < cap; ++i) {
+        out[2 * i] = r[i].start;
+        out[2 * i + 1] = r[i].end;
+    }
+    return 0;
+}
+
+}  // extern "C"
