@@ -54,6 +54,9 @@ struct MemPool {
         size_t b = std::max<size_t>(count * sizeof(T), 16);
         CUDA_CHECK(cudaMalloc(&m->p, b));
         CUDA_CHECK(cudaMemset(m->p, fill, b));
+        // The runtime's stream is non-blocking with respect to the legacy
+        // default stream the fill runs on: finish the fill before any use.
+        CUDA_CHECK(cudaDeviceSynchronize());
         bytes += b;
         T* out = (T*)m->p;
         blocks.push_back(std::move(m));
@@ -100,6 +103,10 @@ struct LeoB200Device {
     LaneState* d_lanes = nullptr;  // device copy of the story lanes' LaneState
     LaneState* d_replay = nullptr;
     uint32_t lane_capacity = 0;
+    // context merge staging (one lane's changed rows at a time; the sync slot list)
+    ContextRow* ctx_stage_rows = nullptr;
+    float* ctx_stage_emb = nullptr;
+    uint32_t* ctx_sync_slots = nullptr;
     // merge scratch
     MergeScratch scratch{};
     size_t scratch_len = 0;
@@ -454,16 +461,17 @@ size_t merge_context(LeoB200Device& dev, uint32_t lane_count, const std::vector<
         std::vector<uint32_t> slots(count);
         std::vector<ContextRow> rows(count);
         std::vector<float> emb((size_t)count * d);
-        MemPool tmp;
-        ContextRow* d_rows = tmp.alloc<ContextRow>(count);
-        float* d_emb = tmp.alloc<float>((size_t)count * d);
+        ContextRow* d_rows = dev.ctx_stage_rows;
+        float* d_emb = dev.ctx_stage_emb;
         gather_context_rows_kernel<<<std::max(1u, std::min(count / 128 + 1, 1024u)), 128, 0, dev.stream>>>(
             lane.st.ctx_list, count, lane.st.p.ctx_keys, lane.st.p.ctx_obs, lane.st.p.ctx_emb, d, d_rows, d_emb);
+        CUDA_CHECK(cudaGetLastError());
         CUDA_CHECK(cudaMemcpyAsync(slots.data(), lane.st.ctx_list, count * 4, cudaMemcpyDeviceToHost, dev.stream));
         CUDA_CHECK(cudaMemcpyAsync(rows.data(), d_rows, count * sizeof(ContextRow), cudaMemcpyDeviceToHost, dev.stream));
         CUDA_CHECK(cudaMemcpyAsync(emb.data(), d_emb, emb.size() * 4, cudaMemcpyDeviceToHost, dev.stream));
         clear_marks_kernel<<<std::max(1u, std::min(count / 128 + 1, 1024u)), 128, 0, dev.stream>>>(lane.st.ctx_list, count,
                                                                                                    lane.st.ctx_mark);
+        CUDA_CHECK(cudaGetLastError());
         CUDA_CHECK(cudaStreamSynchronize(dev.stream));
         // context_deltas_for_slots (parallel.rs:929-973)
         for (uint32_t i = 0; i < count; ++i) {
@@ -560,13 +568,13 @@ size_t merge_context(LeoB200Device& dev, uint32_t lane_count, const std::vector<
             CUDA_CHECK(cudaMemcpyAsync(dev.canon.ctx_emb + (size_t)slot * d, &dev.ctx_emb[(size_t)slot * d], d * 4,
                                        cudaMemcpyHostToDevice, dev.stream));
         }
-        MemPool tmp;
-        uint32_t* d_slots = tmp.alloc<uint32_t>(sync.size());
+        uint32_t* d_slots = dev.ctx_sync_slots;
         CUDA_CHECK(cudaMemcpyAsync(d_slots, sync.data(), sync.size() * 4, cudaMemcpyHostToDevice, dev.stream));
         uint32_t total = (uint32_t)sync.size() * (d + 1);
         scatter_context_rows_kernel<<<std::max(1u, std::min(total / 256 + 1, 4096u)), 256, 0, dev.stream>>>(
             d_slots, (uint32_t)sync.size(), dev.canon.ctx_keys, dev.canon.ctx_obs, dev.canon.ctx_emb, d, dev.d_lanes,
             (int)dev.lanes.size());
+        CUDA_CHECK(cudaGetLastError());
         CUDA_CHECK(cudaStreamSynchronize(dev.stream));
     }
     return merged.size();
@@ -667,6 +675,7 @@ void sync_replay_changes(LeoB200Device& dev, const LaneScalars& rs) {
                                 it.row_len, dev.grid, dev.stream);
         clear_marks_kernel<<<std::max(1u, std::min(it.count / 256 + 1, 4096u)), 256, 0, dev.stream>>>(it.list, it.count,
                                                                                                       it.marks);
+        CUDA_CHECK(cudaGetLastError());
         CUDA_CHECK(cudaStreamSynchronize(dev.stream));
     }
     // Dense tensors: bias and context output weights.
@@ -694,8 +703,10 @@ void sync_replay_changes(LeoB200Device& dev, const LaneScalars& rs) {
             scatter_context_rows_kernel<<<std::max(1u, std::min(total / 256 + 1, 4096u)), 256, 0, dev.stream>>>(
                 rl.st.ctx_list, (uint32_t)slots.size(), dev.canon.ctx_keys, dev.canon.ctx_obs, dev.canon.ctx_emb, d,
                 dev.d_lanes, (int)lane_count);
+        CUDA_CHECK(cudaGetLastError());
         clear_marks_kernel<<<std::max(1u, std::min((uint32_t)slots.size() / 256 + 1, 4096u)), 256, 0, dev.stream>>>(
             rl.st.ctx_list, (uint32_t)slots.size(), rl.st.ctx_mark);
+        CUDA_CHECK(cudaGetLastError());
         CUDA_CHECK(cudaStreamSynchronize(dev.stream));
     }
 }
@@ -1103,6 +1114,9 @@ int leo_b200_open(int device, const LeoB200HostModel* canonical, uint32_t max_la
         dev->d_lane_counts = dev->mem.alloc<uint32_t>(max_lanes);
         dev->d_lane_marks = dev->mem.alloc<uint8_t*>(max_lanes);
         dev->d_lanes = dev->mem.alloc<LaneState>(max_lanes);
+        dev->ctx_stage_rows = dev->mem.alloc<ContextRow>(z.ctx);
+        dev->ctx_stage_emb = dev->mem.alloc<float>(z.ctx_emb);
+        dev->ctx_sync_slots = dev->mem.alloc<uint32_t>(z.ctx);
         dev->d_replay = dev->mem.alloc<LaneState>(1);
         // replay lane: canonical parameters, private transient state
         dev->replay = std::make_unique<Lane>();
@@ -1353,6 +1367,21 @@ int leo_b200_lane_array(LeoB200Device* dev, uint32_t lane, const char* name, voi
             if (!f.empty()) CUDA_CHECK(cudaMemcpy(f.data(), L.step_loss, f.size() * 4, cudaMemcpyDeviceToHost));
         } else if (k == "population_inhibition") {
             f.push_back(sc.population_inhibition);
+        } else if (k == "changed_context_slots" || k == "changed_threshold" || k == "changed_recurrent_weight" ||
+                   k == "changed_input_weight" || k == "changed_output_neurons") {
+            uint32_t* list = k == "changed_context_slots" ? L.st.ctx_list
+                             : k == "changed_threshold"   ? L.st.thr_list
+                             : k == "changed_recurrent_weight" ? L.st.rec_list
+                             : k == "changed_input_weight"     ? L.st.in_list
+                                                               : L.st.out_list;
+            uint32_t count = k == "changed_context_slots" ? sc.ctx_changed
+                             : k == "changed_threshold"   ? sc.thr_changed
+                             : k == "changed_recurrent_weight" ? sc.rec_changed
+                             : k == "changed_input_weight"     ? sc.in_changed
+                                                               : sc.out_changed;
+            std::vector<uint32_t> v(count);
+            if (count) CUDA_CHECK(cudaMemcpy(v.data(), list, count * 4, cudaMemcpyDeviceToHost));
+            for (auto x : v) u.push_back(x);
         } else {
             throw LeoFailure("unknown lane array: " + k);
         }
