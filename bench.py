@@ -1,0 +1,305 @@
+"""Benchmark: training bytes/s of Leo's per-byte story-batch step on B200.
+
+One benchmark step is one logical story batch of the chosen workload (default
+``baseline2``: 65,536 units, fan-in 64, 32 story workers, stories of 256-1024
+bytes, 30 % bounded-surprise replay): the per-story pass over every lane, the
+batch-end FP64 mean merge and lane sync, and serial canonical replay.  The
+metric is input story bytes per second (``input_bytes`` of the reference's
+``benchmark --train``, crates/leo-cli/src/main.rs:716,737,768).
+
+* ``value``: story bytes of the K timed batches (all ranks) / the max over
+  ranks of the batch time measured with CUDA events on the backend's stream.
+* ``e2e``: the same bytes / the max over ranks of the wall time of the public
+  call ``training_story_batch`` with host buffers (story bytes in, per-target
+  losses and summaries out).
+* ``roofline``: the dominant kernel's algorithmic bytes per launch (per-unit
+  figures in DESIGN.md) over its CUDA-event launch time, against the measured
+  HBM copy bandwidth.
+* ``cpu_baseline``: the CPU restatement of the reference backend (oracle/) on
+  a bounded sample of the same workload, timed on this box's host cores.
+
+``--impl reference`` times that CPU implementation alone, one sample batch per
+step.  Under torchrun every rank trains its own replica on its own stories
+(weak scaling); rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "train bytes/sec (box) at 1/2/4/8 B200; wavefront HBM GB/s vs peak"
+UNIT = "bytes/s"
+
+# Algorithmic bytes per unit of work (per-phase minimal traffic, FP32 = 4 B,
+# index = 4 B, branch/delay = 1 B, tick = 4 B).
+BYTES_PER_EVENT = 17 + 64          # target, branch, snapshot, branch r/w + trace record r/w
+BYTES_PER_INPUT_SLOT = 9 + 8 + 64
+BYTES_PER_TOUCHED_SETTLE = 130
+BYTES_PER_TOUCHED_SURROGATE = 16
+BYTES_PER_TOUCHED_HOMEOSTASIS = 12
+BYTES_PER_ELIGIBLE = 101
+BYTES_PER_DESTINATION = 1032
+BYTES_PER_PLASTIC = 20
+
+
+def phase_algorithmic_bytes(p, cfg) -> dict[str, float]:
+    """Algorithmic bytes moved by each phase over the counters' window."""
+    S, D, K = cfg.synapses_per_neuron, cfg.context_embedding_dim, cfg.context_max_order
+    events = p.work_active * S
+    steps = p.work_steps
+    return {
+        "deliver": events * BYTES_PER_EVENT + steps * cfg.input_fanout * BYTES_PER_INPUT_SLOT,
+        "settle": p.work_touched * BYTES_PER_TOUCHED_SETTLE,
+        "select": p.work_active * 8.0,
+        "surrogate": p.work_touched * BYTES_PER_TOUCHED_SURROGATE,
+        "eligible": p.work_eligible * BYTES_PER_ELIGIBLE,
+        "emit_forward": p.work_active * (50 + 8 * S + 1028) + steps * (257 * D * 4 + K * D * 4),
+        "learn": p.work_destinations * BYTES_PER_DESTINATION + p.work_active * 2056
+        + p.work_touched * BYTES_PER_TOUCHED_HOMEOSTASIS,
+        "plasticity": p.work_plastic * BYTES_PER_PLASTIC,
+        "inhibit": p.work_active * 0.2 * S * 16,
+        "epilogue": 0.0,
+    }
+
+
+def measured_peaks() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"leo_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": []}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_sample(workload, threads: int, stories_n: int, story_bytes: int, batches: int) -> dict:
+    """The CPU restatement of the reference backend on a bounded sample."""
+    from leo_b200.model import HostModel
+    from leo_b200.synthetic import story_stream
+    from oracle.oracle_py import OracleModel, OracleRuntime
+
+    cfg = workload.config
+    model = HostModel.initialize(cfg, workload.topology)
+    canonical = OracleRuntime(OracleModel.from_arrays(cfg, model.arrays))
+    stories = story_stream(workload.story_seed + 7919, stories_n * batches, story_bytes, story_bytes)
+    times, nbytes = [], 0
+    for b in range(batches):
+        batch = stories[b * stories_n:(b + 1) * stories_n]
+        t0 = time.perf_counter()
+        canonical.train_story_batch(batch, 2, threads)
+        times.append(time.perf_counter() - t0)
+        nbytes += sum(len(s) for s in batch)
+    total = sum(times)
+    return {"value": nbytes / total, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{batches} batch(es) of {stories_n} stories x {story_bytes} bytes of {workload.name}, "
+                      f"one thread per story, merge and 30% replay included; {total:.1f} s of CPU work",
+            "seconds": total}
+
+
+def run_reference(args, workload) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = min(args.cpu_stories, os.cpu_count() or 1)
+    for _ in range(args.warmup):
+        cpu_sample(workload, threads, args.cpu_stories, args.cpu_bytes, 1)
+    res = cpu_sample(workload, threads, args.cpu_stories, args.cpu_bytes, args.steps)
+    line = {"metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": res["seconds"] * 1000 / max(args.steps, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded order-2 Markov printable-ASCII stories)",
+            "config": {"workload": workload.name, "stories_per_step": args.cpu_stories,
+                       "story_bytes": args.cpu_bytes, "replay_fraction": workload.config.replay_fraction},
+            "impl": "reference",
+            "cpu_baseline": {"value": res["value"], "unit": UNIT, "cores": res["cores"], "kind": "port",
+                             "sample": res["sample"]},
+            "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", default="baseline2")
+    ap.add_argument("--cpu-stories", type=int, default=8)
+    ap.add_argument("--cpu-bytes", type=int, default=256)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--phase-mask", type=int, default=-1, help="phases timed with CUDA events (default: dominant)")
+    args = ap.parse_args()
+
+    from leo_b200.configs import WORKLOADS
+
+    workload = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, workload)
+        return
+
+    import numpy as np
+
+    from leo_b200.backend import GpuBackend
+    from leo_b200.ctypes_types import PHASES, TRAINING
+    from leo_b200.model import HostModel
+    from leo_b200.synthetic import story_stream
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+
+    cfg = workload.config
+    model = HostModel.initialize(cfg, workload.topology)
+    backend = GpuBackend(model, device=local, max_lanes=workload.workers)
+    total_batches = args.warmup + args.steps
+    stories = story_stream(workload.story_seed + 1000 * rank, workload.workers * total_batches,
+                           workload.min_story_bytes, workload.max_story_bytes)
+    batches = [stories[i * workload.workers:(i + 1) * workload.workers] for i in range(total_batches)]
+
+    # Warm-up, also used to find the dominant phase when none is given.
+    mask = args.phase_mask
+    backend.set_phase_timing(0x3FF if mask < 0 else mask)
+    for b in range(args.warmup):
+        backend.training_story_batch(batches[b], TRAINING)
+    warm = backend.perf_stats()
+    if mask < 0:
+        shares = [warm.phase_ms[i] for i in range(10)]
+        mask = 1 << int(np.argmax(shares))
+    backend.set_phase_timing(mask)
+    backend.reset_perf_stats()
+
+    if dist is not None:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    wall = 0.0
+    nbytes = 0
+    h2d = d2h = 0
+    for b in range(args.warmup, total_batches):
+        batch = batches[b]
+        t0 = time.perf_counter()
+        result = backend.training_story_batch(batch, TRAINING)
+        wall += time.perf_counter() - t0
+        nbytes += sum(len(s) for s in batch)
+        h2d += sum(len(s) for s in batch) + 8 * (len(batch) + 1)
+        d2h += 4 * sum(len(x) for x in result.losses) + 48 * len(batch) + 80
+    perf = backend.perf_stats()
+    clk = clocks.stop()
+    device_s = perf.batch_ms / 1000.0
+    times = np.array([device_s, wall, float(nbytes)], dtype=np.float64)
+    if dist is not None:
+        import torch
+
+        t = torch.tensor(times[:2], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        b = torch.tensor([times[2]], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(b, op=dist.ReduceOp.SUM)
+        device_s, wall, total_bytes = float(t[0]), float(t[1]), float(b[0])
+    else:
+        total_bytes = float(nbytes)
+
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        alg = phase_algorithmic_bytes(perf, cfg)
+        timed = [i for i in range(10) if (mask >> i) & 1 and perf.phase_launches[i]]
+        dom = timed[0] if timed else 4
+        name = PHASES[dom]
+        launches = max(perf.phase_launches[dom], 1)
+        per_launch_ms = perf.phase_ms[dom] / launches
+        per_launch_bytes = alg[name] / launches
+        achieved = per_launch_bytes / (per_launch_ms / 1000.0) / 1e9 if per_launch_ms > 0 else 0.0
+        roofline = {"bound": "hbm", "kernel": f"leo_{name}_kernel", "achieved": round(achieved, 3),
+                    "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 6), "peak_source": peak_kind,
+                    "traffic": None, "algorithmic_bytes_per_launch": round(per_launch_bytes, 1),
+                    "launch_ms": round(per_launch_ms, 5), "launches": launches,
+                    "share_of_step_time": round(perf.phase_ms[dom] / max(perf.batch_ms, 1e-9), 4)}
+        line = {
+            "metric": METRIC, "value": round(total_bytes / device_s, 3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(device_s * 1000 / args.steps, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded order-2 Markov printable-ASCII stories), random-init model",
+            "config": {"workload": workload.name, "neurons": cfg.neuron_count,
+                       "synapses_per_neuron": cfg.synapses_per_neuron, "workers": workload.workers,
+                       "story_bytes": [workload.min_story_bytes, workload.max_story_bytes],
+                       "replay_fraction": cfg.replay_fraction,
+                       "parallelism": f"{world} replica(s), {workload.workers} story lanes each",
+                       "l2": "per-batch working set (lanes x ~0.4 GB) exceeds L2"},
+            "e2e": {"value": round(total_bytes / wall, 3), "unit": UNIT, "h2d_bytes_per_step": h2d // args.steps,
+                    "d2h_bytes_per_step": d2h // args.steps},
+            "roofline": roofline, "clocks": clk, "gpu_launches": int(perf.launches),
+            "device_gb": round(backend.device_bytes() / 1e9, 3),
+        }
+        if not args.no_cpu_baseline:
+            res = cpu_sample(workload, min(args.cpu_stories, os.cpu_count() or 1), args.cpu_stories,
+                             args.cpu_bytes, 1)
+            line["cpu_baseline"] = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        print(json.dumps(line), flush=True)
+    backend.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

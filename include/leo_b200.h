@@ -93,6 +93,15 @@ int leo_b200_lane_model(LeoB200Device* device, uint32_t lane, LeoB200HostModel* 
 int leo_b200_lane_array(LeoB200Device* device, uint32_t lane, const char* name, void* out, size_t capacity,
                         size_t* written);
 
+/* Performance counters (LeoB200PerfStats): kernel launches, work units per
+   phase, batch time between CUDA events on the backend's stream, and -- for
+   the phases selected by `mask` (bit p = LeoB200Phase p) -- per-launch CUDA
+   event time, as the reference's phase profiler reports
+   (crates/leo-core/src/cuda.rs:6998, cuda_kernels.cu:5764-5789). */
+int leo_b200_set_phase_timing(LeoB200Device* device, uint32_t mask);
+int leo_b200_perf_stats(LeoB200Device* device, LeoB200PerfStats* out);
+int leo_b200_reset_perf_stats(LeoB200Device* device);
+
 /* Device memory held by the backend, in bytes. */
 size_t leo_b200_device_bytes(LeoB200Device* device);
 

@@ -166,6 +166,43 @@ typedef struct LeoB200BatchReport {
     uint64_t replay_prefix_steps;
 } LeoB200BatchReport;
 
+/* Step phases of the device path, in launch order. */
+#define LEO_B200_PHASES 11
+enum LeoB200Phase {
+    LEO_B200_PHASE_DELIVER = 0,
+    LEO_B200_PHASE_SETTLE = 1,
+    LEO_B200_PHASE_SELECT = 2,
+    LEO_B200_PHASE_SURROGATE = 3,
+    LEO_B200_PHASE_ELIGIBLE = 4,
+    LEO_B200_PHASE_EMIT_FORWARD = 5,
+    LEO_B200_PHASE_LEARN = 6,
+    LEO_B200_PHASE_PLASTICITY = 7,
+    LEO_B200_PHASE_INHIBIT = 8,
+    LEO_B200_PHASE_EPILOGUE = 9,
+    LEO_B200_PHASE_MERGE = 10
+};
+
+/* Performance counters since the last reset.  work_* sum, over lanes and
+   steps, the units each phase processed: due events plus input slots
+   (deliver), touched neurons (settle, surrogate, homeostasis), eligible
+   recurrent plus input slots before compaction (eligibility), learning
+   destinations on plasticity steps (signals), active neurons, and
+   post-compaction slots on plasticity steps (weight updates). */
+typedef struct LeoB200PerfStats {
+    uint64_t launches;
+    uint64_t phase_launches[LEO_B200_PHASES];
+    double phase_ms[LEO_B200_PHASES];
+    uint64_t work_deliver;
+    uint64_t work_touched;
+    uint64_t work_eligible;
+    uint64_t work_destinations;
+    uint64_t work_active;
+    uint64_t work_plastic;
+    uint64_t work_steps;
+    uint64_t batches;
+    double batch_ms;
+} LeoB200PerfStats;
+
 #ifdef __cplusplus
 }
 #endif

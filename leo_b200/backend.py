@@ -93,6 +93,19 @@ class GpuBackend:
     def canonical_tick(self, tick: int) -> None:
         native.check(native.lib().leo_b200_set_canonical_tick(self.handle, tick))
 
+    def set_phase_timing(self, mask: int) -> None:
+        native.check(native.lib().leo_b200_set_phase_timing(self.handle, mask))
+
+    def perf_stats(self):
+        from .ctypes_types import LeoB200PerfStats
+
+        st = LeoB200PerfStats()
+        native.check(native.lib().leo_b200_perf_stats(self.handle, C.byref(st)))
+        return st
+
+    def reset_perf_stats(self) -> None:
+        native.check(native.lib().leo_b200_reset_perf_stats(self.handle))
+
     def device_bytes(self) -> int:
         return native.lib().leo_b200_device_bytes(self.handle)
 

@@ -130,6 +130,9 @@ struct LaneScalars {
     unsigned long long processed_bytes, targets, active_sum, active_peak, synaptic_events;
     unsigned long long numerical_rejections, persistent_ticks, revision_increment, context_applied_steps;
     uint32_t error_flag;
+    // work counters (units per phase, summed over steps; see LeoB200PerfStats)
+    unsigned long long work_deliver, work_touched, work_eligible, work_destinations, work_active, work_plastic,
+        work_steps;
     // last-step metrics
     uint32_t last_active, last_suprathreshold, last_block_selected, last_clipped, last_predicted;
     float last_loss;

@@ -7,9 +7,18 @@
 
 #include "leo_device.cuh"
 
+// Optional CUDA events recorded around each phase's launch: phase p is timed
+// when (mask >> p) & 1, using start[p] / stop[p].
+struct PhaseEvents {
+    uint32_t mask;
+    cudaEvent_t start[11];
+    cudaEvent_t stop[11];
+};
+
 // One per-byte step (all phases) for every lane whose schedule covers step s.
-void leo_launch_step(const LaneState* lanes, int lane_count, uint32_t s, const KernelConsts& kc, int grid,
-                     cudaStream_t stream);
+// Returns the number of kernel launches issued.
+int leo_launch_step(const LaneState* lanes, int lane_count, uint32_t s, const KernelConsts& kc, int grid,
+                    cudaStream_t stream, const PhaseEvents* events);
 size_t leo_select_smem_bytes(const KernelConsts& kc);
 
 // Batch-end sparse merge of one fixed f32 tensor (threshold, recurrent, input,

@@ -123,7 +123,11 @@ struct LeoB200Device {
     bool single_story = false;
     std::vector<std::vector<uint8_t>> batch_stories;
     std::vector<LaneScalars> host_scalars;
-    float last_ms = 0.0f;
+    // performance counters
+    LeoB200PerfStats perf{};
+    uint32_t phase_mask = 0;
+    std::vector<PhaseEvents> phase_pool;
+    cudaEvent_t batch_start = nullptr, batch_stop = nullptr;
 };
 
 namespace {
@@ -351,8 +355,48 @@ void download_params(LeoB200Device& dev, const LaneParams& p, LeoB200HostModel& 
 
 // ---------------------------------------------------------------- stepping
 void run_steps(LeoB200Device& dev, const LaneState* d_lanes, int lane_count, uint32_t begin, uint32_t end) {
-    for (uint32_t s = begin; s < end; ++s) leo_launch_step(d_lanes, lane_count, s, dev.kc, dev.grid, dev.stream);
+    if (dev.phase_mask == 0) {
+        for (uint32_t s = begin; s < end; ++s)
+            dev.perf.launches += leo_launch_step(d_lanes, lane_count, s, dev.kc, dev.grid, dev.stream, nullptr);
+        CUDA_CHECK(cudaGetLastError());
+        return;
+    }
+    // Per-phase CUDA-event timing: one event pair per timed phase per step.
+    size_t steps = end > begin ? end - begin : 0;
+    while (dev.phase_pool.size() < steps) {
+        PhaseEvents pe{};
+        for (int p = 0; p < 11; ++p) {
+            CUDA_CHECK(cudaEventCreate(&pe.start[p]));
+            CUDA_CHECK(cudaEventCreate(&pe.stop[p]));
+        }
+        dev.phase_pool.push_back(pe);
+    }
+    for (uint32_t s = begin; s < end; ++s) {
+        PhaseEvents& pe = dev.phase_pool[s - begin];
+        pe.mask = dev.phase_mask;
+        dev.perf.launches += leo_launch_step(d_lanes, lane_count, s, dev.kc, dev.grid, dev.stream, &pe);
+    }
     CUDA_CHECK(cudaGetLastError());
+    CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+    for (size_t i = 0; i < steps; ++i) {
+        for (int p = 0; p < 10; ++p) {
+            if (!((dev.phase_mask >> p) & 1u)) continue;
+            float ms = 0.0f;
+            CUDA_CHECK(cudaEventElapsedTime(&ms, dev.phase_pool[i].start[p], dev.phase_pool[i].stop[p]));
+            dev.perf.phase_ms[p] += ms;
+            dev.perf.phase_launches[p] += 1;
+        }
+    }
+}
+
+void add_work(LeoB200Device& dev, const LaneScalars& sc) {
+    dev.perf.work_deliver += sc.work_deliver;
+    dev.perf.work_touched += sc.work_touched;
+    dev.perf.work_eligible += sc.work_eligible;
+    dev.perf.work_destinations += sc.work_destinations;
+    dev.perf.work_active += sc.work_active;
+    dev.perf.work_plastic += sc.work_plastic;
+    dev.perf.work_steps += sc.work_steps;
 }
 
 void read_scalars(LeoB200Device& dev, Lane& lane, LaneScalars& out) {
@@ -634,6 +678,7 @@ size_t merge_fixed(LeoB200Device& dev, uint32_t lane_count, const std::vector<La
         mt.kind = t.kind;
         leo_launch_merge_tensor(mt, dev.scratch, (int)lane_count, (int)resident, dev.cfg.abi.weight_min, dev.cfg.abi.weight_max,
                                 dev.kc.topo.neuron_type, (uint32_t)z.s, dev.grid, dev.stream);
+        dev.perf.launches += 4;
         // Each launch sequence reuses the pointer tables: wait before rewriting them.
         CUDA_CHECK(cudaStreamSynchronize(dev.stream));
     }
@@ -775,6 +820,7 @@ void run_canonical_schedule(LeoB200Device& dev, const std::vector<uint32_t>& sch
     LaneScalars sc;
     read_scalars(dev, rl, sc);
     check_error_flag(sc);
+    add_work(dev, sc);
     dev.canonical_tick += schedule.size();
     dev.revision += sc.revision_increment;
     dev.stats.processed_bytes += sc.processed_bytes;
@@ -866,7 +912,7 @@ void batch_begin(LeoB200Device& dev, const uint8_t* bytes, const uint64_t* offse
         dev.batch_lanes = stories;
         upload_lane_table(dev);
     }
-    CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+    CUDA_CHECK(cudaEventRecord(dev.batch_start, dev.stream));
     dev.batch_open = true;
 }
 
@@ -895,6 +941,7 @@ void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySu
         LaneScalars sc;
         read_scalars(dev, *dev.replay, sc);
         check_error_flag(sc);
+        add_work(dev, sc);
         if (!story.empty()) {
             losses[0].resize(story.size() + 1);
             CUDA_CHECK(cudaMemcpy(losses[0].data(), dev.replay->step_loss, losses[0].size() * 4, cudaMemcpyDeviceToHost));
@@ -934,6 +981,7 @@ void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySu
         for (uint32_t l = 0; l < L; ++l) {
             read_scalars(dev, *dev.lanes[l], scal[l]);
             check_error_flag(scal[l]);
+            add_work(dev, scal[l]);
             const auto& story = dev.batch_stories[l];
             if (!story.empty()) {
                 losses[l].resize(story.size() + 1);
@@ -987,6 +1035,12 @@ void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySu
             replay_story(dev, dev.batch_stories[l], losses[l], dev.batch_permission, replay_changes, &rep);
         sync_replay_changes(dev, replay_changes);
     }
+    CUDA_CHECK(cudaEventRecord(dev.batch_stop, dev.stream));
+    CUDA_CHECK(cudaEventSynchronize(dev.batch_stop));
+    float batch_ms = 0.0f;
+    CUDA_CHECK(cudaEventElapsedTime(&batch_ms, dev.batch_start, dev.batch_stop));
+    dev.perf.batch_ms += batch_ms;
+    dev.perf.batches += 1;
     if (losses_out) {
         size_t k = 0;
         for (auto& l : losses)
@@ -1051,6 +1105,8 @@ int leo_b200_open(int device, const LeoB200HostModel* canonical, uint32_t max_la
         CUDA_CHECK(cudaGetDeviceProperties(&prop, device));
         if (prop.major < 10) throw LeoFailure("leo_b200 requires an sm_100 (Blackwell) device");
         CUDA_CHECK(cudaStreamCreateWithFlags(&dev->stream, cudaStreamNonBlocking));
+        CUDA_CHECK(cudaEventCreate(&dev->batch_start));
+        CUDA_CHECK(cudaEventCreate(&dev->batch_stop));
         dev->cfg = canonical->config;
         dev->z = leo_host::sizes_of(dev->cfg);
         dev->kc = make_consts(*dev);
@@ -1138,6 +1194,13 @@ void leo_b200_close(LeoB200Device* dev) {
     cudaSetDevice(dev->device);
     cudaStreamSynchronize(dev->stream);
     cudaStream_t s = dev->stream;
+    for (auto& pe : dev->phase_pool)
+        for (int p = 0; p < 11; ++p) {
+            cudaEventDestroy(pe.start[p]);
+            cudaEventDestroy(pe.stop[p]);
+        }
+    if (dev->batch_start) cudaEventDestroy(dev->batch_start);
+    if (dev->batch_stop) cudaEventDestroy(dev->batch_stop);
     delete dev;
     cudaStreamDestroy(s);
 }
@@ -1391,6 +1454,21 @@ int leo_b200_lane_array(LeoB200Device* dev, uint32_t lane, const char* name, voi
     } catch (const std::exception& e) {
         return fail(e);
     }
+}
+
+int leo_b200_set_phase_timing(LeoB200Device* dev, uint32_t mask) {
+    dev->phase_mask = mask & ((1u << 10) - 1u);
+    return 0;
+}
+
+int leo_b200_perf_stats(LeoB200Device* dev, LeoB200PerfStats* out) {
+    *out = dev->perf;
+    return 0;
+}
+
+int leo_b200_reset_perf_stats(LeoB200Device* dev) {
+    dev->perf = LeoB200PerfStats{};
+    return 0;
 }
 
 size_t leo_b200_device_bytes(LeoB200Device* dev) {

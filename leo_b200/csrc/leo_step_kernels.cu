@@ -186,6 +186,7 @@ __global__ void __launch_bounds__(256) leo_deliver_kernel(const LaneState* __res
         if (blockIdx.x == 0 && threadIdx.x == 0) {
             sc->elig_count[cur ^ 1u] = 0;
             sc->in_elig_count[cur ^ 1u] = 0;
+            sc->work_deliver += events + F;
         }
         uint32_t epoch = s + 1;
         for (uint32_t i = lane_start(l); i < total; i += grid_stride()) {
@@ -1115,10 +1116,21 @@ __global__ void leo_epilogue_kernel(const LaneState* __restrict__ lanes, int lan
     if (l >= lane_count) return;
     const LaneState& ln = lanes[l];
     if (!lane_runs(ln, s)) return;
-    ln.sc->touched_count = 0;
-    ln.sc->dst_count = 0;
+    LaneScalars* sc = ln.sc;
+    bool frozen = LEO_SCHED_PERMISSION(ln.schedule[s]) == kFrozen;
+    uint32_t cur = sc->elig_cur;
+    sc->work_touched += sc->touched_count;
+    sc->work_active += sc->ring_count[s % LEO_RING];
+    sc->work_steps += 1;
+    if (!frozen) sc->work_eligible += sc->elig_count[cur] + sc->in_elig_count[cur];
+    if ((sc->step_flags & 3u) == 3u) {
+        sc->work_destinations += sc->dst_count;
+        sc->work_plastic += sc->elig_count[cur ^ 1u] + sc->in_elig_count[cur ^ 1u];
+    }
+    sc->touched_count = 0;
+    sc->dst_count = 0;
     // The eligibility phase ran (non-frozen step): its output list is now current.
-    if (LEO_SCHED_PERMISSION(ln.schedule[s]) != kFrozen) ln.sc->elig_cur ^= 1u;
+    if (!frozen) sc->elig_cur ^= 1u;
 }
 
 // ----------------------------------------------------------------------------
@@ -1128,18 +1140,45 @@ size_t leo_select_smem_bytes(const KernelConsts& kc) {
     return (size_t)(winners + span) * sizeof(unsigned long long);
 }
 
-void leo_launch_step(const LaneState* lanes, int lane_count, uint32_t s, const KernelConsts& kc, int grid,
-                     cudaStream_t stream) {
+int leo_launch_step(const LaneState* lanes, int lane_count, uint32_t s, const KernelConsts& kc, int grid,
+                    cudaStream_t stream, const PhaseEvents* ev) {
     size_t select_smem = leo_select_smem_bytes(kc);
+    auto begin = [&](int p) {
+        if (ev && ((ev->mask >> p) & 1u)) cudaEventRecord(ev->start[p], stream);
+    };
+    auto end = [&](int p) {
+        if (ev && ((ev->mask >> p) & 1u)) cudaEventRecord(ev->stop[p], stream);
+    };
+    begin(0);
     leo_deliver_kernel<<<grid, 256, 0, stream>>>(lanes, lane_count, s, kc);
+    end(0);
+    begin(1);
     leo_settle_kernel<<<grid, 256, 0, stream>>>(lanes, lane_count, s, kc);
+    end(1);
+    begin(2);
     leo_select_kernel<<<lane_count, 512, select_smem, stream>>>(lanes, s, kc);
+    end(2);
+    begin(3);
     leo_surrogate_kernel<<<grid, 256, 0, stream>>>(lanes, lane_count, s, kc);
+    end(3);
+    begin(4);
     leo_eligible_kernel<<<grid, 256, 0, stream>>>(lanes, lane_count, s, kc);
+    end(4);
+    begin(5);
     leo_emit_forward_kernel<<<lane_count + grid, 288, 0, stream>>>(lanes, lane_count, s, kc);
+    end(5);
+    begin(6);
     leo_learn_kernel<<<grid, 256, 0, stream>>>(lanes, lane_count, s, kc);
+    end(6);
+    begin(7);
     leo_plasticity_kernel<<<grid, 256, 0, stream>>>(lanes, lane_count, s, kc);
+    end(7);
+    begin(8);
     leo_inhibit_kernel<<<grid, 256, 0, stream>>>(lanes, lane_count, s, kc);
+    end(8);
+    begin(9);
     leo_epilogue_kernel<<<(lane_count + 127) / 128, 128, 0, stream>>>(lanes, lane_count, s);
+    end(9);
+    return 10;
 }
 

@@ -131,3 +131,24 @@ class LeoB200BatchReport(C.Structure):
 FROZEN, PROVISIONAL, TRAINING, VERIFIED = 0, 1, 2, 3
 TOPOLOGY_REFERENCE, TOPOLOGY_UNIFORM, TOPOLOGY_ZIPF = 0, 1, 2
 BEGIN_DOCUMENT, END_DOCUMENT, SYMBOL_COUNT, OUTPUT_CLASSES = 256, 257, 258, 257
+
+
+PHASES = ["deliver", "settle", "select", "surrogate", "eligible", "emit_forward", "learn", "plasticity", "inhibit",
+          "epilogue", "merge"]
+
+
+class LeoB200PerfStats(C.Structure):
+    _fields_ = [
+        ("launches", C.c_uint64),
+        ("phase_launches", C.c_uint64 * 11),
+        ("phase_ms", C.c_double * 11),
+        ("work_deliver", C.c_uint64),
+        ("work_touched", C.c_uint64),
+        ("work_eligible", C.c_uint64),
+        ("work_destinations", C.c_uint64),
+        ("work_active", C.c_uint64),
+        ("work_plastic", C.c_uint64),
+        ("work_steps", C.c_uint64),
+        ("batches", C.c_uint64),
+        ("batch_ms", C.c_double),
+    ]

@@ -12,6 +12,7 @@ from .ctypes_types import (
     LeoB200BatchReport,
     LeoB200Config,
     LeoB200HostModel,
+    LeoB200PerfStats,
     LeoB200StorySummary,
 )
 
@@ -63,6 +64,9 @@ def lib() -> C.CDLL:
     L.leo_b200_state_digest.argtypes = [vp, vp]
     L.leo_b200_lane_model.argtypes = [vp, u32, P(LeoB200HostModel)]
     L.leo_b200_lane_array.argtypes = [vp, u32, C.c_char_p, vp, sz, P(sz)]
+    L.leo_b200_set_phase_timing.argtypes = [vp, u32]
+    L.leo_b200_perf_stats.argtypes = [vp, P(LeoB200PerfStats)]
+    L.leo_b200_reset_perf_stats.argtypes = [vp]
     L.leo_b200_device_bytes.argtypes = [vp]
     L.leo_b200_device_bytes.restype = sz
     _lib = L
