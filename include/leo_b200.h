@@ -94,13 +94,17 @@ int leo_b200_lane_array(LeoB200Device* device, uint32_t lane, const char* name, 
                         size_t* written);
 
 /* Performance counters (LeoB200PerfStats): kernel launches, work units per
-   phase, batch time between CUDA events on the backend's stream, and -- for
-   the phases selected by `mask` (bit p = LeoB200Phase p) -- per-launch CUDA
-   event time, as the reference's phase profiler reports
+   phase, per-phase clock counters and CUDA-event time of the wavefront
+   launches, as the reference's phase profiler reports
    (crates/leo-core/src/cuda.rs:6998, cuda_kernels.cu:5764-5789). */
-int leo_b200_set_phase_timing(LeoB200Device* device, uint32_t mask);
 int leo_b200_perf_stats(LeoB200Device* device, LeoB200PerfStats* out);
 int leo_b200_reset_perf_stats(LeoB200Device* device);
+
+/* Execution geometry only (results do not depend on it): CTAs per thread-block
+   cluster for story lanes and for the canonical replay lane; 0 picks the
+   default (the largest size whose clusters all fit at once).  The reference's
+   execution tuner chooses the analogous geometry (crates/leo-core/src/cuda_plan.rs:189-453). */
+int leo_b200_set_cluster_sizes(LeoB200Device* device, uint32_t story_cluster, uint32_t replay_cluster);
 
 /* Device memory held by the backend, in bytes. */
 size_t leo_b200_device_bytes(LeoB200Device* device);

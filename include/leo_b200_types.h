@@ -166,20 +166,20 @@ typedef struct LeoB200BatchReport {
     uint64_t replay_prefix_steps;
 } LeoB200BatchReport;
 
-/* Step phases of the device path, in launch order. */
+/* Phases of one step of the persistent wavefront, in execution order. */
 #define LEO_B200_PHASES 11
 enum LeoB200Phase {
     LEO_B200_PHASE_DELIVER = 0,
     LEO_B200_PHASE_SETTLE = 1,
-    LEO_B200_PHASE_SELECT = 2,
-    LEO_B200_PHASE_SURROGATE = 3,
-    LEO_B200_PHASE_ELIGIBLE = 4,
-    LEO_B200_PHASE_EMIT_FORWARD = 5,
-    LEO_B200_PHASE_LEARN = 6,
-    LEO_B200_PHASE_PLASTICITY = 7,
-    LEO_B200_PHASE_INHIBIT = 8,
-    LEO_B200_PHASE_EPILOGUE = 9,
-    LEO_B200_PHASE_MERGE = 10
+    LEO_B200_PHASE_BLOCKS = 2,
+    LEO_B200_PHASE_ASSEMBLE = 3,
+    LEO_B200_PHASE_SURROGATE = 4,
+    LEO_B200_PHASE_ELIGIBLE = 5,
+    LEO_B200_PHASE_EMIT_FORWARD = 6,
+    LEO_B200_PHASE_LEARN = 7,
+    LEO_B200_PHASE_PLASTICITY = 8,
+    LEO_B200_PHASE_INHIBIT = 9,
+    LEO_B200_PHASE_UNUSED = 10
 };
 
 /* Performance counters since the last reset.  work_* sum, over lanes and
@@ -187,11 +187,17 @@ enum LeoB200Phase {
    (deliver), touched neurons (settle, surrogate, homeostasis), eligible
    recurrent plus input slots before compaction (eligibility), learning
    destinations on plasticity steps (signals), active neurons, and
-   post-compaction slots on plasticity steps (weight updates). */
+   post-compaction slots on plasticity steps (weight updates).  phase_cycles
+   are SM clock cycles spent in each phase (barrier waits included) by the
+   first thread of each lane's first CTA; wavefront_ms is CUDA-event time of
+   the persistent wavefront launches (story_* for the story-pass launches). */
 typedef struct LeoB200PerfStats {
     uint64_t launches;
-    uint64_t phase_launches[LEO_B200_PHASES];
-    double phase_ms[LEO_B200_PHASES];
+    uint64_t wavefront_launches;
+    double wavefront_ms;
+    uint64_t story_wavefront_launches;
+    double story_wavefront_ms;
+    uint64_t phase_cycles[LEO_B200_PHASES];
     uint64_t work_deliver;
     uint64_t work_touched;
     uint64_t work_eligible;
@@ -199,8 +205,11 @@ typedef struct LeoB200PerfStats {
     uint64_t work_active;
     uint64_t work_plastic;
     uint64_t work_steps;
+    uint64_t story_work_steps;
     uint64_t batches;
     double batch_ms;
+    uint32_t story_cluster;
+    uint32_t replay_cluster;
 } LeoB200PerfStats;
 
 #ifdef __cplusplus

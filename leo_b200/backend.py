@@ -93,8 +93,8 @@ class GpuBackend:
     def canonical_tick(self, tick: int) -> None:
         native.check(native.lib().leo_b200_set_canonical_tick(self.handle, tick))
 
-    def set_phase_timing(self, mask: int) -> None:
-        native.check(native.lib().leo_b200_set_phase_timing(self.handle, mask))
+    def set_cluster_sizes(self, story: int = 0, replay: int = 0) -> None:
+        native.check(native.lib().leo_b200_set_cluster_sizes(self.handle, story, replay))
 
     def perf_stats(self):
         from .ctypes_types import LeoB200PerfStats

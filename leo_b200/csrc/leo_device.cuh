@@ -34,6 +34,8 @@
 #define LEO_EMPTY 0xffffffffu
 #define LEO_MAX_CONTEXT_ORDER 16u
 #define LEO_MAX_EMBEDDING 256u
+#define LEO_WAVEFRONT_THREADS 512u  // threads per CTA of the persistent wavefront
+#define LEO_PHASES 11
 
 // Packed topology words.
 #define LEO_TARGET_MASK 0x00ffffffu
@@ -133,6 +135,8 @@ struct LaneScalars {
     // work counters (units per phase, summed over steps; see LeoB200PerfStats)
     unsigned long long work_deliver, work_touched, work_eligible, work_destinations, work_active, work_plastic,
         work_steps;
+    unsigned long long phase_cycles[LEO_PHASES];  // SM clock cycles per phase (first CTA, first thread)
+    uint32_t step_supra;                          // candidates of the current tick (all blocks)
     // last-step metrics
     uint32_t last_active, last_suprathreshold, last_block_selected, last_clipped, last_predicted;
     float last_loss;
@@ -159,6 +163,8 @@ struct LaneState {
     unsigned long long* block_cand;  // [blocks * npb] packed selection keys
     uint32_t* block_cand_count;      // [blocks]
     float* block_cutoff;             // [blocks]
+    unsigned long long* block_winners;  // [blocks * keep] winners of each block in rank order
+    uint32_t* block_nwin;               // [blocks]
     uint32_t* ring_src;         // [9 * max_active]
     float* ring_act;            // [9 * max_active]
     float* ring_val;            // [9 * max_active * S] emitted a * w snapshots
@@ -190,11 +196,9 @@ struct KernelConsts {
     float dropout_rate;
     uint32_t track_changes;
     unsigned long long seed;
-    const uint32_t* exp_keys;
-    const uint32_t* exp_values;
-    const uint32_t* log_keys;
-    const uint32_t* log_values;
-    int exp_count;
-    int log_count;
+    const uint2* exp_table;   // open-addressing (input bits, output bits), empty key 0xffffffff
+    const uint2* log_table;
+    uint32_t exp_mask;        // capacity - 1 (power of two)
+    uint32_t log_mask;
     uint32_t event_capacity;
 };

@@ -7,19 +7,13 @@
 
 #include "leo_device.cuh"
 
-// Optional CUDA events recorded around each phase's launch: phase p is timed
-// when (mask >> p) & 1, using start[p] / stop[p].
-struct PhaseEvents {
-    uint32_t mask;
-    cudaEvent_t start[11];
-    cudaEvent_t stop[11];
-};
-
-// One per-byte step (all phases) for every lane whose schedule covers step s.
-// Returns the number of kernel launches issued.
-int leo_launch_step(const LaneState* lanes, int lane_count, uint32_t s, const KernelConsts& kc, int grid,
-                    cudaStream_t stream, const PhaseEvents* events);
-size_t leo_select_smem_bytes(const KernelConsts& kc);
+// The persistent wavefront: lane_count clusters of `cluster` CTAs, each
+// running its lane's schedule over steps [begin, end).
+cudaError_t leo_launch_wavefront(const LaneState* lanes, int lane_count, uint32_t cluster, uint32_t begin,
+                                 uint32_t end, const KernelConsts& kc, cudaStream_t stream);
+size_t leo_wavefront_smem_bytes(const KernelConsts& kc);
+// Clusters of `cluster` CTAs that can be resident at once.
+cudaError_t leo_wavefront_max_clusters(uint32_t cluster, const KernelConsts& kc, int* out);
 
 // Batch-end sparse merge of one fixed f32 tensor (threshold, recurrent, input,
 // output rows, bias, context output): see leo_merge_kernels.cu.

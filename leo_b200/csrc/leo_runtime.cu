@@ -123,11 +123,11 @@ struct LeoB200Device {
     bool single_story = false;
     std::vector<std::vector<uint8_t>> batch_stories;
     std::vector<LaneScalars> host_scalars;
-    // performance counters
+    // performance counters and execution geometry
     LeoB200PerfStats perf{};
-    uint32_t phase_mask = 0;
-    std::vector<PhaseEvents> phase_pool;
+    uint32_t story_cluster_request = 0, replay_cluster_request = 0;
     cudaEvent_t batch_start = nullptr, batch_stop = nullptr;
+    cudaEvent_t wave_start = nullptr, wave_stop = nullptr;
 };
 
 namespace {
@@ -170,6 +170,8 @@ void allocate_lane_transient(LeoB200Device& dev, Lane& lane) {
     st.block_cand = m.alloc<unsigned long long>((size_t)B * npb);
     st.block_cand_count = m.alloc<uint32_t>(B);
     st.block_cutoff = m.alloc<float>(B);
+    st.block_winners = m.alloc<unsigned long long>((size_t)B * dev.cfg.abi.max_active_per_block);
+    st.block_nwin = m.alloc<uint32_t>(B);
     st.ring_src = m.alloc<uint32_t>((size_t)LEO_RING * maxa);
     st.ring_act = m.alloc<float>((size_t)LEO_RING * maxa);
     st.ring_val = m.alloc<float>((size_t)LEO_RING * maxa * z.s);
@@ -354,42 +356,47 @@ void download_params(LeoB200Device& dev, const LaneParams& p, LeoB200HostModel& 
 }
 
 // ---------------------------------------------------------------- stepping
-void run_steps(LeoB200Device& dev, const LaneState* d_lanes, int lane_count, uint32_t begin, uint32_t end) {
-    if (dev.phase_mask == 0) {
-        for (uint32_t s = begin; s < end; ++s)
-            dev.perf.launches += leo_launch_step(d_lanes, lane_count, s, dev.kc, dev.grid, dev.stream, nullptr);
-        CUDA_CHECK(cudaGetLastError());
-        return;
+// Picks the cluster size for `lanes` concurrent lanes: the requested size,
+// else the largest size (<= 16) whose clusters can all be resident at once.
+uint32_t pick_cluster(LeoB200Device& dev, uint32_t lanes, uint32_t request, uint32_t limit) {
+    if (request) return request;
+    for (uint32_t c = limit; c >= 1; c >>= 1) {
+        int fit = 0;
+        if (leo_wavefront_max_clusters(c, dev.kc, &fit) == cudaSuccess && (uint32_t)fit >= lanes) return c;
+        cudaGetLastError();
     }
-    // Per-phase CUDA-event timing: one event pair per timed phase per step.
-    size_t steps = end > begin ? end - begin : 0;
-    while (dev.phase_pool.size() < steps) {
-        PhaseEvents pe{};
-        for (int p = 0; p < 11; ++p) {
-            CUDA_CHECK(cudaEventCreate(&pe.start[p]));
-            CUDA_CHECK(cudaEventCreate(&pe.stop[p]));
-        }
-        dev.phase_pool.push_back(pe);
-    }
-    for (uint32_t s = begin; s < end; ++s) {
-        PhaseEvents& pe = dev.phase_pool[s - begin];
-        pe.mask = dev.phase_mask;
-        dev.perf.launches += leo_launch_step(d_lanes, lane_count, s, dev.kc, dev.grid, dev.stream, &pe);
-    }
+    return 1;
+}
+
+// Runs steps [begin, end) of every lane in `d_lanes` with one persistent
+// wavefront launch, timed with CUDA events on the backend's stream.
+void run_steps(LeoB200Device& dev, const LaneState* d_lanes, int lane_count, uint32_t begin, uint32_t end,
+               bool story) {
+    if (end <= begin || lane_count == 0) return;
+    uint32_t cluster = story ? pick_cluster(dev, (uint32_t)lane_count, dev.story_cluster_request, 16)
+                             : pick_cluster(dev, 1, dev.replay_cluster_request, 16);
+    CUDA_CHECK(cudaEventRecord(dev.wave_start, dev.stream));
+    CUDA_CHECK(leo_launch_wavefront(d_lanes, lane_count, cluster, begin, end, dev.kc, dev.stream));
     CUDA_CHECK(cudaGetLastError());
-    CUDA_CHECK(cudaStreamSynchronize(dev.stream));
-    for (size_t i = 0; i < steps; ++i) {
-        for (int p = 0; p < 10; ++p) {
-            if (!((dev.phase_mask >> p) & 1u)) continue;
-            float ms = 0.0f;
-            CUDA_CHECK(cudaEventElapsedTime(&ms, dev.phase_pool[i].start[p], dev.phase_pool[i].stop[p]));
-            dev.perf.phase_ms[p] += ms;
-            dev.perf.phase_launches[p] += 1;
-        }
+    CUDA_CHECK(cudaEventRecord(dev.wave_stop, dev.stream));
+    CUDA_CHECK(cudaEventSynchronize(dev.wave_stop));
+    float ms = 0.0f;
+    CUDA_CHECK(cudaEventElapsedTime(&ms, dev.wave_start, dev.wave_stop));
+    dev.perf.launches += 1;
+    dev.perf.wavefront_launches += 1;
+    dev.perf.wavefront_ms += ms;
+    if (story) {
+        dev.perf.story_wavefront_launches += 1;
+        dev.perf.story_wavefront_ms += ms;
+        dev.perf.story_cluster = cluster;
+    } else {
+        dev.perf.replay_cluster = cluster;
     }
 }
 
-void add_work(LeoB200Device& dev, const LaneScalars& sc) {
+void add_work(LeoB200Device& dev, const LaneScalars& sc, bool story) {
+    for (int p = 0; p < LEO_PHASES; ++p) dev.perf.phase_cycles[p] += sc.phase_cycles[p];
+    if (story) dev.perf.story_work_steps += sc.work_steps;
     dev.perf.work_deliver += sc.work_deliver;
     dev.perf.work_touched += sc.work_touched;
     dev.perf.work_eligible += sc.work_eligible;
@@ -816,11 +823,11 @@ void run_canonical_schedule(LeoB200Device& dev, const std::vector<uint32_t>& sch
     carry.bias_dirty = out.bias_dirty;
     carry.ctx_out_dirty = out.ctx_out_dirty;
     CUDA_CHECK(cudaMemcpyAsync(rl.st.sc, &carry, sizeof(carry), cudaMemcpyHostToDevice, dev.stream));
-    run_steps(dev, dev.d_replay, 1, 0, (uint32_t)schedule.size());
+    run_steps(dev, dev.d_replay, 1, 0, (uint32_t)schedule.size(), false);
     LaneScalars sc;
     read_scalars(dev, rl, sc);
     check_error_flag(sc);
-    add_work(dev, sc);
+    add_work(dev, sc, false);
     dev.canonical_tick += schedule.size();
     dev.revision += sc.revision_increment;
     dev.stats.processed_bytes += sc.processed_bytes;
@@ -920,9 +927,9 @@ void batch_steps(LeoB200Device& dev, uint32_t count) {
     if (!dev.batch_open) throw LeoFailure("no story batch in progress");
     uint32_t end = std::min(dev.batch_steps, dev.steps_done + count);
     if (dev.single_story)
-        run_steps(dev, dev.d_replay, 1, dev.steps_done, end);
+        run_steps(dev, dev.d_replay, 1, dev.steps_done, end, false);
     else
-        run_steps(dev, dev.d_lanes, (int)dev.batch_lanes, dev.steps_done, end);
+        run_steps(dev, dev.d_lanes, (int)dev.batch_lanes, dev.steps_done, end, true);
     dev.steps_done = end;
 }
 
@@ -941,7 +948,7 @@ void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySu
         LaneScalars sc;
         read_scalars(dev, *dev.replay, sc);
         check_error_flag(sc);
-        add_work(dev, sc);
+        add_work(dev, sc, true);
         if (!story.empty()) {
             losses[0].resize(story.size() + 1);
             CUDA_CHECK(cudaMemcpy(losses[0].data(), dev.replay->step_loss, losses[0].size() * 4, cudaMemcpyDeviceToHost));
@@ -981,7 +988,7 @@ void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySu
         for (uint32_t l = 0; l < L; ++l) {
             read_scalars(dev, *dev.lanes[l], scal[l]);
             check_error_flag(scal[l]);
-            add_work(dev, scal[l]);
+            add_work(dev, scal[l], true);
             const auto& story = dev.batch_stories[l];
             if (!story.empty()) {
                 losses[l].resize(story.size() + 1);
@@ -1107,6 +1114,8 @@ int leo_b200_open(int device, const LeoB200HostModel* canonical, uint32_t max_la
         CUDA_CHECK(cudaStreamCreateWithFlags(&dev->stream, cudaStreamNonBlocking));
         CUDA_CHECK(cudaEventCreate(&dev->batch_start));
         CUDA_CHECK(cudaEventCreate(&dev->batch_stop));
+        CUDA_CHECK(cudaEventCreate(&dev->wave_start));
+        CUDA_CHECK(cudaEventCreate(&dev->wave_stop));
         dev->cfg = canonical->config;
         dev->z = leo_host::sizes_of(dev->cfg);
         dev->kc = make_consts(*dev);
@@ -1131,21 +1140,27 @@ int leo_b200_open(int device, const LeoB200HostModel* canonical, uint32_t max_la
         t.neuron_type = dev->mem.alloc<uint8_t>(z.n);
         t.excitability = dev->mem.alloc<float>(z.n);
         dev->kc.event_capacity = 4u * t.max_active * t.s + t.f;
-        // libm exception tables (leo_math.cuh)
-        uint32_t* ek = dev->mem.alloc<uint32_t>(LEO_EXP_EXCEPTIONS);
-        uint32_t* ev = dev->mem.alloc<uint32_t>(LEO_EXP_EXCEPTIONS);
-        uint32_t* lk = dev->mem.alloc<uint32_t>(LEO_LOG_EXCEPTIONS);
-        uint32_t* lv = dev->mem.alloc<uint32_t>(LEO_LOG_EXCEPTIONS);
-        CUDA_CHECK(cudaMemcpy(ek, leo_exp_exception_keys, sizeof(leo_exp_exception_keys), cudaMemcpyHostToDevice));
-        CUDA_CHECK(cudaMemcpy(ev, leo_exp_exception_values, sizeof(leo_exp_exception_values), cudaMemcpyHostToDevice));
-        CUDA_CHECK(cudaMemcpy(lk, leo_log_exception_keys, sizeof(leo_log_exception_keys), cudaMemcpyHostToDevice));
-        CUDA_CHECK(cudaMemcpy(lv, leo_log_exception_values, sizeof(leo_log_exception_values), cudaMemcpyHostToDevice));
-        dev->kc.exp_keys = ek;
-        dev->kc.exp_values = ev;
-        dev->kc.log_keys = lk;
-        dev->kc.log_values = lv;
-        dev->kc.exp_count = LEO_EXP_EXCEPTIONS;
-        dev->kc.log_count = LEO_LOG_EXCEPTIONS;
+        // libm exception tables (leo_math.cuh) as open-addressing hash tables
+        auto build_table = [&](const uint32_t* keys, const uint32_t* values, size_t count, uint32_t* mask_out) {
+            size_t cap = 1024;
+            while (cap < count * 3) cap <<= 1;
+            std::vector<uint2> table(cap, make_uint2(0xffffffffu, 0u));
+            uint32_t mask = (uint32_t)cap - 1u;
+            for (size_t i = 0; i < count; ++i) {
+                if (keys[i] == 0xffffffffu) continue;
+                uint32_t h = (keys[i] * 0x9E3779B1u) & mask;
+                while (table[h].x != 0xffffffffu) h = (h + 1u) & mask;
+                table[h] = make_uint2(keys[i], values[i]);
+            }
+            uint2* d = dev->mem.alloc<uint2>(cap);
+            CUDA_CHECK(cudaMemcpy(d, table.data(), cap * sizeof(uint2), cudaMemcpyHostToDevice));
+            *mask_out = mask;
+            return (const uint2*)d;
+        };
+        dev->kc.exp_table = build_table(leo_exp_exception_keys, leo_exp_exception_values, LEO_EXP_EXCEPTIONS,
+                                        &dev->kc.exp_mask);
+        dev->kc.log_table = build_table(leo_log_exception_keys, leo_log_exception_values, LEO_LOG_EXCEPTIONS,
+                                        &dev->kc.log_mask);
         // canonical parameters
         LaneParams& p = dev->canon;
         p.threshold = dev->mem.alloc<float>(z.n);
@@ -1179,8 +1194,7 @@ int leo_b200_open(int device, const LeoB200HostModel* canonical, uint32_t max_la
         dev->replay->st.p = dev->canon;
         allocate_lane_transient(*dev, *dev->replay);
         dev->grid = prop.multiProcessorCount * 4;
-        size_t smem = leo_select_smem_bytes(dev->kc);
-        if (smem > 48 * 1024) throw LeoFailure("block winners exceed the select kernel's shared memory");
+        if (leo_wavefront_smem_bytes(dev->kc) > 64 * 1024) throw LeoFailure("block winners exceed shared memory");
         upload_model(*dev, *canonical);
         *out = dev.release();
         return 0;
@@ -1194,11 +1208,8 @@ void leo_b200_close(LeoB200Device* dev) {
     cudaSetDevice(dev->device);
     cudaStreamSynchronize(dev->stream);
     cudaStream_t s = dev->stream;
-    for (auto& pe : dev->phase_pool)
-        for (int p = 0; p < 11; ++p) {
-            cudaEventDestroy(pe.start[p]);
-            cudaEventDestroy(pe.stop[p]);
-        }
+    if (dev->wave_start) cudaEventDestroy(dev->wave_start);
+    if (dev->wave_stop) cudaEventDestroy(dev->wave_stop);
     if (dev->batch_start) cudaEventDestroy(dev->batch_start);
     if (dev->batch_stop) cudaEventDestroy(dev->batch_stop);
     delete dev;
@@ -1456,8 +1467,14 @@ int leo_b200_lane_array(LeoB200Device* dev, uint32_t lane, const char* name, voi
     }
 }
 
-int leo_b200_set_phase_timing(LeoB200Device* dev, uint32_t mask) {
-    dev->phase_mask = mask & ((1u << 10) - 1u);
+int leo_b200_set_cluster_sizes(LeoB200Device* dev, uint32_t story_cluster, uint32_t replay_cluster) {
+    auto ok = [](uint32_t c) { return c == 0 || c == 1 || c == 2 || c == 4 || c == 8 || c == 16; };
+    if (!ok(story_cluster) || !ok(replay_cluster)) {
+        g_error = "cluster sizes must be 0 (default), 1, 2, 4, 8 or 16";
+        return -1;
+    }
+    dev->story_cluster_request = story_cluster;
+    dev->replay_cluster_request = replay_cluster;
     return 0;
 }
 

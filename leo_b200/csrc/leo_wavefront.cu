@@ -1,0 +1,1271 @@
+// Persistent per-byte wavefront for sm_100a.
+//
+// One thread-block cluster owns one lane (a logical story worker, or the
+// canonical replay lane) and runs a whole step schedule in one launch.  The
+// phases of every step are separated by cluster barriers
+// (barrier.cluster.arrive.release / wait.acquire) instead of kernel
+// boundaries or grid-wide syncs: lanes are independent until the batch end,
+// so no lane ever waits for another and no story is held in lockstep with the
+// longest one.  Per-lane counters live in global memory (L2).
+//
+// Reference counterparts (crates/leo-core/src/runtime.rs = CPU,
+// crates/leo-core/src/cuda_kernels.cu = the reference's GPU wavefront
+// leo_shared_wavefront_persistent_grouped, :5805-6113, which uses 17
+// grid.sync() per byte across all lanes):
+//   deliver    start_tick touches, deliver_due_events, inject_symbol
+//              (runtime.rs:537-639; cuda_kernels.cu:1705-1807) and, on one
+//              warp, context resolve (runtime.rs:641-708, model.rs:173-221)
+//   settle     decay-on-touch, ordered branch accumulation, integration
+//              (runtime.rs:576-603, 710-717, 940-962)
+//   blocks     block-local top-k with the exact (k+1)-th cutoff
+//              (runtime.rs:964-997)
+//   assemble   active list, global cap, population inhibition
+//              (runtime.rs:998-1082; cuda_kernels.cu:2285-2586)
+//   surrogate  selection surrogates and destination Jacobians
+//              (runtime.rs:775-803)
+//   eligible   eligibility traces over the exact worklist, ballot compaction
+//              (runtime.rs:805-918; cuda_kernels.cu:2651-2846)
+//   emit       post-activation dynamics and emission (runtime.rs:920-938,
+//              1084-1106) beside the forward pass on the cluster's first CTA:
+//              logits, context latent, softmax, loss, output bias and context
+//              learning (runtime.rs:1108-1197, 1199-1384)
+//   learn      learning signals, output rows, threshold homeostasis
+//              (runtime.rs:1216-1303, 1567-1593)
+//   plasticity recurrent / input weight updates (runtime.rs:1451-1523)
+//   inhibit    inhibitory homeostasis (runtime.rs:1525-1565) + step epilogue
+// Frozen steps (replay prefixes) run deliver, settle, blocks, assemble and
+// emit only: nothing else can change state on a frozen step.
+//
+// Exactness: every floating-point sum that the CPU forms sequentially is
+// formed sequentially here in the same order (branch inputs in event order,
+// logits over the active list, softmax over the 257 outputs, learning
+// signals over the 257 outputs), no multiply-add is fused (-fmad=false), and
+// exp/ln reproduce the platform libm (leo_math.cuh plus exception tables).
+#include <cooperative_groups.h>
+#include <stdint.h>
+
+#include "leo_device.cuh"
+#include "leo_kernels.h"
+#include "leo_math.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace {
+
+constexpr uint32_t kFrozen = 0;
+constexpr uint32_t kThreads = LEO_WAVEFRONT_THREADS;
+constexpr uint32_t kWarps = kThreads / 32;
+
+__device__ __forceinline__ float clampf(float v, float lo, float hi) {
+    if (v < lo) v = lo;
+    if (v > hi) v = hi;
+    return v;
+}
+// Rust f32::max / f32::min (a NaN operand yields the other operand).
+__device__ __forceinline__ float rmax(float a, float b) {
+    if (isnan(a)) return b;
+    if (isnan(b)) return a;
+    return a > b ? a : (b > a ? b : a);
+}
+__device__ __forceinline__ float rmin(float a, float b) {
+    if (isnan(a)) return b;
+    if (isnan(b)) return a;
+    return a < b ? a : (b < a ? b : a);
+}
+// Rust's f32 Sum folds from -0.0.
+__device__ __forceinline__ float sum3(float a, float b, float c) {
+    float s = -0.0f;
+    s = s + a;
+    s = s + b;
+    s = s + c;
+    return s;
+}
+
+// Open-addressing lookup of the libm exception tables (built by the host from
+// libm_tables.inc): empty slots hold key 0xffffffff, which no domain input has.
+__device__ __forceinline__ bool exception_lookup(const uint2* table, uint32_t mask, uint32_t key, uint32_t* out) {
+    uint32_t h = (key * 0x9E3779B1u) & mask;
+    for (uint32_t probe = 0; probe <= mask; ++probe) {
+        uint2 e = table[h];
+        if (e.x == key) {
+            *out = e.y;
+            return true;
+        }
+        if (e.x == 0xffffffffu) return false;
+        h = (h + 1u) & mask;
+    }
+    return false;
+}
+__device__ __forceinline__ float leo_expf(const KernelConsts& kc, float x) {
+    if (x < -150.0f) return 0.0f;
+    uint32_t out;
+    if (exception_lookup(kc.exp_table, kc.exp_mask, __float_as_uint(x), &out)) return __uint_as_float(out);
+    return __double2float_rn(leo_math::exp_double((double)x));
+}
+__device__ __forceinline__ float leo_logf(const KernelConsts& kc, float x) {
+    uint32_t out;
+    if (exception_lookup(kc.log_table, kc.log_mask, __float_as_uint(x), &out)) return __uint_as_float(out);
+    return __double2float_rn(leo_math::log_double_of_float(x));
+}
+
+// Packed selection key: activation bits (positive floats order like their
+// bits) above the complement of the rotated tie key (runtime.rs:99-101); a
+// larger key is a better candidate.
+__device__ __forceinline__ unsigned long long selection_key(float act, uint32_t neuron, uint32_t rotation,
+                                                            uint32_t n) {
+    uint32_t rotated = (uint32_t)(((unsigned long long)neuron + n - rotation) % n);
+    return ((unsigned long long)__float_as_uint(act) << 32) | (unsigned long long)(0xffffffffu - rotated);
+}
+__device__ __forceinline__ float key_value(unsigned long long key) { return __uint_as_float((uint32_t)(key >> 32)); }
+__device__ __forceinline__ uint32_t key_neuron(unsigned long long key, uint32_t rotation, uint32_t n) {
+    uint32_t rotated = 0xffffffffu - (uint32_t)(key & 0xffffffffu);
+    return (uint32_t)(((unsigned long long)rotated + rotation) % n);
+}
+
+__device__ __forceinline__ Trace load_trace(const Trace* p) {
+    const float4* q = reinterpret_cast<const float4*>(p);
+    float4 a = q[0], b = q[1];
+    Trace t;
+    t.branch_sens = a.x;
+    t.membrane_sens = a.y;
+    t.fatigue_sens = a.z;
+    t.adaptation_sens[0] = a.w;
+    t.adaptation_sens[1] = b.x;
+    t.adaptation_sens[2] = b.y;
+    t.eligibility = b.z;
+    t.tick_mark = __float_as_uint(b.w);
+    return t;
+}
+__device__ __forceinline__ void store_trace(Trace* p, const Trace& t) {
+    float4* q = reinterpret_cast<float4*>(p);
+    q[0] = make_float4(t.branch_sens, t.membrane_sens, t.fatigue_sens, t.adaptation_sens[0]);
+    q[1] = make_float4(t.adaptation_sens[1], t.adaptation_sens[2], t.eligibility, __uint_as_float(t.tick_mark));
+}
+
+// runtime.rs:737-773 advance_{recurrent,input}_trace
+__device__ __forceinline__ void advance_trace(const LeoConfig& c, Trace& t, uint32_t now) {
+    uint32_t last = t.tick_mark >> 1;
+    if (now <= last) return;
+    uint32_t e = now - last;
+    t.branch_sens = t.branch_sens * leo_math::decay_for_elapsed(c.branch_decay, e);
+    t.membrane_sens = t.membrane_sens * leo_math::decay_for_elapsed(c.membrane_decay, e);
+    t.fatigue_sens = t.fatigue_sens * leo_math::decay_for_elapsed(c.fatigue_decay, e);
+    t.adaptation_sens[0] = t.adaptation_sens[0] * leo_math::decay_for_elapsed(c.adaptation_fast_decay, e);
+    t.adaptation_sens[1] = t.adaptation_sens[1] * leo_math::decay_for_elapsed(c.adaptation_medium_decay, e);
+    t.adaptation_sens[2] = t.adaptation_sens[2] * leo_math::decay_for_elapsed(c.adaptation_slow_decay, e);
+    t.tick_mark = (now << 1) | (t.tick_mark & 1u);
+}
+
+// Byte marks set with a 32-bit atomicOr on the containing word; the thread
+// that flips the byte from 0 appends the index.
+__device__ __forceinline__ void mark_and_append(uint8_t* marks, uint32_t* list, uint32_t* count, uint32_t index) {
+    if (marks[index] != 0) return;
+    unsigned int* word = reinterpret_cast<unsigned int*>(reinterpret_cast<uintptr_t>(marks + index) & ~(uintptr_t)3);
+    unsigned int shift = (unsigned int)((reinterpret_cast<uintptr_t>(marks + index) & 3u) * 8u);
+    unsigned int bit = 1u << shift;
+    unsigned int old = atomicOr(word, bit);
+    if ((old & bit) == 0u) list[atomicAdd(count, 1u)] = index;
+}
+
+__device__ __forceinline__ void touch(const LaneState& ln, uint32_t n, uint32_t epoch) {
+    if (atomicExch(&ln.touch_epoch[n], epoch) != epoch) ln.touched[atomicAdd(&ln.sc->touched_count, 1u)] = n;
+}
+
+__device__ __forceinline__ void push_event(const LaneState& ln, uint32_t tb, uint32_t q, float value) {
+    uint32_t old = atomicExch(&ln.ev_head[tb], q);
+    ln.ev_next[q] = old;
+    ln.ev_val[q] = value;
+}
+
+__device__ __forceinline__ void add_destination(const LaneState& ln, uint32_t n, uint32_t epoch) {
+    if (atomicExch(&ln.dst_epoch[n], epoch) != epoch) ln.dst_list[atomicAdd(&ln.sc->dst_count, 1u)] = n;
+}
+
+// ---------------------------------------------------------------------------
+// Context resolve on one warp (runtime.rs:641-699, model.rs:173-221): lane
+// `order - 1` hashes its order and issues all its probe loads at once; the
+// slot choice per order is independent (orders own disjoint partitions); lane
+// 0 then forms the confidence scales in order.
+__device__ void context_resolve_warp(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t symbol,
+                                     bool frozen) {
+    LaneScalars* sc = ln.sc;
+    const LeoConfig& c = kc.cfg;
+    const uint32_t lane = threadIdx.x & 31u, K = kc.topo.k;
+    uint32_t len = sc->ctx_history_len;
+    // history push (runtime.rs:642-646)
+    uint32_t hist[LEO_MAX_CONTEXT_ORDER];
+    for (uint32_t i = 0; i < len; ++i) hist[i] = sc->ctx_history[i];
+    if (len == K) {
+        for (uint32_t i = 0; i + 1 < K; ++i) hist[i] = hist[i + 1];
+        len = K - 1;
+    }
+    hist[len++] = symbol;
+    bool enabled = frozen;
+    if (!frozen) {
+        enabled = true;
+        if (kc.dropout_rate > 0.0f) {  // runtime.rs:103-116 context_survives_dropout
+            unsigned long long tick = sc->base_tick + s;
+            unsigned long long v = kc.seed ^ (tick * 0x9e3779b97f4a7c15ull) ^
+                                   ((unsigned long long)symbol * 0xbf58476d1ce4e5b9ull);
+            v = (v ^ (v >> 30)) * 0xbf58476d1ce4e5b9ull;
+            v = (v ^ (v >> 27)) * 0x94d049bb133111ebull;
+            v ^= v >> 31;
+            enabled = (float)(uint32_t)(v >> 40) / (float)(1u << 24) >= kc.dropout_rate;
+        }
+    }
+    bool allocate = !frozen && enabled;
+    uint32_t available = len < K ? len : K;
+    int32_t slot = -1;
+    uint32_t probes = 0;
+    float scale = 0.0f;
+    uint32_t order = lane + 1;
+    if (enabled && order <= available) {
+        unsigned long long h = 0xcbf29ce484222325ull ^ (unsigned long long)order;
+        for (uint32_t i = len - order; i < len; ++i) {
+            uint32_t sym = hist[i];
+            for (int byte = 0; byte < 4; ++byte) {
+                h ^= (unsigned long long)((sym >> (8 * byte)) & 0xffu);
+                h *= 0x100000001b3ull;
+            }
+        }
+        unsigned long long key = h > 1ull ? h : 1ull;
+        uint32_t spo = kc.topo.spo, limit = c.context_probe_limit, D = kc.topo.d;
+        uint32_t base = (order - 1) * spo, start = (uint32_t)(key % (unsigned long long)spo);
+        constexpr uint32_t kBatch = 8;
+        int32_t empty = -1;
+        uint32_t weakest = base + start, weakest_obs = 0xffffffffu;
+        for (uint32_t off0 = 0; off0 < limit && slot < 0; off0 += kBatch) {
+            unsigned long long keys[kBatch];
+            uint32_t obs[kBatch];
+            uint32_t n = limit - off0 < kBatch ? limit - off0 : kBatch;
+#pragma unroll
+            for (uint32_t j = 0; j < kBatch; ++j) {
+                if (j < n) {
+                    uint32_t sl = base + (start + off0 + j) % spo;
+                    keys[j] = ln.p.ctx_keys[sl];
+                    obs[j] = ln.p.ctx_obs[sl];
+                }
+            }
+            for (uint32_t j = 0; j < n; ++j) {
+                uint32_t sl = base + (start + off0 + j) % spo;
+                ++probes;
+                if (keys[j] == key) {
+                    slot = (int32_t)sl;
+                    break;
+                }
+                if (keys[j] == 0ull && empty < 0) empty = (int32_t)sl;
+                if (obs[j] < weakest_obs) {
+                    weakest_obs = obs[j];
+                    weakest = sl;
+                }
+            }
+        }
+        if (slot < 0 && allocate) {
+            uint32_t sl = empty >= 0 ? (uint32_t)empty : weakest;
+            if (ln.p.ctx_keys[sl] != key) {
+                ln.p.ctx_keys[sl] = key;
+                ln.p.ctx_obs[sl] = 0;
+                for (uint32_t k = 0; k < D; ++k) ln.p.ctx_emb[(size_t)sl * D + k] = 0.0f;
+            }
+            slot = (int32_t)sl;
+        }
+        if (slot >= 0) {
+            float o = (float)ln.p.ctx_obs[slot];
+            float confidence = o / (o + (float)c.context_confidence_observations);
+            scale = confidence * (float)order;
+        }
+    }
+    __syncwarp();
+    if (lane == 0) {
+        for (uint32_t i = 0; i < len; ++i) sc->ctx_history[i] = hist[i];
+        sc->ctx_history_len = len;
+        sc->ctx_applied = enabled ? 1u : 0u;
+    }
+    uint32_t total_probes = probes;
+    for (int o = 16; o > 0; o >>= 1) total_probes += __shfl_xor_sync(0xffffffffu, total_probes, o);
+    // scale_sum in order (runtime.rs:661-677): lane 0 walks the orders.
+    uint32_t count = 0;
+    float scale_sum = 0.0f;
+    uint32_t slots[LEO_MAX_CONTEXT_ORDER];
+    float scales[LEO_MAX_CONTEXT_ORDER];
+    for (uint32_t i = 0; i < K; ++i) {
+        int32_t si = __shfl_sync(0xffffffffu, slot, (int)i);
+        float sci = __shfl_sync(0xffffffffu, scale, (int)i);
+        if (si >= 0) {
+            slots[count] = (uint32_t)si;
+            scales[count] = sci;
+            ++count;
+            scale_sum = scale_sum + sci;
+        }
+    }
+    if (lane == 0) {
+        if (scale_sum > 0.0f)
+            for (uint32_t i = 0; i < count; ++i) scales[i] = scales[i] / scale_sum;
+        for (uint32_t i = 0; i < count; ++i) {
+            sc->ctx_slots[i] = slots[i];
+            sc->ctx_scales[i] = scales[i];
+        }
+        sc->ctx_count = count;
+        sc->ctx_probes = total_probes;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// deliver (runtime.rs:537-639).  Work item order within a lane is the CPU's
+// event order: previous actives, then due events from emission ticks s-8,
+// s-4, s-2, s-1 (rank, then slot), then the symbol's input slots; the event
+// index q encodes that order.
+__device__ void phase_deliver(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t worker,
+                              uint32_t workers, bool learn, uint32_t symbol) {
+    const uint32_t S = kc.topo.s, F = kc.topo.f, maxa = kc.topo.max_active;
+    LaneScalars* sc = ln.sc;
+    uint32_t prev = s >= 1 ? sc->ring_count[(s - 1) % LEO_RING] : 0u;
+    uint32_t a8 = s >= 8 ? sc->ring_count[(s - 8) % LEO_RING] : 0u;
+    uint32_t a4 = s >= 4 ? sc->ring_count[(s - 4) % LEO_RING] : 0u;
+    uint32_t a2 = s >= 2 ? sc->ring_count[(s - 2) % LEO_RING] : 0u;
+    uint32_t e8 = a8 * S, e4 = a4 * S, e2 = a2 * S, e1 = prev * S;
+    uint32_t events = e8 + e4 + e2 + e1;
+    uint32_t total = prev + events + F;
+    const uint32_t cur = sc->elig_cur;
+    if (worker == 0) {
+        sc->elig_count[cur ^ 1u] = 0;
+        sc->in_elig_count[cur ^ 1u] = 0;
+        sc->work_deliver += events + F;
+    }
+    const uint32_t epoch = s + 1;
+    for (uint32_t i = worker; i < total; i += workers) {
+        if (i < prev) {
+            touch(ln, ln.ring_src[((s - 1) % LEO_RING) * maxa + i], epoch);
+            continue;
+        }
+        uint32_t q = i - prev;
+        if (q < events) {
+            uint32_t d, off;
+            if (q < e8) {
+                d = 8; off = q;
+            } else if (q < e8 + e4) {
+                d = 4; off = q - e8;
+            } else if (q < e8 + e4 + e2) {
+                d = 2; off = q - e8 - e4;
+            } else {
+                d = 1; off = q - e8 - e4 - e2;
+            }
+            uint32_t entry = (s - d) % LEO_RING;
+            uint32_t r = off / S, j = off - r * S;
+            uint32_t src = ln.ring_src[entry * maxa + r];
+            uint32_t slot = src * S + j;
+            uint32_t word = kc.topo.rec_word[slot];
+            if (LEO_WORD_DELAY(word) != d) continue;
+            uint32_t n = word & LEO_TARGET_MASK, b = LEO_WORD_BRANCH(word);
+            float value = ln.ring_val[((size_t)entry * maxa + r) * S + j];
+            touch(ln, n, epoch);
+            push_event(ln, n * 4 + b, q, value);
+            if (learn) {  // activate_recurrent_trace (runtime.rs:719-726); one event per slot per tick
+                float a = ln.ring_act[entry * maxa + r];
+                Trace t = load_trace(&ln.traces[slot]);
+                advance_trace(kc.cfg, t, s);
+                t.branch_sens = t.branch_sens + a;
+                if ((t.tick_mark & 1u) == 0u) {
+                    t.tick_mark |= 1u;
+                    ln.elig[cur][atomicAdd(&sc->elig_count[cur], 1u)] = make_uint4(slot, word, 0u, 0u);
+                }
+                store_trace(&ln.traces[slot], t);
+            }
+        } else {
+            uint32_t f = q - events;
+            uint32_t slot = symbol * F + f;
+            uint32_t word = kc.topo.in_word[slot];
+            uint32_t n = word & LEO_TARGET_MASK, b = LEO_WORD_BRANCH(word);
+            touch(ln, n, epoch);
+            push_event(ln, n * 4 + b, q, ln.p.in_weight[slot]);
+            if (learn) {
+                Trace t = load_trace(&ln.in_traces[slot]);
+                advance_trace(kc.cfg, t, s);
+                t.branch_sens = t.branch_sens + 1.0f;
+                if ((t.tick_mark & 1u) == 0u) {
+                    t.tick_mark |= 1u;
+                    ln.in_elig[cur][atomicAdd(&sc->in_elig_count[cur], 1u)] = make_uint4(slot, word, 0u, 0u);
+                }
+                store_trace(&ln.in_traces[slot], t);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// settle (runtime.rs:576-603, 710-717, 541-548, 947-962).
+__device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t worker,
+                             uint32_t workers) {
+    const LeoConfig& c = kc.cfg;
+    const uint32_t npb = kc.topo.npb, n_count = kc.topo.n;
+    constexpr int kCap = 24;
+    LaneScalars* sc = ln.sc;
+    uint32_t count = sc->touched_count;
+    float pop_inh = sc->population_inhibition;
+    uint32_t rotation = (uint32_t)((sc->base_tick + s) % (unsigned long long)n_count);
+    for (uint32_t i = worker; i < count; i += workers) {
+        uint32_t n = ln.touched[i];
+        NeuronCold cold = ln.cold[n];
+        float4 br = ln.branches[n];
+        if (s > cold.branch_tick) {
+            float dec = leo_math::decay_for_elapsed(c.branch_decay, s - cold.branch_tick);
+            br.x = br.x * dec;
+            br.y = br.y * dec;
+            br.z = br.z * dec;
+            br.w = br.w * dec;
+            cold.branch_tick = s;
+        }
+        if (s > cold.neuron_tick) {
+            uint32_t e = s - cold.neuron_tick;
+            cold.membrane = cold.membrane * leo_math::decay_for_elapsed(c.membrane_decay, e);
+            cold.fatigue = cold.fatigue * leo_math::decay_for_elapsed(c.fatigue_decay, e);
+            cold.adaptation[0] = cold.adaptation[0] * leo_math::decay_for_elapsed(c.adaptation_fast_decay, e);
+            cold.adaptation[1] = cold.adaptation[1] * leo_math::decay_for_elapsed(c.adaptation_medium_decay, e);
+            cold.adaptation[2] = cold.adaptation[2] * leo_math::decay_for_elapsed(c.adaptation_slow_decay, e);
+            cold.neuron_tick = s;
+        }
+        float acc[4] = {br.x, br.y, br.z, br.w};
+        for (int b = 0; b < 4; ++b) {
+            uint32_t head = ln.ev_head[n * 4 + b];
+            if (head == LEO_EMPTY) continue;
+            ln.ev_head[n * 4 + b] = LEO_EMPTY;
+            uint32_t qs[kCap];
+            float vs[kCap];
+            int k = 0;
+            uint32_t p = head;
+            while (p != LEO_EMPTY && k < kCap) {
+                qs[k] = p;
+                vs[k] = ln.ev_val[p];
+                p = ln.ev_next[p];
+                ++k;
+            }
+            float a = acc[b];
+            if (p == LEO_EMPTY) {
+                for (int x = 1; x < k; ++x) {  // insertion sort by event order
+                    uint32_t qk = qs[x];
+                    float vk = vs[x];
+                    int y = x - 1;
+                    while (y >= 0 && qs[y] > qk) {
+                        qs[y + 1] = qs[y];
+                        vs[y + 1] = vs[y];
+                        --y;
+                    }
+                    qs[y + 1] = qk;
+                    vs[y + 1] = vk;
+                }
+                for (int x = 0; x < k; ++x) a = a + vs[x];
+            } else {
+                // A long list (hot target): add in ascending event order by repeated scans.
+                uint32_t last = 0u;
+                bool first = true;
+                for (;;) {
+                    uint32_t best = LEO_EMPTY;
+                    float bv = 0.0f;
+                    for (uint32_t it = head; it != LEO_EMPTY; it = ln.ev_next[it]) {
+                        if ((first || it > last) && (best == LEO_EMPTY || it < best)) {
+                            best = it;
+                            bv = ln.ev_val[it];
+                        }
+                    }
+                    if (best == LEO_EMPTY) break;
+                    a = a + bv;
+                    last = best;
+                    first = false;
+                }
+            }
+            acc[b] = a;
+        }
+        br = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        NeuronHot& hot = ln.hot[n];
+        hot.activation = 0.0f;
+        bool refractory = hot.refractory_until > s;
+        if (!refractory) {
+            float gate = clampf(br.w, 0.0f, 1.0f);
+            float inhibitory = br.y;
+            float net = br.x + br.z * gate + inhibitory;
+            float adaptation = sum3(cold.adaptation[0], cold.adaptation[1], cold.adaptation[2]);
+            float drive = kc.topo.excitability[n] * net - cold.fatigue - adaptation - pop_inh;
+            cold.membrane = cold.membrane + drive;
+            float act = clampf(cold.membrane - ln.p.threshold[n], 0.0f, 1.0f);
+            if (act > 0.0f) {
+                uint32_t blk = n / npb;
+                uint32_t pos = atomicAdd(&ln.block_cand_count[blk], 1u);
+                ln.block_cand[(size_t)blk * npb + pos] = selection_key(act, n, rotation, n_count);
+            }
+        }
+        ln.cold[n] = cold;
+        ln.branches[n] = br;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// blocks: block-local top-k and the exact (k+1)-th cutoff (runtime.rs:964-997),
+// one warp per block; keys are unique, so "largest key below the previous
+// winner" enumerates the block in rank order.
+__device__ void phase_blocks(const LaneState& ln, const KernelConsts& kc, uint32_t gwarp, uint32_t gwarps) {
+    const uint32_t B = kc.topo.blocks, npb = kc.topo.npb, keep = kc.topo.keep;
+    const uint32_t lane = threadIdx.x & 31u;
+    uint32_t supra = 0;
+    for (uint32_t b = gwarp; b < B; b += gwarps) {
+        uint32_t count = ln.block_cand_count[b];
+        const unsigned long long* cand = ln.block_cand + (size_t)b * npb;
+        constexpr uint32_t kLocal = 8;
+        unsigned long long mine[kLocal];
+        uint32_t held = 0;
+        for (uint32_t idx = lane; idx < count && held < kLocal; idx += 32) mine[held++] = cand[idx];
+        bool spill = count > 32 * kLocal;
+        unsigned long long prev = ~0ull;
+        uint32_t rounds = count < keep + 1 ? count : keep + 1;
+        float cutoff = 0.0f;
+        for (uint32_t k = 0; k < rounds; ++k) {
+            unsigned long long best = 0ull;
+            for (uint32_t h = 0; h < held; ++h)
+                if (mine[h] < prev && mine[h] > best) best = mine[h];
+            if (spill)
+                for (uint32_t idx = lane + 32 * kLocal; idx < count; idx += 32) {
+                    unsigned long long key = cand[idx];
+                    if (key < prev && key > best) best = key;
+                }
+            for (int o = 16; o > 0; o >>= 1) {
+                unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+                best = other > best ? other : best;
+            }
+            if (k < keep) {
+                if (lane == 0) ln.block_winners[(size_t)b * keep + k] = best;
+            } else {
+                cutoff = key_value(best);
+            }
+            prev = best;
+        }
+        if (lane == 0) {
+            ln.block_nwin[b] = count < keep ? count : keep;
+            ln.block_cutoff[b] = count > keep ? cutoff : 0.0f;
+            ln.block_cand_count[b] = 0;
+            supra += count;
+        }
+    }
+    if (lane == 0 && supra) atomicAdd(&ln.sc->step_supra, supra);
+}
+
+// ---------------------------------------------------------------------------
+// assemble (one CTA): active list in block order, the global cap
+// (runtime.rs:998-1064), population inhibition (runtime.rs:1076-1082), the
+// active ring entry, activations, and the actives as learning destinations.
+__device__ void phase_assemble(const LaneState& ln, uint32_t s, const KernelConsts& kc,
+                               unsigned long long* sorted) {
+    __shared__ uint32_t s_offset[1025];
+    __shared__ uint32_t s_warp_sums[kWarps];
+    LaneScalars* sc = ln.sc;
+    const LeoConfig& c = kc.cfg;
+    const uint32_t B = kc.topo.blocks, keep = kc.topo.keep, n_count = kc.topo.n, maxa = kc.topo.max_active;
+    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+    const uint32_t rotation = (uint32_t)((sc->base_tick + s) % (unsigned long long)n_count);
+    // exclusive scan of block winner counts (B <= 1024, two blocks per thread)
+    uint32_t b0 = 2 * tid, b1 = 2 * tid + 1;
+    uint32_t v0 = b0 < B ? ln.block_nwin[b0] : 0u, v1 = b1 < B ? ln.block_nwin[b1] : 0u;
+    uint32_t pair = v0 + v1, incl = pair;
+    for (int o = 1; o < 32; o <<= 1) {
+        uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= (uint32_t)o) incl += y;
+    }
+    if (lane == 31) s_warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t w = lane < kWarps ? s_warp_sums[lane] : 0u, wi = w;
+        for (int o = 1; o < 32; o <<= 1) {
+            uint32_t y = __shfl_up_sync(0xffffffffu, wi, o);
+            if (lane >= (uint32_t)o) wi += y;
+        }
+        if (lane < kWarps) s_warp_sums[lane] = wi - w;
+    }
+    __syncthreads();
+    uint32_t excl = s_warp_sums[warp] + incl - pair;
+    if (b0 < B) s_offset[b0] = excl;
+    if (b1 < B) s_offset[b1] = excl + v0;
+    if (tid == kThreads - 1) s_offset[B] = excl + pair;  // thread kThreads-1 holds the grand total
+    __syncthreads();
+    uint32_t selected = s_offset[B];
+    for (uint32_t i = tid; i < B * keep; i += kThreads) {
+        uint32_t b = i / keep, k = i - b * keep;
+        if (k < ln.block_nwin[b]) sorted[s_offset[b] + k] = ln.block_winners[i];
+    }
+    __syncthreads();
+    uint32_t cap = c.max_active_global;
+    uint32_t active = selected;
+    float pop_cutoff = 0.0f;
+    uint32_t clipped = 0;
+    bool redundant = cap >= B * keep;
+    if (!redundant && selected > 0) {
+        // Global rank (runtime.rs:1014-1030): bitonic sort descending.
+        uint32_t span = 1;
+        while (span < selected) span <<= 1;
+        for (uint32_t i = selected + tid; i < span; i += kThreads) sorted[i] = 0ull;
+        __syncthreads();
+        for (uint32_t width = 2; width <= span; width <<= 1) {
+            for (uint32_t stride = width >> 1; stride > 0; stride >>= 1) {
+                for (uint32_t i = tid; i < span; i += kThreads) {
+                    uint32_t other = i ^ stride;
+                    if (other > i) {
+                        bool descending = (i & width) == 0;
+                        unsigned long long a = sorted[i], b = sorted[other];
+                        if (descending ? (a < b) : (a > b)) {
+                            sorted[i] = b;
+                            sorted[other] = a;
+                        }
+                    }
+                }
+                __syncthreads();
+            }
+        }
+        if (selected > cap) {
+            pop_cutoff = clampf(key_value(sorted[cap]), 0.0f, c.population_inhibition_max);
+            clipped = selected - cap;
+            active = cap;
+        }
+    }
+    uint32_t entry = s % LEO_RING;
+    for (uint32_t r = tid; r < active; r += kThreads) {
+        unsigned long long key = sorted[r];
+        uint32_t n = key_neuron(key, rotation, n_count);
+        float act = key_value(key);
+        ln.ring_src[entry * maxa + r] = n;
+        ln.ring_act[entry * maxa + r] = act;
+        ln.hot[n].activation = act;
+        add_destination(ln, n, s + 1);  // every active neuron is a destination (runtime.rs:1240-1245)
+    }
+    if (tid == 0) {
+        sc->ring_count[entry] = active;
+        float activity = (float)active / (float)(n_count > 0 ? n_count : 1);
+        float error = activity - c.target_activity;
+        sc->population_inhibition =
+            clampf(sc->population_inhibition + c.population_inhibition_rate * error, 0.0f, c.population_inhibition_max);
+        sc->population_cutoff = redundant ? 0.0f : pop_cutoff;
+        sc->last_active = active;
+        sc->last_suprathreshold = sc->step_supra;
+        sc->last_block_selected = selected;
+        sc->last_clipped = clipped;
+        sc->step_supra = 0;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// surrogate: runtime.rs:787-803 plus the Jacobians of runtime.rs:775-783 /
+// learning.rs:28-50, packed into the 32-byte record the eligibility gather reads.
+__device__ void phase_surrogate(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t worker,
+                                uint32_t workers) {
+    const LeoConfig& c = kc.cfg;
+    const uint32_t npb = kc.topo.npb;
+    LaneScalars* sc = ln.sc;
+    uint32_t count = sc->touched_count;
+    float pop_cutoff = sc->population_cutoff;
+    for (uint32_t i = worker; i < count; i += workers) {
+        uint32_t n = ln.touched[i];
+        NeuronHot h = ln.hot[n];
+        bool refractory = h.refractory_until > s;
+        bool selected = h.activation > 0.0f;
+        float surrogate = 0.0f;
+        if (!refractory) {
+            float margin = ln.cold[n].membrane - ln.p.threshold[n];
+            float cutoff = rmax(ln.block_cutoff[n / npb], pop_cutoff);
+            float direct = (selected && margin > 0.0f && margin < 1.0f) ? 1.0f : 0.0f;
+            surrogate = direct;
+            if (c.surrogate_width > 0.0f && c.surrogate_gain > 0.0f) {
+                float boundary = clampf(1.0f - fabsf(margin - cutoff) / c.surrogate_width, 0.0f, 1.0f);
+                surrogate = direct + c.surrogate_gain * boundary;
+            }
+        }
+        float4 br = ln.branches[n];
+        float exc = kc.topo.excitability[n];
+        float gate = clampf(br.w, 0.0f, 1.0f);
+        float gate_derivative = (br.w > 0.0f && br.w < 1.0f) ? 1.0f : 0.0f;
+        h.tag = ((s + 1u) << 2) | (selected ? 2u : 0u) | (refractory ? 0u : 1u);
+        h.surrogate = surrogate;
+        h.j_exc = exc;
+        h.j_temporal = exc * gate;
+        h.j_gate = exc * br.z * gate_derivative;
+        ln.hot[n] = h;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// eligible: runtime.rs:832-918 over the recurrent and input worklists.  Kept
+// slots go to the next worklist with one atomic per warp (ballot compaction)
+// and their destinations become learning destinations.
+template <bool kInput>
+__device__ __forceinline__ void eligibility_item(const LaneState& ln, const KernelConsts& kc, uint32_t s, uint4 entry,
+                                                 bool valid, uint32_t next) {
+    const LeoConfig& c = kc.cfg;
+    LaneScalars* sc = ln.sc;
+    bool keep = false;
+    uint32_t dest = 0;
+    float e = 0.0f;
+    if (valid) {
+        Trace* tp = kInput ? &ln.in_traces[entry.x] : &ln.traces[entry.x];
+        Trace t = load_trace(tp);
+        advance_trace(c, t, s);
+        dest = entry.y & LEO_TARGET_MASK;
+        uint32_t branch = LEO_WORD_BRANCH(entry.y);
+        NeuronHot h = ln.hot[dest];
+        bool touched_now = (h.tag >> 2) == s + 1u;
+        if (!(touched_now && (h.tag & 1u))) {
+            e = t.eligibility * c.eligibility_decay;
+        } else {
+            float j = branch == 2u ? h.j_temporal : (branch == 3u ? h.j_gate : h.j_exc);
+            float adaptation_sum = sum3(t.adaptation_sens[0], t.adaptation_sens[1], t.adaptation_sens[2]);
+            float ms = t.membrane_sens + j * t.branch_sens - t.fatigue_sens - adaptation_sum;
+            t.membrane_sens = ms;
+            e = h.surrogate * ms;
+        }
+        t.eligibility = e;
+        if (touched_now && (h.tag & 2u)) {
+            t.fatigue_sens = t.fatigue_sens + c.fatigue_gain * e;
+            t.adaptation_sens[0] = t.adaptation_sens[0] + c.adaptation_fast_gain * e;
+            t.adaptation_sens[1] = t.adaptation_sens[1] + c.adaptation_medium_gain * e;
+            t.adaptation_sens[2] = t.adaptation_sens[2] + c.adaptation_slow_gain * e;
+        }
+        float mag = rmax(rmax(rmax(fabsf(t.branch_sens), fabsf(t.membrane_sens)), fabsf(t.fatigue_sens)), fabsf(e));
+        mag = rmax(mag, fabsf(t.adaptation_sens[0]));
+        mag = rmax(mag, fabsf(t.adaptation_sens[1]));
+        mag = rmax(mag, fabsf(t.adaptation_sens[2]));
+        keep = mag > c.eligibility_epsilon;
+        t.tick_mark = (t.tick_mark & ~1u) | (keep ? 1u : 0u);
+        store_trace(tp, t);
+    }
+    unsigned int ballot = __ballot_sync(0xffffffffu, keep);
+    uint32_t lane = threadIdx.x & 31u;
+    uint32_t base = 0;
+    if (ballot) {
+        uint32_t* counter = kInput ? &sc->in_elig_count[next] : &sc->elig_count[next];
+        int leader = __ffs(ballot) - 1;
+        if ((int)lane == leader) base = atomicAdd(counter, (uint32_t)__popc(ballot));
+        base = __shfl_sync(0xffffffffu, base, leader);
+    }
+    if (keep) {
+        uint32_t pos = base + (uint32_t)__popc(ballot & ((1u << lane) - 1u));
+        uint4* out = kInput ? ln.in_elig[next] : ln.elig[next];
+        out[pos] = make_uint4(entry.x, entry.y, __float_as_uint(e), 0u);
+        add_destination(ln, dest, s + 1);
+    }
+}
+
+__device__ void phase_eligible(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t worker,
+                               uint32_t workers) {
+    LaneScalars* sc = ln.sc;
+    const uint32_t cur = sc->elig_cur, next = cur ^ 1u;
+    uint32_t rec = sc->elig_count[cur], inp = sc->in_elig_count[cur];
+    uint32_t rec_pad = (rec + 31u) & ~31u;
+    uint32_t total = rec_pad + inp;
+    // Warp-uniform iteration over warp-aligned ranges: each ballot covers one list.
+    for (uint32_t base = worker & ~31u; base < total; base += workers) {
+        uint32_t i = base + (threadIdx.x & 31u);
+        if (base < rec_pad) {
+            bool valid = i < rec;
+            uint4 entry = valid ? ln.elig[cur][i] : make_uint4(0, 0, 0, 0);
+            eligibility_item<false>(ln, kc, s, entry, valid, next);
+        } else {
+            uint32_t k = i - rec_pad;
+            bool valid = k < inp;
+            uint4 entry = valid ? ln.in_elig[cur][k] : make_uint4(0, 0, 0, 0);
+            eligibility_item<true>(ln, kc, s, entry, valid, next);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// forward (one CTA): logits, context latent, softmax, loss, errors, output bias
+// and context learning (runtime.rs:1108-1197, 1199-1384), step statistics
+// (runtime.rs:1595-1622).
+__device__ void phase_forward(const LaneState& ln, uint32_t s, const KernelConsts& kc) {
+    __shared__ float s_logits[LEO_OUTPUT_STRIDE];
+    __shared__ float s_probs[LEO_OUTPUT_STRIDE];
+    __shared__ float s_latent[LEO_MAX_EMBEDDING];
+    __shared__ float s_grad[LEO_MAX_EMBEDDING];
+    __shared__ float s_act[1024];
+    __shared__ uint32_t s_src[1024];
+    __shared__ float s_max, s_sum;
+    LaneScalars* sc = ln.sc;
+    const LeoConfig& c = kc.cfg;
+    const uint32_t D = kc.topo.d, S = kc.topo.s, maxa = kc.topo.max_active;
+    const uint32_t sched = ln.schedule[s];
+    const uint32_t perm = LEO_SCHED_PERMISSION(sched);
+    const int target = LEO_SCHED_TARGET(sched);
+    const uint32_t symbol = LEO_SCHED_SYMBOL(sched);
+    const bool frozen = perm == kFrozen;
+    const uint32_t entry = s % LEO_RING;
+    const uint32_t active = sc->ring_count[entry];
+    const uint32_t tid = threadIdx.x;
+    const int target_index = target < 0 ? -1 : (target < 256 ? target : 256);
+
+    for (uint32_t r = tid; r < active; r += kThreads) {
+        s_src[r] = ln.ring_src[entry * maxa + r];
+        s_act[r] = ln.ring_act[entry * maxa + r];
+    }
+    __syncthreads();
+    // logits (runtime.rs:1109-1116): bias, then each active neuron in active order
+    if (tid < LEO_OUTPUT_CLASSES) {
+        float logit = ln.p.out_bias[tid];
+        const float* w = ln.p.out_weight + tid;
+        uint32_t r = 0;
+        for (; r + 4 <= active; r += 4) {
+            float w0 = w[(size_t)s_src[r] * LEO_OUTPUT_STRIDE];
+            float w1 = w[(size_t)s_src[r + 1] * LEO_OUTPUT_STRIDE];
+            float w2 = w[(size_t)s_src[r + 2] * LEO_OUTPUT_STRIDE];
+            float w3 = w[(size_t)s_src[r + 3] * LEO_OUTPUT_STRIDE];
+            logit = logit + w0 * s_act[r];
+            logit = logit + w1 * s_act[r + 1];
+            logit = logit + w2 * s_act[r + 2];
+            logit = logit + w3 * s_act[r + 3];
+        }
+        for (; r < active; ++r) logit = logit + w[(size_t)s_src[r] * LEO_OUTPUT_STRIDE] * s_act[r];
+        s_logits[tid] = logit;
+    }
+    // context latent (runtime.rs:1118-1136)
+    uint32_t ctx_count = sc->ctx_count;
+    if (tid < D) {
+        float v = 0.0f;
+        for (uint32_t i = 0; i < ctx_count; ++i) {
+            float scale = sc->ctx_scales[i];
+            if (scale <= 0.0f) continue;
+            v = v + ln.p.ctx_emb[(size_t)sc->ctx_slots[i] * D + tid] * scale;
+        }
+        s_latent[tid] = v;
+    }
+    __syncthreads();
+    if (ctx_count > 0 && tid < LEO_OUTPUT_CLASSES) {
+        float contribution = 0.0f;
+        for (uint32_t k = 0; k < D; ++k) contribution = contribution + ln.p.ctx_out[(size_t)tid * D + k] * s_latent[k];
+        s_logits[tid] = s_logits[tid] + contribution;
+    }
+    __syncthreads();
+    // normalize_probabilities (runtime.rs:1167-1188)
+    if (tid < 32) {
+        float m = -INFINITY;
+        for (uint32_t o = tid; o < LEO_OUTPUT_CLASSES; o += 32) m = rmax(m, s_logits[o]);
+        for (int off = 16; off > 0; off >>= 1) m = rmax(m, __shfl_xor_sync(0xffffffffu, m, off));
+        if (tid == 0) s_max = m;
+    }
+    __syncthreads();
+    if (tid < LEO_OUTPUT_CLASSES) s_probs[tid] = leo_expf(kc, s_logits[tid] - s_max);
+    __syncthreads();
+    if (tid == 0) {
+        float sum = 0.0f;
+        for (uint32_t o = 0; o < LEO_OUTPUT_CLASSES; ++o) sum = sum + s_probs[o];
+        s_sum = sum;
+    }
+    __syncthreads();
+    if (tid < LEO_OUTPUT_CLASSES) {
+        float sum = s_sum;
+        float p = (!isfinite(sum) || sum <= 0.0f) ? 1.0f / (float)LEO_OUTPUT_CLASSES : s_probs[tid] / sum;
+        s_probs[tid] = p;
+        ln.probs[tid] = p;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        // argmax_probability (runtime.rs:1190-1197): the lowest index among equal maxima
+        int best = 0;
+        for (uint32_t o = 1; o < LEO_OUTPUT_CLASSES; ++o)
+            if (s_probs[o] > s_probs[best]) best = (int)o;
+        sc->last_predicted = best == 256 ? 257u : (uint32_t)best;
+        float loss = 0.0f;
+        if (target_index >= 0) loss = -leo_logf(kc, rmax(s_probs[target_index], 1.0e-12f));
+        sc->last_loss = loss;
+        ln.step_loss[s] = loss;
+    }
+    __syncthreads();
+
+    float strength = kc.strength[perm];
+    bool learning = target_index >= 0 && strength > 0.0f;
+    if (learning) {
+        float target_weight = target_index == 256 ? kc.end_document_weight : 1.0f;
+        float supervised = strength * target_weight;
+        // plasticity_step (config.rs:137-145)
+        uint32_t window = kc.plasticity_window > 0 ? kc.plasticity_window : 1u;
+        uint32_t phase = sc->plasticity_phase;
+        uint32_t step = (phase < window - 1 ? phase : window - 1) + 1;
+        float plasticity = 0.0f;
+        uint32_t next_phase = step;
+        if (step == window || target_index == 256) {
+            plasticity = (float)step;
+            next_phase = 0;
+        }
+        if (tid < LEO_OUTPUT_CLASSES) {
+            float err = tid == (uint32_t)target_index ? s_probs[tid] - 1.0f : s_probs[tid];
+            s_probs[tid] = err;  // errors (runtime.rs:1205-1206)
+            ln.errors[tid] = err;
+            float raw = -c.output_learning_rate * supervised * err;
+            float bias = ln.p.out_bias[tid] + clampf(raw, -c.max_update, c.max_update);
+            ln.p.out_bias[tid] = bias;
+            if (!isfinite(bias)) atomicOr(&sc->error_flag, LEO_ERR_NONFINITE_BIAS);
+        }
+        __syncthreads();
+        if (sc->ctx_applied && ctx_count > 0) {  // update_context_projection (runtime.rs:1318-1384)
+            if (tid < D) {
+                float g = 0.0f;
+                for (uint32_t o = 0; o < LEO_OUTPUT_CLASSES; ++o) g = g + ln.p.ctx_out[(size_t)o * D + tid] * s_probs[o];
+                s_grad[tid] = g;
+            }
+            __syncthreads();
+            float lr = c.context_learning_rate;
+            for (uint32_t i = tid; i < LEO_OUTPUT_CLASSES * D; i += kThreads) {
+                uint32_t o = i / D, k = i - o * D;
+                float gradient = s_probs[o] * s_latent[k];
+                float delta = clampf(-lr * supervised * gradient, -c.max_update, c.max_update);
+                float updated = clampf(ln.p.ctx_out[i] + delta, c.weight_min, c.weight_max);
+                if (!isfinite(updated)) atomicOr(&sc->error_flag, LEO_ERR_NONFINITE_CONTEXT);
+                ln.p.ctx_out[i] = updated;
+            }
+            for (uint32_t i = tid; i < ctx_count * D; i += kThreads) {
+                uint32_t ci = i / D, k = i - ci * D;
+                uint32_t slot = sc->ctx_slots[ci];
+                float gradient = sc->ctx_scales[ci] * s_grad[k];
+                float delta = clampf(-lr * supervised * gradient, -c.max_update, c.max_update);
+                size_t idx = (size_t)slot * D + k;
+                float updated = clampf(ln.p.ctx_emb[idx] + delta, c.weight_min, c.weight_max);
+                if (!isfinite(updated)) atomicOr(&sc->error_flag, LEO_ERR_NONFINITE_CONTEXT);
+                ln.p.ctx_emb[idx] = updated;
+            }
+            __syncthreads();
+            if (tid == 0) {
+                for (uint32_t ci = 0; ci < ctx_count; ++ci) {
+                    uint32_t slot = sc->ctx_slots[ci];
+                    if (kc.track_changes && ln.ctx_mark[slot] == 0) {
+                        ln.ctx_mark[slot] = 1;
+                        ln.ctx_list[sc->ctx_changed++] = slot;
+                    }
+                    if (ln.p.ctx_obs[slot] != 0xffffffffu) ln.p.ctx_obs[slot] += 1;
+                }
+                if (kc.track_changes) sc->ctx_out_dirty = 1;
+            }
+        }
+        if (tid == 0) {
+            sc->step_flags = 1u | (plasticity > 0.0f ? 2u : 0u) | 4u;
+            sc->step_strength = strength;
+            sc->step_supervised = supervised;
+            sc->step_consolidated = supervised * plasticity;
+            sc->plasticity_phase = next_phase;
+            sc->revision_increment += 1;
+            if (kc.track_changes) sc->bias_dirty = 1;
+        }
+    } else if (tid == 0) {
+        sc->step_flags = frozen ? 0u : 4u;
+    }
+    if (tid == 0 && !frozen) {  // update_statistics (runtime.rs:1595-1622)
+        if (symbol < 256) sc->processed_bytes += 1;
+        if (target_index >= 0) {
+            sc->loss_sum += (double)sc->last_loss;
+            sc->targets += 1;
+        }
+        sc->active_sum += active;
+        if (active > sc->active_peak) sc->active_peak = active;
+        sc->synaptic_events += (unsigned long long)active * S;
+        sc->persistent_ticks += 1;
+        sc->context_applied_steps += sc->ctx_applied ? 1 : 0;
+    }
+}
+
+// emit: post-activation dynamics and emission (runtime.rs:920-938, 1084-1106).
+__device__ void phase_emit(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t worker,
+                           uint32_t workers) {
+    const LeoConfig& c = kc.cfg;
+    const uint32_t S = kc.topo.s, maxa = kc.topo.max_active;
+    uint32_t entry = s % LEO_RING;
+    uint32_t total = ln.sc->ring_count[entry] * S;
+    for (uint32_t i = worker; i < total; i += workers) {
+        uint32_t r = i / S, j = i - r * S;
+        uint32_t n = ln.ring_src[entry * maxa + r];
+        float a = ln.ring_act[entry * maxa + r];
+        if (j == 0) {
+            NeuronCold cold = ln.cold[n];
+            cold.fatigue = cold.fatigue + c.fatigue_gain * a;
+            cold.adaptation[0] = cold.adaptation[0] + c.adaptation_fast_gain * a;
+            cold.adaptation[1] = cold.adaptation[1] + c.adaptation_medium_gain * a;
+            cold.adaptation[2] = cold.adaptation[2] + c.adaptation_slow_gain * a;
+            cold.membrane = cold.membrane - ln.p.threshold[n] * c.membrane_reset_fraction;
+            ln.cold[n] = cold;
+            ln.hot[n].refractory_until = s + c.refractory_ticks + 1u;
+        }
+        ln.ring_val[((size_t)entry * maxa + r) * S + j] = a * ln.p.rec_weight[(size_t)n * S + j];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// learn: learning signals for every destination (runtime.rs:1246-1262), the
+// output row of each active destination after its signal (runtime.rs:1267-1283),
+// threshold homeostasis over the touched neurons (runtime.rs:1567-1593).
+__device__ void phase_learn(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t worker,
+                            uint32_t workers) {
+    __shared__ float s_err[LEO_OUTPUT_STRIDE];
+    const LeoConfig& c = kc.cfg;
+    const uint32_t n_count = kc.topo.n;
+    LaneScalars* sc = ln.sc;
+    uint32_t flags = sc->step_flags;
+    bool learning = flags & 1u, plastic = flags & 2u, persistent = flags & 4u;
+    uint32_t dsts = learning ? sc->dst_count : 0u;
+    uint32_t touched = persistent ? sc->touched_count : 0u;
+    uint32_t total = dsts + touched;
+    for (uint32_t o = threadIdx.x; o < LEO_OUTPUT_CLASSES; o += kThreads) s_err[o] = ln.errors[o];
+    __syncthreads();
+    float supervised = sc->step_supervised;
+    uint32_t active = sc->ring_count[s % LEO_RING];
+    float pop_error = (float)active / (float)(n_count > 0 ? n_count : 1) - c.target_activity;
+    for (uint32_t i = worker; i < total; i += workers) {
+        if (i < dsts) {
+            uint32_t n = ln.dst_list[i];
+            float* row = ln.p.out_weight + (size_t)n * LEO_OUTPUT_STRIDE;
+            if (plastic) {
+                float signal = 0.0f;
+                const float4* r4 = reinterpret_cast<const float4*>(row);
+                for (uint32_t q = 0; q < 64; ++q) {
+                    float4 w = r4[q];
+                    signal = signal + w.x * s_err[4 * q];
+                    signal = signal + w.y * s_err[4 * q + 1];
+                    signal = signal + w.z * s_err[4 * q + 2];
+                    signal = signal + w.w * s_err[4 * q + 3];
+                }
+                signal = signal + row[256] * s_err[256];
+                ln.signal[n] = signal;
+            }
+            float a = ln.hot[n].activation;
+            if (a > 0.0f) {
+                for (uint32_t o = 0; o < LEO_OUTPUT_CLASSES; ++o) {
+                    float raw = -c.output_learning_rate * supervised * s_err[o] * a;
+                    float delta = clampf(raw, -c.max_update, c.max_update);
+                    row[o] = clampf(row[o] + delta, c.weight_min, c.weight_max);
+                }
+                if (kc.track_changes) mark_and_append(ln.out_mark, ln.out_list, &sc->out_changed, n);
+            }
+        } else {
+            uint32_t n = ln.touched[i - dsts];
+            float local = ln.hot[n].activation > 0.0f ? 1.0f : 0.0f;
+            float local_error = local - c.target_activity;
+            float delta = c.threshold_homeostasis_rate * (local_error + pop_error);
+            float old_t = ln.p.threshold[n];
+            float new_t = clampf(old_t + delta, 0.05f, 2.0f);
+            if (new_t != old_t && kc.track_changes) mark_and_append(ln.thr_mark, ln.thr_list, &sc->thr_changed, n);
+            ln.p.threshold[n] = new_t;
+        }
+    }
+}
+
+// plasticity: update_recurrent_synapses / update_input_synapses
+// (runtime.rs:1451-1523) over the post-compaction worklists.
+__device__ void phase_plasticity(const LaneState& ln, const KernelConsts& kc, uint32_t worker, uint32_t workers) {
+    const LeoConfig& c = kc.cfg;
+    const uint32_t S = kc.topo.s;
+    LaneScalars* sc = ln.sc;
+    if ((sc->step_flags & 3u) != 3u) return;
+    float strength = sc->step_consolidated;
+    const uint32_t next = sc->elig_cur ^ 1u;
+    uint32_t rec = sc->elig_count[next], inp = sc->in_elig_count[next];
+    uint32_t total = rec + inp;
+    for (uint32_t i = worker; i < total; i += workers) {
+        if (i < rec) {
+            uint4 e4 = ln.elig[next][i];
+            uint32_t slot = e4.x, dest = e4.y & LEO_TARGET_MASK;
+            float gradient = ln.signal[dest] * __uint_as_float(e4.z);
+            float delta = clampf(-c.recurrent_learning_rate * strength * gradient, -c.max_update, c.max_update);
+            float old_w = ln.p.rec_weight[slot];
+            float nw = clampf(old_w + delta, c.weight_min, c.weight_max);
+            nw = kc.topo.neuron_type[slot / S] == 0 ? rmax(nw, 0.0f) : rmin(nw, 0.0f);
+            if (!isfinite(nw)) {
+                atomicOr(&sc->error_flag, LEO_ERR_NONFINITE_RECURRENT);
+                atomicAdd(&sc->numerical_rejections, 1ull);
+            }
+            if (nw != old_w && kc.track_changes) mark_and_append(ln.rec_mark, ln.rec_list, &sc->rec_changed, slot);
+            ln.p.rec_weight[slot] = nw;
+        } else {
+            uint4 e4 = ln.in_elig[next][i - rec];
+            uint32_t slot = e4.x, dest = e4.y & LEO_TARGET_MASK;
+            float gradient = ln.signal[dest] * __uint_as_float(e4.z);
+            float delta = clampf(-c.recurrent_learning_rate * strength * gradient, -c.max_update, c.max_update);
+            float old_w = ln.p.in_weight[slot];
+            float nw = clampf(old_w + delta, 0.0f, c.weight_max);
+            if (!isfinite(nw)) atomicOr(&sc->error_flag, LEO_ERR_NONFINITE_INPUT);
+            if (nw != old_w && kc.track_changes) mark_and_append(ln.in_mark, ln.in_list, &sc->in_changed, slot);
+            ln.p.in_weight[slot] = nw;
+        }
+    }
+}
+
+// inhibit: apply_inhibitory_homeostasis (runtime.rs:1525-1565), after the
+// recurrent update.
+__device__ void phase_inhibit(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t worker,
+                              uint32_t workers) {
+    const LeoConfig& c = kc.cfg;
+    const uint32_t S = kc.topo.s, maxa = kc.topo.max_active;
+    LaneScalars* sc = ln.sc;
+    if (!(sc->step_flags & 1u)) return;
+    float strength = sc->step_strength;
+    uint32_t entry = s % LEO_RING;
+    uint32_t total = sc->ring_count[entry] * S;
+    for (uint32_t i = worker; i < total; i += workers) {
+        uint32_t r = i / S, j = i - r * S;
+        uint32_t src = ln.ring_src[entry * maxa + r];
+        if (kc.topo.neuron_type[src] == 0) continue;
+        float sa = ln.ring_act[entry * maxa + r];
+        uint32_t slot = src * S + j;
+        uint32_t target = kc.topo.rec_word[slot] & LEO_TARGET_MASK;
+        float tact = ln.hot[target].activation > 0.0f ? 1.0f : 0.0f;
+        float err = tact - c.target_activity;
+        float delta = clampf(-c.inhibitory_learning_rate * strength * sa * err, -c.max_update, c.max_update);
+        float old_w = ln.p.rec_weight[slot];
+        float nw = clampf(old_w + delta, c.weight_min, 0.0f);
+        if (!isfinite(nw)) atomicOr(&sc->error_flag, LEO_ERR_NONFINITE_INHIBITORY);
+        if (nw != old_w && kc.track_changes) mark_and_append(ln.rec_mark, ln.rec_list, &sc->rec_changed, slot);
+        ln.p.rec_weight[slot] = nw;
+    }
+}
+
+// Step epilogue (one thread): work counters, per-tick counter reset, and the
+// worklist swap after an eligibility phase.
+__device__ void step_epilogue(const LaneState& ln, uint32_t s, bool frozen) {
+    LaneScalars* sc = ln.sc;
+    uint32_t cur = sc->elig_cur;
+    sc->work_touched += sc->touched_count;
+    sc->work_active += sc->ring_count[s % LEO_RING];
+    sc->work_steps += 1;
+    if (!frozen) sc->work_eligible += sc->elig_count[cur] + sc->in_elig_count[cur];
+    if ((sc->step_flags & 3u) == 3u) {
+        sc->work_destinations += sc->dst_count;
+        sc->work_plastic += sc->elig_count[cur ^ 1u] + sc->in_elig_count[cur ^ 1u];
+    }
+    sc->touched_count = 0;
+    sc->dst_count = 0;
+    if (!frozen) sc->elig_cur = cur ^ 1u;
+}
+
+__device__ __forceinline__ unsigned long long clock_now() { return clock64(); }
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// The persistent wavefront: cluster blockIdx.x / C runs lane `cluster` through
+// steps [begin, end) of its schedule.
+__global__ void __launch_bounds__(kThreads, 1)
+    leo_wavefront_kernel(const LaneState* __restrict__ lanes, uint32_t begin, uint32_t end, KernelConsts kc) {
+    extern __shared__ unsigned long long smem_sorted[];
+    cg::cluster_group cluster = cg::this_cluster();
+    const uint32_t C = cluster.num_blocks();
+    const uint32_t rank = cluster.block_rank();
+    const LaneState& ln = lanes[blockIdx.x / C];
+    LaneScalars* sc = ln.sc;
+    const uint32_t steps = sc->steps;
+    const uint32_t worker = rank * kThreads + threadIdx.x, workers = C * kThreads;
+    const uint32_t gwarp = rank * kWarps + (threadIdx.x >> 5), gwarps = C * kWarps;
+    const bool timer = rank == 0 && threadIdx.x == 0;
+    unsigned long long t0 = 0, acc[LEO_PHASES] = {0};
+    auto mark = [&](int p) {
+        if (timer) {
+            unsigned long long t = clock_now();
+            acc[p] += t - t0;
+            t0 = t;
+        }
+    };
+    if (timer) t0 = clock_now();
+    for (uint32_t s = begin; s < end && s < steps; ++s) {
+        const uint32_t sched = ln.schedule[s];
+        const bool frozen = LEO_SCHED_PERMISSION(sched) == kFrozen;
+        const uint32_t symbol = LEO_SCHED_SYMBOL(sched);
+        // deliver; the cluster's last warp first resolves the context
+        if (rank == C - 1 && (threadIdx.x >> 5) == kWarps - 1) context_resolve_warp(ln, s, kc, symbol, frozen);
+        phase_deliver(ln, s, kc, worker, workers, !frozen, symbol);
+        cluster.sync();
+        mark(0);
+        phase_settle(ln, s, kc, worker, workers);
+        cluster.sync();
+        mark(1);
+        phase_blocks(ln, kc, gwarp, gwarps);
+        cluster.sync();
+        mark(2);
+        if (rank == 0) phase_assemble(ln, s, kc, smem_sorted);
+        cluster.sync();
+        mark(3);
+        if (!frozen) {
+            phase_surrogate(ln, s, kc, worker, workers);
+            cluster.sync();
+            mark(4);
+            phase_eligible(ln, s, kc, worker, workers);
+            cluster.sync();
+            mark(5);
+        }
+        // emit beside the forward pass (the first CTA runs the forward)
+        const bool forward = !frozen || LEO_SCHED_TARGET(sched) >= 0;
+        if (rank == 0 && forward) phase_forward(ln, s, kc);
+        if (C == 1) {
+            if (forward) __syncthreads();
+            phase_emit(ln, s, kc, threadIdx.x, kThreads);
+        } else if (forward) {
+            if (rank > 0) phase_emit(ln, s, kc, worker - kThreads, workers - kThreads);
+        } else {
+            phase_emit(ln, s, kc, worker, workers);
+        }
+        if (frozen && worker == 0) {
+            if (!forward) sc->step_flags = 0;
+            step_epilogue(ln, s, true);
+        }
+        cluster.sync();
+        mark(6);
+        if (!frozen) {
+            phase_learn(ln, s, kc, worker, workers);
+            cluster.sync();
+            mark(7);
+            phase_plasticity(ln, kc, worker, workers);
+            cluster.sync();
+            mark(8);
+            phase_inhibit(ln, s, kc, worker, workers);
+            if (worker == 0) step_epilogue(ln, s, false);
+            cluster.sync();
+            mark(9);
+        }
+    }
+    if (timer)
+        for (int p = 0; p < LEO_PHASES; ++p) sc->phase_cycles[p] += acc[p];
+}
+
+size_t leo_wavefront_smem_bytes(const KernelConsts& kc) {
+    uint32_t winners = kc.topo.blocks * kc.topo.keep, span = 1;
+    while (span < winners) span <<= 1;
+    return (size_t)span * sizeof(unsigned long long);
+}
+
+cudaError_t leo_launch_wavefront(const LaneState* lanes, int lane_count, uint32_t cluster, uint32_t begin,
+                                 uint32_t end, const KernelConsts& kc, cudaStream_t stream) {
+    static bool configured = false;
+    size_t smem = leo_wavefront_smem_bytes(kc);
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(leo_wavefront_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             64 * 1024);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(leo_wavefront_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)lane_count * cluster, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, leo_wavefront_kernel, lanes, begin, end, kc);
+}
+
+cudaError_t leo_wavefront_max_clusters(uint32_t cluster, const KernelConsts& kc, int* out) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cluster, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = leo_wavefront_smem_bytes(kc);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaOccupancyMaxActiveClusters(out, leo_wavefront_kernel, &cfg);
+}

@@ -133,15 +133,18 @@ TOPOLOGY_REFERENCE, TOPOLOGY_UNIFORM, TOPOLOGY_ZIPF = 0, 1, 2
 BEGIN_DOCUMENT, END_DOCUMENT, SYMBOL_COUNT, OUTPUT_CLASSES = 256, 257, 258, 257
 
 
-PHASES = ["deliver", "settle", "select", "surrogate", "eligible", "emit_forward", "learn", "plasticity", "inhibit",
-          "epilogue", "merge"]
+PHASES = ["deliver", "settle", "blocks", "assemble", "surrogate", "eligible", "emit_forward", "learn",
+          "plasticity", "inhibit", "unused"]
 
 
 class LeoB200PerfStats(C.Structure):
     _fields_ = [
         ("launches", C.c_uint64),
-        ("phase_launches", C.c_uint64 * 11),
-        ("phase_ms", C.c_double * 11),
+        ("wavefront_launches", C.c_uint64),
+        ("wavefront_ms", C.c_double),
+        ("story_wavefront_launches", C.c_uint64),
+        ("story_wavefront_ms", C.c_double),
+        ("phase_cycles", C.c_uint64 * 11),
         ("work_deliver", C.c_uint64),
         ("work_touched", C.c_uint64),
         ("work_eligible", C.c_uint64),
@@ -149,6 +152,9 @@ class LeoB200PerfStats(C.Structure):
         ("work_active", C.c_uint64),
         ("work_plastic", C.c_uint64),
         ("work_steps", C.c_uint64),
+        ("story_work_steps", C.c_uint64),
         ("batches", C.c_uint64),
         ("batch_ms", C.c_double),
+        ("story_cluster", C.c_uint32),
+        ("replay_cluster", C.c_uint32),
     ]

@@ -64,7 +64,7 @@ def lib() -> C.CDLL:
     L.leo_b200_state_digest.argtypes = [vp, vp]
     L.leo_b200_lane_model.argtypes = [vp, u32, P(LeoB200HostModel)]
     L.leo_b200_lane_array.argtypes = [vp, u32, C.c_char_p, vp, sz, P(sz)]
-    L.leo_b200_set_phase_timing.argtypes = [vp, u32]
+    L.leo_b200_set_cluster_sizes.argtypes = [vp, u32, u32]
     L.leo_b200_perf_stats.argtypes = [vp, P(LeoB200PerfStats)]
     L.leo_b200_reset_perf_stats.argtypes = [vp]
     L.leo_b200_device_bytes.argtypes = [vp]
