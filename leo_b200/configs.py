@@ -159,6 +159,8 @@ WORKLOADS = {
     "probe": Workload("probe", PROBE, TOPOLOGY_REFERENCE, 4, 64, 256, 1024),
     "baseline1": Workload("baseline1", BASELINE1, TOPOLOGY_UNIFORM, 4, 64, 256, 1024),
     "baseline2": Workload("baseline2", BASELINE2, TOPOLOGY_UNIFORM, 32, 10_000, 256, 1024),
+    "baseline2-replay-off": Workload("baseline2-replay-off", replace(BASELINE2, replay_fraction=0.0),
+                                     TOPOLOGY_UNIFORM, 32, 10_000, 256, 1024),
     "baseline3": Workload("baseline3", BASELINE3, TOPOLOGY_ZIPF, 64, 50_000, 512, 2048),
     "baseline4": Workload("baseline4", BASELINE3, TOPOLOGY_ZIPF, 128, 50_000, 512, 2048),
 }

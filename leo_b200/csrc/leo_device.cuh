@@ -152,6 +152,12 @@ struct DeviceTopology {
 
 struct LaneState {
     LaneParams p;
+    // Canonical output rows.  A lane's private row equals the canonical row
+    // until the lane changes it (out_mark set): the batch-end sync restores that
+    // invariant and the canonical model is constant during a story pass, so
+    // unchanged rows are read from the shared canonical copy (one L2-resident
+    // matrix for every lane instead of one per lane).
+    const float* canon_out_weight;
     LaneScalars* sc;
     const uint32_t* schedule;   // [steps]
     float* step_loss;           // [steps] loss per step (0 when untargeted)

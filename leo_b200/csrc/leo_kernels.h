@@ -12,6 +12,7 @@
 cudaError_t leo_launch_wavefront(const LaneState* lanes, int lane_count, uint32_t cluster, uint32_t begin,
                                  uint32_t end, const KernelConsts& kc, cudaStream_t stream);
 size_t leo_wavefront_smem_bytes(const KernelConsts& kc);
+cudaError_t leo_wavefront_configure();
 // Clusters of `cluster` CTAs that can be resident at once.
 cudaError_t leo_wavefront_max_clusters(uint32_t cluster, const KernelConsts& kc, int* out);
 

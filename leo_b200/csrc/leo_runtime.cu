@@ -160,6 +160,7 @@ void allocate_lane_transient(LeoB200Device& dev, Lane& lane) {
     const ModelSizes& z = dev.z;
     MemPool& m = lane.mem;
     LaneState& st = lane.st;
+    st.canon_out_weight = dev.canon.out_weight;
     uint32_t maxa = dev.cfg.abi.max_active_global, B = dev.cfg.abi.block_count, npb = dev.cfg.abi.neurons_per_block;
     st.sc = m.alloc<LaneScalars>(1);
     st.hot = m.alloc<NeuronHot>(z.n);
@@ -362,8 +363,11 @@ uint32_t pick_cluster(LeoB200Device& dev, uint32_t lanes, uint32_t request, uint
     if (request) return request;
     for (uint32_t c = limit; c >= 1; c >>= 1) {
         int fit = 0;
-        if (leo_wavefront_max_clusters(c, dev.kc, &fit) == cudaSuccess && (uint32_t)fit >= lanes) return c;
-        cudaGetLastError();
+        if (leo_wavefront_max_clusters(c, dev.kc, &fit) != cudaSuccess) {
+            cudaGetLastError();  // this size is not supported here; try a smaller one
+            continue;
+        }
+        if ((uint32_t)fit >= lanes) return c;
     }
     return 1;
 }
@@ -1194,7 +1198,8 @@ int leo_b200_open(int device, const LeoB200HostModel* canonical, uint32_t max_la
         dev->replay->st.p = dev->canon;
         allocate_lane_transient(*dev, *dev->replay);
         dev->grid = prop.multiProcessorCount * 4;
-        if (leo_wavefront_smem_bytes(dev->kc) > 64 * 1024) throw LeoFailure("block winners exceed shared memory");
+        if (leo_wavefront_smem_bytes(dev->kc) > 96 * 1024) throw LeoFailure("block winners exceed shared memory");
+        CUDA_CHECK(leo_wavefront_configure());
         upload_model(*dev, *canonical);
         *out = dev.release();
         return 0;

@@ -744,7 +744,11 @@ __device__ __forceinline__ void eligibility_item(const LaneState& ln, const Kern
         uint32_t pos = base + (uint32_t)__popc(ballot & ((1u << lane) - 1u));
         uint4* out = kInput ? ln.in_elig[next] : ln.elig[next];
         out[pos] = make_uint4(entry.x, entry.y, __float_as_uint(e), 0u);
-        add_destination(ln, dest, s + 1);
+        // A slot with eligibility +-0 leaves its weight bit-for-bit unchanged
+        // (old + (+-0) = old for every weight the model can hold, since no
+        // update produces -0), so only nonzero-eligibility slots need their
+        // destination's learning signal.
+        if (e != 0.0f) add_destination(ln, dest, s + 1);
     }
 }
 
@@ -781,7 +785,7 @@ __device__ void phase_forward(const LaneState& ln, uint32_t s, const KernelConst
     __shared__ float s_latent[LEO_MAX_EMBEDDING];
     __shared__ float s_grad[LEO_MAX_EMBEDDING];
     __shared__ float s_act[1024];
-    __shared__ uint32_t s_src[1024];
+    __shared__ const float* s_row[1024];
     __shared__ float s_max, s_sum;
     LaneScalars* sc = ln.sc;
     const LeoConfig& c = kc.cfg;
@@ -797,26 +801,27 @@ __device__ void phase_forward(const LaneState& ln, uint32_t s, const KernelConst
     const int target_index = target < 0 ? -1 : (target < 256 ? target : 256);
 
     for (uint32_t r = tid; r < active; r += kThreads) {
-        s_src[r] = ln.ring_src[entry * maxa + r];
+        uint32_t n = ln.ring_src[entry * maxa + r];
+        const float* rows = ln.out_mark[n] ? ln.p.out_weight : ln.canon_out_weight;
+        s_row[r] = rows + (size_t)n * LEO_OUTPUT_STRIDE;
         s_act[r] = ln.ring_act[entry * maxa + r];
     }
     __syncthreads();
     // logits (runtime.rs:1109-1116): bias, then each active neuron in active order
     if (tid < LEO_OUTPUT_CLASSES) {
         float logit = ln.p.out_bias[tid];
-        const float* w = ln.p.out_weight + tid;
         uint32_t r = 0;
         for (; r + 4 <= active; r += 4) {
-            float w0 = w[(size_t)s_src[r] * LEO_OUTPUT_STRIDE];
-            float w1 = w[(size_t)s_src[r + 1] * LEO_OUTPUT_STRIDE];
-            float w2 = w[(size_t)s_src[r + 2] * LEO_OUTPUT_STRIDE];
-            float w3 = w[(size_t)s_src[r + 3] * LEO_OUTPUT_STRIDE];
+            float w0 = s_row[r][tid];
+            float w1 = s_row[r + 1][tid];
+            float w2 = s_row[r + 2][tid];
+            float w3 = s_row[r + 3][tid];
             logit = logit + w0 * s_act[r];
             logit = logit + w1 * s_act[r + 1];
             logit = logit + w2 * s_act[r + 2];
             logit = logit + w3 * s_act[r + 3];
         }
-        for (; r < active; ++r) logit = logit + w[(size_t)s_src[r] * LEO_OUTPUT_STRIDE] * s_act[r];
+        for (; r < active; ++r) logit = logit + s_row[r][tid] * s_act[r];
         s_logits[tid] = logit;
     }
     // context latent (runtime.rs:1118-1136)
@@ -992,58 +997,87 @@ __device__ void phase_emit(const LaneState& ln, uint32_t s, const KernelConsts& 
 // learn: learning signals for every destination (runtime.rs:1246-1262), the
 // output row of each active destination after its signal (runtime.rs:1267-1283),
 // threshold homeostasis over the touched neurons (runtime.rs:1567-1593).
+//
+// Signals: each warp takes 32 destination rows.  For each 32-column chunk it
+// loads a 32 x 32 tile (lane j reads column j of every row: one coalesced
+// 128-byte segment per row, 32 independent loads in flight per lane), stores
+// it transposed into padded shared memory, and lane r then adds row r's 32
+// products in column order.  Every row's sum is formed strictly in output
+// order, exactly like the CPU's sequential loop.
+__device__ __forceinline__ const float* output_row(const LaneState& ln, uint32_t n) {
+    return (ln.out_mark[n] ? ln.p.out_weight : ln.canon_out_weight) + (size_t)n * LEO_OUTPUT_STRIDE;
+}
+
 __device__ void phase_learn(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t worker,
-                            uint32_t workers) {
+                            uint32_t workers, uint32_t gwarp, uint32_t gwarps, float (*s_tile)[32][33]) {
     __shared__ float s_err[LEO_OUTPUT_STRIDE];
     const LeoConfig& c = kc.cfg;
     const uint32_t n_count = kc.topo.n;
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     LaneScalars* sc = ln.sc;
     uint32_t flags = sc->step_flags;
     bool learning = flags & 1u, plastic = flags & 2u, persistent = flags & 4u;
     uint32_t dsts = learning ? sc->dst_count : 0u;
     uint32_t touched = persistent ? sc->touched_count : 0u;
-    uint32_t total = dsts + touched;
     for (uint32_t o = threadIdx.x; o < LEO_OUTPUT_CLASSES; o += kThreads) s_err[o] = ln.errors[o];
     __syncthreads();
     float supervised = sc->step_supervised;
-    uint32_t active = sc->ring_count[s % LEO_RING];
-    float pop_error = (float)active / (float)(n_count > 0 ? n_count : 1) - c.target_activity;
-    for (uint32_t i = worker; i < total; i += workers) {
-        if (i < dsts) {
-            uint32_t n = ln.dst_list[i];
-            float* row = ln.p.out_weight + (size_t)n * LEO_OUTPUT_STRIDE;
-            if (plastic) {
-                float signal = 0.0f;
-                const float4* r4 = reinterpret_cast<const float4*>(row);
-                for (uint32_t q = 0; q < 64; ++q) {
-                    float4 w = r4[q];
-                    signal = signal + w.x * s_err[4 * q];
-                    signal = signal + w.y * s_err[4 * q + 1];
-                    signal = signal + w.z * s_err[4 * q + 2];
-                    signal = signal + w.w * s_err[4 * q + 3];
+    // Learning signals, 32 destinations per warp, then -- by the lane that owns
+    // the row, after its signal was read -- the output row of an active
+    // destination.  Every destination occurs once in the list, so no other
+    // thread reads a row that this warp rewrites.
+    for (uint32_t base = gwarp * 32u; base < dsts; base += gwarps * 32u) {
+        uint32_t rows = dsts - base < 32u ? dsts - base : 32u;
+        uint32_t my_n = lane < rows ? ln.dst_list[base + lane] : 0u;
+        const float* my_row = output_row(ln, my_n);
+        if (plastic) {
+            float signal = 0.0f;
+            for (uint32_t chunk = 0; chunk < 8; ++chunk) {
+                float v[32];
+#pragma unroll
+                for (uint32_t r = 0; r < 32; ++r) {
+                    const float* row = (const float*)__shfl_sync(0xffffffffu, (unsigned long long)my_row, (int)r);
+                    v[r] = r < rows ? row[chunk * 32u + lane] : 0.0f;
                 }
-                signal = signal + row[256] * s_err[256];
-                ln.signal[n] = signal;
+#pragma unroll
+                for (uint32_t r = 0; r < 32; ++r) s_tile[warp][r][lane] = v[r];
+                __syncwarp();
+                if (lane < rows) {
+#pragma unroll
+                    for (uint32_t j = 0; j < 32; ++j) signal = signal + s_tile[warp][lane][j] * s_err[chunk * 32u + j];
+                }
+                __syncwarp();
             }
-            float a = ln.hot[n].activation;
+            if (lane < rows) {
+                signal = signal + my_row[256] * s_err[256];
+                ln.signal[my_n] = signal;
+            }
+        }
+        if (lane < rows) {
+            float a = ln.hot[my_n].activation;
             if (a > 0.0f) {
+                float* row = ln.p.out_weight + (size_t)my_n * LEO_OUTPUT_STRIDE;
                 for (uint32_t o = 0; o < LEO_OUTPUT_CLASSES; ++o) {
                     float raw = -c.output_learning_rate * supervised * s_err[o] * a;
                     float delta = clampf(raw, -c.max_update, c.max_update);
-                    row[o] = clampf(row[o] + delta, c.weight_min, c.weight_max);
+                    row[o] = clampf(my_row[o] + delta, c.weight_min, c.weight_max);
                 }
-                if (kc.track_changes) mark_and_append(ln.out_mark, ln.out_list, &sc->out_changed, n);
+                if (kc.track_changes) mark_and_append(ln.out_mark, ln.out_list, &sc->out_changed, my_n);
             }
-        } else {
-            uint32_t n = ln.touched[i - dsts];
-            float local = ln.hot[n].activation > 0.0f ? 1.0f : 0.0f;
-            float local_error = local - c.target_activity;
-            float delta = c.threshold_homeostasis_rate * (local_error + pop_error);
-            float old_t = ln.p.threshold[n];
-            float new_t = clampf(old_t + delta, 0.05f, 2.0f);
-            if (new_t != old_t && kc.track_changes) mark_and_append(ln.thr_mark, ln.thr_list, &sc->thr_changed, n);
-            ln.p.threshold[n] = new_t;
         }
+    }
+    // threshold homeostasis
+    uint32_t active = sc->ring_count[s % LEO_RING];
+    float pop_error = (float)active / (float)(n_count > 0 ? n_count : 1) - c.target_activity;
+    for (uint32_t i = worker; i < touched; i += workers) {
+        uint32_t n = ln.touched[i];
+        float local = ln.hot[n].activation > 0.0f ? 1.0f : 0.0f;
+        float local_error = local - c.target_activity;
+        float delta = c.threshold_homeostasis_rate * (local_error + pop_error);
+        float old_t = ln.p.threshold[n];
+        float new_t = clampf(old_t + delta, 0.05f, 2.0f);
+        if (new_t != old_t && kc.track_changes) mark_and_append(ln.thr_mark, ln.thr_list, &sc->thr_changed, n);
+        ln.p.threshold[n] = new_t;
     }
 }
 
@@ -1061,6 +1095,7 @@ __device__ void phase_plasticity(const LaneState& ln, const KernelConsts& kc, ui
     for (uint32_t i = worker; i < total; i += workers) {
         if (i < rec) {
             uint4 e4 = ln.elig[next][i];
+            if (__uint_as_float(e4.z) == 0.0f) continue;  // unchanged weight (see eligibility_item)
             uint32_t slot = e4.x, dest = e4.y & LEO_TARGET_MASK;
             float gradient = ln.signal[dest] * __uint_as_float(e4.z);
             float delta = clampf(-c.recurrent_learning_rate * strength * gradient, -c.max_update, c.max_update);
@@ -1075,6 +1110,7 @@ __device__ void phase_plasticity(const LaneState& ln, const KernelConsts& kc, ui
             ln.p.rec_weight[slot] = nw;
         } else {
             uint4 e4 = ln.in_elig[next][i - rec];
+            if (__uint_as_float(e4.z) == 0.0f) continue;
             uint32_t slot = e4.x, dest = e4.y & LEO_TARGET_MASK;
             float gradient = ln.signal[dest] * __uint_as_float(e4.z);
             float delta = clampf(-c.recurrent_learning_rate * strength * gradient, -c.max_update, c.max_update);
@@ -1206,7 +1242,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         cluster.sync();
         mark(6);
         if (!frozen) {
-            phase_learn(ln, s, kc, worker, workers);
+            phase_learn(ln, s, kc, worker, workers, gwarp, gwarps, reinterpret_cast<float (*)[32][33]>(smem_sorted));
             cluster.sync();
             mark(7);
             phase_plasticity(ln, kc, worker, workers);
@@ -1222,24 +1258,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int p = 0; p < LEO_PHASES; ++p) sc->phase_cycles[p] += acc[p];
 }
 
+// Dynamic shared memory: the assemble phase's sort buffer and the learn
+// phase's transpose tiles share one region (the phases never overlap).
 size_t leo_wavefront_smem_bytes(const KernelConsts& kc) {
     uint32_t winners = kc.topo.blocks * kc.topo.keep, span = 1;
     while (span < winners) span <<= 1;
-    return (size_t)span * sizeof(unsigned long long);
+    size_t sort = (size_t)span * sizeof(unsigned long long);
+    size_t tiles = (size_t)kWarps * 32 * 33 * sizeof(float);
+    return sort > tiles ? sort : tiles;
+}
+
+// Function attributes the launches and occupancy queries rely on; called
+// once per device before either.
+cudaError_t leo_wavefront_configure() {
+    cudaError_t e = cudaFuncSetAttribute(leo_wavefront_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(leo_wavefront_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
 }
 
 cudaError_t leo_launch_wavefront(const LaneState* lanes, int lane_count, uint32_t cluster, uint32_t begin,
                                  uint32_t end, const KernelConsts& kc, cudaStream_t stream) {
-    static bool configured = false;
     size_t smem = leo_wavefront_smem_bytes(kc);
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(leo_wavefront_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             64 * 1024);
-        if (e != cudaSuccess) return e;
-        e = cudaFuncSetAttribute(leo_wavefront_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)lane_count * cluster, 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
