@@ -55,12 +55,13 @@ BYTES_PER_PLASTIC = 20
 def phase_algorithmic_bytes(p, cfg) -> dict[str, float]:
     """Algorithmic bytes moved by each phase over the counters' window."""
     S, D, K = cfg.synapses_per_neuron, cfg.context_embedding_dim, cfg.context_max_order
-    events = p.work_active * S
+    events = p.work_active * S  # every emitted event is delivered once
     steps = p.work_steps
     return {
         "deliver": events * BYTES_PER_EVENT + steps * cfg.input_fanout * BYTES_PER_INPUT_SLOT,
         "settle": p.work_touched * BYTES_PER_TOUCHED_SETTLE,
-        "select": p.work_active * 8.0,
+        "blocks": p.work_active * 8.0,
+        "assemble": p.work_active * 8.0,
         "surrogate": p.work_touched * BYTES_PER_TOUCHED_SURROGATE,
         "eligible": p.work_eligible * BYTES_PER_ELIGIBLE,
         "emit_forward": p.work_active * (50 + 8 * S + 1028) + steps * (257 * D * 4 + K * D * 4),
@@ -68,7 +69,6 @@ def phase_algorithmic_bytes(p, cfg) -> dict[str, float]:
         + p.work_touched * BYTES_PER_TOUCHED_HOMEOSTASIS,
         "plasticity": p.work_plastic * BYTES_PER_PLASTIC,
         "inhibit": p.work_active * 0.2 * S * 16,
-        "epilogue": 0.0,
     }
 
 
@@ -133,7 +133,8 @@ def cpu_sample(workload, threads: int, stories_n: int, story_bytes: int, batches
     cfg = workload.config
     model = HostModel.initialize(cfg, workload.topology)
     canonical = OracleRuntime(OracleModel.from_arrays(cfg, model.arrays))
-    stories = story_stream(workload.story_seed + 7919, stories_n * batches, story_bytes, story_bytes)
+    lo, hi = (story_bytes, story_bytes) if story_bytes else (workload.min_story_bytes, workload.max_story_bytes)
+    stories = story_stream(workload.story_seed + 7919, stories_n * batches, lo, hi)
     times, nbytes = [], 0
     for b in range(batches):
         batch = stories[b * stories_n:(b + 1) * stories_n]
@@ -143,8 +144,8 @@ def cpu_sample(workload, threads: int, stories_n: int, story_bytes: int, batches
         nbytes += sum(len(s) for s in batch)
     total = sum(times)
     return {"value": nbytes / total, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{batches} batch(es) of {stories_n} stories x {story_bytes} bytes of {workload.name}, "
-                      f"one thread per story, merge and 30% replay included; {total:.1f} s of CPU work",
+            "sample": f"{batches} batch(es) of {stories_n} stories ({nbytes} bytes, lengths {lo}-{hi}) of "
+                      f"{workload.name}, one thread per story, merge and replay included; {total:.1f} s of CPU work",
             "seconds": total}
 
 
@@ -176,10 +177,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", default="baseline2")
-    ap.add_argument("--cpu-stories", type=int, default=8)
-    ap.add_argument("--cpu-bytes", type=int, default=256)
+    ap.add_argument("--cpu-stories", type=int, default=16)
+    ap.add_argument("--cpu-bytes", type=int, default=0, help="fixed CPU sample story length (0: workload's range)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--phase-mask", type=int, default=-1, help="phases timed with CUDA events (default: dominant)")
     args = ap.parse_args()
 
     from leo_b200.configs import WORKLOADS
@@ -217,16 +217,8 @@ def main() -> None:
                            workload.min_story_bytes, workload.max_story_bytes)
     batches = [stories[i * workload.workers:(i + 1) * workload.workers] for i in range(total_batches)]
 
-    # Warm-up, also used to find the dominant phase when none is given.
-    mask = args.phase_mask
-    backend.set_phase_timing(0x3FF if mask < 0 else mask)
     for b in range(args.warmup):
         backend.training_story_batch(batches[b], TRAINING)
-    warm = backend.perf_stats()
-    if mask < 0:
-        shares = [warm.phase_ms[i] for i in range(10)]
-        mask = 1 << int(np.argmax(shares))
-    backend.set_phase_timing(mask)
     backend.reset_perf_stats()
 
     if dist is not None:
@@ -262,18 +254,21 @@ def main() -> None:
     if rank == 0:
         peak, peak_kind = measured_peaks()
         alg = phase_algorithmic_bytes(perf, cfg)
-        timed = [i for i in range(10) if (mask >> i) & 1 and perf.phase_launches[i]]
-        dom = timed[0] if timed else 4
-        name = PHASES[dom]
-        launches = max(perf.phase_launches[dom], 1)
-        per_launch_ms = perf.phase_ms[dom] / launches
-        per_launch_bytes = alg[name] / launches
+        launches = max(perf.wavefront_launches, 1)
+        per_launch_ms = perf.wavefront_ms / launches
+        per_launch_bytes = sum(alg.values()) / launches
         achieved = per_launch_bytes / (per_launch_ms / 1000.0) / 1e9 if per_launch_ms > 0 else 0.0
-        roofline = {"bound": "hbm", "kernel": f"leo_{name}_kernel", "achieved": round(achieved, 3),
+        cycles = np.array(list(perf.phase_cycles)[:10], dtype=np.float64)
+        shares = {PHASES[i]: round(float(cycles[i] / max(cycles.sum(), 1.0)), 4) for i in range(10)}
+        story_launches = max(perf.story_wavefront_launches, 1)
+        roofline = {"bound": "hbm", "kernel": "leo_wavefront_kernel", "achieved": round(achieved, 3),
                     "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 6), "peak_source": peak_kind,
                     "traffic": None, "algorithmic_bytes_per_launch": round(per_launch_bytes, 1),
-                    "launch_ms": round(per_launch_ms, 5), "launches": launches,
-                    "share_of_step_time": round(perf.phase_ms[dom] / max(perf.batch_ms, 1e-9), 4)}
+                    "launch_ms": round(per_launch_ms, 4), "launches": int(perf.wavefront_launches),
+                    "share_of_step_time": round(perf.wavefront_ms / max(perf.batch_ms, 1e-9), 4),
+                    "story_pass_launch_ms": round(perf.story_wavefront_ms / story_launches, 3),
+                    "phase_cycle_shares": shares,
+                    "clusters": {"story": perf.story_cluster, "replay": perf.replay_cluster}}
         line = {
             "metric": METRIC, "value": round(total_bytes / device_s, 3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(device_s * 1000 / args.steps, 3),

@@ -186,8 +186,9 @@ enum LeoB200Phase {
    steps, the units each phase processed: due events plus input slots
    (deliver), touched neurons (settle, surrogate, homeostasis), eligible
    recurrent plus input slots before compaction (eligibility), learning
-   destinations on plasticity steps (signals), active neurons, and
-   post-compaction slots on plasticity steps (weight updates).  phase_cycles
+   destinations on plasticity steps (signals), active neurons, and kept
+   slots with nonzero eligibility (the only weight updates that change a
+   weight).  phase_cycles
    are SM clock cycles spent in each phase (barrier waits included) by the
    first thread of each lane's first CTA; wavefront_ms is CUDA-event time of
    the persistent wavefront launches (story_* for the story-pass launches). */

@@ -161,6 +161,8 @@ WORKLOADS = {
     "baseline2": Workload("baseline2", BASELINE2, TOPOLOGY_UNIFORM, 32, 10_000, 256, 1024),
     "baseline2-replay-off": Workload("baseline2-replay-off", replace(BASELINE2, replay_fraction=0.0),
                                      TOPOLOGY_UNIFORM, 32, 10_000, 256, 1024),
+    # Small case of the baseline2 model for kernel captures: 2 lanes of short stories.
+    "profile": Workload("profile", BASELINE2, TOPOLOGY_UNIFORM, 2, 64, 80, 96),
     "baseline3": Workload("baseline3", BASELINE3, TOPOLOGY_ZIPF, 64, 50_000, 512, 2048),
     "baseline4": Workload("baseline4", BASELINE3, TOPOLOGY_ZIPF, 128, 50_000, 512, 2048),
 }

@@ -693,7 +693,7 @@ __device__ void phase_surrogate(const LaneState& ln, uint32_t s, const KernelCon
 // and their destinations become learning destinations.
 template <bool kInput>
 __device__ __forceinline__ void eligibility_item(const LaneState& ln, const KernelConsts& kc, uint32_t s, uint4 entry,
-                                                 bool valid, uint32_t next) {
+                                                 bool valid, uint32_t next, uint32_t& plastic) {
     const LeoConfig& c = kc.cfg;
     LaneScalars* sc = ln.sc;
     bool keep = false;
@@ -733,6 +733,7 @@ __device__ __forceinline__ void eligibility_item(const LaneState& ln, const Kern
     }
     unsigned int ballot = __ballot_sync(0xffffffffu, keep);
     uint32_t lane = threadIdx.x & 31u;
+    plastic += (keep && e != 0.0f) ? 1u : 0u;
     uint32_t base = 0;
     if (ballot) {
         uint32_t* counter = kInput ? &sc->in_elig_count[next] : &sc->elig_count[next];
@@ -759,20 +760,24 @@ __device__ void phase_eligible(const LaneState& ln, uint32_t s, const KernelCons
     uint32_t rec = sc->elig_count[cur], inp = sc->in_elig_count[cur];
     uint32_t rec_pad = (rec + 31u) & ~31u;
     uint32_t total = rec_pad + inp;
+    uint32_t plastic = 0;
     // Warp-uniform iteration over warp-aligned ranges: each ballot covers one list.
     for (uint32_t base = worker & ~31u; base < total; base += workers) {
         uint32_t i = base + (threadIdx.x & 31u);
         if (base < rec_pad) {
             bool valid = i < rec;
             uint4 entry = valid ? ln.elig[cur][i] : make_uint4(0, 0, 0, 0);
-            eligibility_item<false>(ln, kc, s, entry, valid, next);
+            eligibility_item<false>(ln, kc, s, entry, valid, next, plastic);
         } else {
             uint32_t k = i - rec_pad;
             bool valid = k < inp;
             uint4 entry = valid ? ln.in_elig[cur][k] : make_uint4(0, 0, 0, 0);
-            eligibility_item<true>(ln, kc, s, entry, valid, next);
+            eligibility_item<true>(ln, kc, s, entry, valid, next, plastic);
         }
     }
+    // Work counter: one add per warp per step (kept slots with nonzero eligibility).
+    plastic = __reduce_add_sync(0xffffffffu, plastic);
+    if ((threadIdx.x & 31u) == 0u && plastic) atomicAdd(&sc->work_plastic, (unsigned long long)plastic);
 }
 
 // ---------------------------------------------------------------------------
@@ -1161,10 +1166,7 @@ __device__ void step_epilogue(const LaneState& ln, uint32_t s, bool frozen) {
     sc->work_active += sc->ring_count[s % LEO_RING];
     sc->work_steps += 1;
     if (!frozen) sc->work_eligible += sc->elig_count[cur] + sc->in_elig_count[cur];
-    if ((sc->step_flags & 3u) == 3u) {
-        sc->work_destinations += sc->dst_count;
-        sc->work_plastic += sc->elig_count[cur ^ 1u] + sc->in_elig_count[cur ^ 1u];
-    }
+    if ((sc->step_flags & 3u) == 3u) sc->work_destinations += sc->dst_count;
     sc->touched_count = 0;
     sc->dst_count = 0;
     if (!frozen) sc->elig_cur = cur ^ 1u;

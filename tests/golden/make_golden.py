@@ -1,0 +1,75 @@
+"""Generate the golden story-batch fixtures from the CPU oracle.
+
+Usage: ``python tests/golden/make_golden.py`` (writes ``story_batches.json``
+beside this file).
+
+The reference holds no value-level golden vectors for the story batch (its
+historical digests need a corpus that is not available), so these fixtures
+record what the oracle -- the restatement of the reference CPU backend, itself
+pinned by the reference's known-answer tests -- produces on seeded synthetic
+stories: the SHA-256 of the story bytes, and after each logical batch the
+``training_state_hash`` (crates/leo-cli/src/main.rs:1151-1202), the SHA-256 of
+the per-target losses (f32 little-endian), the batch report, the replay ranges
+(crates/leo-cli/src/training.rs:1782-1830), the parameter revision and the
+training statistics.  Both the oracle (on CPU) and the GPU path (on a B200) are
+checked against them.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
+sys.path.insert(0, str(ROOT))
+
+# (workload, batches, stories per batch)
+CASES = [("test", 3, 4), ("probe", 1, 4), ("baseline1", 1, 4)]
+
+
+def record_batches(workload_name: str, batches: int, per_batch: int) -> dict:
+    from leo_b200.configs import WORKLOADS
+    from leo_b200.ctypes_types import TRAINING
+    from leo_b200.synthetic import story_stream
+    from oracle.oracle_py import OracleModel, OracleRuntime
+
+    w = WORKLOADS[workload_name]
+    stories = story_stream(w.story_seed, batches * per_batch, w.min_story_bytes, w.max_story_bytes)
+    model = OracleModel.initialize(w.config, w.topology)
+    rt = OracleRuntime(model)
+    out = {"workload": workload_name, "stories_per_batch": per_batch,
+           "initial_state_hash": rt.model.training_state_hash().hex(), "batches": []}
+    for b in range(batches):
+        batch = stories[b * per_batch:(b + 1) * per_batch]
+        report, losses, ranges = rt.train_story_batch(batch, TRAINING, 0)
+        gen, rev, stats = rt.model.scalars()
+        out["batches"].append({
+            "stories_sha256": hashlib.sha256(b"".join(batch)).hexdigest(),
+            "story_lengths": [len(s) for s in batch],
+            "state_hash": rt.model.training_state_hash().hex(),
+            "losses_sha256": hashlib.sha256(losses.astype("<f4").tobytes()).hexdigest(),
+            "mean_loss": report.mean_loss,
+            "report": {k: int(getattr(report, k)) for k, _ in report._fields_ if k != "mean_loss"},
+            "replay_ranges": ranges,
+            "generation": int(gen),
+            "parameter_revision": int(rev),
+            "statistics": {k: (float(getattr(stats, k)) if k == "training_loss_sum" else int(getattr(stats, k)))
+                           for k, _ in stats._fields_},
+            "canonical_tick": int(rt.tick),
+        })
+    return out
+
+
+def main() -> None:
+    from oracle import oracle_py
+
+    oracle_py.build()
+    data = {"generator": "tests/golden/make_golden.py", "cases": [record_batches(*c) for c in CASES]}
+    (HERE / "story_batches.json").write_text(json.dumps(data, indent=1, sort_keys=True) + "\n")
+
+
+if __name__ == "__main__":
+    main()

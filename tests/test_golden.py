@@ -1,0 +1,83 @@
+"""Golden story-batch fixtures (``tests/golden/story_batches.json``, made by
+``tests/golden/make_golden.py`` from the oracle).
+
+The CPU test pins the oracle and the synthetic story generator against the
+committed records; the GPU test checks the product path through the public
+``GpuBackend.training_story_batch`` (the C-ABI ``leo_b200_train_story_batch``)
+against the same records: bit-exact state hash, per-target losses, batch
+report counts, revision, statistics and canonical tick.
+"""
+
+import hashlib
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+GOLDEN = json.loads((Path(__file__).resolve().parent / "golden" / "story_batches.json").read_text())
+CASES = {c["workload"]: c for c in GOLDEN["cases"]}
+
+
+def _stories(case):
+    from leo_b200.configs import WORKLOADS
+    from leo_b200.synthetic import story_stream
+
+    w = WORKLOADS[case["workload"]]
+    n = case["stories_per_batch"]
+    stories = story_stream(w.story_seed, n * len(case["batches"]), w.min_story_bytes, w.max_story_bytes)
+    return w, [stories[i * n:(i + 1) * n] for i in range(len(case["batches"]))]
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_synthetic_stories_match_golden(name):
+    case = CASES[name]
+    _, batches = _stories(case)
+    for rec, batch in zip(case["batches"], batches):
+        assert hashlib.sha256(b"".join(batch)).hexdigest() == rec["stories_sha256"]
+        assert [len(s) for s in batch] == rec["story_lengths"]
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_oracle_matches_golden(oracle_lib, name):
+    from leo_b200.ctypes_types import TRAINING
+
+    case = CASES[name]
+    w, batches = _stories(case)
+    rt = oracle_lib.OracleRuntime(oracle_lib.OracleModel.initialize(w.config, w.topology))
+    assert rt.model.training_state_hash().hex() == case["initial_state_hash"]
+    for rec, batch in zip(case["batches"], batches):
+        report, losses, ranges = rt.train_story_batch(batch, TRAINING, 0)
+        assert rt.model.training_state_hash().hex() == rec["state_hash"]
+        assert hashlib.sha256(losses.astype("<f4").tobytes()).hexdigest() == rec["losses_sha256"]
+        assert [[list(r) for r in s] for s in ranges] == rec["replay_ranges"]
+        for k, v in rec["report"].items():
+            assert int(getattr(report, k)) == v, k
+        assert rt.tick == rec["canonical_tick"]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_gpu_story_batch_matches_golden(native_lib, name):
+    from leo_b200.backend import GpuBackend
+    from leo_b200.ctypes_types import TRAINING
+    from leo_b200.model import HostModel
+
+    case = CASES[name]
+    w, batches = _stories(case)
+    model = HostModel.initialize(w.config, w.topology)
+    assert model.training_state_hash().hex() == case["initial_state_hash"]
+    with GpuBackend(model, device=0, max_lanes=case["stories_per_batch"]) as backend:
+        for i, (rec, batch) in enumerate(zip(case["batches"], batches)):
+            result = backend.training_story_batch(batch, TRAINING)
+            assert backend.state_digest().hex() == rec["state_hash"], f"batch {i}"
+            losses = np.concatenate(result.losses).astype("<f4")
+            assert hashlib.sha256(losses.tobytes()).hexdigest() == rec["losses_sha256"], f"batch {i}"
+            for k, v in rec["report"].items():
+                assert int(getattr(result.report, k)) == v, (i, k)
+            assert backend.canonical_tick == rec["canonical_tick"]
+            m = backend.synchronize_model()
+            assert m.parameter_revision == rec["parameter_revision"]
+            for k, v in rec["statistics"].items():
+                got = getattr(m.statistics, k)
+                assert (got == v) if k != "training_loss_sum" else got == pytest.approx(v, rel=0, abs=0), (i, k)
