@@ -618,7 +618,12 @@ __device__ void phase_assemble(const LaneState& ln, uint32_t s, const KernelCons
             }
         }
         if (selected > cap) {
-            pop_cutoff = clampf(key_value(sorted[cap]), 0.0f, c.population_inhibition_max);
+            // The cutoff is the first clipped neuron's margin clamped to
+            // [0, population_inhibition_max] -- not its activation, which is
+            // clamped to [0, 1] -- so a saturated neuron can set a cutoff
+            // above 1 (runtime.rs:1045-1050).
+            const uint32_t cut = key_neuron(sorted[cap], rotation, n_count);
+            pop_cutoff = clampf(ln.cold[cut].membrane - ln.p.threshold[cut], 0.0f, c.population_inhibition_max);
             clipped = selected - cap;
             active = cap;
         }

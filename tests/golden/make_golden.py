@@ -26,24 +26,39 @@ HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
 sys.path.insert(0, str(ROOT))
 
-# (workload, batches, stories per batch)
-CASES = [("test", 3, 4), ("probe", 1, 4), ("baseline1", 1, 4)]
+# (case name, workload, batches, stories per batch, min / max story bytes, story seed)
+CASES = [
+    ("test", "test", 3, 4, 8, 48, 0),
+    ("test-8", "test", 2, 8, 8, 64, 17),
+    ("probe", "probe", 1, 4, 256, 1024, 0),
+    ("baseline1", "baseline1", 2, 4, 256, 1024, 0),
+    ("baseline2-short", "baseline2", 2, 4, 48, 96, 5),
+]
 
 
-def record_batches(workload_name: str, batches: int, per_batch: int) -> dict:
+def case_stories(case: dict) -> list[list[bytes]]:
+    """The case's stories, split into its batches."""
+    from leo_b200.synthetic import story_stream
+
+    n = case["stories_per_batch"]
+    stories = story_stream(case["story_seed"], n * case["batch_count"], case["min_story_bytes"],
+                           case["max_story_bytes"])
+    return [stories[i * n:(i + 1) * n] for i in range(case["batch_count"])]
+
+
+def record_batches(name: str, workload_name: str, batches: int, per_batch: int, min_bytes: int, max_bytes: int,
+                   seed: int) -> dict:
     from leo_b200.configs import WORKLOADS
     from leo_b200.ctypes_types import TRAINING
-    from leo_b200.synthetic import story_stream
     from oracle.oracle_py import OracleModel, OracleRuntime
 
     w = WORKLOADS[workload_name]
-    stories = story_stream(w.story_seed, batches * per_batch, w.min_story_bytes, w.max_story_bytes)
+    out = {"name": name, "workload": workload_name, "stories_per_batch": per_batch, "batch_count": batches,
+           "min_story_bytes": min_bytes, "max_story_bytes": max_bytes, "story_seed": seed, "batches": []}
     model = OracleModel.initialize(w.config, w.topology)
     rt = OracleRuntime(model)
-    out = {"workload": workload_name, "stories_per_batch": per_batch,
-           "initial_state_hash": rt.model.training_state_hash().hex(), "batches": []}
-    for b in range(batches):
-        batch = stories[b * per_batch:(b + 1) * per_batch]
+    out["initial_state_hash"] = rt.model.training_state_hash().hex()
+    for batch in case_stories(out):
         report, losses, ranges = rt.train_story_batch(batch, TRAINING, 0)
         gen, rev, stats = rt.model.scalars()
         out["batches"].append({

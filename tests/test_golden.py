@@ -15,18 +15,20 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-GOLDEN = json.loads((Path(__file__).resolve().parent / "golden" / "story_batches.json").read_text())
-CASES = {c["workload"]: c for c in GOLDEN["cases"]}
+HERE = Path(__file__).resolve().parent
+GOLDEN = json.loads((HERE / "golden" / "story_batches.json").read_text())
+CASES = {c["name"]: c for c in GOLDEN["cases"]}
 
 
 def _stories(case):
-    from leo_b200.configs import WORKLOADS
-    from leo_b200.synthetic import story_stream
+    import sys
 
-    w = WORKLOADS[case["workload"]]
-    n = case["stories_per_batch"]
-    stories = story_stream(w.story_seed, n * len(case["batches"]), w.min_story_bytes, w.max_story_bytes)
-    return w, [stories[i * n:(i + 1) * n] for i in range(len(case["batches"]))]
+    from leo_b200.configs import WORKLOADS
+
+    sys.path.insert(0, str(HERE / "golden"))
+    from make_golden import case_stories
+
+    return WORKLOADS[case["workload"]], case_stories(case)
 
 
 @pytest.mark.parametrize("name", sorted(CASES))
