@@ -109,6 +109,26 @@ int leo_b200_set_cluster_sizes(LeoB200Device* device, uint32_t story_cluster, ui
 /* Device memory held by the backend, in bytes. */
 size_t leo_b200_device_bytes(LeoB200Device* device);
 
+/* Batch-end sparse mean apply of one FP32 tensor plus the sync of its
+   replicas, on device memory the caller owns: apply_sparse_scaled
+   (crates/leo-core/src/parallel.rs:975-1022) with divisor = `stories`, then the
+   clamp projection of parallel.rs:1226-1233 ([lo, hi]; pass -inf/+inf for
+   none), then the merged values written into each of `replica_count` replica
+   copies (the packed-update scatter, crates/leo-core/src/cuda.rs:2869-3080).
+   Story s owns entries story_offsets[s] .. story_offsets[s + 1] of `indices`
+   (sorted, strictly increasing, < length) and `deltas` (finite); the offsets
+   and the replica pointer table are HOST arrays, everything else is device
+   memory on `device`.  Invalid input is rejected before anything is written.
+   At most 256 stories and 64 replicas per call.  `stream` is a cudaStream_t
+   (NULL: the legacy default stream); the call waits for it and stores the
+   number of merged indices in *updates.  Scratch (a tile table of
+   stories x (length / 4096 + 1) words) is allocated on first use per device
+   and kept; calls on one device are serialised. */
+int leo_b200_sparse_mean_apply(int device, float* target, uint32_t length, const uint32_t* indices,
+                               const float* deltas, const uint64_t* story_offsets, uint32_t stories, float lo,
+                               float hi, float* const* replicas, uint32_t replica_count, void* stream,
+                               uint32_t* updates);
+
 #ifdef __cplusplus
 }
 #endif

@@ -55,3 +55,6 @@ void leo_launch_merge_tensor(const MergeTensor& t, const MergeScratch& m, int la
 // Writes base[list[i] * row + o] (o < row_len) into every lane tensor.
 void leo_launch_scatter_rows(float** lane_values, int lanes, const float* base, const uint32_t* list, uint32_t count,
                              uint32_t row, uint32_t row_len, int grid, cudaStream_t stream);
+
+// Sets the text leo_b200_last_error() returns on this thread.
+void leo_set_last_error(const char* what);

@@ -1063,6 +1063,9 @@ void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySu
 }  // namespace
 
 // ============================================================================ C ABI
+// Error text for C-ABI entry points defined in other translation units.
+void leo_set_last_error(const char* what) { g_error = what; }
+
 extern "C" {
 
 const char* leo_b200_last_error(void) { return g_error.c_str(); }

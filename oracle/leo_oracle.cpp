@@ -1812,6 +1812,18 @@ MergeMetrics apply_deltas_with_divisor(Model& master, const std::vector<SparseMo
 }
 }  // namespace
 
+size_t sparse_mean_apply(std::vector<float>& target, const std::vector<std::vector<SparseF32Delta>>& stories, float lo,
+                         float hi) {
+    if (stories.empty()) throw LeoError(LeoError::Internal, "cannot merge an empty worker batch");
+    std::vector<const std::vector<SparseF32Delta>*> groups;
+    for (auto& s : stories) groups.push_back(&s);
+    size_t updates = apply_sparse_scaled(target, groups, stories.size());
+    // projection of parallel.rs:1226-1233 (output-weight clamp) over every delta index
+    for (auto& s : stories)
+        for (auto& u : s) target[u.index] = clampf(target[u.index], lo, hi);
+    return updates;
+}
+
 MergeMetrics apply_mean_deltas(Model& master, const std::vector<SparseModelDelta>& deltas) {
     return apply_deltas_with_divisor(master, deltas, deltas.size());
 }

@@ -306,6 +306,10 @@ struct SparseModelDelta {
 struct MergeMetrics { size_t workers = 0, fixed_parameter_updates = 0, context_keys = 0; };
 MergeMetrics apply_mean_deltas(Model& master, const std::vector<SparseModelDelta>& deltas);
 MergeMetrics apply_sum_deltas(Model& master, const std::vector<SparseModelDelta>& deltas);
+// apply_sparse_scaled (parallel.rs:975-1022) of one tensor with divisor = stories,
+// then the clamp projection of parallel.rs:1226-1233; returns the union size.
+size_t sparse_mean_apply(std::vector<float>& target, const std::vector<std::vector<SparseF32Delta>>& stories, float lo,
+                         float hi);
 StatisticsDelta statistics_delta(const Statistics& before, const Statistics& after);
 
 // ---- training policy, crates/leo-cli/src/training.rs -------------------------

@@ -412,6 +412,23 @@ int leo_oracle_mean_of_models(void* master, void* const* trained, size_t count, 
     }
 }
 
+// One tensor's batch-end sparse mean apply: stories' sorted (index, delta)
+// lists in CSR form (offsets has stories + 1 entries).
+int leo_oracle_sparse_mean_apply(float* target, size_t length, const uint32_t* indices, const float* deltas,
+                                 const uint64_t* offsets, size_t stories, float lo, float hi, size_t* updates) {
+    try {
+        std::vector<float> t(target, target + length);
+        std::vector<std::vector<SparseF32Delta>> lists(stories);
+        for (size_t s = 0; s < stories; ++s)
+            for (uint64_t j = offsets[s]; j < offsets[s + 1]; ++j) lists[s].push_back({indices[j], deltas[j]});
+        *updates = sparse_mean_apply(t, lists, lo, hi);
+        std::copy(t.begin(), t.end(), target);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
 int leo_oracle_select_replay_ranges(const float* losses, size_t n, float fraction, size_t segment, uint64_t* out,
                                     size_t cap, size_t* count) {
     std::vector<float> l(losses, losses + n);

@@ -70,6 +70,7 @@ def lib() -> C.CDLL:
         L.leo_oracle_runtime_array.argtypes = [vp, C.c_char_p, C.POINTER(vp), C.POINTER(sz), C.POINTER(sz)]
         L.leo_oracle_train_story_batch.argtypes = [vp, vp, vp, sz, C.c_int, sz, vp, vp, vp, vp]
         L.leo_oracle_mean_of_models.argtypes = [vp, vp, sz, C.c_int]
+        L.leo_oracle_sparse_mean_apply.argtypes = [vp, sz, vp, vp, vp, sz, C.c_float, C.c_float, C.POINTER(sz)]
         L.leo_oracle_select_replay_ranges.argtypes = [C.c_void_p, sz, C.c_float, sz, vp, sz, C.POINTER(sz)]
         _lib = L
     return _lib
@@ -270,6 +271,20 @@ def select_replay_ranges(losses: np.ndarray, fraction: float, segment: int) -> l
     lib().leo_oracle_select_replay_ranges(losses.ctypes.data, len(losses), fraction, segment, out.ctypes.data,
                                           len(losses) + 1, C.byref(cnt))
     return [(int(out[2 * i]), int(out[2 * i + 1])) for i in range(cnt.value)]
+
+
+def sparse_mean_apply(target: np.ndarray, indices: np.ndarray, deltas: np.ndarray, offsets: np.ndarray,
+                      lo: float, hi: float) -> int:
+    """apply_sparse_scaled (parallel.rs:975-1022) + clamp, in place on ``target``."""
+    t = np.ascontiguousarray(target, dtype=np.float32)
+    idx = np.ascontiguousarray(indices, dtype=np.uint32)
+    dl = np.ascontiguousarray(deltas, dtype=np.float32)
+    off = np.ascontiguousarray(offsets, dtype=np.uint64)
+    updates = C.c_size_t()
+    _check(lib().leo_oracle_sparse_mean_apply(t.ctypes.data, t.size, idx.ctypes.data, dl.ctypes.data, off.ctypes.data,
+                                              off.size - 1, lo, hi, C.byref(updates)))
+    target[...] = t
+    return updates.value
 
 
 def sha256(data: bytes) -> bytes:
