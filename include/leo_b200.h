@@ -129,6 +129,27 @@ int leo_b200_sparse_mean_apply(int device, float* target, uint32_t length, const
                                float hi, float* const* replicas, uint32_t replica_count, void* stream,
                                uint32_t* updates);
 
+/* The same apply with NO device allocation: no counterpart in the reference
+   (which allocates its scratch with cuMemAlloc).  For callers that must not
+   allocate device memory inside the call: cudaFree synchronises the whole
+   device (stalling every other stream, NCCL's included), a process whose HBM
+   is already reserved by a caching allocator can fail a fresh cudaMalloc for
+   a small scratch, and latency-bounded loops must not enter the allocator.
+   Scratch is a fixed 1 MiB device array compiled into the library: the call
+   accepts stories * (ceil(length / 4096) + 1) <= 262080 (for example 63
+   stories at length 2^24, or 256 stories up to length 4,165,632) and rejects
+   larger inputs with an error before any device work; the other limits and
+   the results are those of leo_b200_sparse_mean_apply.  The first call on a
+   device resolves the array's address (cudaGetSymbolAddress); make that first
+   call before any stream capture begins.  Every call zeroes the counters at
+   the head of the array on `stream` before its kernels run.  All calls on one
+   device share the array: calls that overlap in time race, so the caller
+   serialises them. */
+int leo_b200_sparse_mean_apply_static(int device, float* target, uint32_t length, const uint32_t* indices,
+                                      const float* deltas, const uint64_t* story_offsets, uint32_t stories,
+                                      float lo, float hi, float* const* replicas, uint32_t replica_count,
+                                      void* stream, uint32_t* updates);
+
 #ifdef __cplusplus
 }
 #endif

@@ -156,6 +156,29 @@ struct DeviceScratch {
 
 DeviceScratch g_scratch[LEO_SPARSE_APPLY_MAX_DEVICES];
 
+// Fixed scratch of leo_b200_sparse_mean_apply_static: 1 MiB of device memory
+// reserved when the module loads, so that entry point never allocates.  Its
+// first LEO_SPARSE_APPLY_COUNTERS words are counters that every call zeroes
+// before its kernels run; the tile table after them is written in full by
+// every call and needs no initial value.  One array per device, shared by
+// every call on that device: calls that overlap in time (two host threads, or
+// two streams without ordering between them) race on it.
+static __device__ __align__(256) uint32_t leo_sparse_apply_static_scratch[LEO_SPARSE_APPLY_STATIC_WORDS];
+
+// Device address of that array, resolved once per device (cudaGetSymbolAddress).
+uint32_t* g_static_scratch[LEO_SPARSE_APPLY_MAX_DEVICES];
+std::mutex g_static_lock;
+
+uint32_t* static_scratch_address(int device) {
+    std::lock_guard<std::mutex> guard(g_static_lock);
+    if (g_static_scratch[device] == nullptr) {
+        void* ptr = nullptr;
+        check(cudaGetSymbolAddress(&ptr, leo_sparse_apply_static_scratch), "cudaGetSymbolAddress(static scratch)");
+        g_static_scratch[device] = static_cast<uint32_t*>(ptr);
+    }
+    return g_static_scratch[device];
+}
+
 }  // namespace
 
 size_t leo_sparse_apply_scratch_words(uint32_t length, uint32_t stories) {
@@ -251,6 +274,39 @@ int leo_b200_sparse_mean_apply(int device, float* target, uint32_t length, const
             sc.words = words;
         }
         a.scratch = sc.ptr;
+        const uint32_t n = leo_sparse_apply_run(a, (cudaStream_t)stream);
+        if (updates) *updates = n;
+        cudaSetDevice(previous);
+        return 0;
+    } catch (const std::exception& e) {
+        leo_set_last_error(e.what());
+        if (previous >= 0) cudaSetDevice(previous);
+        return -1;
+    }
+}
+
+// The variant of leo_b200_sparse_mean_apply that allocates nothing: its
+// scratch is the fixed array above.  Every CUDA call it makes is a device
+// selection, an asynchronous memset / copy on the caller's stream, the two
+// kernel launches and a stream synchronisation; the first call on a device also
+// resolves the array's address with cudaGetSymbolAddress.
+int leo_b200_sparse_mean_apply_static(int device, float* target, uint32_t length, const uint32_t* indices,
+                                      const float* deltas, const uint64_t* story_offsets, uint32_t stories,
+                                      float lo, float hi, float* const* replicas, uint32_t replica_count,
+                                      void* stream, uint32_t* updates) {
+    int previous = -1;
+    try {
+        if (device < 0 || device >= LEO_SPARSE_APPLY_MAX_DEVICES) throw ApplyFailure("invalid device ordinal");
+        SparseApplyArgs a;
+        leo_sparse_apply_prepare(a, target, length, indices, deltas, story_offsets, stories, lo, hi, replicas,
+                                 replica_count);
+        const size_t words = leo_sparse_apply_scratch_words(length, stories);
+        if (words > LEO_SPARSE_APPLY_STATIC_WORDS)
+            throw ApplyFailure("input too large for the fixed 1 MiB scratch: stories * (ceil(length / 4096) + 1) must "
+                               "not exceed 262080 (use leo_b200_sparse_mean_apply)");
+        check(cudaGetDevice(&previous), "cudaGetDevice");
+        check(cudaSetDevice(device), "cudaSetDevice");
+        a.scratch = static_scratch_address(device);
         const uint32_t n = leo_sparse_apply_run(a, (cudaStream_t)stream);
         if (updates) *updates = n;
         cudaSetDevice(previous);

@@ -10,6 +10,7 @@
 #define LEO_SPARSE_APPLY_MAX_REPLICAS 64u  // replicas per call (pointers travel as a kernel parameter)
 #define LEO_SPARSE_APPLY_MAX_DEVICES 64
 #define LEO_SPARSE_APPLY_COUNTERS 64u      // leading scratch words: [0] merged count, [1] error flags
+#define LEO_SPARSE_APPLY_STATIC_WORDS 262144u  // fixed scratch of the allocation-free entry point: 1 MiB
 
 #define LEO_SPARSE_APPLY_ERR_RANGE 1u
 #define LEO_SPARSE_APPLY_ERR_ORDER 2u
