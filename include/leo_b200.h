@@ -106,6 +106,14 @@ int leo_b200_reset_perf_stats(LeoB200Device* device);
    execution tuner chooses the analogous geometry (crates/leo-core/src/cuda_plan.rs:189-453). */
 int leo_b200_set_cluster_sizes(LeoB200Device* device, uint32_t story_cluster, uint32_t replay_cluster);
 
+/* Execution geometry only: with the default story cluster size (0), the story
+   pass runs in launches of `steps` steps (default 32; four times that while
+   the lanes' loads are within 3x of the median), and before each launch
+   the SMs are re-divided among the lanes that still have steps, in proportion
+   to the work per step each lane reported (the reference's execution tuner
+   plays this role statically, crates/leo-core/src/cuda_plan.rs:189-453). */
+int leo_b200_set_story_chunk(LeoB200Device* device, uint32_t steps);
+
 /* Device memory held by the backend, in bytes. */
 size_t leo_b200_device_bytes(LeoB200Device* device);
 

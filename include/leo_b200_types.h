@@ -211,6 +211,9 @@ typedef struct LeoB200PerfStats {
     double batch_ms;
     uint32_t story_cluster;
     uint32_t replay_cluster;
+    uint64_t story_lane_launches[5]; /* story-pass lane launches at cluster size 1, 2, 4, 8, 16 */
+    int32_t fit_clusters[3];         /* co-resident clusters of 4, 8 and 16 CTAs */
+    int32_t sm_count;
 } LeoB200PerfStats;
 
 #ifdef __cplusplus

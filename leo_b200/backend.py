@@ -96,6 +96,9 @@ class GpuBackend:
     def set_cluster_sizes(self, story: int = 0, replay: int = 0) -> None:
         native.check(native.lib().leo_b200_set_cluster_sizes(self.handle, story, replay))
 
+    def set_story_chunk(self, steps: int) -> None:
+        native.check(native.lib().leo_b200_set_story_chunk(self.handle, steps))
+
     def perf_stats(self):
         from .ctypes_types import LeoB200PerfStats
 

@@ -191,6 +191,10 @@ struct LaneState {
     uint8_t* in_mark;   uint32_t* in_list;    // [258*F]
     uint8_t* out_mark;  uint32_t* out_list;   // [N]
     uint8_t* ctx_mark;  uint32_t* ctx_list;   // [C]
+    // Where the first CTA reports the lane's work per step (eligible slots +
+    // events emitted + touched neurons) at the end of each launch; the host
+    // sizes the next launch's clusters from it.  Null: not reported.
+    uint32_t* load_out;
 };
 
 struct KernelConsts {

@@ -126,6 +126,16 @@ struct LeoB200Device {
     // performance counters and execution geometry
     LeoB200PerfStats perf{};
     uint32_t story_cluster_request = 0, replay_cluster_request = 0;
+    // Adaptive story-pass geometry: per-lane load reported by the kernel, the
+    // lane table of one chunk's launches, and streams for concurrent launches.
+    int sm_count = 0;
+    int fit16 = 0, fit8 = 0, fit4 = 0;  // co-resident clusters of 16 / 8 / 4 CTAs
+    uint32_t story_chunk = 32;        // steps per story-pass launch while lane loads are skewed
+    uint32_t* d_lane_load = nullptr;  // [max_lanes + 1], last entry: replay lane
+    LaneState* d_group_table = nullptr;
+    std::vector<uint32_t> lane_steps;
+    cudaStream_t aux[4] = {nullptr, nullptr, nullptr, nullptr};
+    cudaEvent_t fork = nullptr, join[4] = {nullptr, nullptr, nullptr, nullptr};
     cudaEvent_t batch_start = nullptr, batch_stop = nullptr;
     cudaEvent_t wave_start = nullptr, wave_stop = nullptr;
 };
@@ -271,6 +281,7 @@ void ensure_lanes(LeoB200Device& dev, uint32_t count) {
         auto lane = std::make_unique<Lane>();
         allocate_lane_params(dev, *lane);
         allocate_lane_transient(dev, *lane);
+        lane->st.load_out = dev.d_lane_load + dev.lanes.size();
         copy_params(dev, lane->st.p, dev.canon);
         dev.lanes.push_back(std::move(lane));
     }
@@ -396,6 +407,131 @@ void run_steps(LeoB200Device& dev, const LaneState* d_lanes, int lane_count, uin
     } else {
         dev.perf.replay_cluster = cluster;
     }
+}
+
+// Cluster sizes for one chunk of the story pass.  Model of a lane's time per
+// step with c CTAs (fitted to measured lanes of config 2): 50 us of latency
+// plus 0.01 us per unit of reported load, divided by c^0.8.  Starting from one
+// CTA per lane, the lane with the largest modelled time doubles its cluster
+// (up to 16) while the sizes still pack: clusters of 4 or more CTAs occupy
+// whole 4-SM units of one GPC (fit4 such units co-reside), at most fit8 / fit16
+// clusters of 8 / 16, and 1- or 2-CTA clusters fill the SMs outside the units
+// and any unused units.  The chunk's time is its slowest lane, so the greedy
+// stops when that lane cannot grow.  Results do not depend on the sizes.
+double modelled_step_us(uint32_t load, uint32_t c) { return 50.0 + 0.01 * (double)load / std::pow((double)c, 0.8); }
+
+bool sizes_pack(const LeoB200Device& dev, const int n[5]) {
+    if (n[4] > dev.fit16 || n[3] + 2 * n[4] > dev.fit8) return false;
+    const int units = n[2] + 2 * n[3] + 4 * n[4];
+    const int small = n[0] + 2 * n[1];
+    const int outside = std::max(0, dev.sm_count - 4 * dev.fit4);
+    return units + (std::max(0, small - outside) + 3) / 4 <= dev.fit4;
+}
+
+std::vector<uint32_t> assign_clusters(const LeoB200Device& dev, const std::vector<uint32_t>& lanes,
+                                      const std::vector<uint32_t>& load) {
+    std::vector<uint32_t> c(lanes.size(), 1u);
+    std::vector<bool> settled(lanes.size(), false);  // at 16 CTAs, or no longer packable
+    int n[5] = {(int)lanes.size(), 0, 0, 0, 0};
+    if (!sizes_pack(dev, n)) return c;
+    for (;;) {
+        size_t worst = lanes.size();
+        double worst_t = -1.0;
+        for (size_t i = 0; i < lanes.size(); ++i) {
+            if (settled[i]) continue;
+            const double t = modelled_step_us(load[lanes[i]], c[i]);
+            if (t > worst_t) {
+                worst_t = t;
+                worst = i;
+            }
+        }
+        if (worst == lanes.size()) break;
+        const int k = __builtin_ctz(c[worst]);
+        n[k] -= 1;
+        n[k + 1] += 1;
+        if (!sizes_pack(dev, n)) {
+            // The slowest growable lane cannot grow: stop here, so that a
+            // smaller lane never takes the units the slower one needs next.
+            n[k] += 1;
+            n[k + 1] -= 1;
+            break;
+        }
+        c[worst] *= 2u;
+        if (c[worst] == 16u) settled[worst] = true;
+    }
+    return c;
+}
+
+// The story pass in chunks of `story_chunk` steps; each chunk launches one
+// wavefront per cluster size in use (concurrently, on separate streams) over
+// the lanes that still have steps, sized from the loads the previous chunk
+// reported.
+void run_story_adaptive(LeoB200Device& dev, int lane_count, uint32_t begin, uint32_t end) {
+    std::vector<uint32_t> load(lane_count, 1u), reported(lane_count, 0u);
+    CUDA_CHECK(cudaEventRecord(dev.wave_start, dev.stream));
+    uint32_t largest = 0;
+    uint32_t chunk = std::max(dev.story_chunk, 1u);
+    for (uint32_t s = begin; s < end;) {
+        const uint32_t e = std::min(end, s + chunk);
+        std::vector<uint32_t> act;
+        for (int l = 0; l < lane_count; ++l)
+            if (dev.lane_steps[l] > s) act.push_back((uint32_t)l);
+        if (act.empty()) break;
+        const std::vector<uint32_t> c = assign_clusters(dev, act, load);
+        std::vector<LaneState> table;
+        std::vector<std::pair<uint32_t, uint32_t>> groups;  // (cluster size, lanes)
+        for (uint32_t size = 16; size >= 1; size >>= 1) {
+            uint32_t count = 0;
+            for (size_t i = 0; i < act.size(); ++i)
+                if (c[i] == size) {
+                    table.push_back(dev.lanes[act[i]]->st);
+                    ++count;
+                }
+            dev.perf.story_lane_launches[__builtin_ctz(size)] += count;
+            if (count) groups.push_back({size, count});
+            largest = std::max(largest, count ? size : 0u);
+        }
+        CUDA_CHECK(cudaMemcpyAsync(dev.d_group_table, table.data(), table.size() * sizeof(LaneState),
+                                   cudaMemcpyHostToDevice, dev.stream));
+        CUDA_CHECK(cudaEventRecord(dev.fork, dev.stream));
+        size_t offset = 0;
+        for (size_t g = 0; g < groups.size(); ++g) {
+            cudaStream_t st = g == 0 ? dev.stream : dev.aux[g - 1];
+            if (g > 0) CUDA_CHECK(cudaStreamWaitEvent(st, dev.fork, 0));
+            CUDA_CHECK(leo_launch_wavefront(dev.d_group_table + offset, (int)groups[g].second, groups[g].first, s, e,
+                                            dev.kc, st));
+            CUDA_CHECK(cudaGetLastError());
+            if (g > 0) CUDA_CHECK(cudaEventRecord(dev.join[g - 1], st));
+            offset += groups[g].second;
+            dev.perf.launches += 1;
+            dev.perf.wavefront_launches += 1;
+            dev.perf.story_wavefront_launches += 1;
+        }
+        for (size_t g = 1; g < groups.size(); ++g) CUDA_CHECK(cudaStreamWaitEvent(dev.stream, dev.join[g - 1], 0));
+        CUDA_CHECK(cudaMemcpyAsync(reported.data(), dev.d_lane_load, lane_count * sizeof(uint32_t),
+                                   cudaMemcpyDeviceToHost, dev.stream));
+        CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+        for (int l = 0; l < lane_count; ++l) load[l] = std::max(reported[l], 1u);
+        s = e;
+        // Lanes of similar load gain nothing from re-division, and every chunk
+        // boundary makes each lane wait for the chunk's slowest: use chunks four
+        // times longer until some lane's load is three times the median.
+        std::vector<uint32_t> live;
+        for (int l = 0; l < lane_count; ++l)
+            if (dev.lane_steps[l] > s) live.push_back(load[l]);
+        if (!live.empty()) {
+            std::sort(live.begin(), live.end());
+            const bool skewed = (double)live.back() > 3.0 * (double)live[live.size() / 2];
+            chunk = std::max(dev.story_chunk, 1u) * (skewed ? 1u : 4u);
+        }
+    }
+    CUDA_CHECK(cudaEventRecord(dev.wave_stop, dev.stream));
+    CUDA_CHECK(cudaEventSynchronize(dev.wave_stop));
+    float ms = 0.0f;
+    CUDA_CHECK(cudaEventElapsedTime(&ms, dev.wave_start, dev.wave_stop));
+    dev.perf.wavefront_ms += ms;
+    dev.perf.story_wavefront_ms += ms;
+    dev.perf.story_cluster = largest;
 }
 
 void add_work(LeoB200Device& dev, const LaneScalars& sc, bool story) {
@@ -909,6 +1045,7 @@ void batch_begin(LeoB200Device& dev, const uint8_t* bytes, const uint64_t* offse
         dev.batch_steps = dev.batch_stories[0].empty() ? 0 : (uint32_t)sched.size();
     } else {
         ensure_lanes(dev, stories);
+        dev.lane_steps.assign(stories, 0u);
         for (uint32_t i = 0; i < stories; ++i) {
             Lane& lane = *dev.lanes[i];
             const auto& story = dev.batch_stories[i];
@@ -919,6 +1056,7 @@ void batch_begin(LeoB200Device& dev, const uint8_t* bytes, const uint64_t* offse
             // Forked workers start a fresh runtime at tick 0 (backend.rs:486-488).
             reset_lane(dev, lane, 0ull, steps);
             dev.batch_steps = std::max(dev.batch_steps, steps);
+            dev.lane_steps[i] = steps;
         }
         dev.batch_lanes = stories;
         upload_lane_table(dev);
@@ -932,8 +1070,10 @@ void batch_steps(LeoB200Device& dev, uint32_t count) {
     uint32_t end = std::min(dev.batch_steps, dev.steps_done + count);
     if (dev.single_story)
         run_steps(dev, dev.d_replay, 1, dev.steps_done, end, false);
-    else
+    else if (dev.story_cluster_request)
         run_steps(dev, dev.d_lanes, (int)dev.batch_lanes, dev.steps_done, end, true);
+    else
+        run_story_adaptive(dev, (int)dev.batch_lanes, dev.steps_done, end);
     dev.steps_done = end;
 }
 
@@ -1196,6 +1336,12 @@ int leo_b200_open(int device, const LeoB200HostModel* canonical, uint32_t max_la
         dev->ctx_stage_emb = dev->mem.alloc<float>(z.ctx_emb);
         dev->ctx_sync_slots = dev->mem.alloc<uint32_t>(z.ctx);
         dev->d_replay = dev->mem.alloc<LaneState>(1);
+        dev->d_lane_load = dev->mem.alloc<uint32_t>(max_lanes + 1);
+        dev->d_group_table = dev->mem.alloc<LaneState>(max_lanes);
+        for (cudaStream_t& st : dev->aux) CUDA_CHECK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+        CUDA_CHECK(cudaEventCreateWithFlags(&dev->fork, cudaEventDisableTiming));
+        for (cudaEvent_t& ev : dev->join) CUDA_CHECK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+        dev->sm_count = prop.multiProcessorCount;
         // replay lane: canonical parameters, private transient state
         dev->replay = std::make_unique<Lane>();
         dev->replay->st.p = dev->canon;
@@ -1203,6 +1349,19 @@ int leo_b200_open(int device, const LeoB200HostModel* canonical, uint32_t max_la
         dev->grid = prop.multiProcessorCount * 4;
         if (leo_wavefront_smem_bytes(dev->kc) > 96 * 1024) throw LeoFailure("block winners exceed shared memory");
         CUDA_CHECK(leo_wavefront_configure());
+        if (leo_wavefront_max_clusters(16, dev->kc, &dev->fit16) != cudaSuccess) {
+            cudaGetLastError();
+            dev->fit16 = 0;
+        }
+        if (leo_wavefront_max_clusters(8, dev->kc, &dev->fit8) != cudaSuccess) {
+            cudaGetLastError();
+            dev->fit8 = 0;
+        }
+        if (leo_wavefront_max_clusters(4, dev->kc, &dev->fit4) != cudaSuccess) {
+            cudaGetLastError();
+            dev->fit4 = 0;
+        }
+        dev->replay->st.load_out = dev->d_lane_load + max_lanes;
         upload_model(*dev, *canonical);
         *out = dev.release();
         return 0;
@@ -1220,6 +1379,11 @@ void leo_b200_close(LeoB200Device* dev) {
     if (dev->wave_stop) cudaEventDestroy(dev->wave_stop);
     if (dev->batch_start) cudaEventDestroy(dev->batch_start);
     if (dev->batch_stop) cudaEventDestroy(dev->batch_stop);
+    if (dev->fork) cudaEventDestroy(dev->fork);
+    for (cudaEvent_t ev : dev->join)
+        if (ev) cudaEventDestroy(ev);
+    for (cudaStream_t st : dev->aux)
+        if (st) cudaStreamDestroy(st);
     delete dev;
     cudaStreamDestroy(s);
 }
@@ -1486,8 +1650,18 @@ int leo_b200_set_cluster_sizes(LeoB200Device* dev, uint32_t story_cluster, uint3
     return 0;
 }
 
+int leo_b200_set_story_chunk(LeoB200Device* dev, uint32_t steps) {
+    if (steps == 0) return fail(LeoFailure("story chunk must be at least one step"));
+    dev->story_chunk = steps;
+    return 0;
+}
+
 int leo_b200_perf_stats(LeoB200Device* dev, LeoB200PerfStats* out) {
     *out = dev->perf;
+    out->fit_clusters[0] = dev->fit4;
+    out->fit_clusters[1] = dev->fit8;
+    out->fit_clusters[2] = dev->fit16;
+    out->sm_count = dev->sm_count;
     return 0;
 }
 

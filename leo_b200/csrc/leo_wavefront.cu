@@ -1261,8 +1261,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             mark(9);
         }
     }
-    if (timer)
+    if (timer) {
         for (int p = 0; p < LEO_PHASES; ++p) sc->phase_cycles[p] += acc[p];
+        if (ln.load_out) {
+            const uint32_t cur = sc->elig_cur;
+            const unsigned long long load = (unsigned long long)sc->elig_count[cur] + sc->in_elig_count[cur] +
+                                            (unsigned long long)sc->last_active * kc.topo.s + sc->touched_count;
+            *ln.load_out = load > 0xffffffffull ? 0xffffffffu : (uint32_t)load;
+        }
+    }
 }
 
 // Dynamic shared memory: the assemble phase's sort buffer and the learn

@@ -157,4 +157,7 @@ class LeoB200PerfStats(C.Structure):
         ("batch_ms", C.c_double),
         ("story_cluster", C.c_uint32),
         ("replay_cluster", C.c_uint32),
+        ("story_lane_launches", C.c_uint64 * 5),
+        ("fit_clusters", C.c_int32 * 3),
+        ("sm_count", C.c_int32),
     ]

@@ -56,6 +56,7 @@ def lib() -> C.CDLL:
     L.leo_b200_canonical_tick.argtypes = [vp]
     L.leo_b200_canonical_tick.restype = u64
     L.leo_b200_set_canonical_tick.argtypes = [vp, u64]
+    L.leo_b200_set_story_chunk.argtypes = [vp, u32]
     L.leo_b200_sparse_mean_apply.argtypes = [C.c_int, vp, u32, vp, vp, vp, u32, C.c_float, C.c_float, vp, u32, vp,
                                              P(u32)]
     L.leo_b200_sparse_mean_apply_static.argtypes = L.leo_b200_sparse_mean_apply.argtypes

@@ -83,3 +83,25 @@ def test_gpu_story_batch_matches_golden(native_lib, name):
             for k, v in rec["statistics"].items():
                 got = getattr(m.statistics, k)
                 assert (got == v) if k != "training_loss_sum" else got == pytest.approx(v, rel=0, abs=0), (i, k)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("geometry", [(1, 1, 64), (4, 16, 64), (0, 2, 7), (0, 0, 1)],
+                         ids=["fixed1", "fixed4-replay16", "adaptive-chunk7", "adaptive-chunk1"])
+def test_gpu_result_does_not_depend_on_geometry(native_lib, geometry):
+    """Cluster sizes and the adaptive story-pass chunking change only how the
+    work is spread over SMs: the golden state hashes hold for every geometry."""
+    from leo_b200.backend import GpuBackend
+    from leo_b200.ctypes_types import TRAINING
+    from leo_b200.model import HostModel
+
+    story_c, replay_c, chunk = geometry
+    case = CASES["baseline1"]
+    w, batches = _stories(case)
+    model = HostModel.initialize(w.config, w.topology)
+    with GpuBackend(model, device=0, max_lanes=case["stories_per_batch"]) as backend:
+        backend.set_cluster_sizes(story_c, replay_c)
+        backend.set_story_chunk(chunk)
+        for i, (rec, batch) in enumerate(zip(case["batches"], batches)):
+            backend.training_story_batch(batch, TRAINING)
+            assert backend.state_digest().hex() == rec["state_hash"], f"batch {i}"
