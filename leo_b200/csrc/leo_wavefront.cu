@@ -167,8 +167,19 @@ __device__ __forceinline__ void mark_and_append(uint8_t* marks, uint32_t* list, 
     if ((old & bit) == 0u) list[atomicAdd(count, 1u)] = index;
 }
 
+// Appends `item` to a list whose length lives at *count, one atomic per group
+// of converged threads (the list order is free: every consumer treats these
+// lists as sets).
+__device__ __forceinline__ void append_coalesced(uint32_t* list, uint32_t* count, uint32_t item) {
+    cg::coalesced_group g = cg::coalesced_threads();
+    uint32_t base = 0;
+    if (g.thread_rank() == 0) base = atomicAdd(count, g.size());
+    base = g.shfl(base, 0);
+    list[base + g.thread_rank()] = item;
+}
+
 __device__ __forceinline__ void touch(const LaneState& ln, uint32_t n, uint32_t epoch) {
-    if (atomicExch(&ln.touch_epoch[n], epoch) != epoch) ln.touched[atomicAdd(&ln.sc->touched_count, 1u)] = n;
+    if (atomicExch(&ln.touch_epoch[n], epoch) != epoch) append_coalesced(ln.touched, &ln.sc->touched_count, n);
 }
 
 __device__ __forceinline__ void push_event(const LaneState& ln, uint32_t tb, uint32_t q, float value) {
@@ -178,7 +189,7 @@ __device__ __forceinline__ void push_event(const LaneState& ln, uint32_t tb, uin
 }
 
 __device__ __forceinline__ void add_destination(const LaneState& ln, uint32_t n, uint32_t epoch) {
-    if (atomicExch(&ln.dst_epoch[n], epoch) != epoch) ln.dst_list[atomicAdd(&ln.sc->dst_count, 1u)] = n;
+    if (atomicExch(&ln.dst_epoch[n], epoch) != epoch) append_coalesced(ln.dst_list, &ln.sc->dst_count, n);
 }
 
 // ---------------------------------------------------------------------------
@@ -367,7 +378,11 @@ __device__ void phase_deliver(const LaneState& ln, uint32_t s, const KernelConst
                 t.branch_sens = t.branch_sens + a;
                 if ((t.tick_mark & 1u) == 0u) {
                     t.tick_mark |= 1u;
-                    ln.elig[cur][atomicAdd(&sc->elig_count[cur], 1u)] = make_uint4(slot, word, 0u, 0u);
+                    cg::coalesced_group g = cg::coalesced_threads();
+                    uint32_t base = 0;
+                    if (g.thread_rank() == 0) base = atomicAdd(&sc->elig_count[cur], g.size());
+                    base = g.shfl(base, 0);
+                    ln.elig[cur][base + g.thread_rank()] = make_uint4(slot, word, 0u, 0u);
                 }
                 store_trace(&ln.traces[slot], t);
             }
@@ -384,7 +399,11 @@ __device__ void phase_deliver(const LaneState& ln, uint32_t s, const KernelConst
                 t.branch_sens = t.branch_sens + 1.0f;
                 if ((t.tick_mark & 1u) == 0u) {
                     t.tick_mark |= 1u;
-                    ln.in_elig[cur][atomicAdd(&sc->in_elig_count[cur], 1u)] = make_uint4(slot, word, 0u, 0u);
+                    cg::coalesced_group g = cg::coalesced_threads();
+                    uint32_t base = 0;
+                    if (g.thread_rank() == 0) base = atomicAdd(&sc->in_elig_count[cur], g.size());
+                    base = g.shfl(base, 0);
+                    ln.in_elig[cur][base + g.thread_rank()] = make_uint4(slot, word, 0u, 0u);
                 }
                 store_trace(&ln.in_traces[slot], t);
             }
@@ -425,37 +444,63 @@ __device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts
             cold.neuron_tick = s;
         }
         float acc[4] = {br.x, br.y, br.z, br.w};
-        for (int b = 0; b < 4; ++b) {
-            uint32_t head = ln.ev_head[n * 4 + b];
-            if (head == LEO_EMPTY) continue;
-            ln.ev_head[n * 4 + b] = LEO_EMPTY;
-            uint32_t qs[kCap];
-            float vs[kCap];
-            int k = 0;
-            uint32_t p = head;
-            while (p != LEO_EMPTY && k < kCap) {
-                qs[k] = p;
-                vs[k] = ln.ev_val[p];
-                p = ln.ev_next[p];
+        // The four (target, branch) event lists, walked in lockstep so their
+        // hops overlap; events are summed per branch in ascending event order.
+        const uint4 heads = *reinterpret_cast<const uint4*>(&ln.ev_head[n * 4]);
+        if ((heads.x & heads.y & heads.z & heads.w) != LEO_EMPTY)
+            *reinterpret_cast<uint4*>(&ln.ev_head[n * 4]) = make_uint4(LEO_EMPTY, LEO_EMPTY, LEO_EMPTY, LEO_EMPTY);
+        uint32_t p[4] = {heads.x, heads.y, heads.z, heads.w};
+        uint32_t keys[kCap];
+        float vals[kCap];
+        int k = 0;
+        bool overflow = false;
+        while ((p[0] & p[1] & p[2] & p[3]) != LEO_EMPTY) {
+            uint32_t nxt[4];
+            float v[4];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                nxt[b] = LEO_EMPTY;
+                if (p[b] != LEO_EMPTY) {
+                    nxt[b] = ln.ev_next[p[b]];
+                    v[b] = ln.ev_val[p[b]];
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                if (p[b] == LEO_EMPTY) continue;
+                if (k == kCap) {
+                    overflow = true;
+                    break;
+                }
+                keys[k] = ((uint32_t)b << 24) | p[b];
+                vals[k] = v[b];
                 ++k;
             }
-            float a = acc[b];
-            if (p == LEO_EMPTY) {
-                for (int x = 1; x < k; ++x) {  // insertion sort by event order
-                    uint32_t qk = qs[x];
-                    float vk = vs[x];
-                    int y = x - 1;
-                    while (y >= 0 && qs[y] > qk) {
-                        qs[y + 1] = qs[y];
-                        vs[y + 1] = vs[y];
-                        --y;
-                    }
-                    qs[y + 1] = qk;
-                    vs[y + 1] = vk;
+            if (overflow) break;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) p[b] = nxt[b];
+        }
+        if (!overflow) {
+            for (int x = 1; x < k; ++x) {  // insertion sort by (branch, event order)
+                uint32_t kk = keys[x];
+                float vk = vals[x];
+                int y = x - 1;
+                while (y >= 0 && keys[y] > kk) {
+                    keys[y + 1] = keys[y];
+                    vals[y + 1] = vals[y];
+                    --y;
                 }
-                for (int x = 0; x < k; ++x) a = a + vs[x];
-            } else {
-                // A long list (hot target): add in ascending event order by repeated scans.
+                keys[y + 1] = kk;
+                vals[y + 1] = vk;
+            }
+            for (int x = 0; x < k; ++x) acc[keys[x] >> 24] = acc[keys[x] >> 24] + vals[x];
+        } else {
+            // A long list (hot target): per branch, add in ascending event
+            // order by repeated scans of the list.
+            const uint32_t head4[4] = {heads.x, heads.y, heads.z, heads.w};
+            for (int b = 0; b < 4; ++b) {
+                const uint32_t head = head4[b];
+                float a = acc[b];
                 uint32_t last = 0u;
                 bool first = true;
                 for (;;) {
@@ -472,8 +517,8 @@ __device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts
                     last = best;
                     first = false;
                 }
+                acc[b] = a;
             }
-            acc[b] = a;
         }
         br = make_float4(acc[0], acc[1], acc[2], acc[3]);
         NeuronHot& hot = ln.hot[n];
