@@ -83,6 +83,42 @@ int leo_b200_batch_steps(LeoB200Device* device, uint32_t count, uint32_t* steps_
 int leo_b200_batch_finish(LeoB200Device* device, LeoB200BatchReport* report, LeoB200StorySummary* summaries,
                           float* losses);
 
+/* One logical batch sharded over several devices (exact data parallelism,
+   MultiGpuBatchTrainer::train_story_batch, crates/leo-cli/src/training.rs:
+   1212-1420, with its default serial canonical replay).  Every rank passes the
+   whole batch and runs stories [first, first + count) on its lanes; the caller
+   exchanges the merge between the rank-local steps (leo_b200/parallel.py does
+   it over torch.distributed / NCCL):
+     shard_begin, shard_local (this rank's story reports, losses and keyed
+     context deltas), then for each fixed tensor t < LEO_B200_FIXED_TENSORS:
+       shard_marks     element marks of this rank's lanes (device buffer of
+                       shard_tensor_elements bytes), MAX-all-reduced by the caller
+       shard_plan      sorted merge list from the reduced marks -> count
+       shard_accumulate  partial[count] (FP64, device): rank 0 starts from 0.0,
+                       rank r > 0 adds to the sums received from rank r - 1
+       shard_finalize  last rank: merged values (f32, device) from the sums
+       shard_commit    every rank: the broadcast values into the canonical
+                       tensor and every resident lane
+     shard_finish with every story's report, losses and context deltas in
+     story order: keyed context merge, statistics, revision, the serial replay
+     of every story (identical on every rank) and the report.
+   One GPU running the whole batch and N ranks running its shards end with the
+   same training_state_hash.  A batch of one story is not sharded (use
+   leo_b200_train_story_batch on every rank). */
+int leo_b200_shard_begin(LeoB200Device* device, const uint8_t* bytes, const uint64_t* offsets, uint32_t stories,
+                         uint32_t first, uint32_t count, int permission);
+int leo_b200_shard_local(LeoB200Device* device, LeoB200ShardStory* stories, float* losses, size_t* context_bytes);
+int leo_b200_shard_context(LeoB200Device* device, uint8_t* out, size_t capacity);
+int leo_b200_shard_tensor_elements(LeoB200Device* device, uint32_t tensor, size_t* elements);
+int leo_b200_shard_marks(LeoB200Device* device, uint32_t tensor, uint8_t* marks);
+int leo_b200_shard_plan(LeoB200Device* device, uint32_t tensor, const uint8_t* marks, uint32_t* count);
+int leo_b200_shard_accumulate(LeoB200Device* device, uint32_t tensor, double* partial, int first);
+int leo_b200_shard_finalize(LeoB200Device* device, uint32_t tensor, const double* partial, float* values);
+int leo_b200_shard_commit(LeoB200Device* device, uint32_t tensor, const float* values);
+int leo_b200_shard_finish(LeoB200Device* device, const LeoB200ShardStory* stories, const float* losses,
+                          const uint8_t* context, const uint64_t* context_offsets, uint64_t fixed_updates,
+                          LeoB200BatchReport* report, LeoB200StorySummary* summaries, float* losses_out);
+
 /* training_state_hash of the canonical device model. */
 int leo_b200_state_digest(LeoB200Device* device, uint8_t out[32]);
 

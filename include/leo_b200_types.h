@@ -166,6 +166,27 @@ typedef struct LeoB200BatchReport {
     uint64_t replay_prefix_steps;
 } LeoB200BatchReport;
 
+/* One story of a sharded logical batch, as the rank that ran it reports it for
+   the batch-end merge on every rank: the story's statistics delta
+   (parallel.rs:1115-1137; `loss_sum` is the lane's running
+   training_loss_sum, which started at the canonical value) and its length. */
+typedef struct LeoB200ShardStory {
+    double loss_sum;
+    uint64_t processed_bytes;
+    uint64_t targets;
+    uint64_t active_sum;
+    uint64_t active_peak;
+    uint64_t synaptic_events;
+    uint64_t numerical_rejections;
+    uint64_t persistent_ticks;
+    uint64_t revision_increment;
+    uint64_t context_applied_steps;
+    uint64_t story_bytes;
+} LeoB200ShardStory;
+
+/* Fixed tensors merged at the batch end, in merge order. */
+#define LEO_B200_FIXED_TENSORS 6
+
 /* Phases of one step of the persistent wavefront, in execution order. */
 #define LEO_B200_PHASES 11
 enum LeoB200Phase {

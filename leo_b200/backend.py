@@ -47,6 +47,7 @@ class GpuBackend:
 
     def __init__(self, model: HostModel, device: int = 0, max_lanes: int = 64):
         self.config: Config = model.config
+        self.device = device
         self.model = model.copy()
         handle = C.c_void_p()
         hm = self.model.view()

@@ -56,5 +56,21 @@ void leo_launch_merge_tensor(const MergeTensor& t, const MergeScratch& m, int la
 void leo_launch_scatter_rows(float** lane_values, int lanes, const float* base, const uint32_t* list, uint32_t count,
                              uint32_t row, uint32_t row_len, int grid, cudaStream_t stream);
 
+// Rank-local steps of the sharded (multi-GPU) merge; see leo_shard_kernels.cu.
+void leo_launch_shard_marks(const MergeTensor& t, int lanes, uint8_t* marks, int grid, cudaStream_t stream);
+size_t leo_compact_scratch_blocks(size_t length);
+void leo_launch_compact(const uint8_t* marks, size_t length, uint32_t* list, uint32_t* total, uint32_t* block_scratch,
+                        cudaStream_t stream);
+void leo_launch_shard_accumulate(float** lane_values, int lanes, const float* base, const uint32_t* list,
+                                 uint32_t count, double* partial, int first, uint32_t* error_flag, int grid,
+                                 cudaStream_t stream);
+void leo_launch_shard_finalize(const float* base, const uint32_t* list, uint32_t count, const double* partial,
+                               float* values, double divisor, uint32_t kind, float wmin, float wmax,
+                               const uint8_t* neuron_type, uint32_t synapses_per_neuron, uint32_t* error_flag,
+                               int grid, cudaStream_t stream);
+void leo_launch_shard_commit(float* base, const uint32_t* list, uint32_t count, const float* values,
+                             float** lane_values, int lanes, int grid, cudaStream_t stream);
+void leo_launch_shard_sync_own(const MergeTensor& t, int lanes, int grid, cudaStream_t stream);
+
 // Sets the text leo_b200_last_error() returns on this thread.
 void leo_set_last_error(const char* what);

@@ -23,24 +23,9 @@
 
 #include "leo_device.cuh"
 #include "leo_kernels.h"
+#include "leo_projection.cuh"
 
 namespace {
-
-__device__ __forceinline__ float clampf(float v, float lo, float hi) {
-    if (v < lo) v = lo;
-    if (v > hi) v = hi;
-    return v;
-}
-__device__ __forceinline__ float rmax(float a, float b) {
-    if (isnan(a)) return b;
-    if (isnan(b)) return a;
-    return a > b ? a : (b > a ? b : a);
-}
-__device__ __forceinline__ float rmin(float a, float b) {
-    if (isnan(a)) return b;
-    if (isnan(b)) return a;
-    return a < b ? a : (b < a ? b : a);
-}
 
 __device__ __forceinline__ bool set_byte_mark(uint8_t* marks, uint32_t index) {
     unsigned int* word = reinterpret_cast<unsigned int*>(reinterpret_cast<uintptr_t>(marks + index) & ~(uintptr_t)3);
@@ -97,16 +82,7 @@ __global__ void __launch_bounds__(256) merge_apply_kernel(MergeTensor t, MergeSc
         }
         if (!any) continue;
         float v = before + __double2float_rn(sum / (double)lanes);
-        switch (t.kind) {
-            case LEO_PROJECT_THRESHOLD: v = clampf(v, 0.05f, 2.0f); break;
-            case LEO_PROJECT_RECURRENT:
-                v = clampf(v, wmin, wmax);
-                v = neuron_type[u / synapses_per_neuron] == 0 ? rmax(v, 0.0f) : rmin(v, 0.0f);
-                break;
-            case LEO_PROJECT_INPUT: v = clampf(v, 0.0f, wmax); break;
-            case LEO_PROJECT_WEIGHT: v = clampf(v, wmin, wmax); break;
-            default: break;
-        }
+        v = leo_project(v, t.kind, (size_t)u, wmin, wmax, neuron_type, synapses_per_neuron);
         if (!isfinite(v)) atomicOr(m.error_flag, 1u);
         t.base[idx] = v;
         ++applied;

@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <array>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -122,6 +123,19 @@ struct LeoB200Device {
     int batch_permission = LEO_B200_TRAINING;
     bool single_story = false;
     std::vector<std::vector<uint8_t>> batch_stories;
+    // sharded batch (multi-GPU data parallelism): this rank's lanes run
+    // stories [shard_first, shard_first + batch_lanes) of batch_stories
+    bool shard_mode = false;
+    uint32_t shard_first = 0;
+    bool shard_local_done = false;
+    std::vector<LaneScalars> shard_scal;
+    std::vector<uint8_t> shard_ctx_blob;       // local stories' keyed context deltas, serialised
+    std::vector<uint32_t> shard_ctx_slots;     // local lanes' changed context slots
+    uint32_t* shard_list[LEO_B200_FIXED_TENSORS] = {};
+    uint32_t shard_count[LEO_B200_FIXED_TENSORS] = {};
+    uint32_t* compact_blocks = nullptr;
+    uint32_t* compact_total = nullptr;
+    uint32_t* shard_error = nullptr;
     std::vector<LaneScalars> host_scalars;
     // performance counters and execution geometry
     LeoB200PerfStats perf{};
@@ -637,57 +651,66 @@ uint32_t resolve_allocate(LeoB200Device& dev, uint32_t order, unsigned long long
     return slot;
 }
 
-// Reads each lane's changed context rows, merges them by (order, key) into the
-// host mirror exactly as apply_context_deltas does, uploads the changed
-// canonical rows and syncs every lane.  Returns the number of merged keys.
-size_t merge_context(LeoB200Device& dev, uint32_t lane_count, const std::vector<LaneScalars>& scal) {
+// context_deltas_for_slots (parallel.rs:929-973) of one lane: reads the
+// lane's changed context rows, forms (order, key) deltas against the host
+// mirror of the canonical context, clears the lane's context marks.  Returns
+// the deltas sorted by (order, key) and appends the lane's changed slots.
+std::vector<CtxDelta> collect_lane_context(LeoB200Device& dev, Lane& lane, uint32_t count,
+                                           std::vector<uint32_t>& changed_slots) {
+    std::vector<CtxDelta> out;
+    if (count == 0) return out;
     const ModelSizes& z = dev.z;
     uint32_t d = (uint32_t)z.d, spo = dev.cfg.abi.context_slots_per_order;
-    std::vector<std::vector<CtxDelta>> per_lane(lane_count);
-    std::vector<uint32_t> lane_slots_union;
-    for (uint32_t l = 0; l < lane_count; ++l) {
-        uint32_t count = scal[l].ctx_changed;
-        if (count == 0) continue;
-        Lane& lane = *dev.lanes[l];
-        std::vector<uint32_t> slots(count);
-        std::vector<ContextRow> rows(count);
-        std::vector<float> emb((size_t)count * d);
-        ContextRow* d_rows = dev.ctx_stage_rows;
-        float* d_emb = dev.ctx_stage_emb;
-        gather_context_rows_kernel<<<std::max(1u, std::min(count / 128 + 1, 1024u)), 128, 0, dev.stream>>>(
-            lane.st.ctx_list, count, lane.st.p.ctx_keys, lane.st.p.ctx_obs, lane.st.p.ctx_emb, d, d_rows, d_emb);
-        CUDA_CHECK(cudaGetLastError());
-        CUDA_CHECK(cudaMemcpyAsync(slots.data(), lane.st.ctx_list, count * 4, cudaMemcpyDeviceToHost, dev.stream));
-        CUDA_CHECK(cudaMemcpyAsync(rows.data(), d_rows, count * sizeof(ContextRow), cudaMemcpyDeviceToHost, dev.stream));
-        CUDA_CHECK(cudaMemcpyAsync(emb.data(), d_emb, emb.size() * 4, cudaMemcpyDeviceToHost, dev.stream));
-        clear_marks_kernel<<<std::max(1u, std::min(count / 128 + 1, 1024u)), 128, 0, dev.stream>>>(lane.st.ctx_list, count,
-                                                                                                   lane.st.ctx_mark);
-        CUDA_CHECK(cudaGetLastError());
-        CUDA_CHECK(cudaStreamSynchronize(dev.stream));
-        // context_deltas_for_slots (parallel.rs:929-973)
-        for (uint32_t i = 0; i < count; ++i) {
-            lane_slots_union.push_back(slots[i]);
-            unsigned long long key = rows[i].key;
-            if (key == 0) continue;
-            uint32_t order = slots[i] / spo + 1;
-            long bs = find_slot(dev, order, key);
-            uint32_t bobs = bs >= 0 ? dev.ctx_obs[bs] : 0;
-            CtxDelta cd{order, key, std::vector<float>(d), 0};
-            bool changed = false;
-            for (uint32_t k = 0; k < d; ++k) {
-                float before = bs >= 0 ? dev.ctx_emb[(size_t)bs * d + k] : 0.0f;
-                float delta = emb[(size_t)i * d + k] - before;
-                changed |= delta != 0.0f;
-                cd.emb_delta[k] = delta;
-            }
-            cd.obs_inc = rows[i].obs > bobs ? rows[i].obs - bobs : 0;
-            if (changed || cd.obs_inc > 0) per_lane[l].push_back(std::move(cd));
+    std::vector<uint32_t> slots(count);
+    std::vector<ContextRow> rows(count);
+    std::vector<float> emb((size_t)count * d);
+    ContextRow* d_rows = dev.ctx_stage_rows;
+    float* d_emb = dev.ctx_stage_emb;
+    gather_context_rows_kernel<<<std::max(1u, std::min(count / 128 + 1, 1024u)), 128, 0, dev.stream>>>(
+        lane.st.ctx_list, count, lane.st.p.ctx_keys, lane.st.p.ctx_obs, lane.st.p.ctx_emb, d, d_rows, d_emb);
+    CUDA_CHECK(cudaGetLastError());
+    CUDA_CHECK(cudaMemcpyAsync(slots.data(), lane.st.ctx_list, count * 4, cudaMemcpyDeviceToHost, dev.stream));
+    CUDA_CHECK(cudaMemcpyAsync(rows.data(), d_rows, count * sizeof(ContextRow), cudaMemcpyDeviceToHost, dev.stream));
+    CUDA_CHECK(cudaMemcpyAsync(emb.data(), d_emb, emb.size() * 4, cudaMemcpyDeviceToHost, dev.stream));
+    clear_marks_kernel<<<std::max(1u, std::min(count / 128 + 1, 1024u)), 128, 0, dev.stream>>>(lane.st.ctx_list, count,
+                                                                                               lane.st.ctx_mark);
+    CUDA_CHECK(cudaGetLastError());
+    CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+    for (uint32_t i = 0; i < count; ++i) {
+        changed_slots.push_back(slots[i]);
+        unsigned long long key = rows[i].key;
+        if (key == 0) continue;
+        uint32_t order = slots[i] / spo + 1;
+        long bs = find_slot(dev, order, key);
+        uint32_t bobs = bs >= 0 ? dev.ctx_obs[bs] : 0;
+        CtxDelta cd{order, key, std::vector<float>(d), 0};
+        bool changed = false;
+        for (uint32_t k = 0; k < d; ++k) {
+            float before = bs >= 0 ? dev.ctx_emb[(size_t)bs * d + k] : 0.0f;
+            float delta = emb[(size_t)i * d + k] - before;
+            changed |= delta != 0.0f;
+            cd.emb_delta[k] = delta;
         }
-        std::sort(per_lane[l].begin(), per_lane[l].end(), [](const CtxDelta& a, const CtxDelta& b) {
-            return a.order != b.order ? a.order < b.order : a.key < b.key;
-        });
+        cd.obs_inc = rows[i].obs > bobs ? rows[i].obs - bobs : 0;
+        if (changed || cd.obs_inc > 0) out.push_back(std::move(cd));
     }
-    // k-way merge by (order, key) in lane order (parallel.rs:1045-1089)
+    std::sort(out.begin(), out.end(), [](const CtxDelta& a, const CtxDelta& b) {
+        return a.order != b.order ? a.order < b.order : a.key < b.key;
+    });
+    return out;
+}
+
+// apply_context_deltas (parallel.rs:1024-1113) of every story's deltas, in
+// story order, into the host mirror; projection (parallel.rs:1226-1233) and
+// validation (parallel.rs:1317-1334); uploads the changed canonical rows and
+// syncs every resident lane at them and at `lane_slots` (the resident lanes'
+// own changed slots).  Returns the number of merged keys.
+size_t merge_context_deltas(LeoB200Device& dev, const std::vector<std::vector<CtxDelta>>& per_story, size_t divisor,
+                            const std::vector<uint32_t>& lane_slots) {
+    const ModelSizes& z = dev.z;
+    const uint32_t d = (uint32_t)z.d;
+    const size_t stories = per_story.size();
+    // k-way merge by (order, key) in story order (parallel.rs:1045-1089)
     struct Merged {
         uint32_t order;
         unsigned long long key;
@@ -695,22 +718,24 @@ size_t merge_context(LeoB200Device& dev, uint32_t lane_count, const std::vector<
         uint64_t obs;
     };
     std::vector<Merged> merged;
-    std::vector<size_t> pos(lane_count, 0);
+    std::vector<size_t> pos(stories, 0);
     for (;;) {
         bool any = false;
         std::pair<uint32_t, unsigned long long> next{0, 0};
-        for (uint32_t l = 0; l < lane_count; ++l) {
-            if (pos[l] < per_lane[l].size()) {
-                auto k = std::make_pair(per_lane[l][pos[l]].order, per_lane[l][pos[l]].key);
+        for (size_t l = 0; l < stories; ++l) {
+            if (pos[l] < per_story[l].size()) {
+                auto k = std::make_pair(per_story[l][pos[l]].order, per_story[l][pos[l]].key);
                 if (!any || k < next) next = k;
                 any = true;
             }
         }
         if (!any) break;
         Merged m{next.first, next.second, std::vector<double>(d, 0.0), 0};
-        for (uint32_t l = 0; l < lane_count; ++l) {
-            if (pos[l] < per_lane[l].size() && per_lane[l][pos[l]].order == next.first && per_lane[l][pos[l]].key == next.second) {
-                const CtxDelta& u = per_lane[l][pos[l]];
+        for (size_t l = 0; l < stories; ++l) {
+            if (pos[l] < per_story[l].size() && per_story[l][pos[l]].order == next.first &&
+                per_story[l][pos[l]].key == next.second) {
+                const CtxDelta& u = per_story[l][pos[l]];
+                if (u.emb_delta.size() != d) throw LeoFailure("invalid keyed context worker delta");
                 for (uint32_t k = 0; k < d; ++k) {
                     if (!std::isfinite(u.emb_delta[k])) throw LeoFailure("invalid keyed context worker delta");
                     m.sum[k] += (double)u.emb_delta[k];
@@ -729,15 +754,14 @@ size_t merge_context(LeoB200Device& dev, uint32_t lane_count, const std::vector<
     std::vector<uint32_t> canon_slots;
     for (auto& u : merged) {
         uint32_t slot = resolve_allocate(dev, u.order, u.key, canon_slots);
-        for (uint32_t k = 0; k < d; ++k) dev.ctx_emb[(size_t)slot * d + k] += (float)(u.sum[k] / (double)lane_count);
+        for (uint32_t k = 0; k < d; ++k) dev.ctx_emb[(size_t)slot * d + k] += (float)(u.sum[k] / (double)divisor);
         uint64_t add = std::min<uint64_t>(u.obs, 0xffffffffull);
         dev.ctx_obs[slot] = (uint32_t)std::min<uint64_t>((uint64_t)dev.ctx_obs[slot] + add, 0xffffffffull);
         canon_slots.push_back(slot);
     }
-    // projection (parallel.rs:1226-1233) and validation (parallel.rs:1317-1334)
     float lo = dev.cfg.abi.weight_min, hi = dev.cfg.abi.weight_max;
-    for (uint32_t l = 0; l < lane_count; ++l) {
-        for (auto& u : per_lane[l]) {
+    for (size_t l = 0; l < stories; ++l) {
+        for (auto& u : per_story[l]) {
             long slot = find_slot(dev, u.order, u.key);
             if (slot < 0) continue;
             for (uint32_t k = 0; k < d; ++k) {
@@ -747,9 +771,8 @@ size_t merge_context(LeoB200Device& dev, uint32_t lane_count, const std::vector<
             }
         }
     }
-    // upload changed canonical rows, then sync every lane's changed and canonical-changed slots
     std::vector<uint32_t> sync = canon_slots;
-    sync.insert(sync.end(), lane_slots_union.begin(), lane_slots_union.end());
+    sync.insert(sync.end(), lane_slots.begin(), lane_slots.end());
     std::sort(sync.begin(), sync.end());
     sync.erase(std::unique(sync.begin(), sync.end()), sync.end());
     if (!sync.empty()) {
@@ -771,6 +794,15 @@ size_t merge_context(LeoB200Device& dev, uint32_t lane_count, const std::vector<
     return merged.size();
 }
 
+// The single-GPU batch: every story is a resident lane.
+size_t merge_context(LeoB200Device& dev, uint32_t lane_count, const std::vector<LaneScalars>& scal) {
+    std::vector<std::vector<CtxDelta>> per_lane(lane_count);
+    std::vector<uint32_t> lane_slots;
+    for (uint32_t l = 0; l < lane_count; ++l)
+        per_lane[l] = collect_lane_context(dev, *dev.lanes[l], scal[l].ctx_changed, lane_slots);
+    return merge_context_deltas(dev, per_lane, lane_count, lane_slots);
+}
+
 // ---------------------------------------------------------------- fixed tensor merge
 struct TensorSpec {
     float* LaneParams::*member;
@@ -780,9 +812,9 @@ struct TensorSpec {
     uint32_t row, row_len, length, kind;
 };
 
-size_t merge_fixed(LeoB200Device& dev, uint32_t lane_count, const std::vector<LaneScalars>& scal) {
-    const ModelSizes& z = dev.z;
-    const TensorSpec specs[] = {
+// The six fixed tensors in merge order (parallel.rs:715-798).
+std::array<TensorSpec, LEO_B200_FIXED_TENSORS> fixed_specs(const ModelSizes& z) {
+    return {{
         {&LaneParams::threshold, &LaneState::thr_list, &LaneState::thr_mark, &LaneScalars::thr_changed, 1, 1,
          (uint32_t)z.n, LEO_PROJECT_THRESHOLD},
         {&LaneParams::rec_weight, &LaneState::rec_list, &LaneState::rec_mark, &LaneScalars::rec_changed, 1, 1,
@@ -793,7 +825,12 @@ size_t merge_fixed(LeoB200Device& dev, uint32_t lane_count, const std::vector<La
          LEO_OUTPUT_STRIDE, LEO_OUTPUT_CLASSES, (uint32_t)z.n, LEO_PROJECT_WEIGHT},
         {&LaneParams::out_bias, nullptr, nullptr, nullptr, 1, 1, LEO_OUTPUT_CLASSES, LEO_PROJECT_NONE},
         {&LaneParams::ctx_out, nullptr, nullptr, nullptr, 1, 1, (uint32_t)z.ctx_out, LEO_PROJECT_WEIGHT},
-    };
+    }};
+}
+
+size_t merge_fixed(LeoB200Device& dev, uint32_t lane_count, const std::vector<LaneScalars>& scal) {
+    const ModelSizes& z = dev.z;
+    const auto specs = fixed_specs(z);
     uint32_t zero = 0;
     CUDA_CHECK(cudaMemcpyAsync(dev.scratch.updates, &zero, 4, cudaMemcpyHostToDevice, dev.stream));
     const uint32_t resident = (uint32_t)dev.lanes.size();
@@ -1200,6 +1237,267 @@ void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySu
     if (report) *report = rep;
 }
 
+
+// ---------------------------------------------------------------- sharded batch (multi-GPU)
+// The logical batch's stories are split into contiguous ranges, one per rank
+// (work_balanced_story_ranges, training.rs:926-964); every rank holds every
+// story (for the serial replay) and runs its range on its lanes.  The merge
+// is exchanged by the caller between the rank-local steps below, so that
+// every rank ends with the same canonical model as one GPU running the whole
+// batch (MultiGpuBatchTrainer::train_story_batch, training.rs:1212-1420, with
+// the default serial canonical replay).
+
+size_t tensor_elements(const TensorSpec& t) { return (size_t)t.length * t.row; }
+
+void shard_begin(LeoB200Device& dev, const uint8_t* bytes, const uint64_t* offsets, uint32_t stories, uint32_t first,
+                 uint32_t count, int permission) {
+    if (dev.batch_open) throw LeoFailure("a story batch is already in progress");
+    if (stories < 2) throw LeoFailure("a sharded batch needs at least two stories (one story trains the canonical model)");
+    if (first > stories || count > stories - first) throw LeoFailure("shard range exceeds the batch");
+    if (permission < 0 || permission > 3) throw LeoFailure("invalid permission");
+    dev.batch_stories.assign(stories, {});
+    for (uint32_t i = 0; i < stories; ++i) dev.batch_stories[i].assign(bytes + offsets[i], bytes + offsets[i + 1]);
+    dev.batch_permission = permission;
+    dev.single_story = false;
+    dev.shard_mode = true;
+    dev.shard_first = first;
+    dev.shard_local_done = false;
+    dev.steps_done = 0;
+    dev.batch_steps = 0;
+    ensure_lanes(dev, count);
+    dev.lane_steps.assign(count, 0u);
+    std::vector<uint32_t> sched;
+    for (uint32_t i = 0; i < count; ++i) {
+        Lane& lane = *dev.lanes[i];
+        const auto& story = dev.batch_stories[first + i];
+        story_schedule(story, permission, sched);
+        uint32_t steps = story.empty() ? 0 : (uint32_t)sched.size();
+        ensure_schedule(lane, sched.size());
+        CUDA_CHECK(cudaMemcpyAsync(lane.schedule, sched.data(), sched.size() * 4, cudaMemcpyHostToDevice, dev.stream));
+        reset_lane(dev, lane, 0ull, steps);
+        dev.batch_steps = std::max(dev.batch_steps, steps);
+        dev.lane_steps[i] = steps;
+    }
+    dev.batch_lanes = count;
+    upload_lane_table(dev);
+    if (!dev.compact_total) {
+        const auto specs = fixed_specs(dev.z);
+        size_t blocks = 1;
+        for (int t = 0; t < LEO_B200_FIXED_TENSORS; ++t) {
+            dev.shard_list[t] = dev.mem.alloc<uint32_t>(std::max<size_t>(tensor_elements(specs[t]), 1));
+            blocks = std::max(blocks, leo_compact_scratch_blocks(tensor_elements(specs[t])));
+        }
+        dev.compact_blocks = dev.mem.alloc<uint32_t>(blocks);
+        dev.compact_total = dev.mem.alloc<uint32_t>(1);
+        dev.shard_error = dev.mem.alloc<uint32_t>(1);
+    }
+    CUDA_CHECK(cudaEventRecord(dev.batch_start, dev.stream));
+    dev.batch_open = true;
+}
+
+void require_shard(const LeoB200Device& dev) {
+    if (!dev.batch_open || !dev.shard_mode) throw LeoFailure("no sharded story batch in progress");
+}
+
+// Finishes this rank's story pass and reports its stories.
+void shard_local(LeoB200Device& dev, LeoB200ShardStory* out, float* losses_out) {
+    require_shard(dev);
+    if (dev.shard_local_done) throw LeoFailure("the shard's stories were already reported");
+    batch_steps(dev, dev.batch_steps);
+    CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+    const uint32_t L = dev.batch_lanes;
+    dev.shard_scal.assign(L, LaneScalars{});
+    size_t k = 0;
+    dev.shard_ctx_blob.clear();
+    dev.shard_ctx_slots.clear();
+    const uint32_t d = (uint32_t)dev.z.d;
+    for (uint32_t l = 0; l < L; ++l) {
+        LaneScalars& sc = dev.shard_scal[l];
+        read_scalars(dev, *dev.lanes[l], sc);
+        check_error_flag(sc);
+        add_work(dev, sc, true);
+        const auto& story = dev.batch_stories[dev.shard_first + l];
+        LeoB200ShardStory r{};
+        r.loss_sum = sc.loss_sum;
+        r.processed_bytes = sc.processed_bytes;
+        r.targets = sc.targets;
+        r.active_sum = sc.active_sum;
+        r.active_peak = sc.active_peak;
+        r.synaptic_events = sc.synaptic_events;
+        r.numerical_rejections = sc.numerical_rejections;
+        r.persistent_ticks = sc.persistent_ticks;
+        r.revision_increment = sc.revision_increment;
+        r.context_applied_steps = sc.context_applied_steps;
+        r.story_bytes = story.size();
+        if (out) out[l] = r;
+        if (!story.empty()) {
+            if (losses_out)
+                CUDA_CHECK(cudaMemcpy(losses_out + k, dev.lanes[l]->step_loss, (story.size() + 1) * 4,
+                                      cudaMemcpyDeviceToHost));
+            k += story.size() + 1;
+        }
+        // keyed context deltas: u32 count, then per entry u32 order, u32
+        // observation increment, u64 key, f32 delta[embedding_dim]
+        auto deltas = collect_lane_context(dev, *dev.lanes[l], sc.ctx_changed, dev.shard_ctx_slots);
+        auto put = [&](const void* p, size_t n) {
+            const uint8_t* b = static_cast<const uint8_t*>(p);
+            dev.shard_ctx_blob.insert(dev.shard_ctx_blob.end(), b, b + n);
+        };
+        uint32_t n = (uint32_t)deltas.size();
+        put(&n, 4);
+        for (const CtxDelta& u : deltas) {
+            put(&u.order, 4);
+            put(&u.obs_inc, 4);
+            put(&u.key, 8);
+            put(u.emb_delta.data(), (size_t)d * 4);
+        }
+    }
+    dev.shard_local_done = true;
+}
+
+MergeTensor shard_tensor(LeoB200Device& dev, int t) {
+    require_shard(dev);
+    if (t < 0 || t >= LEO_B200_FIXED_TENSORS) throw LeoFailure("fixed tensor index out of range");
+    if (!dev.shard_local_done) throw LeoFailure("report the shard's stories before merging");
+    const TensorSpec spec = fixed_specs(dev.z)[t];
+    const uint32_t resident = (uint32_t)dev.lanes.size(), L = dev.batch_lanes;
+    std::vector<float*> ptrs(std::max(resident, 1u));
+    std::vector<uint32_t*> lists(std::max(L, 1u));
+    std::vector<uint32_t> counts(std::max(L, 1u));
+    std::vector<uint8_t*> marks(std::max(L, 1u));
+    for (uint32_t l = 0; l < resident; ++l) ptrs[l] = dev.lanes[l]->st.p.*spec.member;
+    for (uint32_t l = 0; l < L; ++l) {
+        LaneState& st = dev.lanes[l]->st;
+        lists[l] = spec.list ? st.*spec.list : nullptr;
+        counts[l] = spec.count ? dev.shard_scal[l].*spec.count : spec.length;
+        marks[l] = spec.marks ? st.*spec.marks : nullptr;
+    }
+    if (resident)
+        CUDA_CHECK(cudaMemcpyAsync(dev.d_lane_ptrs, ptrs.data(), resident * sizeof(float*), cudaMemcpyHostToDevice,
+                                   dev.stream));
+    if (L) {
+        CUDA_CHECK(cudaMemcpyAsync(dev.d_lane_lists, lists.data(), L * sizeof(uint32_t*), cudaMemcpyHostToDevice, dev.stream));
+        CUDA_CHECK(cudaMemcpyAsync(dev.d_lane_counts, counts.data(), L * 4, cudaMemcpyHostToDevice, dev.stream));
+        CUDA_CHECK(cudaMemcpyAsync(dev.d_lane_marks, marks.data(), L * sizeof(uint8_t*), cudaMemcpyHostToDevice, dev.stream));
+    }
+    MergeTensor mt{};
+    mt.lane_values = dev.d_lane_ptrs;
+    mt.base = dev.canon.*spec.member;
+    mt.lane_lists = spec.list ? dev.d_lane_lists : nullptr;
+    mt.lane_counts = dev.d_lane_counts;
+    mt.lane_marks = spec.marks ? dev.d_lane_marks : nullptr;
+    mt.row = spec.row;
+    mt.row_len = spec.row_len;
+    mt.length = spec.length;
+    mt.kind = spec.kind;
+    return mt;
+}
+
+void shard_finish(LeoB200Device& dev, const LeoB200ShardStory* all, const float* all_losses, const uint8_t* ctx,
+                  const uint64_t* ctx_offsets, uint64_t fixed_updates, LeoB200BatchReport* report,
+                  LeoB200StorySummary* summaries, float* losses_out) {
+    require_shard(dev);
+    if (!dev.shard_local_done) throw LeoFailure("report the shard's stories before finishing");
+    const uint32_t stories = (uint32_t)dev.batch_stories.size();
+    const uint32_t d = (uint32_t)dev.z.d;
+    LeoB200BatchReport rep{};
+    rep.stories = stories;
+    rep.workers = stories;
+    rep.fixed_parameter_updates = fixed_updates;
+    std::vector<std::vector<float>> losses(stories);
+    size_t k = 0;
+    for (uint32_t i = 0; i < stories; ++i) {
+        const auto& story = dev.batch_stories[i];
+        if (all[i].story_bytes != story.size()) throw LeoFailure("shard story reports do not match the batch");
+        if (!story.empty()) {
+            losses[i].assign(all_losses + k, all_losses + k + story.size() + 1);
+            k += story.size() + 1;
+        }
+        rep.input_bytes += story.size();
+    }
+    // keyed context: every story's deltas in story order
+    std::vector<std::vector<CtxDelta>> per_story(stories);
+    for (uint32_t i = 0; i < stories; ++i) {
+        const uint8_t* p = ctx + ctx_offsets[i];
+        const uint8_t* end = ctx + ctx_offsets[i + 1];
+        auto take = [&](void* dst, size_t n) {
+            if (p + n > end) throw LeoFailure("malformed keyed context deltas");
+            std::memcpy(dst, p, n);
+            p += n;
+        };
+        uint32_t n = 0;
+        take(&n, 4);
+        for (uint32_t e = 0; e < n; ++e) {
+            CtxDelta u{0, 0, std::vector<float>(d), 0};
+            take(&u.order, 4);
+            take(&u.obs_inc, 4);
+            take(&u.key, 8);
+            take(u.emb_delta.data(), (size_t)d * 4);
+            if (u.order == 0 || u.order > dev.cfg.abi.context_max_order || u.key == 0)
+                throw LeoFailure("invalid keyed context worker delta");
+            per_story[i].push_back(std::move(u));
+        }
+        if (p != end) throw LeoFailure("malformed keyed context deltas");
+    }
+    const double canon_loss = dev.stats.training_loss_sum;
+    rep.context_keys = merge_context_deltas(dev, per_story, stories, dev.shard_ctx_slots);
+    // statistics and revision (parallel.rs:1115-1167) in story order
+    for (uint32_t i = 0; i < stories; ++i) {
+        const LeoB200ShardStory& sc = all[i];
+        dev.stats.processed_bytes += sc.processed_bytes;
+        dev.stats.processed_stories += sc.story_bytes == 0 ? 0 : 1;
+        dev.stats.training_loss_sum += sc.loss_sum - canon_loss;
+        dev.stats.training_targets += sc.targets;
+        dev.stats.active_neurons_sum += sc.active_sum;
+        dev.stats.active_neurons_peak = std::max<uint64_t>(dev.stats.active_neurons_peak, sc.active_peak);
+        dev.stats.synaptic_events += sc.synaptic_events;
+        dev.stats.numerical_rejections += sc.numerical_rejections;
+        dev.stats.persistent_ticks += sc.persistent_ticks;
+        dev.revision += sc.revision_increment;
+        if (summaries) {
+            summaries[i].training_loss_sum = 0.0;
+            for (float v : losses[i]) summaries[i].training_loss_sum += (double)v;
+            summaries[i].training_targets = sc.targets;
+            summaries[i].active_neurons_sum = sc.active_sum;
+            summaries[i].active_neurons_peak = sc.active_peak;
+            summaries[i].synaptic_events = sc.synaptic_events;
+            summaries[i].context_applied_steps = sc.context_applied_steps;
+        }
+    }
+    double weighted = 0.0;
+    size_t targets = 0;
+    for (uint32_t i = 0; i < stories; ++i) {
+        double sum = 0.0;
+        for (float v : losses[i]) sum += (double)v;
+        double mean = sum / (double)std::max<size_t>(losses[i].size(), 1);
+        weighted += mean * (double)losses[i].size();
+        targets += losses[i].size();
+    }
+    rep.targets = targets;
+    rep.mean_loss = weighted / (double)std::max<size_t>(targets, 1);
+    // Serial canonical replay of every story on every rank: identical inputs
+    // and arithmetic keep the replicas bit-identical without a broadcast.
+    LaneScalars replay_changes{};
+    for (uint32_t i = 0; i < stories; ++i)
+        replay_story(dev, dev.batch_stories[i], losses[i], dev.batch_permission, replay_changes, &rep);
+    sync_replay_changes(dev, replay_changes);
+    CUDA_CHECK(cudaEventRecord(dev.batch_stop, dev.stream));
+    CUDA_CHECK(cudaEventSynchronize(dev.batch_stop));
+    float batch_ms = 0.0f;
+    CUDA_CHECK(cudaEventElapsedTime(&batch_ms, dev.batch_start, dev.batch_stop));
+    dev.perf.batch_ms += batch_ms;
+    dev.perf.batches += 1;
+    dev.batch_open = false;
+    dev.shard_mode = false;
+    dev.shard_local_done = false;
+    if (losses_out) {
+        size_t j = 0;
+        for (auto& l : losses)
+            for (float v : l) losses_out[j++] = v;
+    }
+    if (report) *report = rep;
+}
+
 }  // namespace
 
 // ============================================================================ C ABI
@@ -1466,6 +1764,151 @@ int leo_b200_train_story_batch(LeoB200Device* dev, const uint8_t* bytes, const u
         return 0;
     } catch (const std::exception& e) {
         dev->batch_open = false;
+        return fail(e);
+    }
+}
+
+int leo_b200_shard_begin(LeoB200Device* dev, const uint8_t* bytes, const uint64_t* offsets, uint32_t stories,
+                         uint32_t first, uint32_t count, int permission) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        shard_begin(*dev, bytes, offsets, stories, first, count, permission);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_shard_local(LeoB200Device* dev, LeoB200ShardStory* stories, float* losses, size_t* context_bytes) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        shard_local(*dev, stories, losses);
+        if (context_bytes) *context_bytes = dev->shard_ctx_blob.size();
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_shard_context(LeoB200Device* dev, uint8_t* out, size_t capacity) {
+    try {
+        require_shard(*dev);
+        if (capacity < dev->shard_ctx_blob.size()) throw LeoFailure("context buffer too small");
+        if (!dev->shard_ctx_blob.empty()) std::memcpy(out, dev->shard_ctx_blob.data(), dev->shard_ctx_blob.size());
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_shard_tensor_elements(LeoB200Device* dev, uint32_t tensor, size_t* elements) {
+    if (tensor >= LEO_B200_FIXED_TENSORS) return fail(LeoFailure("fixed tensor index out of range"));
+    *elements = tensor_elements(fixed_specs(dev->z)[tensor]);
+    return 0;
+}
+
+int leo_b200_shard_marks(LeoB200Device* dev, uint32_t tensor, uint8_t* marks) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        MergeTensor mt = shard_tensor(*dev, (int)tensor);
+        const size_t n = tensor_elements(fixed_specs(dev->z)[tensor]);
+        CUDA_CHECK(cudaMemsetAsync(marks, 0, n, dev->stream));
+        leo_launch_shard_marks(mt, (int)dev->batch_lanes, marks, dev->grid, dev->stream);
+        CUDA_CHECK(cudaGetLastError());
+        CUDA_CHECK(cudaStreamSynchronize(dev->stream));
+        dev->perf.launches += 1;
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_shard_plan(LeoB200Device* dev, uint32_t tensor, const uint8_t* marks, uint32_t* count) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        shard_tensor(*dev, (int)tensor);
+        const size_t n = tensor_elements(fixed_specs(dev->z)[tensor]);
+        leo_launch_compact(marks, n, dev->shard_list[tensor], dev->compact_total, dev->compact_blocks, dev->stream);
+        CUDA_CHECK(cudaGetLastError());
+        uint32_t total = 0;
+        CUDA_CHECK(cudaMemcpyAsync(&total, dev->compact_total, 4, cudaMemcpyDeviceToHost, dev->stream));
+        CUDA_CHECK(cudaStreamSynchronize(dev->stream));
+        dev->shard_count[tensor] = total;
+        dev->perf.launches += 3;
+        *count = total;
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_shard_accumulate(LeoB200Device* dev, uint32_t tensor, double* partial, int first) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        MergeTensor mt = shard_tensor(*dev, (int)tensor);
+        CUDA_CHECK(cudaMemsetAsync(dev->shard_error, 0, 4, dev->stream));
+        leo_launch_shard_accumulate(mt.lane_values, (int)dev->batch_lanes, mt.base, dev->shard_list[tensor],
+                                    dev->shard_count[tensor], partial, first, dev->shard_error, dev->grid, dev->stream);
+        CUDA_CHECK(cudaGetLastError());
+        uint32_t err = 0;
+        CUDA_CHECK(cudaMemcpyAsync(&err, dev->shard_error, 4, cudaMemcpyDeviceToHost, dev->stream));
+        CUDA_CHECK(cudaStreamSynchronize(dev->stream));
+        dev->perf.launches += 1;
+        if (err) throw LeoFailure("invalid sparse worker parameter delta");
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_shard_finalize(LeoB200Device* dev, uint32_t tensor, const double* partial, float* values) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        MergeTensor mt = shard_tensor(*dev, (int)tensor);
+        CUDA_CHECK(cudaMemsetAsync(dev->shard_error, 0, 4, dev->stream));
+        leo_launch_shard_finalize(mt.base, dev->shard_list[tensor], dev->shard_count[tensor], partial, values,
+                                  (double)dev->batch_stories.size(), mt.kind, dev->cfg.abi.weight_min,
+                                  dev->cfg.abi.weight_max, dev->kc.topo.neuron_type, (uint32_t)dev->z.s,
+                                  dev->shard_error, dev->grid, dev->stream);
+        CUDA_CHECK(cudaGetLastError());
+        uint32_t err = 0;
+        CUDA_CHECK(cudaMemcpyAsync(&err, dev->shard_error, 4, cudaMemcpyDeviceToHost, dev->stream));
+        CUDA_CHECK(cudaStreamSynchronize(dev->stream));
+        dev->perf.launches += 1;
+        if (err) throw LeoFailure("merged parameter became non-finite");
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_shard_commit(LeoB200Device* dev, uint32_t tensor, const float* values) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        MergeTensor mt = shard_tensor(*dev, (int)tensor);
+        leo_launch_shard_commit(mt.base, dev->shard_list[tensor], dev->shard_count[tensor], values, mt.lane_values,
+                                (int)dev->lanes.size(), dev->grid, dev->stream);
+        leo_launch_shard_sync_own(mt, (int)dev->batch_lanes, dev->grid, dev->stream);
+        CUDA_CHECK(cudaGetLastError());
+        CUDA_CHECK(cudaStreamSynchronize(dev->stream));
+        dev->perf.launches += 2;
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_shard_finish(LeoB200Device* dev, const LeoB200ShardStory* stories, const float* losses,
+                          const uint8_t* context, const uint64_t* context_offsets, uint64_t fixed_updates,
+                          LeoB200BatchReport* report, LeoB200StorySummary* summaries, float* losses_out) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        shard_finish(*dev, stories, losses, context, context_offsets, fixed_updates, report, summaries, losses_out);
+        return 0;
+    } catch (const std::exception& e) {
+        dev->batch_open = false;
+        dev->shard_mode = false;
+        dev->shard_local_done = false;
         return fail(e);
     }
 }

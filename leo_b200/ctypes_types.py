@@ -113,6 +113,25 @@ class LeoB200StorySummary(C.Structure):
     ]
 
 
+class LeoB200ShardStory(C.Structure):
+    _fields_ = [
+        ("loss_sum", C.c_double),
+        ("processed_bytes", C.c_uint64),
+        ("targets", C.c_uint64),
+        ("active_sum", C.c_uint64),
+        ("active_peak", C.c_uint64),
+        ("synaptic_events", C.c_uint64),
+        ("numerical_rejections", C.c_uint64),
+        ("persistent_ticks", C.c_uint64),
+        ("revision_increment", C.c_uint64),
+        ("context_applied_steps", C.c_uint64),
+        ("story_bytes", C.c_uint64),
+    ]
+
+
+FIXED_TENSORS = 6
+
+
 class LeoB200BatchReport(C.Structure):
     _fields_ = [
         ("workers", C.c_uint64),

@@ -10,6 +10,7 @@ from pathlib import Path
 
 from .ctypes_types import (
     LeoB200BatchReport,
+    LeoB200ShardStory,
     LeoB200Config,
     LeoB200HostModel,
     LeoB200PerfStats,
@@ -57,6 +58,17 @@ def lib() -> C.CDLL:
     L.leo_b200_canonical_tick.restype = u64
     L.leo_b200_set_canonical_tick.argtypes = [vp, u64]
     L.leo_b200_set_story_chunk.argtypes = [vp, u32]
+    L.leo_b200_shard_begin.argtypes = [vp, vp, vp, u32, u32, u32, C.c_int]
+    L.leo_b200_shard_local.argtypes = [vp, P(LeoB200ShardStory), vp, P(sz)]
+    L.leo_b200_shard_context.argtypes = [vp, vp, sz]
+    L.leo_b200_shard_tensor_elements.argtypes = [vp, u32, P(sz)]
+    L.leo_b200_shard_marks.argtypes = [vp, u32, vp]
+    L.leo_b200_shard_plan.argtypes = [vp, u32, vp, P(u32)]
+    L.leo_b200_shard_accumulate.argtypes = [vp, u32, vp, C.c_int]
+    L.leo_b200_shard_finalize.argtypes = [vp, u32, vp, vp]
+    L.leo_b200_shard_commit.argtypes = [vp, u32, vp]
+    L.leo_b200_shard_finish.argtypes = [vp, P(LeoB200ShardStory), vp, vp, vp, u64, P(LeoB200BatchReport),
+                                        P(LeoB200StorySummary), vp]
     L.leo_b200_sparse_mean_apply.argtypes = [C.c_int, vp, u32, vp, vp, vp, u32, C.c_float, C.c_float, vp, u32, vp,
                                              P(u32)]
     L.leo_b200_sparse_mean_apply_static.argtypes = L.leo_b200_sparse_mean_apply.argtypes
