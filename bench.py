@@ -19,8 +19,11 @@ metric is input story bytes per second (``input_bytes`` of the reference's
   a bounded sample of the same workload, timed on this box's host cores.
 
 ``--impl reference`` times that CPU implementation alone, one sample batch per
-step.  Under torchrun every rank trains its own replica on its own stories
-(weak scaling); rank 0 prints one JSON line.
+step.  Under torchrun (N GPUs) one logical batch holds ``workers`` x N stories,
+sharded over the ranks with the exact batch-end merge exchanged over NCCL and
+the serial replay run on every rank (``leo_b200.parallel``; weak scaling: the
+lanes per GPU stay fixed); rank 0 prints one JSON line with the max-over-ranks
+batch time.
 """
 
 from __future__ import annotations
@@ -200,25 +203,40 @@ def main() -> None:
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     dist = None
+    ex = None
     if world > 1:
         import datetime
 
         import torch
         import torch.distributed as dist
 
+        from leo_b200.parallel import TorchExchange
+
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device(f"cuda:{local}"))
+        host_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=300))
+        ex = TorchExchange(None, host_group)
+
+    from leo_b200.parallel import sharded_story_batch
 
     cfg = workload.config
     model = HostModel.initialize(cfg, workload.topology)
-    backend = GpuBackend(model, device=local, max_lanes=workload.workers)
+    # Weak scaling: every GPU runs `workers` story lanes of one logical batch of workers x N stories.
+    per_batch = workload.workers * world
+    backend = GpuBackend(model, device=local, max_lanes=2 * workload.workers)
     total_batches = args.warmup + args.steps
-    stories = story_stream(workload.story_seed + 1000 * rank, workload.workers * total_batches,
-                           workload.min_story_bytes, workload.max_story_bytes)
-    batches = [stories[i * workload.workers:(i + 1) * workload.workers] for i in range(total_batches)]
+    stories = story_stream(workload.story_seed, per_batch * total_batches, workload.min_story_bytes,
+                           workload.max_story_bytes)
+    batches = [stories[i * per_batch:(i + 1) * per_batch] for i in range(total_batches)]
+
+    def run_batch(batch):
+        if ex is None:
+            return backend.training_story_batch(batch, TRAINING)
+        return sharded_story_batch(backend, ex, batch, TRAINING)
 
     for b in range(args.warmup):
-        backend.training_story_batch(batches[b], TRAINING)
+        run_batch(batches[b])
     backend.reset_perf_stats()
 
     if dist is not None:
@@ -231,7 +249,7 @@ def main() -> None:
     for b in range(args.warmup, total_batches):
         batch = batches[b]
         t0 = time.perf_counter()
-        result = backend.training_story_batch(batch, TRAINING)
+        result = run_batch(batch)
         wall += time.perf_counter() - t0
         nbytes += sum(len(s) for s in batch)
         h2d += sum(len(s) for s in batch) + 8 * (len(batch) + 1)
@@ -245,11 +263,8 @@ def main() -> None:
 
         t = torch.tensor(times[:2], dtype=torch.float64, device=f"cuda:{local}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        b = torch.tensor([times[2]], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(b, op=dist.ReduceOp.SUM)
-        device_s, wall, total_bytes = float(t[0]), float(t[1]), float(b[0])
-    else:
-        total_bytes = float(nbytes)
+        device_s, wall = float(t[0]), float(t[1])
+    total_bytes = float(nbytes)  # every rank passes the whole logical batch
 
     if rank == 0:
         peak, peak_kind = measured_peaks()
@@ -278,7 +293,9 @@ def main() -> None:
                        "synapses_per_neuron": cfg.synapses_per_neuron, "workers": workload.workers,
                        "story_bytes": [workload.min_story_bytes, workload.max_story_bytes],
                        "replay_fraction": cfg.replay_fraction,
-                       "parallelism": f"{world} replica(s), {workload.workers} story lanes each",
+                       "parallelism": f"dp{world}: one logical batch of {per_batch} stories sharded over {world} GPU(s)"
+                                      f" ({workload.workers} lanes each), exact merge over NCCL, serial replay",
+                       "global_batch": per_batch,
                        "l2": "per-batch working set (lanes x ~0.4 GB) exceeds L2"},
             "e2e": {"value": round(total_bytes / wall, 3), "unit": UNIT, "h2d_bytes_per_step": h2d // args.steps,
                     "d2h_bytes_per_step": d2h // args.steps},
