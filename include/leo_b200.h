@@ -150,6 +150,20 @@ int leo_b200_set_cluster_sizes(LeoB200Device* device, uint32_t story_cluster, ui
    plays this role statically, crates/leo-core/src/cuda_plan.rs:189-453). */
 int leo_b200_set_story_chunk(LeoB200Device* device, uint32_t steps);
 
+/* Execution geometry only: neurons whose recurrent in-degree is at least
+   `min_in_degree` are hubs -- their events per step go to a contiguous buffer
+   sorted by event order instead of a per-target linked list, which keeps
+   power-law topologies (a few targets receiving thousands of events per step)
+   from serialising on one list.  0 restores the default,
+   max(4 x synapses_per_neuron, 8 x neuron_count / max_active_global).  A hub
+   with more than `cta_events` events in a step (1..2048; 0: 256) is sorted
+   and summed by a whole CTA, one with at most `thread_events` (1..16; 0: 16)
+   by a single thread, one in between by a warp.  Only before the first story
+   batch.  leo_b200_hub_count reports the plan. */
+int leo_b200_set_hub_threshold(LeoB200Device* device, uint32_t min_in_degree, uint32_t cta_events,
+                               uint32_t thread_events);
+int leo_b200_hub_count(LeoB200Device* device, uint32_t* hubs, uint64_t* events_per_lane);
+
 /* Device memory held by the backend, in bytes. */
 size_t leo_b200_device_bytes(LeoB200Device* device);
 

@@ -200,7 +200,7 @@ enum LeoB200Phase {
     LEO_B200_PHASE_LEARN = 7,
     LEO_B200_PHASE_PLASTICITY = 8,
     LEO_B200_PHASE_INHIBIT = 9,
-    LEO_B200_PHASE_UNUSED = 10
+    LEO_B200_PHASE_SETTLE_HUBS = 10 /* part of SETTLE: hub targets, as the first CTA sees it */
 };
 
 /* Performance counters since the last reset.  work_* sum, over lanes and

@@ -97,6 +97,14 @@ class GpuBackend:
     def set_cluster_sizes(self, story: int = 0, replay: int = 0) -> None:
         native.check(native.lib().leo_b200_set_cluster_sizes(self.handle, story, replay))
 
+    def set_hub_threshold(self, min_in_degree: int, cta_events: int = 0, thread_events: int = 0) -> None:
+        native.check(native.lib().leo_b200_set_hub_threshold(self.handle, min_in_degree, cta_events, thread_events))
+
+    def hub_plan(self) -> tuple[int, int]:
+        hubs, events = C.c_uint32(), C.c_uint64()
+        native.check(native.lib().leo_b200_hub_count(self.handle, C.byref(hubs), C.byref(events)))
+        return hubs.value, events.value
+
     def set_story_chunk(self, steps: int) -> None:
         native.check(native.lib().leo_b200_set_story_chunk(self.handle, steps))
 

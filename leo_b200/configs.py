@@ -164,6 +164,8 @@ WORKLOADS = {
     # Small case of the baseline2 model for kernel captures: 2 lanes of short stories.
     "profile": Workload("profile", BASELINE2, TOPOLOGY_UNIFORM, 2, 64, 80, 96),
     "baseline3": Workload("baseline3", BASELINE3, TOPOLOGY_ZIPF, 64, 50_000, 512, 2048),
+    # Small case of the baseline3 model: 4 lanes of short stories.
+    "baseline3-small": Workload("baseline3-small", BASELINE3, TOPOLOGY_ZIPF, 4, 64, 64, 128),
     "baseline4": Workload("baseline4", BASELINE3, TOPOLOGY_ZIPF, 128, 50_000, 512, 2048),
 }
 

@@ -137,6 +137,7 @@ struct LaneScalars {
         work_steps;
     unsigned long long phase_cycles[LEO_PHASES];  // SM clock cycles per phase (first CTA, first thread)
     uint32_t step_supra;                          // candidates of the current tick (all blocks)
+    uint32_t hub_next;                            // next hub a warp takes in settle (reset after settle)
     // last-step metrics
     uint32_t last_active, last_suprathreshold, last_block_selected, last_clipped, last_predicted;
     float last_loss;
@@ -148,6 +149,17 @@ struct DeviceTopology {
     const uint32_t* in_word;       // [258*F]
     const uint8_t* neuron_type;    // [N]
     const float* excitability;     // [N]
+    // Hub targets: neurons whose in-degree makes long event lists per step
+    // (power-law topologies).  Their events go to a contiguous per-hub buffer
+    // that one CTA sorts by event order, instead of a linked list.
+    uint32_t hubs;                 // number of hubs (0: none)
+    uint32_t hub_sort_capacity;    // largest power of two a hub's events may need when sorted
+    uint32_t hub_cta_events;       // hubs with more events than this in a step are settled by a whole CTA
+    uint32_t hub_thread_events;    // hubs with at most this many events are settled by one thread
+    const int32_t* hub_of;         // [N] hub index or -1
+    const uint32_t* hub_offset;    // [hubs] start of the hub's segment in a lane's hub_events
+    const uint32_t* hub_capacity;  // [hubs] events the hub can receive in one step
+    const uint32_t* hub_neuron;    // [hubs] neuron of each hub
 };
 
 struct LaneState {
@@ -177,8 +189,8 @@ struct LaneState {
     uint32_t* ev_head;          // [N * 4]
     uint32_t* ev_next;          // [event capacity]
     float* ev_val;              // [event capacity]
-    uint4* elig[2];             // recurrent worklists {slot, word, eligibility bits, 0}
-    uint4* in_elig[2];          // input worklists
+    uint2* elig[2];             // recurrent worklists {slot, eligibility bits}
+    uint2* in_elig[2];          // input worklists
     Trace* traces;              // [N*S]
     Trace* in_traces;           // [258*F]
     uint32_t* dst_list;         // [N]
@@ -191,6 +203,11 @@ struct LaneState {
     uint8_t* in_mark;   uint32_t* in_list;    // [258*F]
     uint8_t* out_mark;  uint32_t* out_list;   // [N]
     uint8_t* ctx_mark;  uint32_t* ctx_list;   // [C]
+    // Hub events of the current step: per-hub counts and keys (the values
+    // are stored by event order in ev_val, like listed events).
+    uint32_t* hub_count;                // [hubs]
+    uint32_t* hub_events;               // [sum of hub capacities] keys: branch << 30 | event order
+    uint32_t* hub_sort;                 // [hub_sort_capacity] when a hub's keys exceed the shared-memory sort
     // Where the first CTA reports the lane's work per step (eligible slots +
     // events emitted + touched neurons) at the end of each launch; the host
     // sizes the next launch's clusters from it.  Null: not reported.

@@ -148,6 +148,12 @@ struct LeoB200Device {
     uint32_t* d_lane_load = nullptr;  // [max_lanes + 1], last entry: replay lane
     LaneState* d_group_table = nullptr;
     std::vector<uint32_t> lane_steps;
+    // Hub targets (see DeviceTopology): the plan and the threshold it used.
+    uint32_t hub_min_in_degree = 0;   // 0: default, max(4 S, 8 N / max_active_global)
+    uint32_t hub_cta_events = 256;    // more events than this per step: the hub is settled by a CTA
+    uint32_t hub_thread_events = 16;  // at most this many: by one thread; in between: by one warp
+    uint64_t hub_events_total = 0;    // sum of hub capacities (entries per lane)
+    std::vector<int32_t> hub_of_host;
     cudaStream_t aux[4] = {nullptr, nullptr, nullptr, nullptr};
     cudaEvent_t fork = nullptr, join[4] = {nullptr, nullptr, nullptr, nullptr};
     cudaEvent_t batch_start = nullptr, batch_stop = nullptr;
@@ -180,6 +186,19 @@ KernelConsts make_consts(LeoB200Device& dev) {
     return kc;
 }
 
+// Per-lane hub buffers for the current hub plan (none without hubs).
+void allocate_lane_hubs(LeoB200Device& dev, Lane& lane) {
+    const DeviceTopology& t = dev.kc.topo;
+    LaneState& st = lane.st;
+    st.hub_count = nullptr;
+    st.hub_events = nullptr;
+    st.hub_sort = nullptr;
+    if (t.hubs == 0) return;
+    st.hub_count = lane.mem.alloc<uint32_t>(t.hubs);
+    st.hub_events = lane.mem.alloc<uint32_t>(std::max<uint64_t>(dev.hub_events_total, 1));
+    if (t.hub_sort_capacity > 32768) st.hub_sort = lane.mem.alloc<uint32_t>(t.hub_sort_capacity);
+}
+
 void allocate_lane_transient(LeoB200Device& dev, Lane& lane) {
     const ModelSizes& z = dev.z;
     MemPool& m = lane.mem;
@@ -204,8 +223,8 @@ void allocate_lane_transient(LeoB200Device& dev, Lane& lane) {
     st.ev_next = m.alloc<uint32_t>(dev.kc.event_capacity);
     st.ev_val = m.alloc<float>(dev.kc.event_capacity);
     for (int i = 0; i < 2; ++i) {
-        st.elig[i] = m.alloc<uint4>(z.synapses);
-        st.in_elig[i] = m.alloc<uint4>(z.inputs);
+        st.elig[i] = m.alloc<uint2>(z.synapses);
+        st.in_elig[i] = m.alloc<uint2>(z.inputs);
     }
     st.traces = m.alloc<Trace>(z.synapses);
     st.in_traces = m.alloc<Trace>(z.inputs);
@@ -224,6 +243,7 @@ void allocate_lane_transient(LeoB200Device& dev, Lane& lane) {
     st.out_list = m.alloc<uint32_t>(z.n);
     st.ctx_mark = m.alloc<uint8_t>((z.ctx + 3) & ~(size_t)3);
     st.ctx_list = m.alloc<uint32_t>(z.ctx);
+    allocate_lane_hubs(dev, lane);
 }
 
 void allocate_lane_params(LeoB200Device& dev, Lane& lane) {
@@ -271,6 +291,7 @@ void reset_lane(LeoB200Device& dev, Lane& lane, unsigned long long base_tick, ui
     CUDA_CHECK(cudaMemsetAsync(st.block_cand_count, 0, dev.cfg.abi.block_count * 4, s));
     CUDA_CHECK(cudaMemsetAsync(st.traces, 0, z.synapses * sizeof(Trace), s));
     CUDA_CHECK(cudaMemsetAsync(st.in_traces, 0, z.inputs * sizeof(Trace), s));
+    if (st.hub_count) CUDA_CHECK(cudaMemsetAsync(st.hub_count, 0, dev.kc.topo.hubs * 4, s));
     LaneScalars sc{};
     sc.base_tick = base_tick;
     sc.steps = steps;
@@ -309,6 +330,98 @@ void upload_lane_table(LeoB200Device& dev) {
     if (count)
         CUDA_CHECK(cudaMemcpyAsync(dev.d_lanes, table.data(), count * sizeof(LaneState), cudaMemcpyHostToDevice, dev.stream));
     CUDA_CHECK(cudaMemcpyAsync(dev.d_replay, &dev.replay->st, sizeof(LaneState), cudaMemcpyHostToDevice, dev.stream));
+}
+
+// ---------------------------------------------------------------- hub targets
+// Targets whose recurrent in-degree is at least the threshold become hubs.
+// A hub's capacity per step: every slot delivers at most once per step (a
+// slot has one delay), so at most min(in-degree, max_active_global x the
+// largest number of slots one source has to the hub) recurrent events, plus
+// the most input slots one symbol has to it.
+std::vector<int32_t> plan_hubs(LeoB200Device& dev, const uint32_t* recurrent_target, const uint32_t* input_target,
+                               bool upload) {
+    const ModelSizes& z = dev.z;
+    const uint32_t N = (uint32_t)z.n, S = (uint32_t)z.s, F = (uint32_t)z.f;
+    const uint32_t maxa = dev.cfg.abi.max_active_global;
+    uint32_t threshold = dev.hub_min_in_degree;
+    if (threshold == 0) threshold = std::max<uint32_t>(4 * S, (uint32_t)((8ull * N + maxa - 1) / maxa));
+    std::vector<uint32_t> degree(N, 0), mult(N, 0), in_max(N, 0);
+    std::vector<uint32_t> row(S);
+    for (uint32_t src = 0; src < N; ++src) {
+        for (uint32_t j = 0; j < S; ++j) row[j] = recurrent_target[(size_t)src * S + j];
+        std::sort(row.begin(), row.end());
+        for (uint32_t j = 0; j < S;) {
+            uint32_t e = j;
+            while (e < S && row[e] == row[j]) ++e;
+            degree[row[j]] += e - j;
+            mult[row[j]] = std::max(mult[row[j]], e - j);
+            j = e;
+        }
+    }
+    std::vector<uint32_t> in_row(F);
+    for (uint32_t sym = 0; sym < LEO_B200_SYMBOL_COUNT; ++sym) {
+        for (uint32_t f = 0; f < F; ++f) in_row[f] = input_target[(size_t)sym * F + f];
+        std::sort(in_row.begin(), in_row.end());
+        for (uint32_t f = 0; f < F;) {
+            uint32_t e = f;
+            while (e < F && in_row[e] == in_row[f]) ++e;
+            in_max[in_row[f]] = std::max(in_max[in_row[f]], e - f);
+            f = e;
+        }
+    }
+    // Hubs in descending capacity (ties by neuron): the CTA tier deals them
+    // round-robin over the cluster and the warp tier takes the largest first.
+    std::vector<std::pair<uint64_t, uint32_t>> ranked;
+    for (uint32_t n = 0; n < N; ++n) {
+        if (degree[n] < threshold) continue;
+        const uint64_t cap = std::min<uint64_t>(degree[n], (uint64_t)maxa * mult[n]) + in_max[n];
+        ranked.push_back({cap, n});
+    }
+    std::sort(ranked.begin(), ranked.end(), [](const auto& a, const auto& b) {
+        return a.first != b.first ? a.first > b.first : a.second < b.second;
+    });
+    std::vector<int32_t> hub_of(N, -1);
+    std::vector<uint32_t> offset, capacity, neuron;
+    uint64_t total = 0, largest = 0;
+    for (const auto& [cap, n] : ranked) {
+        hub_of[n] = (int32_t)neuron.size();
+        offset.push_back((uint32_t)total);
+        capacity.push_back((uint32_t)cap);
+        neuron.push_back(n);
+        total += cap;
+        largest = std::max(largest, cap);
+        if (total >= 0xffffffffull) throw LeoFailure("hub event capacity exceeds 32-bit offsets");
+    }
+    if (!upload) return hub_of;
+    DeviceTopology& t = dev.kc.topo;
+    t.hubs = (uint32_t)neuron.size();
+    t.hub_cta_events = dev.hub_cta_events;
+    t.hub_thread_events = std::min(dev.hub_thread_events, dev.hub_cta_events);
+    uint32_t sort_cap = 1;
+    while (sort_cap < largest) sort_cap <<= 1;
+    t.hub_sort_capacity = t.hubs ? sort_cap : 0;
+    dev.hub_events_total = total;
+    dev.hub_of_host = hub_of;
+    if (t.hubs) {
+        int32_t* d_of = dev.mem.alloc<int32_t>(N);
+        uint32_t* d_off = dev.mem.alloc<uint32_t>(t.hubs);
+        uint32_t* d_cap = dev.mem.alloc<uint32_t>(t.hubs);
+        uint32_t* d_neuron = dev.mem.alloc<uint32_t>(t.hubs);
+        CUDA_CHECK(cudaMemcpy(d_of, hub_of.data(), N * 4, cudaMemcpyHostToDevice));
+        CUDA_CHECK(cudaMemcpy(d_off, offset.data(), t.hubs * 4, cudaMemcpyHostToDevice));
+        CUDA_CHECK(cudaMemcpy(d_cap, capacity.data(), t.hubs * 4, cudaMemcpyHostToDevice));
+        CUDA_CHECK(cudaMemcpy(d_neuron, neuron.data(), t.hubs * 4, cudaMemcpyHostToDevice));
+        t.hub_of = d_of;
+        t.hub_offset = d_off;
+        t.hub_capacity = d_cap;
+        t.hub_neuron = d_neuron;
+    } else {
+        t.hub_of = nullptr;
+        t.hub_offset = nullptr;
+        t.hub_capacity = nullptr;
+        t.hub_neuron = nullptr;
+    }
+    return hub_of;
 }
 
 // ---------------------------------------------------------------- model I/O
@@ -1641,11 +1754,12 @@ int leo_b200_open(int device, const LeoB200HostModel* canonical, uint32_t max_la
         for (cudaEvent_t& ev : dev->join) CUDA_CHECK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
         dev->sm_count = prop.multiProcessorCount;
         // replay lane: canonical parameters, private transient state
+        plan_hubs(*dev, canonical->recurrent_target, canonical->input_target, true);
         dev->replay = std::make_unique<Lane>();
         dev->replay->st.p = dev->canon;
         allocate_lane_transient(*dev, *dev->replay);
         dev->grid = prop.multiProcessorCount * 4;
-        if (leo_wavefront_smem_bytes(dev->kc) > 96 * 1024) throw LeoFailure("block winners exceed shared memory");
+        if (leo_wavefront_smem_bytes(dev->kc) > 160 * 1024) throw LeoFailure("block winners exceed shared memory");
         CUDA_CHECK(leo_wavefront_configure());
         if (leo_wavefront_max_clusters(16, dev->kc, &dev->fit16) != cudaSuccess) {
             cudaGetLastError();
@@ -1691,6 +1805,8 @@ int leo_b200_upload_canonical(LeoB200Device* dev, const LeoB200HostModel* model)
         const char* e = leo_host::validate_model(*model);
         if (*e) throw LeoFailure(e);
         CUDA_CHECK(cudaSetDevice(dev->device));
+        if (plan_hubs(*dev, model->recurrent_target, model->input_target, false) != dev->hub_of_host)
+            throw LeoFailure("the recurrent topology changed: open a new backend for it");
         upload_model(*dev, *model);
         return 0;
     } catch (const std::exception& e) {
@@ -2035,10 +2151,10 @@ int leo_b200_lane_array(LeoB200Device* dev, uint32_t lane, const char* name, voi
         } else if (k == "eligible_recurrent_slots" || k == "eligible_input_slots") {
             bool input = k == "eligible_input_slots";
             uint32_t count = input ? sc.in_elig_count[sc.elig_cur] : sc.elig_count[sc.elig_cur];
-            std::vector<uint4> e(count);
+            std::vector<uint2> e(count);
             if (count)
                 CUDA_CHECK(cudaMemcpy(e.data(), input ? L.st.in_elig[sc.elig_cur] : L.st.elig[sc.elig_cur],
-                                      count * sizeof(uint4), cudaMemcpyDeviceToHost));
+                                      count * sizeof(uint2), cudaMemcpyDeviceToHost));
             for (auto& x : e) u.push_back(x.x);
         } else if (k == "active") {
             uint32_t entry = (dev->steps_done + LEO_RING - 1) % LEO_RING;
@@ -2096,6 +2212,38 @@ int leo_b200_set_cluster_sizes(LeoB200Device* dev, uint32_t story_cluster, uint3
 int leo_b200_set_story_chunk(LeoB200Device* dev, uint32_t steps) {
     if (steps == 0) return fail(LeoFailure("story chunk must be at least one step"));
     dev->story_chunk = steps;
+    return 0;
+}
+
+int leo_b200_set_hub_threshold(LeoB200Device* dev, uint32_t min_in_degree, uint32_t cta_events,
+                               uint32_t thread_events) {
+    try {
+        if (cta_events > 2048) throw LeoFailure("cta_events must be in 0..=2048 (0: default 256)");
+        if (thread_events > 16) throw LeoFailure("thread_events must be in 0..=16 (0: default 16)");
+        if (!dev->lanes.empty() || dev->batch_open)
+            throw LeoFailure("the hub threshold must be set before the first story batch");
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        const ModelSizes& z = dev->z;
+        std::vector<uint32_t> rec(z.synapses), in(z.inputs);
+        CUDA_CHECK(cudaMemcpy(rec.data(), dev->kc.topo.rec_word, z.synapses * 4, cudaMemcpyDeviceToHost));
+        CUDA_CHECK(cudaMemcpy(in.data(), dev->kc.topo.in_word, z.inputs * 4, cudaMemcpyDeviceToHost));
+        for (auto& w : rec) w &= LEO_TARGET_MASK;
+        for (auto& w : in) w &= LEO_TARGET_MASK;
+        dev->hub_min_in_degree = min_in_degree;
+        dev->hub_cta_events = cta_events ? cta_events : 256;
+        dev->hub_thread_events = thread_events ? thread_events : 16;
+        plan_hubs(*dev, rec.data(), in.data(), true);
+        if (leo_wavefront_smem_bytes(dev->kc) > 160 * 1024) throw LeoFailure("hub sort exceeds shared memory");
+        allocate_lane_hubs(*dev, *dev->replay);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_hub_count(LeoB200Device* dev, uint32_t* hubs, uint64_t* events_per_lane) {
+    if (hubs) *hubs = dev->kc.topo.hubs;
+    if (events_per_lane) *events_per_lane = dev->hub_events_total;
     return 0;
 }
 

@@ -50,6 +50,13 @@
 
 namespace cg = cooperative_groups;
 
+// Hub event keys sorted in shared memory when their padded count fits (128 KB of 4-byte keys).
+constexpr uint32_t kHubSortShared = 32768;
+// Largest event count a hub's thread-level sort handles (kc.topo.hub_thread_events <= this).
+constexpr uint32_t kHubThreadEvents = 16;
+// Largest event count a warp sorts in its slice of shared memory (16 warps x 2048 x 4 B = 128 KB).
+constexpr uint32_t kHubWarpEvents = 2048;
+
 namespace {
 
 constexpr uint32_t kFrozen = 0;
@@ -179,6 +186,9 @@ __device__ __forceinline__ void append_coalesced(uint32_t* list, uint32_t* count
 }
 
 __device__ __forceinline__ void touch(const LaneState& ln, uint32_t n, uint32_t epoch) {
+    // A plain read skips the atomic for targets already touched this step
+    // (hub targets receive thousands of events per step).
+    if (*(volatile uint32_t*)&ln.touch_epoch[n] == epoch) return;
     if (atomicExch(&ln.touch_epoch[n], epoch) != epoch) append_coalesced(ln.touched, &ln.sc->touched_count, n);
 }
 
@@ -186,6 +196,27 @@ __device__ __forceinline__ void push_event(const LaneState& ln, uint32_t tb, uin
     uint32_t old = atomicExch(&ln.ev_head[tb], q);
     ln.ev_next[q] = old;
     ln.ev_val[q] = value;
+}
+
+// A hub target's event: its value is stored by event order (as for listed
+// events) and its key (branch << 30 | event order) appended to the hub's
+// segment, one atomic per group of converged threads with the same hub; the
+// order is restored by sorting the keys in settle.  Capacity is an upper
+// bound computed from the topology.
+constexpr uint32_t kEventOrderMask = 0x3fffffffu;
+__device__ __forceinline__ void hub_push(const LaneState& ln, const KernelConsts& kc, int32_t h, uint32_t key,
+                                         float value) {
+    cg::coalesced_group g = cg::coalesced_threads();
+    cg::coalesced_group peers = cg::labeled_partition(g, h);
+    uint32_t base = 0;
+    if (peers.thread_rank() == 0) base = atomicAdd(&ln.hub_count[h], peers.size());
+    base = peers.shfl(base, 0);
+    const uint32_t pos = base + peers.thread_rank();
+    ln.ev_val[key & kEventOrderMask] = value;
+    if (pos < kc.topo.hub_capacity[h])
+        ln.hub_events[kc.topo.hub_offset[h] + pos] = key;
+    else
+        atomicOr(&ln.sc->error_flag, LEO_ERR_CAPACITY);
 }
 
 __device__ __forceinline__ void add_destination(const LaneState& ln, uint32_t n, uint32_t epoch) {
@@ -370,7 +401,11 @@ __device__ void phase_deliver(const LaneState& ln, uint32_t s, const KernelConst
             uint32_t n = word & LEO_TARGET_MASK, b = LEO_WORD_BRANCH(word);
             float value = ln.ring_val[((size_t)entry * maxa + r) * S + j];
             touch(ln, n, epoch);
-            push_event(ln, n * 4 + b, q, value);
+            const int32_t h = kc.topo.hubs ? kc.topo.hub_of[n] : -1;
+            if (h >= 0)
+                hub_push(ln, kc, h, (b << 30) | q, value);
+            else
+                push_event(ln, n * 4 + b, q, value);
             if (learn) {  // activate_recurrent_trace (runtime.rs:719-726); one event per slot per tick
                 float a = ln.ring_act[entry * maxa + r];
                 Trace t = load_trace(&ln.traces[slot]);
@@ -382,7 +417,7 @@ __device__ void phase_deliver(const LaneState& ln, uint32_t s, const KernelConst
                     uint32_t base = 0;
                     if (g.thread_rank() == 0) base = atomicAdd(&sc->elig_count[cur], g.size());
                     base = g.shfl(base, 0);
-                    ln.elig[cur][base + g.thread_rank()] = make_uint4(slot, word, 0u, 0u);
+                    ln.elig[cur][base + g.thread_rank()] = make_uint2(slot, 0u);
                 }
                 store_trace(&ln.traces[slot], t);
             }
@@ -392,7 +427,11 @@ __device__ void phase_deliver(const LaneState& ln, uint32_t s, const KernelConst
             uint32_t word = kc.topo.in_word[slot];
             uint32_t n = word & LEO_TARGET_MASK, b = LEO_WORD_BRANCH(word);
             touch(ln, n, epoch);
-            push_event(ln, n * 4 + b, q, ln.p.in_weight[slot]);
+            const int32_t h = kc.topo.hubs ? kc.topo.hub_of[n] : -1;
+            if (h >= 0)
+                hub_push(ln, kc, h, (b << 30) | q, ln.p.in_weight[slot]);
+            else
+                push_event(ln, n * 4 + b, q, ln.p.in_weight[slot]);
             if (learn) {
                 Trace t = load_trace(&ln.in_traces[slot]);
                 advance_trace(kc.cfg, t, s);
@@ -403,7 +442,7 @@ __device__ void phase_deliver(const LaneState& ln, uint32_t s, const KernelConst
                     uint32_t base = 0;
                     if (g.thread_rank() == 0) base = atomicAdd(&sc->in_elig_count[cur], g.size());
                     base = g.shfl(base, 0);
-                    ln.in_elig[cur][base + g.thread_rank()] = make_uint4(slot, word, 0u, 0u);
+                    ln.in_elig[cur][base + g.thread_rank()] = make_uint2(slot, 0u);
                 }
                 store_trace(&ln.in_traces[slot], t);
             }
@@ -413,36 +452,288 @@ __device__ void phase_deliver(const LaneState& ln, uint32_t s, const KernelConst
 
 // ---------------------------------------------------------------------------
 // settle (runtime.rs:576-603, 710-717, 541-548, 947-962).
-__device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t worker,
-                             uint32_t workers) {
-    const LeoConfig& c = kc.cfg;
+
+// Decay-on-touch of one neuron's branches and state.
+__device__ __forceinline__ void settle_decay(const LeoConfig& c, uint32_t s, NeuronCold& cold, float4& br) {
+    if (s > cold.branch_tick) {
+        float dec = leo_math::decay_for_elapsed(c.branch_decay, s - cold.branch_tick);
+        br.x = br.x * dec;
+        br.y = br.y * dec;
+        br.z = br.z * dec;
+        br.w = br.w * dec;
+        cold.branch_tick = s;
+    }
+    if (s > cold.neuron_tick) {
+        uint32_t e = s - cold.neuron_tick;
+        cold.membrane = cold.membrane * leo_math::decay_for_elapsed(c.membrane_decay, e);
+        cold.fatigue = cold.fatigue * leo_math::decay_for_elapsed(c.fatigue_decay, e);
+        cold.adaptation[0] = cold.adaptation[0] * leo_math::decay_for_elapsed(c.adaptation_fast_decay, e);
+        cold.adaptation[1] = cold.adaptation[1] * leo_math::decay_for_elapsed(c.adaptation_medium_decay, e);
+        cold.adaptation[2] = cold.adaptation[2] * leo_math::decay_for_elapsed(c.adaptation_slow_decay, e);
+        cold.neuron_tick = s;
+    }
+}
+
+// Integration and block candidate after the branch sums; stores the neuron.
+__device__ __forceinline__ void settle_integrate(const LaneState& ln, const KernelConsts& kc, uint32_t n, uint32_t s,
+                                                 NeuronCold cold, float4 br, float pop_inh, uint32_t rotation) {
     const uint32_t npb = kc.topo.npb, n_count = kc.topo.n;
+    NeuronHot& hot = ln.hot[n];
+    hot.activation = 0.0f;
+    bool refractory = hot.refractory_until > s;
+    if (!refractory) {
+        float gate = clampf(br.w, 0.0f, 1.0f);
+        float inhibitory = br.y;
+        float net = br.x + br.z * gate + inhibitory;
+        float adaptation = sum3(cold.adaptation[0], cold.adaptation[1], cold.adaptation[2]);
+        float drive = kc.topo.excitability[n] * net - cold.fatigue - adaptation - pop_inh;
+        cold.membrane = cold.membrane + drive;
+        float act = clampf(cold.membrane - ln.p.threshold[n], 0.0f, 1.0f);
+        if (act > 0.0f) {
+            uint32_t blk = n / npb;
+            uint32_t pos = atomicAdd(&ln.block_cand_count[blk], 1u);
+            ln.block_cand[(size_t)blk * npb + pos] = selection_key(act, n, rotation, n_count);
+        }
+    }
+    ln.cold[n] = cold;
+    ln.branches[n] = br;
+}
+
+// Bounds of one branch in a hub's sorted keys (branch in the top two bits).
+__device__ __forceinline__ uint32_t hub_branch_begin(const uint32_t* keys, uint32_t k, uint32_t branch) {
+    uint32_t lo = 0, hi = k;
+    while (lo < hi) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if ((keys[mid] >> 30) < branch)
+            lo = mid + 1;
+        else
+            hi = mid;
+    }
+    return lo;
+}
+
+// Strictly sequential sum of vals[lo, hi) onto `a`, loads issued eight at a time.
+__device__ __forceinline__ float ordered_sum(const float* vals, uint32_t lo, uint32_t hi, float a) {
+    uint32_t i = lo;
+    for (; i + 8 <= hi; i += 8) {
+        float v[8];
+#pragma unroll
+        for (int x = 0; x < 8; ++x) v[x] = vals[i + x];
+#pragma unroll
+        for (int x = 0; x < 8; ++x) a = a + v[x];
+    }
+    for (; i < hi; ++i) a = a + vals[i];
+    return a;
+}
+
+// keys[i] = src[i] for i < k and the sort padding for k <= i < P, for the
+// group's threads (tid, stride `lanes`), eight loads in flight per thread.
+__device__ __forceinline__ void load_keys(uint32_t* keys, const uint32_t* __restrict__ src, uint32_t k, uint32_t P,
+                                          uint32_t tid, uint32_t lanes) {
+    for (uint32_t base = tid; base < P; base += lanes * 8) {
+        uint32_t v[8];
+#pragma unroll
+        for (int x = 0; x < 8; ++x) {
+            const uint32_t i = base + x * lanes;
+            v[x] = i < k ? src[i] : 0xffffffffu;
+        }
+#pragma unroll
+        for (int x = 0; x < 8; ++x) {
+            const uint32_t i = base + x * lanes;
+            if (i < P) keys[i] = v[x];
+        }
+    }
+}
+
+// Replaces sorted keys[0, k) by their events' values (by event order).
+__device__ __forceinline__ void gather_values(uint32_t* keys, const float* __restrict__ ev_val, uint32_t k, uint32_t tid,
+                                              uint32_t lanes) {
+    float* vals = reinterpret_cast<float*>(keys);
+    for (uint32_t base = tid; base < k; base += lanes * 8) {
+        float v[8];
+#pragma unroll
+        for (int x = 0; x < 8; ++x) {
+            const uint32_t i = base + x * lanes;
+            v[x] = i < k ? ev_val[keys[i] & kEventOrderMask] : 0.0f;
+        }
+#pragma unroll
+        for (int x = 0; x < 8; ++x) {
+            const uint32_t i = base + x * lanes;
+            if (i < k) vals[i] = v[x];
+        }
+    }
+}
+
+struct BlockSync {
+    __device__ void operator()() const { __syncthreads(); }
+};
+struct WarpSync {
+    __device__ void operator()() const { __syncwarp(); }
+};
+
+// Bitonic sort (ascending) of P 4-byte keys by the `lanes` threads of `tid`'s
+// group; `sync` orders the group between stages.
+template <typename Sync>
+__device__ __forceinline__ void bitonic_sort_keys(uint32_t* keys, uint32_t P, uint32_t tid, uint32_t lanes, Sync sync) {
+    for (uint32_t width = 2; width <= P; width <<= 1) {
+        for (uint32_t stride = width >> 1; stride > 0; stride >>= 1) {
+            for (uint32_t i = tid; i < P; i += lanes) {
+                const uint32_t other = i ^ stride;
+                if (other > i) {
+                    const bool up = (i & width) == 0;
+                    const uint32_t x = keys[i], y = keys[other];
+                    if (up ? (x > y) : (x < y)) {
+                        keys[i] = y;
+                        keys[other] = x;
+                    }
+                }
+            }
+            sync();
+        }
+    }
+}
+
+// Hubs by event count this step: more than hub_cta_events -> one CTA per hub
+// (hubs h = rank, rank + C, ...); more than hub_thread_events -> one warp per
+// hub; the rest are settled by one thread in phase_settle.  A tier sorts the
+// hub's keys (branch << 30 | event order), replaces each key by its event's
+// value in place, and sums each branch's values in ascending event order.
+__device__ void settle_hubs(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t rank, uint32_t C,
+                            uint32_t* smem, float pop_inh, uint32_t rotation) {
+    __shared__ float s_acc[4];
+    __shared__ uint32_t s_bound[5];
+    __shared__ NeuronCold s_cold;
+    const uint32_t H = kc.topo.hubs, tid = threadIdx.x;
+    for (uint32_t h = rank; h < H; h += C) {
+        const uint32_t k = ln.hub_count[h];
+        if (k <= kc.topo.hub_cta_events) continue;  // none, or few: a warp or a thread settles it
+        const uint32_t n = kc.topo.hub_neuron[h];
+        const uint32_t* ev = ln.hub_events + kc.topo.hub_offset[h];
+        uint32_t P = 1;
+        while (P < k) P <<= 1;
+        uint32_t* keys = P <= kHubSortShared ? smem : ln.hub_sort;
+        load_keys(keys, ev, k, P, tid, kThreads);
+        if (tid == 0) {
+            NeuronCold cold = ln.cold[n];
+            float4 br = ln.branches[n];
+            settle_decay(kc.cfg, s, cold, br);
+            s_cold = cold;
+            s_acc[0] = br.x;
+            s_acc[1] = br.y;
+            s_acc[2] = br.z;
+            s_acc[3] = br.w;
+        }
+        __syncthreads();
+        bitonic_sort_keys(keys, P, tid, kThreads, BlockSync{});
+        if (tid <= 4) s_bound[tid] = tid == 4 ? k : hub_branch_begin(keys, k, tid);
+        __syncthreads();
+        gather_values(keys, ln.ev_val, k, tid, kThreads);
+        __syncthreads();
+        const float* vals = reinterpret_cast<const float*>(keys);
+        if (tid < 4) s_acc[tid] = ordered_sum(vals, s_bound[tid], s_bound[tid + 1], s_acc[tid]);
+        __syncthreads();
+        if (tid == 0) settle_integrate(ln, kc, n, s, s_cold, make_float4(s_acc[0], s_acc[1], s_acc[2], s_acc[3]),
+                                       pop_inh, rotation);
+        __syncthreads();
+    }
+    // Medium hubs: one warp each, sorted in the warp's slice of shared memory.
+    // Warps take hubs one at a time from a shared counter, largest capacity
+    // first, and stop at the first hub whose capacity fits the thread tier.
+    const uint32_t lane = tid & 31u, warp = tid >> 5;
+    uint32_t* wkeys = smem + (size_t)warp * kHubWarpEvents;
+    for (;;) {
+        uint32_t h = 0;
+        if (lane == 0) h = atomicAdd(&ln.sc->hub_next, 1u);
+        h = __shfl_sync(0xffffffffu, h, 0);
+        if (h >= H || kc.topo.hub_capacity[h] <= kc.topo.hub_thread_events) break;
+        {
+        const uint32_t k = ln.hub_count[h];
+        if (k <= kc.topo.hub_thread_events || k > kc.topo.hub_cta_events) continue;
+        const uint32_t n = kc.topo.hub_neuron[h];
+        const uint32_t* ev = ln.hub_events + kc.topo.hub_offset[h];
+        uint32_t P = 32;
+        while (P < k) P <<= 1;
+        load_keys(wkeys, ev, k, P, lane, 32u);
+        __syncwarp();
+        bitonic_sort_keys(wkeys, P, lane, 32u, WarpSync{});
+        const uint32_t bound = lane <= 4 ? (lane == 4 ? k : hub_branch_begin(wkeys, k, lane)) : 0u;
+        __syncwarp();
+        gather_values(wkeys, ln.ev_val, k, lane, 32u);
+        const float* wvals = reinterpret_cast<const float*>(wkeys);
+        NeuronCold cold;
+        float4 br = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (lane == 0) {
+            cold = ln.cold[n];
+            br = ln.branches[n];
+            settle_decay(kc.cfg, s, cold, br);
+        }
+        br.x = __shfl_sync(0xffffffffu, br.x, 0);
+        br.y = __shfl_sync(0xffffffffu, br.y, 0);
+        br.z = __shfl_sync(0xffffffffu, br.z, 0);
+        br.w = __shfl_sync(0xffffffffu, br.w, 0);
+        const uint32_t next_bound = __shfl_down_sync(0xffffffffu, bound, 1);
+        __syncwarp();
+        float a = 0.0f;
+        if (lane < 4) a = ordered_sum(wvals, bound, next_bound, lane == 0 ? br.x : (lane == 1 ? br.y : (lane == 2 ? br.z : br.w)));
+        const float a1 = __shfl_sync(0xffffffffu, a, 1), a2 = __shfl_sync(0xffffffffu, a, 2),
+                    a3 = __shfl_sync(0xffffffffu, a, 3);
+        if (lane == 0) settle_integrate(ln, kc, n, s, cold, make_float4(a, a1, a2, a3), pop_inh, rotation);
+        __syncwarp();
+        }
+    }
+}
+
+__device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t worker,
+                             uint32_t workers, uint32_t rank, uint32_t C, uint32_t* smem) {
+    const LeoConfig& c = kc.cfg;
+    const uint32_t n_count = kc.topo.n;
     constexpr int kCap = 24;
     LaneScalars* sc = ln.sc;
     uint32_t count = sc->touched_count;
     float pop_inh = sc->population_inhibition;
     uint32_t rotation = (uint32_t)((sc->base_tick + s) % (unsigned long long)n_count);
+    if (kc.topo.hubs) {
+        const unsigned long long t0 = clock64();
+        settle_hubs(ln, s, kc, rank, C, smem, pop_inh, rotation);
+        // Hub share of settle (first CTA), reported as the last phase counter.
+        if (rank == 0 && threadIdx.x == 0) sc->phase_cycles[LEO_PHASES - 1] += clock64() - t0;
+    }
     for (uint32_t i = worker; i < count; i += workers) {
         uint32_t n = ln.touched[i];
-        NeuronCold cold = ln.cold[n];
-        float4 br = ln.branches[n];
-        if (s > cold.branch_tick) {
-            float dec = leo_math::decay_for_elapsed(c.branch_decay, s - cold.branch_tick);
-            br.x = br.x * dec;
-            br.y = br.y * dec;
-            br.z = br.z * dec;
-            br.w = br.w * dec;
-            cold.branch_tick = s;
+        NeuronCold cold;
+        float4 br;
+        if (kc.topo.hubs) {
+            const int32_t h = kc.topo.hub_of[n];
+            const uint32_t k = h >= 0 ? ln.hub_count[h] : 0u;
+            if (k > kc.topo.hub_thread_events) continue;  // settled by a warp or a CTA above
+            if (k > 0) {
+                // A hub with few events: sort its keys (branch, event order) here.
+                const uint32_t* ev = ln.hub_events + kc.topo.hub_offset[h];
+                uint32_t e[kHubThreadEvents];
+                for (uint32_t x = 0; x < k; ++x) e[x] = ev[x];
+                for (uint32_t x = 1; x < k; ++x) {
+                    const uint32_t v = e[x];
+                    int y = (int)x - 1;
+                    while (y >= 0 && e[y] > v) {
+                        e[y + 1] = e[y];
+                        --y;
+                    }
+                    e[y + 1] = v;
+                }
+                float vals[kHubThreadEvents];
+                for (uint32_t x = 0; x < k; ++x) vals[x] = ln.ev_val[e[x] & kEventOrderMask];
+                cold = ln.cold[n];
+                br = ln.branches[n];
+                settle_decay(c, s, cold, br);
+                float acc[4] = {br.x, br.y, br.z, br.w};
+                for (uint32_t x = 0; x < k; ++x) acc[e[x] >> 30] = acc[e[x] >> 30] + vals[x];
+                settle_integrate(ln, kc, n, s, cold, make_float4(acc[0], acc[1], acc[2], acc[3]), pop_inh, rotation);
+                continue;
+            }
         }
-        if (s > cold.neuron_tick) {
-            uint32_t e = s - cold.neuron_tick;
-            cold.membrane = cold.membrane * leo_math::decay_for_elapsed(c.membrane_decay, e);
-            cold.fatigue = cold.fatigue * leo_math::decay_for_elapsed(c.fatigue_decay, e);
-            cold.adaptation[0] = cold.adaptation[0] * leo_math::decay_for_elapsed(c.adaptation_fast_decay, e);
-            cold.adaptation[1] = cold.adaptation[1] * leo_math::decay_for_elapsed(c.adaptation_medium_decay, e);
-            cold.adaptation[2] = cold.adaptation[2] * leo_math::decay_for_elapsed(c.adaptation_slow_decay, e);
-            cold.neuron_tick = s;
-        }
+        cold = ln.cold[n];
+        br = ln.branches[n];
+        settle_decay(c, s, cold, br);
         float acc[4] = {br.x, br.y, br.z, br.w};
         // The four (target, branch) event lists, walked in lockstep so their
         // hops overlap; events are summed per branch in ascending event order.
@@ -521,25 +812,7 @@ __device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts
             }
         }
         br = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        NeuronHot& hot = ln.hot[n];
-        hot.activation = 0.0f;
-        bool refractory = hot.refractory_until > s;
-        if (!refractory) {
-            float gate = clampf(br.w, 0.0f, 1.0f);
-            float inhibitory = br.y;
-            float net = br.x + br.z * gate + inhibitory;
-            float adaptation = sum3(cold.adaptation[0], cold.adaptation[1], cold.adaptation[2]);
-            float drive = kc.topo.excitability[n] * net - cold.fatigue - adaptation - pop_inh;
-            cold.membrane = cold.membrane + drive;
-            float act = clampf(cold.membrane - ln.p.threshold[n], 0.0f, 1.0f);
-            if (act > 0.0f) {
-                uint32_t blk = n / npb;
-                uint32_t pos = atomicAdd(&ln.block_cand_count[blk], 1u);
-                ln.block_cand[(size_t)blk * npb + pos] = selection_key(act, n, rotation, n_count);
-            }
-        }
-        ln.cold[n] = cold;
-        ln.branches[n] = br;
+        settle_integrate(ln, kc, n, s, cold, br, pop_inh, rotation);
     }
 }
 
@@ -742,7 +1015,7 @@ __device__ void phase_surrogate(const LaneState& ln, uint32_t s, const KernelCon
 // slots go to the next worklist with one atomic per warp (ballot compaction)
 // and their destinations become learning destinations.
 template <bool kInput>
-__device__ __forceinline__ void eligibility_item(const LaneState& ln, const KernelConsts& kc, uint32_t s, uint4 entry,
+__device__ __forceinline__ void eligibility_item(const LaneState& ln, const KernelConsts& kc, uint32_t s, uint2 entry,
                                                  bool valid, uint32_t next, uint32_t& plastic) {
     const LeoConfig& c = kc.cfg;
     LaneScalars* sc = ln.sc;
@@ -751,10 +1024,11 @@ __device__ __forceinline__ void eligibility_item(const LaneState& ln, const Kern
     float e = 0.0f;
     if (valid) {
         Trace* tp = kInput ? &ln.in_traces[entry.x] : &ln.traces[entry.x];
+        const uint32_t word = kInput ? kc.topo.in_word[entry.x] : kc.topo.rec_word[entry.x];
         Trace t = load_trace(tp);
         advance_trace(c, t, s);
-        dest = entry.y & LEO_TARGET_MASK;
-        uint32_t branch = LEO_WORD_BRANCH(entry.y);
+        dest = word & LEO_TARGET_MASK;
+        uint32_t branch = LEO_WORD_BRANCH(word);
         NeuronHot h = ln.hot[dest];
         bool touched_now = (h.tag >> 2) == s + 1u;
         if (!(touched_now && (h.tag & 1u))) {
@@ -793,8 +1067,8 @@ __device__ __forceinline__ void eligibility_item(const LaneState& ln, const Kern
     }
     if (keep) {
         uint32_t pos = base + (uint32_t)__popc(ballot & ((1u << lane) - 1u));
-        uint4* out = kInput ? ln.in_elig[next] : ln.elig[next];
-        out[pos] = make_uint4(entry.x, entry.y, __float_as_uint(e), 0u);
+        uint2* out = kInput ? ln.in_elig[next] : ln.elig[next];
+        out[pos] = make_uint2(entry.x, __float_as_uint(e));
         // A slot with eligibility +-0 leaves its weight bit-for-bit unchanged
         // (old + (+-0) = old for every weight the model can hold, since no
         // update produces -0), so only nonzero-eligibility slots need their
@@ -816,12 +1090,12 @@ __device__ void phase_eligible(const LaneState& ln, uint32_t s, const KernelCons
         uint32_t i = base + (threadIdx.x & 31u);
         if (base < rec_pad) {
             bool valid = i < rec;
-            uint4 entry = valid ? ln.elig[cur][i] : make_uint4(0, 0, 0, 0);
+            uint2 entry = valid ? ln.elig[cur][i] : make_uint2(0, 0);
             eligibility_item<false>(ln, kc, s, entry, valid, next, plastic);
         } else {
             uint32_t k = i - rec_pad;
             bool valid = k < inp;
-            uint4 entry = valid ? ln.in_elig[cur][k] : make_uint4(0, 0, 0, 0);
+            uint2 entry = valid ? ln.in_elig[cur][k] : make_uint2(0, 0);
             eligibility_item<true>(ln, kc, s, entry, valid, next, plastic);
         }
     }
@@ -1149,10 +1423,10 @@ __device__ void phase_plasticity(const LaneState& ln, const KernelConsts& kc, ui
     uint32_t total = rec + inp;
     for (uint32_t i = worker; i < total; i += workers) {
         if (i < rec) {
-            uint4 e4 = ln.elig[next][i];
-            if (__uint_as_float(e4.z) == 0.0f) continue;  // unchanged weight (see eligibility_item)
-            uint32_t slot = e4.x, dest = e4.y & LEO_TARGET_MASK;
-            float gradient = ln.signal[dest] * __uint_as_float(e4.z);
+            const uint2 e2 = ln.elig[next][i];
+            if (__uint_as_float(e2.y) == 0.0f) continue;  // unchanged weight (see eligibility_item)
+            uint32_t slot = e2.x, dest = kc.topo.rec_word[slot] & LEO_TARGET_MASK;
+            float gradient = ln.signal[dest] * __uint_as_float(e2.y);
             float delta = clampf(-c.recurrent_learning_rate * strength * gradient, -c.max_update, c.max_update);
             float old_w = ln.p.rec_weight[slot];
             float nw = clampf(old_w + delta, c.weight_min, c.weight_max);
@@ -1164,10 +1438,10 @@ __device__ void phase_plasticity(const LaneState& ln, const KernelConsts& kc, ui
             if (nw != old_w && kc.track_changes) mark_and_append(ln.rec_mark, ln.rec_list, &sc->rec_changed, slot);
             ln.p.rec_weight[slot] = nw;
         } else {
-            uint4 e4 = ln.in_elig[next][i - rec];
-            if (__uint_as_float(e4.z) == 0.0f) continue;
-            uint32_t slot = e4.x, dest = e4.y & LEO_TARGET_MASK;
-            float gradient = ln.signal[dest] * __uint_as_float(e4.z);
+            const uint2 e2 = ln.in_elig[next][i - rec];
+            if (__uint_as_float(e2.y) == 0.0f) continue;
+            uint32_t slot = e2.x, dest = kc.topo.in_word[slot] & LEO_TARGET_MASK;
+            float gradient = ln.signal[dest] * __uint_as_float(e2.y);
             float delta = clampf(-c.recurrent_learning_rate * strength * gradient, -c.max_update, c.max_update);
             float old_w = ln.p.in_weight[slot];
             float nw = clampf(old_w + delta, 0.0f, c.weight_max);
@@ -1259,9 +1533,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         phase_deliver(ln, s, kc, worker, workers, !frozen, symbol);
         cluster.sync();
         mark(0);
-        phase_settle(ln, s, kc, worker, workers);
+        phase_settle(ln, s, kc, worker, workers, rank, C, reinterpret_cast<uint32_t*>(smem_sorted));
         cluster.sync();
         mark(1);
+        for (uint32_t h = worker; h < kc.topo.hubs; h += workers) ln.hub_count[h] = 0;
+        if (worker == 0) sc->hub_next = 0;
         phase_blocks(ln, kc, gwarp, gwarps);
         cluster.sync();
         mark(2);
@@ -1324,13 +1600,22 @@ size_t leo_wavefront_smem_bytes(const KernelConsts& kc) {
     while (span < winners) span <<= 1;
     size_t sort = (size_t)span * sizeof(unsigned long long);
     size_t tiles = (size_t)kWarps * 32 * 33 * sizeof(float);
-    return sort > tiles ? sort : tiles;
+    size_t bytes = sort > tiles ? sort : tiles;
+    if (kc.topo.hubs) {
+        // the warps' sort slices, or one CTA's sort, whichever is larger
+        size_t warps = (size_t)kWarps * kHubWarpEvents * sizeof(uint32_t);
+        size_t cta = (size_t)(kc.topo.hub_sort_capacity < kHubSortShared ? kc.topo.hub_sort_capacity : kHubSortShared) *
+                     sizeof(uint32_t);
+        size_t hub = warps > cta ? warps : cta;
+        bytes = bytes > hub ? bytes : hub;
+    }
+    return bytes;
 }
 
 // Function attributes the launches and occupancy queries rely on; called
 // once per device before either.
 cudaError_t leo_wavefront_configure() {
-    cudaError_t e = cudaFuncSetAttribute(leo_wavefront_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    cudaError_t e = cudaFuncSetAttribute(leo_wavefront_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(leo_wavefront_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
 }

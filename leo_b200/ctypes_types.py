@@ -153,7 +153,7 @@ BEGIN_DOCUMENT, END_DOCUMENT, SYMBOL_COUNT, OUTPUT_CLASSES = 256, 257, 258, 257
 
 
 PHASES = ["deliver", "settle", "blocks", "assemble", "surrogate", "eligible", "emit_forward", "learn",
-          "plasticity", "inhibit", "unused"]
+          "plasticity", "inhibit", "settle_hubs"]
 
 
 class LeoB200PerfStats(C.Structure):

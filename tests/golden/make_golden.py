@@ -33,6 +33,7 @@ CASES = [
     ("probe", "probe", 1, 4, 256, 1024, 0),
     ("baseline1", "baseline1", 2, 4, 256, 1024, 0),
     ("baseline2-short", "baseline2", 2, 4, 48, 96, 5),
+    ("baseline3-short", "baseline3", 1, 4, 24, 48, 9),
 ]
 
 
