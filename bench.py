@@ -75,6 +75,17 @@ def phase_algorithmic_bytes(p, cfg) -> dict[str, float]:
     }
 
 
+def dram_traffic(workload: str, algorithmic_bytes_per_launch: float):
+    """DRAM bytes per launch of the wavefront kernel: the ratio of DRAM traffic to
+    algorithmic bytes from the committed ncu capture of this workload, applied to
+    this run's algorithmic bytes per launch (None without a capture)."""
+    path = ROOT / "profiles" / f"leo_wavefront_kernel-dram-{workload}.json"
+    if not path.exists():
+        return None, None
+    data = json.loads(path.read_text())
+    return round(data["dram_per_algorithmic_byte"] * algorithmic_bytes_per_launch, 1), path.name
+
+
 def measured_peaks() -> tuple[float, str]:
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
@@ -276,9 +287,11 @@ def main() -> None:
         cycles = np.array(list(perf.phase_cycles)[:10], dtype=np.float64)
         shares = {PHASES[i]: round(float(cycles[i] / max(cycles.sum(), 1.0)), 4) for i in range(10)}
         story_launches = max(perf.story_wavefront_launches, 1)
+        traffic, traffic_source = dram_traffic(workload.name, per_launch_bytes)
         roofline = {"bound": "hbm", "kernel": "leo_wavefront_kernel", "achieved": round(achieved, 3),
                     "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 6), "peak_source": peak_kind,
-                    "traffic": None, "algorithmic_bytes_per_launch": round(per_launch_bytes, 1),
+                    "traffic": traffic, "traffic_source": traffic_source,
+                    "algorithmic_bytes_per_launch": round(per_launch_bytes, 1),
                     "launch_ms": round(per_launch_ms, 4), "launches": int(perf.wavefront_launches),
                     "share_of_step_time": round(perf.wavefront_ms / max(perf.batch_ms, 1e-9), 4),
                     "story_pass_launch_ms": round(perf.story_wavefront_ms / story_launches, 3),
