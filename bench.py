@@ -184,6 +184,123 @@ def run_reference(args, workload) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_sparse_apply_micro(args) -> None:
+    """Config 5: the batch-end sparse delta apply + replica sync of one 2^24-entry
+    FP32 tensor at several densities.  Stories' sorted delta lists are generated
+    on the device (each rank its contiguous share), all-gathered over NCCL when
+    N > 1, and every rank applies all of them in story order with
+    ``leo_b200_sparse_mean_apply`` (identical results on every rank).  Prints
+    one JSON line per density: the apply's HBM GB/s (algorithmic bytes / CUDA
+    event time) and the all-gather's NVLink GB/s (bytes received per GPU)."""
+    import datetime
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from leo_b200.sparse_apply import sparse_mean_apply
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    n = 1 << 24
+    stories, replicas = args.micro_stories, args.micro_replicas
+    per = [stories // world + (1 if r < stories % world else 0) for r in range(world)]
+    first = sum(per[:rank])
+    peak, peak_kind = measured_peaks()
+    for density in [float(x) for x in args.densities.split(",")]:
+        idx_parts, val_parts, counts = [], [], []
+        for sid in range(first, first + per[rank]):
+            g = torch.Generator(device=dev)
+            g.manual_seed(7000 + sid)
+            idx = torch.nonzero(torch.rand(n, generator=g, device=dev) < density).flatten().to(torch.int32)
+            val = torch.randn(idx.numel(), generator=g, device=dev) * 1e-3
+            idx_parts.append(idx)
+            val_parts.append(val)
+            counts.append(idx.numel())
+        local_idx = torch.cat(idx_parts) if idx_parts else torch.zeros(0, dtype=torch.int32, device=dev)
+        local_val = torch.cat(val_parts) if val_parts else torch.zeros(0, device=dev)
+        gather_ms, nvlink_bytes = 0.0, 0
+        if world > 1:
+            sizes = [None] * world
+            dist.all_gather_object(sizes, counts)
+            longest = max(sum(c) for c in sizes)
+            pad_idx = torch.zeros(longest, dtype=torch.int32, device=dev)
+            pad_val = torch.zeros(longest, device=dev)
+            pad_idx[: local_idx.numel()] = local_idx
+            pad_val[: local_val.numel()] = local_val
+            all_idx = torch.empty(world * longest, dtype=torch.int32, device=dev)
+            all_val = torch.empty(world * longest, device=dev)
+            dist.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            dist.all_gather_into_tensor(all_idx, pad_idx)
+            dist.all_gather_into_tensor(all_val, pad_val)
+            e1.record()
+            torch.cuda.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            gather_ms = float(t[0])
+            nvlink_bytes = (world - 1) * longest * 8
+            flat_counts = [c for rc in sizes for c in rc]
+            keep = []
+            for r in range(world):
+                total_r = sum(sizes[r])
+                keep.append((r * longest, r * longest + total_r))
+            indices = torch.cat([all_idx[a:b] for a, b in keep])
+            deltas = torch.cat([all_val[a:b] for a, b in keep])
+        else:
+            flat_counts = counts
+            indices, deltas = local_idx, local_val
+        offsets = np.zeros(len(flat_counts) + 1, dtype=np.uint64)
+        offsets[1:] = np.cumsum(flat_counts)
+        g = torch.Generator(device=dev)
+        g.manual_seed(4242)
+        base = torch.rand(n, generator=g, device=dev) * 2.0 - 1.0
+        target = base.clone()
+        reps = [base.clone() for _ in range(replicas)]
+        updates = 0
+        for _ in range(args.warmup):
+            updates = sparse_mean_apply(target, indices, deltas, offsets, -1.0, 1.0, reps)
+        times = []
+        for _ in range(args.steps):
+            target.copy_(base)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record()
+            updates = sparse_mean_apply(target, indices, deltas, offsets, -1.0, 1.0, reps)
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        ms = float(np.mean(times))
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t[0])
+        entries = int(offsets[-1])
+        alg = 8.0 * entries + (8.0 + 4.0 * replicas) * updates
+        hbm = alg / (ms / 1000.0) / 1e9
+        if rank == 0:
+            line = {"metric": "sparse delta apply + replica sync (config 5)", "density": density, "n_gpus": world,
+                    "stories": stories, "replicas": replicas, "elements": n, "entries": entries,
+                    "merged": updates, "apply_ms": round(ms, 4), "steps": args.steps, "warmup": args.warmup,
+                    "roofline": {"bound": "hbm", "achieved": round(hbm, 1), "peak": peak, "unit": "GB/s",
+                                 "frac": round(hbm / peak, 4), "peak_source": peak_kind,
+                                 "algorithmic_bytes": alg},
+                    "nvlink": {"gather_ms": round(gather_ms, 4), "bytes_received_per_gpu": nvlink_bytes,
+                               "GB_per_s": round(nvlink_bytes / (gather_ms / 1000.0) / 1e9, 1) if gather_ms else None},
+                    "l2": "target + replicas exceed L2"}
+            print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -194,7 +311,15 @@ def main() -> None:
     ap.add_argument("--cpu-stories", type=int, default=16)
     ap.add_argument("--cpu-bytes", type=int, default=0, help="fixed CPU sample story length (0: workload's range)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--micro", choices=["sparse-apply"], default=None,
+                    help="run a microbenchmark instead of the training step (config 5)")
+    ap.add_argument("--densities", default="0.001,0.01,0.1")
+    ap.add_argument("--micro-stories", type=int, default=32)
+    ap.add_argument("--micro-replicas", type=int, default=8)
     args = ap.parse_args()
+    if args.micro == "sparse-apply":
+        run_sparse_apply_micro(args)
+        return
 
     from leo_b200.configs import WORKLOADS
 
