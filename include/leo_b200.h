@@ -138,7 +138,10 @@ int leo_b200_reset_perf_stats(LeoB200Device* device);
 
 /* Execution geometry only (results do not depend on it): CTAs per thread-block
    cluster for story lanes and for the canonical replay lane; 0 picks the
-   default (the largest size whose clusters all fit at once).  The reference's
+   default (story: re-divided by lane load, see leo_b200_set_story_chunk;
+   replay: a 16-CTA cluster, or the whole GPU -- one CTA per SM with grid-wide
+   phase barriers -- when the replay lane's last reported work per step is
+   large).  LEO_B200_WHOLE_GPU forces the whole-GPU replay launch.  The reference's
    execution tuner chooses the analogous geometry (crates/leo-core/src/cuda_plan.rs:189-453). */
 int leo_b200_set_cluster_sizes(LeoB200Device* device, uint32_t story_cluster, uint32_t replay_cluster);
 

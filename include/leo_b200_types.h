@@ -184,6 +184,10 @@ typedef struct LeoB200ShardStory {
     uint64_t story_bytes;
 } LeoB200ShardStory;
 
+/* Replay geometry of leo_b200_set_cluster_sizes: the replay lane over the
+   whole GPU, one CTA per SM with grid-wide phase barriers. */
+#define LEO_B200_WHOLE_GPU 0xFFFFFFFFu
+
 /* Fixed tensors merged at the batch end, in merge order. */
 #define LEO_B200_FIXED_TENSORS 6
 
@@ -233,6 +237,7 @@ typedef struct LeoB200PerfStats {
     uint32_t story_cluster;
     uint32_t replay_cluster;
     uint64_t story_lane_launches[5]; /* story-pass lane launches at cluster size 1, 2, 4, 8, 16 */
+    uint64_t whole_gpu_launches;     /* replay launches over the whole GPU (one CTA per SM) */
     int32_t fit_clusters[3];         /* co-resident clusters of 4, 8 and 16 CTAs */
     int32_t sm_count;
 } LeoB200PerfStats;

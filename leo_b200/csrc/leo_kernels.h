@@ -13,6 +13,11 @@ cudaError_t leo_launch_wavefront(const LaneState* lanes, int lane_count, uint32_
                                  uint32_t end, const KernelConsts& kc, cudaStream_t stream);
 size_t leo_wavefront_smem_bytes(const KernelConsts& kc);
 cudaError_t leo_wavefront_configure();
+// One lane over `ctas` CTAs (one per SM) in a cooperative launch.
+cudaError_t leo_launch_wavefront_grid(const LaneState* lane, uint32_t ctas, uint32_t begin, uint32_t end,
+                                      const KernelConsts& kc, cudaStream_t stream);
+// CTAs of the whole-GPU launch that can be resident at once (0: none).
+cudaError_t leo_wavefront_grid_ctas(const KernelConsts& kc, int sms, int* out);
 // Clusters of `cluster` CTAs that can be resident at once.
 cudaError_t leo_wavefront_max_clusters(uint32_t cluster, const KernelConsts& kc, int* out);
 

@@ -144,6 +144,8 @@ struct LeoB200Device {
     // lane table of one chunk's launches, and streams for concurrent launches.
     int sm_count = 0;
     int fit16 = 0, fit8 = 0, fit4 = 0;  // co-resident clusters of 16 / 8 / 4 CTAs
+    int grid_ctas = 0;                  // CTAs of the whole-GPU replay launch (0: unavailable)
+    uint32_t replay_load = 0;           // work per step the replay lane reported last
     uint32_t story_chunk = 32;        // steps per story-pass launch while lane loads are skewed
     uint32_t* d_lane_load = nullptr;  // [max_lanes + 1], last entry: replay lane
     LaneState* d_group_table = nullptr;
@@ -512,13 +514,28 @@ uint32_t pick_cluster(LeoB200Device& dev, uint32_t lanes, uint32_t request, uint
 
 // Runs steps [begin, end) of every lane in `d_lanes` with one persistent
 // wavefront launch, timed with CUDA events on the backend's stream.
+// Replay steps whose reported work per step is above this use the whole GPU
+// (one CTA per SM, grid barriers) instead of one 16-CTA cluster: a grid
+// barrier costs a few microseconds more, which pays off once a step moves
+// more than ~50k units of work (fitted to measured replay steps).
+constexpr uint32_t kWholeGpuLoad = 50000;
+
 void run_steps(LeoB200Device& dev, const LaneState* d_lanes, int lane_count, uint32_t begin, uint32_t end,
                bool story) {
     if (end <= begin || lane_count == 0) return;
-    uint32_t cluster = story ? pick_cluster(dev, (uint32_t)lane_count, dev.story_cluster_request, 16)
-                             : pick_cluster(dev, 1, dev.replay_cluster_request, 16);
+    const bool whole_gpu = !story && lane_count == 1 && dev.grid_ctas > 0 &&
+                           (dev.replay_cluster_request == LEO_B200_WHOLE_GPU ||
+                            (dev.replay_cluster_request == 0 && dev.replay_load > kWholeGpuLoad));
+    uint32_t cluster = 0;
+    if (!whole_gpu)
+        cluster = story ? pick_cluster(dev, (uint32_t)lane_count, dev.story_cluster_request, 16)
+                        : pick_cluster(dev, 1, dev.replay_cluster_request == LEO_B200_WHOLE_GPU
+                                                   ? 0u : dev.replay_cluster_request, 16);
     CUDA_CHECK(cudaEventRecord(dev.wave_start, dev.stream));
-    CUDA_CHECK(leo_launch_wavefront(d_lanes, lane_count, cluster, begin, end, dev.kc, dev.stream));
+    if (whole_gpu)
+        CUDA_CHECK(leo_launch_wavefront_grid(d_lanes, (uint32_t)dev.grid_ctas, begin, end, dev.kc, dev.stream));
+    else
+        CUDA_CHECK(leo_launch_wavefront(d_lanes, lane_count, cluster, begin, end, dev.kc, dev.stream));
     CUDA_CHECK(cudaGetLastError());
     CUDA_CHECK(cudaEventRecord(dev.wave_stop, dev.stream));
     CUDA_CHECK(cudaEventSynchronize(dev.wave_stop));
@@ -532,7 +549,10 @@ void run_steps(LeoB200Device& dev, const LaneState* d_lanes, int lane_count, uin
         dev.perf.story_wavefront_ms += ms;
         dev.perf.story_cluster = cluster;
     } else {
-        dev.perf.replay_cluster = cluster;
+        dev.perf.replay_cluster = whole_gpu ? (uint32_t)dev.grid_ctas : cluster;
+        if (whole_gpu) dev.perf.whole_gpu_launches += 1;
+        if (lane_count == 1)
+            CUDA_CHECK(cudaMemcpy(&dev.replay_load, dev.d_lane_load + dev.lane_capacity, 4, cudaMemcpyDeviceToHost));
     }
 }
 
@@ -1774,6 +1794,10 @@ int leo_b200_open(int device, const LeoB200HostModel* canonical, uint32_t max_la
             dev->fit4 = 0;
         }
         dev->replay->st.load_out = dev->d_lane_load + max_lanes;
+        if (leo_wavefront_grid_ctas(dev->kc, dev->sm_count, &dev->grid_ctas) != cudaSuccess) {
+            cudaGetLastError();
+            dev->grid_ctas = 0;
+        }
         upload_model(*dev, *canonical);
         *out = dev.release();
         return 0;
@@ -2200,8 +2224,12 @@ int leo_b200_lane_array(LeoB200Device* dev, uint32_t lane, const char* name, voi
 
 int leo_b200_set_cluster_sizes(LeoB200Device* dev, uint32_t story_cluster, uint32_t replay_cluster) {
     auto ok = [](uint32_t c) { return c == 0 || c == 1 || c == 2 || c == 4 || c == 8 || c == 16; };
-    if (!ok(story_cluster) || !ok(replay_cluster)) {
-        g_error = "cluster sizes must be 0 (default), 1, 2, 4, 8 or 16";
+    if (!ok(story_cluster) || !(ok(replay_cluster) || replay_cluster == LEO_B200_WHOLE_GPU)) {
+        g_error = "cluster sizes must be 0 (default), 1, 2, 4, 8 or 16 (replay also LEO_B200_WHOLE_GPU)";
+        return -1;
+    }
+    if (replay_cluster == LEO_B200_WHOLE_GPU && dev->grid_ctas == 0) {
+        g_error = "the whole-GPU replay launch is not available on this device";
         return -1;
     }
     dev->story_cluster_request = story_cluster;

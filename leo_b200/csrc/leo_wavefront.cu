@@ -1,12 +1,14 @@
 // Persistent per-byte wavefront for sm_100a.
 //
 // One thread-block cluster owns one lane (a logical story worker, or the
-// canonical replay lane) and runs a whole step schedule in one launch.  The
-// phases of every step are separated by cluster barriers
+// canonical replay lane) and runs a span of its step schedule in one launch.
+// The phases of every step are separated by cluster barriers
 // (barrier.cluster.arrive.release / wait.acquire) instead of kernel
 // boundaries or grid-wide syncs: lanes are independent until the batch end,
 // so no lane ever waits for another and no story is held in lockstep with the
-// longest one.  Per-lane counters live in global memory (L2).
+// longest one.  The replay lane alone may instead run over the whole GPU
+// (leo_wavefront_grid_kernel, grid barriers) when its steps are heavy.
+// Per-lane counters live in global memory (L2).
 //
 // Reference counterparts (crates/leo-core/src/runtime.rs = CPU,
 // crates/leo-core/src/cuda_kernels.cu = the reference's GPU wavefront
@@ -1501,14 +1503,12 @@ __device__ __forceinline__ unsigned long long clock_now() { return clock64(); }
 }  // namespace
 
 // ---------------------------------------------------------------------------
-// The persistent wavefront: cluster blockIdx.x / C runs lane `cluster` through
-// steps [begin, end) of its schedule.
-__global__ void __launch_bounds__(kThreads, 1)
-    leo_wavefront_kernel(const LaneState* __restrict__ lanes, uint32_t begin, uint32_t end, KernelConsts kc) {
-    extern __shared__ unsigned long long smem_sorted[];
-    cg::cluster_group cluster = cg::this_cluster();
-    const uint32_t C = cluster.num_blocks();
-    const uint32_t rank = cluster.block_rank();
+// The persistent wavefront: the C CTAs of group blockIdx.x / C run that lane
+// through steps [begin, end) of its schedule, `sync` separating the phases.
+template <typename Sync>
+__device__ __forceinline__ void wavefront_steps(const LaneState* __restrict__ lanes, uint32_t begin, uint32_t end,
+                                                const KernelConsts& kc, uint32_t C, uint32_t rank, Sync sync,
+                                                unsigned long long* smem_sorted) {
     const LaneState& ln = lanes[blockIdx.x / C];
     LaneScalars* sc = ln.sc;
     const uint32_t steps = sc->steps;
@@ -1531,25 +1531,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         // deliver; the cluster's last warp first resolves the context
         if (rank == C - 1 && (threadIdx.x >> 5) == kWarps - 1) context_resolve_warp(ln, s, kc, symbol, frozen);
         phase_deliver(ln, s, kc, worker, workers, !frozen, symbol);
-        cluster.sync();
+        sync();
         mark(0);
         phase_settle(ln, s, kc, worker, workers, rank, C, reinterpret_cast<uint32_t*>(smem_sorted));
-        cluster.sync();
+        sync();
         mark(1);
         for (uint32_t h = worker; h < kc.topo.hubs; h += workers) ln.hub_count[h] = 0;
         if (worker == 0) sc->hub_next = 0;
         phase_blocks(ln, kc, gwarp, gwarps);
-        cluster.sync();
+        sync();
         mark(2);
         if (rank == 0) phase_assemble(ln, s, kc, smem_sorted);
-        cluster.sync();
+        sync();
         mark(3);
         if (!frozen) {
             phase_surrogate(ln, s, kc, worker, workers);
-            cluster.sync();
+            sync();
             mark(4);
             phase_eligible(ln, s, kc, worker, workers);
-            cluster.sync();
+            sync();
             mark(5);
         }
         // emit beside the forward pass (the first CTA runs the forward)
@@ -1567,18 +1567,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!forward) sc->step_flags = 0;
             step_epilogue(ln, s, true);
         }
-        cluster.sync();
+        sync();
         mark(6);
         if (!frozen) {
             phase_learn(ln, s, kc, worker, workers, gwarp, gwarps, reinterpret_cast<float (*)[32][33]>(smem_sorted));
-            cluster.sync();
+            sync();
             mark(7);
             phase_plasticity(ln, kc, worker, workers);
-            cluster.sync();
+            sync();
             mark(8);
             phase_inhibit(ln, s, kc, worker, workers);
             if (worker == 0) step_epilogue(ln, s, false);
-            cluster.sync();
+            sync();
             mark(9);
         }
     }
@@ -1591,6 +1591,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             *ln.load_out = load > 0xffffffffull ? 0xffffffffu : (uint32_t)load;
         }
     }
+}
+
+// A thread-block cluster per lane (phases separated by cluster barriers).
+__global__ void __launch_bounds__(kThreads, 1)
+    leo_wavefront_kernel(const LaneState* __restrict__ lanes, uint32_t begin, uint32_t end, KernelConsts kc) {
+    extern __shared__ unsigned long long smem_sorted[];
+    cg::cluster_group cluster = cg::this_cluster();
+    wavefront_steps(lanes, begin, end, kc, cluster.num_blocks(), cluster.block_rank(), [&] { cluster.sync(); },
+                    smem_sorted);
+}
+
+// One lane over the whole GPU: one CTA per SM in a cooperative launch, phases
+// separated by grid barriers.  For replay steps whose work (millions of
+// eligible slots on large models) needs more bandwidth than one cluster's SMs.
+__global__ void __launch_bounds__(kThreads, 1)
+    leo_wavefront_grid_kernel(const LaneState* __restrict__ lanes, uint32_t begin, uint32_t end, KernelConsts kc) {
+    extern __shared__ unsigned long long smem_sorted[];
+    cg::grid_group grid = cg::this_grid();
+    wavefront_steps(lanes, begin, end, kc, gridDim.x, blockIdx.x, [&] { grid.sync(); }, smem_sorted);
 }
 
 // Dynamic shared memory: the assemble phase's sort buffer and the learn
@@ -1617,6 +1636,8 @@ size_t leo_wavefront_smem_bytes(const KernelConsts& kc) {
 cudaError_t leo_wavefront_configure() {
     cudaError_t e = cudaFuncSetAttribute(leo_wavefront_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(leo_wavefront_grid_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(leo_wavefront_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
 }
 
@@ -1636,6 +1657,29 @@ cudaError_t leo_launch_wavefront(const LaneState* lanes, int lane_count, uint32_
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, leo_wavefront_kernel, lanes, begin, end, kc);
+}
+
+cudaError_t leo_launch_wavefront_grid(const LaneState* lane, uint32_t ctas, uint32_t begin, uint32_t end,
+                                      const KernelConsts& kc, cudaStream_t stream) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ctas, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = leo_wavefront_smem_bytes(kc);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, leo_wavefront_grid_kernel, lane, begin, end, kc);
+}
+
+cudaError_t leo_wavefront_grid_ctas(const KernelConsts& kc, int sms, int* out) {
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, leo_wavefront_grid_kernel, kThreads,
+                                                                  leo_wavefront_smem_bytes(kc));
+    *out = per_sm >= 1 ? sms : 0;
+    return e;
 }
 
 cudaError_t leo_wavefront_max_clusters(uint32_t cluster, const KernelConsts& kc, int* out) {

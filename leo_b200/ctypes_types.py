@@ -130,6 +130,7 @@ class LeoB200ShardStory(C.Structure):
 
 
 FIXED_TENSORS = 6
+WHOLE_GPU = 0xFFFFFFFF
 
 
 class LeoB200BatchReport(C.Structure):
@@ -177,6 +178,7 @@ class LeoB200PerfStats(C.Structure):
         ("story_cluster", C.c_uint32),
         ("replay_cluster", C.c_uint32),
         ("story_lane_launches", C.c_uint64 * 5),
+        ("whole_gpu_launches", C.c_uint64),
         ("fit_clusters", C.c_int32 * 3),
         ("sm_count", C.c_int32),
     ]

@@ -91,9 +91,12 @@ def test_gpu_story_batch_matches_golden(native_lib, name):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("geometry", [(1, 1, 64), (4, 16, 64), (0, 2, 7), (0, 0, 1)],
-                         ids=["fixed1", "fixed4-replay16", "adaptive-chunk7", "adaptive-chunk1"])
-def test_gpu_result_does_not_depend_on_geometry(native_lib, geometry):
+@pytest.mark.parametrize("geometry,case_name", [
+    ((1, 1, 64), "baseline1"), ((4, 16, 64), "baseline1"), ((0, 2, 7), "baseline1"), ((0, 0, 1), "baseline1"),
+    ((0, 0xFFFFFFFF, 32), "baseline1"), ((0, 0xFFFFFFFF, 32), "baseline3-short"), ((2, 0xFFFFFFFF, 16), "test-8"),
+], ids=["fixed1", "fixed4-replay16", "adaptive-chunk7", "adaptive-chunk1", "whole-gpu-replay",
+        "whole-gpu-replay-hubs", "whole-gpu-replay-test8"])
+def test_gpu_result_does_not_depend_on_geometry(native_lib, geometry, case_name):
     """Cluster sizes and the adaptive story-pass chunking change only how the
     work is spread over SMs: the golden state hashes hold for every geometry."""
     from leo_b200.backend import GpuBackend
@@ -101,7 +104,7 @@ def test_gpu_result_does_not_depend_on_geometry(native_lib, geometry):
     from leo_b200.model import HostModel
 
     story_c, replay_c, chunk = geometry
-    case = CASES["baseline1"]
+    case = CASES[case_name]
     w, batches = _stories(case)
     model = HostModel.initialize(w.config, w.topology)
     with GpuBackend(model, device=0, max_lanes=case["stories_per_batch"]) as backend:
