@@ -648,7 +648,6 @@ __device__ void settle_hubs(const LaneState& ln, uint32_t s, const KernelConsts&
         if (lane == 0) h = atomicAdd(&ln.sc->hub_next, 1u);
         h = __shfl_sync(0xffffffffu, h, 0);
         if (h >= H || kc.topo.hub_capacity[h] <= kc.topo.hub_thread_events) break;
-        {
         const uint32_t k = ln.hub_count[h];
         if (k <= kc.topo.hub_thread_events || k > kc.topo.hub_cta_events) continue;
         const uint32_t n = kc.topo.hub_neuron[h];
@@ -681,7 +680,6 @@ __device__ void settle_hubs(const LaneState& ln, uint32_t s, const KernelConsts&
                     a3 = __shfl_sync(0xffffffffu, a, 3);
         if (lane == 0) settle_integrate(ln, kc, n, s, cold, make_float4(a, a1, a2, a3), pop_inh, rotation);
         __syncwarp();
-        }
     }
 }
 
