@@ -231,7 +231,7 @@ __device__ __forceinline__ void add_destination(const LaneState& ln, uint32_t n,
 // slot choice per order is independent (orders own disjoint partitions); lane
 // 0 then forms the confidence scales in order.
 __device__ void context_resolve_warp(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t symbol,
-                                     bool frozen) {
+                                     bool frozen, bool forward) {
     LaneScalars* sc = ln.sc;
     const LeoConfig& c = kc.cfg;
     const uint32_t lane = threadIdx.x & 31u, K = kc.topo.k;
@@ -257,6 +257,10 @@ __device__ void context_resolve_warp(const LaneState& ln, uint32_t s, const Kern
             enabled = (float)(uint32_t)(v >> 40) / (float)(1u << 24) >= kc.dropout_rate;
         }
     }
+    // A frozen step without a target runs no forward pass and no learning, the
+    // only readers of the resolved slots, and resolving never allocates when
+    // frozen: only the history push matters for it.
+    if (!forward) enabled = false;
     bool allocate = !frozen && enabled;
     uint32_t available = len < K ? len : K;
     int32_t slot = -1;
@@ -476,21 +480,32 @@ __device__ __forceinline__ void settle_decay(const LeoConfig& c, uint32_t s, Neu
     }
 }
 
+// Per-neuron values settle needs after the branch sums, loaded up front so
+// their latency overlaps the event-list walk.
+struct SettlePre {
+    float threshold, excitability;
+    uint32_t refractory_until;
+};
+
+__device__ __forceinline__ SettlePre settle_preload(const LaneState& ln, const KernelConsts& kc, uint32_t n) {
+    return SettlePre{ln.p.threshold[n], kc.topo.excitability[n], ln.hot[n].refractory_until};
+}
+
 // Integration and block candidate after the branch sums; stores the neuron.
 __device__ __forceinline__ void settle_integrate(const LaneState& ln, const KernelConsts& kc, uint32_t n, uint32_t s,
-                                                 NeuronCold cold, float4 br, float pop_inh, uint32_t rotation) {
+                                                 NeuronCold cold, float4 br, float pop_inh, uint32_t rotation,
+                                                 SettlePre pre) {
     const uint32_t npb = kc.topo.npb, n_count = kc.topo.n;
-    NeuronHot& hot = ln.hot[n];
-    hot.activation = 0.0f;
-    bool refractory = hot.refractory_until > s;
+    ln.hot[n].activation = 0.0f;
+    bool refractory = pre.refractory_until > s;
     if (!refractory) {
         float gate = clampf(br.w, 0.0f, 1.0f);
         float inhibitory = br.y;
         float net = br.x + br.z * gate + inhibitory;
         float adaptation = sum3(cold.adaptation[0], cold.adaptation[1], cold.adaptation[2]);
-        float drive = kc.topo.excitability[n] * net - cold.fatigue - adaptation - pop_inh;
+        float drive = pre.excitability * net - cold.fatigue - adaptation - pop_inh;
         cold.membrane = cold.membrane + drive;
-        float act = clampf(cold.membrane - ln.p.threshold[n], 0.0f, 1.0f);
+        float act = clampf(cold.membrane - pre.threshold, 0.0f, 1.0f);
         if (act > 0.0f) {
             uint32_t blk = n / npb;
             uint32_t pos = atomicAdd(&ln.block_cand_count[blk], 1u);
@@ -635,7 +650,7 @@ __device__ void settle_hubs(const LaneState& ln, uint32_t s, const KernelConsts&
         if (tid < 4) s_acc[tid] = ordered_sum(vals, s_bound[tid], s_bound[tid + 1], s_acc[tid]);
         __syncthreads();
         if (tid == 0) settle_integrate(ln, kc, n, s, s_cold, make_float4(s_acc[0], s_acc[1], s_acc[2], s_acc[3]),
-                                       pop_inh, rotation);
+                                       pop_inh, rotation, settle_preload(ln, kc, n));
         __syncthreads();
     }
     // Medium hubs: one warp each, sorted in the warp's slice of shared memory.
@@ -678,7 +693,8 @@ __device__ void settle_hubs(const LaneState& ln, uint32_t s, const KernelConsts&
         if (lane < 4) a = ordered_sum(wvals, bound, next_bound, lane == 0 ? br.x : (lane == 1 ? br.y : (lane == 2 ? br.z : br.w)));
         const float a1 = __shfl_sync(0xffffffffu, a, 1), a2 = __shfl_sync(0xffffffffu, a, 2),
                     a3 = __shfl_sync(0xffffffffu, a, 3);
-        if (lane == 0) settle_integrate(ln, kc, n, s, cold, make_float4(a, a1, a2, a3), pop_inh, rotation);
+        if (lane == 0)
+            settle_integrate(ln, kc, n, s, cold, make_float4(a, a1, a2, a3), pop_inh, rotation, settle_preload(ln, kc, n));
         __syncwarp();
     }
 }
@@ -727,12 +743,14 @@ __device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts
                 settle_decay(c, s, cold, br);
                 float acc[4] = {br.x, br.y, br.z, br.w};
                 for (uint32_t x = 0; x < k; ++x) acc[e[x] >> 30] = acc[e[x] >> 30] + vals[x];
-                settle_integrate(ln, kc, n, s, cold, make_float4(acc[0], acc[1], acc[2], acc[3]), pop_inh, rotation);
+                settle_integrate(ln, kc, n, s, cold, make_float4(acc[0], acc[1], acc[2], acc[3]), pop_inh, rotation,
+                                 settle_preload(ln, kc, n));
                 continue;
             }
         }
         cold = ln.cold[n];
         br = ln.branches[n];
+        const SettlePre pre = settle_preload(ln, kc, n);
         settle_decay(c, s, cold, br);
         float acc[4] = {br.x, br.y, br.z, br.w};
         // The four (target, branch) event lists, walked in lockstep so their
@@ -812,7 +830,7 @@ __device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts
             }
         }
         br = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        settle_integrate(ln, kc, n, s, cold, br, pop_inh, rotation);
+        settle_integrate(ln, kc, n, s, cold, br, pop_inh, rotation, pre);
     }
 }
 
@@ -1527,7 +1545,8 @@ __device__ __forceinline__ void wavefront_steps(const LaneState* __restrict__ la
         const bool frozen = LEO_SCHED_PERMISSION(sched) == kFrozen;
         const uint32_t symbol = LEO_SCHED_SYMBOL(sched);
         // deliver; the cluster's last warp first resolves the context
-        if (rank == C - 1 && (threadIdx.x >> 5) == kWarps - 1) context_resolve_warp(ln, s, kc, symbol, frozen);
+        if (rank == C - 1 && (threadIdx.x >> 5) == kWarps - 1)
+            context_resolve_warp(ln, s, kc, symbol, frozen, !frozen || LEO_SCHED_TARGET(sched) >= 0);
         phase_deliver(ln, s, kc, worker, workers, !frozen, symbol);
         sync();
         mark(0);
