@@ -46,6 +46,11 @@ class GpuBackend:
     """One CUDA device holding a canonical model and up to ``max_lanes`` story lanes."""
 
     def __init__(self, model: HostModel, device: int = 0, max_lanes: int = 64):
+        if model.config.replay_stateful_batch:
+            # Streaming replay (one trajectory carried across the selected
+            # ranges, crates/leo-cli/src/training.rs:74-90) is a different
+            # replay policy from the serial canonical replay built here.
+            raise native.LeoError("replay.stateful_batch is not supported by this backend")
         self.config: Config = model.config
         self.device = device
         self.model = model.copy()
