@@ -47,6 +47,10 @@
 #define LEO_SCHED_TARGET(w) ((int)(((w) >> 9) & 0x3ffu) - 1)
 #define LEO_SCHED_PERMISSION(w) (((w) >> 19) & 3u)
 
+__host__ __device__ __forceinline__ uint32_t leo_schedule_word(uint32_t symbol, int target, uint32_t permission) {
+    return symbol | ((uint32_t)(target + 1) << 9) | (permission << 19);
+}
+
 // Error flag bits (reported to the host after a batch).
 #define LEO_ERR_NONFINITE_BIAS 1u
 #define LEO_ERR_NONFINITE_OUTPUT 2u

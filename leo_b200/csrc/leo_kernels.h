@@ -21,6 +21,11 @@ cudaError_t leo_wavefront_grid_ctas(const KernelConsts& kc, int sms, int* out);
 // Clusters of `cluster` CTAs that can be resident at once.
 cudaError_t leo_wavefront_max_clusters(uint32_t cluster, const KernelConsts& kc, int* out);
 
+// Every lane's step schedule from the batch's story bytes (leo_schedule.cu):
+// lane i's story is bytes[offsets[i], offsets[i + 1]), written to lanes[i].schedule.
+cudaError_t leo_launch_build_schedules(const uint8_t* bytes, const uint64_t* offsets, const LaneState* lanes,
+                                       uint32_t count, uint32_t permission, cudaStream_t stream);
+
 // Batch-end sparse merge of one fixed f32 tensor (threshold, recurrent, input,
 // output rows, bias, context output): see leo_merge_kernels.cu.
 struct MergeTensor {

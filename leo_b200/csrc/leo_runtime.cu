@@ -123,6 +123,10 @@ struct LeoB200Device {
     int batch_permission = LEO_B200_TRAINING;
     bool single_story = false;
     std::vector<std::vector<uint8_t>> batch_stories;
+    // The batch's story bytes staged for the on-device schedule builder.
+    std::vector<uint8_t> h_stage;
+    std::unique_ptr<DevMem> d_stage;
+    size_t stage_capacity = 0;
     // sharded batch (multi-GPU data parallelism): this rank's lanes run
     // stories [shard_first, shard_first + batch_lanes) of batch_stories
     bool shard_mode = false;
@@ -170,7 +174,7 @@ int fail(const std::exception& e) {
 }
 
 uint32_t schedule_word(uint32_t symbol, int target, int permission) {
-    return symbol | ((uint32_t)(target + 1) << 9) | ((uint32_t)permission << 19);
+    return leo_schedule_word(symbol, target, (uint32_t)permission);
 }
 
 KernelConsts make_consts(LeoB200Device& dev) {
@@ -1180,14 +1184,33 @@ void replay_story(LeoB200Device& dev, const std::vector<uint8_t>& story, const s
     if (report) report->replay_segments += ranges.size();
 }
 
-void story_schedule(const std::vector<uint8_t>& story, int permission, std::vector<uint32_t>& out) {
-    out.clear();
-    size_t len = story.size();
-    for (size_t s = 0; s <= len; ++s) {
-        uint32_t symbol = s == 0 ? LEO_B200_BEGIN_DOCUMENT : story[s - 1];
-        int target = s < len ? story[s] : (int)LEO_B200_END_DOCUMENT;
-        out.push_back(schedule_word(symbol, target, permission));
+// Uploads stories [first, first + count) of the batch in one copy (offsets,
+// then bytes) and builds their schedules on the device into the schedule
+// buffers named by the device LaneState table `table` (already uploaded on
+// the stream).  Every lane's schedule buffer holds at least story length + 1.
+void build_schedules(LeoB200Device& dev, uint32_t first, uint32_t count, int permission, const LaneState* table) {
+    std::vector<uint64_t> offsets(count + 1, 0);
+    for (uint32_t i = 0; i < count; ++i) offsets[i + 1] = offsets[i] + dev.batch_stories[first + i].size();
+    const size_t head = offsets.size() * sizeof(uint64_t);
+    const size_t need = head + offsets[count];
+    dev.h_stage.resize(need);
+    std::memcpy(dev.h_stage.data(), offsets.data(), head);
+    for (uint32_t i = 0; i < count; ++i) {
+        const auto& story = dev.batch_stories[first + i];
+        if (!story.empty()) std::memcpy(dev.h_stage.data() + head + offsets[i], story.data(), story.size());
     }
+    if (dev.stage_capacity < need) {
+        const size_t cap = std::max<size_t>({need, 2 * dev.stage_capacity, (size_t)1 << 16});
+        dev.d_stage.reset();
+        auto m = std::make_unique<DevMem>();
+        CUDA_CHECK(cudaMalloc(&m->p, cap));
+        dev.d_stage = std::move(m);
+        dev.stage_capacity = cap;
+    }
+    uint8_t* d = static_cast<uint8_t*>(dev.d_stage->p);
+    CUDA_CHECK(cudaMemcpyAsync(d, dev.h_stage.data(), need, cudaMemcpyHostToDevice, dev.stream));
+    CUDA_CHECK(leo_launch_build_schedules(d + head, reinterpret_cast<const uint64_t*>(d), table, count,
+                                          (uint32_t)permission, dev.stream));
 }
 
 // ---------------------------------------------------------------- batch
@@ -1202,27 +1225,25 @@ void batch_begin(LeoB200Device& dev, const uint8_t* bytes, const uint64_t* offse
     dev.single_story = stories == 1;
     dev.steps_done = 0;
     dev.batch_steps = 0;
-    std::vector<uint32_t> sched;
     if (dev.single_story) {
         // training.rs:1548-1581: one story trains the canonical runtime directly.
-        story_schedule(dev.batch_stories[0], permission, sched);
+        const auto& story = dev.batch_stories[0];
+        const uint32_t steps = story.empty() ? 0 : (uint32_t)story.size() + 1;
         Lane& rl = *dev.replay;
-        ensure_schedule(rl, sched.size());
-        CUDA_CHECK(cudaMemcpyAsync(rl.schedule, sched.data(), sched.size() * 4, cudaMemcpyHostToDevice, dev.stream));
-        reset_lane(dev, rl, dev.canonical_tick, (uint32_t)(dev.batch_stories[0].empty() ? 0 : sched.size()));
+        ensure_schedule(rl, story.size() + 1);
+        reset_lane(dev, rl, dev.canonical_tick, steps);
         CUDA_CHECK(cudaMemcpyAsync(dev.d_replay, &rl.st, sizeof(LaneState), cudaMemcpyHostToDevice, dev.stream));
+        build_schedules(dev, 0, 1, permission, dev.d_replay);
         dev.batch_lanes = 0;
-        dev.batch_steps = dev.batch_stories[0].empty() ? 0 : (uint32_t)sched.size();
+        dev.batch_steps = steps;
     } else {
         ensure_lanes(dev, stories);
         dev.lane_steps.assign(stories, 0u);
         for (uint32_t i = 0; i < stories; ++i) {
             Lane& lane = *dev.lanes[i];
             const auto& story = dev.batch_stories[i];
-            story_schedule(story, permission, sched);
-            uint32_t steps = story.empty() ? 0 : (uint32_t)sched.size();
-            ensure_schedule(lane, sched.size());
-            CUDA_CHECK(cudaMemcpyAsync(lane.schedule, sched.data(), sched.size() * 4, cudaMemcpyHostToDevice, dev.stream));
+            const uint32_t steps = story.empty() ? 0 : (uint32_t)story.size() + 1;
+            ensure_schedule(lane, story.size() + 1);
             // Forked workers start a fresh runtime at tick 0 (backend.rs:486-488).
             reset_lane(dev, lane, 0ull, steps);
             dev.batch_steps = std::max(dev.batch_steps, steps);
@@ -1230,6 +1251,7 @@ void batch_begin(LeoB200Device& dev, const uint8_t* bytes, const uint64_t* offse
         }
         dev.batch_lanes = stories;
         upload_lane_table(dev);
+        build_schedules(dev, 0, stories, permission, dev.d_lanes);
     }
     CUDA_CHECK(cudaEventRecord(dev.batch_start, dev.stream));
     dev.batch_open = true;
@@ -1399,20 +1421,18 @@ void shard_begin(LeoB200Device& dev, const uint8_t* bytes, const uint64_t* offse
     dev.batch_steps = 0;
     ensure_lanes(dev, count);
     dev.lane_steps.assign(count, 0u);
-    std::vector<uint32_t> sched;
     for (uint32_t i = 0; i < count; ++i) {
         Lane& lane = *dev.lanes[i];
         const auto& story = dev.batch_stories[first + i];
-        story_schedule(story, permission, sched);
-        uint32_t steps = story.empty() ? 0 : (uint32_t)sched.size();
-        ensure_schedule(lane, sched.size());
-        CUDA_CHECK(cudaMemcpyAsync(lane.schedule, sched.data(), sched.size() * 4, cudaMemcpyHostToDevice, dev.stream));
+        const uint32_t steps = story.empty() ? 0 : (uint32_t)story.size() + 1;
+        ensure_schedule(lane, story.size() + 1);
         reset_lane(dev, lane, 0ull, steps);
         dev.batch_steps = std::max(dev.batch_steps, steps);
         dev.lane_steps[i] = steps;
     }
     dev.batch_lanes = count;
     upload_lane_table(dev);
+    build_schedules(dev, first, count, permission, dev.d_lanes);
     if (!dev.compact_total) {
         const auto specs = fixed_specs(dev.z);
         size_t blocks = 1;
