@@ -441,4 +441,14 @@ int leo_oracle_select_replay_ranges(const float* losses, size_t n, float fractio
     return 0;
 }
 
+// shuffled_story_order (crates/leo-cli/src/training/dataset.rs:9-13): the
+// identity order shuffled by SplitMix64(seed + pass + 1), wrapping.
+void leo_oracle_shuffled_story_order(uint64_t count, uint64_t seed, uint64_t pass, uint64_t* out) {
+    std::vector<uint64_t> order(count);
+    for (uint64_t i = 0; i < count; ++i) order[i] = i;
+    SplitMix64 rng(seed + pass + 1);
+    rng.shuffle(order);
+    std::copy(order.begin(), order.end(), out);
+}
+
 }  // extern "C"

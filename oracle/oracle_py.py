@@ -287,6 +287,14 @@ def sparse_mean_apply(target: np.ndarray, indices: np.ndarray, deltas: np.ndarra
     return updates.value
 
 
+def shuffled_story_order(count: int, seed: int, pass_index: int) -> np.ndarray:
+    """shuffled_story_order (crates/leo-cli/src/training/dataset.rs:9-13)."""
+    out = np.zeros(max(count, 1), dtype=np.uint64)
+    lib().leo_oracle_shuffled_story_order(C.c_uint64(count), C.c_uint64(seed % 2**64), C.c_uint64(pass_index % 2**64),
+                                          out.ctypes.data_as(C.c_void_p))
+    return out[:count]
+
+
 def sha256(data: bytes) -> bytes:
     out = (C.c_uint8 * 32)()
     buf = np.frombuffer(data, dtype=np.uint8).copy() if data else np.zeros(1, np.uint8)
