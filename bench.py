@@ -438,6 +438,9 @@ def main() -> None:
             "e2e": {"value": round(total_bytes / wall, 3), "unit": UNIT, "h2d_bytes_per_step": h2d // args.steps,
                     "d2h_bytes_per_step": d2h // args.steps},
             "roofline": roofline, "clocks": clk, "gpu_launches": int(perf.launches),
+            "batch_end_ms_per_step": {k: round(getattr(perf, k) / args.steps, 2)
+                                      for k in ("collect_ms", "merge_fixed_ms", "merge_context_ms", "replay_ms",
+                                                "replay_sync_ms")},
             "device_gb": round(backend.device_bytes() / 1e9, 3),
         }
         if not args.no_cpu_baseline:

@@ -240,6 +240,13 @@ typedef struct LeoB200PerfStats {
     uint64_t whole_gpu_launches;     /* replay launches over the whole GPU (one CTA per SM) */
     int32_t fit_clusters[3];         /* co-resident clusters of 4, 8 and 16 CTAs */
     int32_t sm_count;
+    /* Host wall time of the batch-end steps, summed over batches (each step
+       ends with a stream synchronize, so wall time covers its device work). */
+    double collect_ms;        /* lane scalars, losses and error flags read back */
+    double merge_fixed_ms;    /* FP64 mean merge of the six fixed tensors */
+    double merge_context_ms;  /* keyed context merge and lane context sync */
+    double replay_ms;         /* serial canonical replay, range selection to last segment */
+    double replay_sync_ms;    /* replay's changed rows into every lane */
 } LeoB200PerfStats;
 
 #ifdef __cplusplus

@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <chrono>
 #include <array>
 #include <cmath>
 #include <cstdio>
@@ -167,6 +168,12 @@ struct LeoB200Device {
 };
 
 namespace {
+
+// Wall milliseconds since `t0`; the batch-end steps it times each end with a
+// stream synchronize.
+double ms_since(std::chrono::steady_clock::time_point t0) {
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+}
 
 int fail(const std::exception& e) {
     g_error = e.what();
@@ -723,21 +730,45 @@ __global__ void gather_context_rows_kernel(const uint32_t* __restrict__ slots, u
     }
 }
 
+// Writes staged context rows (key, observations, embedding) at their slots
+// into the canonical tables and every resident lane.
 __global__ void scatter_context_rows_kernel(const uint32_t* __restrict__ slots, uint32_t count,
-                                            const unsigned long long* __restrict__ src_keys,
-                                            const uint32_t* __restrict__ src_obs, const float* __restrict__ src_emb,
-                                            uint32_t d, const LaneState* lanes, int lane_count) {
-    uint32_t total = count * (d + 1);
+                                            const ContextRow* __restrict__ rows, const float* __restrict__ emb,
+                                            uint32_t d, LaneParams canon, const LaneState* lanes, int lane_count) {
+    const uint32_t total = count * (d + 1);
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-        uint32_t r = i / (d + 1), k = i - r * (d + 1);
-        uint32_t slot = slots[r];
+        const uint32_t r = i / (d + 1), k = i - r * (d + 1);
+        const uint32_t slot = slots[r];
+        if (k == d) {
+            const ContextRow row = rows[r];
+            canon.ctx_keys[slot] = row.key;
+            canon.ctx_obs[slot] = row.obs;
+            for (int l = 0; l < lane_count; ++l) {
+                lanes[l].p.ctx_keys[slot] = row.key;
+                lanes[l].p.ctx_obs[slot] = row.obs;
+            }
+        } else {
+            const float v = emb[(size_t)r * d + k];
+            canon.ctx_emb[(size_t)slot * d + k] = v;
+            for (int l = 0; l < lane_count; ++l) lanes[l].p.ctx_emb[(size_t)slot * d + k] = v;
+        }
+    }
+}
+
+// Copies canonical context rows at `slots` into every resident lane.
+__global__ void broadcast_context_rows_kernel(const uint32_t* __restrict__ slots, uint32_t count, LaneParams canon,
+                                              uint32_t d, const LaneState* lanes, int lane_count) {
+    const uint32_t total = count * (d + 1);
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const uint32_t r = i / (d + 1), k = i - r * (d + 1);
+        const uint32_t slot = slots[r];
         for (int l = 0; l < lane_count; ++l) {
             const LaneParams& p = lanes[l].p;
             if (k == d) {
-                p.ctx_keys[slot] = src_keys[slot];
-                p.ctx_obs[slot] = src_obs[slot];
+                p.ctx_keys[slot] = canon.ctx_keys[slot];
+                p.ctx_obs[slot] = canon.ctx_obs[slot];
             } else {
-                p.ctx_emb[(size_t)slot * d + k] = src_emb[(size_t)slot * d + k];
+                p.ctx_emb[(size_t)slot * d + k] = canon.ctx_emb[(size_t)slot * d + k];
             }
         }
     }
@@ -913,17 +944,23 @@ size_t merge_context_deltas(LeoB200Device& dev, const std::vector<std::vector<Ct
     std::sort(sync.begin(), sync.end());
     sync.erase(std::unique(sync.begin(), sync.end()), sync.end());
     if (!sync.empty()) {
-        for (uint32_t slot : sync) {
-            CUDA_CHECK(cudaMemcpyAsync(dev.canon.ctx_keys + slot, &dev.ctx_keys[slot], 8, cudaMemcpyHostToDevice, dev.stream));
-            CUDA_CHECK(cudaMemcpyAsync(dev.canon.ctx_obs + slot, &dev.ctx_obs[slot], 4, cudaMemcpyHostToDevice, dev.stream));
-            CUDA_CHECK(cudaMemcpyAsync(dev.canon.ctx_emb + (size_t)slot * d, &dev.ctx_emb[(size_t)slot * d], d * 4,
-                                       cudaMemcpyHostToDevice, dev.stream));
+        // Stage the rows from the host mirror and scatter them in one kernel
+        // (three copies for the whole list, not three per slot).
+        const uint32_t n = (uint32_t)sync.size();
+        std::vector<ContextRow> rows(n);
+        std::vector<float> emb((size_t)n * d);
+        for (uint32_t i = 0; i < n; ++i) {
+            const uint32_t slot = sync[i];
+            rows[i] = ContextRow{dev.ctx_keys[slot], dev.ctx_obs[slot]};
+            std::copy_n(dev.ctx_emb.begin() + (size_t)slot * d, d, emb.begin() + (size_t)i * d);
         }
-        uint32_t* d_slots = dev.ctx_sync_slots;
-        CUDA_CHECK(cudaMemcpyAsync(d_slots, sync.data(), sync.size() * 4, cudaMemcpyHostToDevice, dev.stream));
-        uint32_t total = (uint32_t)sync.size() * (d + 1);
+        CUDA_CHECK(cudaMemcpyAsync(dev.ctx_sync_slots, sync.data(), n * 4, cudaMemcpyHostToDevice, dev.stream));
+        CUDA_CHECK(cudaMemcpyAsync(dev.ctx_stage_rows, rows.data(), n * sizeof(ContextRow), cudaMemcpyHostToDevice,
+                                   dev.stream));
+        CUDA_CHECK(cudaMemcpyAsync(dev.ctx_stage_emb, emb.data(), emb.size() * 4, cudaMemcpyHostToDevice, dev.stream));
+        const uint32_t total = n * (d + 1);
         scatter_context_rows_kernel<<<std::max(1u, std::min(total / 256 + 1, 4096u)), 256, 0, dev.stream>>>(
-            d_slots, (uint32_t)sync.size(), dev.canon.ctx_keys, dev.canon.ctx_obs, dev.canon.ctx_emb, d, dev.d_lanes,
+            dev.ctx_sync_slots, n, dev.ctx_stage_rows, dev.ctx_stage_emb, d, dev.canon, dev.d_lanes,
             (int)dev.lanes.size());
         CUDA_CHECK(cudaGetLastError());
         CUDA_CHECK(cudaStreamSynchronize(dev.stream));
@@ -1054,26 +1091,36 @@ void sync_replay_changes(LeoB200Device& dev, const LaneScalars& rs) {
     }
     // Context rows: refresh the host mirror and scatter the canonical rows.
     if (rs.ctx_changed) {
-        std::vector<uint32_t> slots(rs.ctx_changed);
-        CUDA_CHECK(cudaMemcpy(slots.data(), rl.st.ctx_list, slots.size() * 4, cudaMemcpyDeviceToHost));
         // Allocation without a learning step cannot happen on a training
         // replay step, so the changed list covers every slot replay rewrote.
-        for (uint32_t slot : slots) {
-            CUDA_CHECK(cudaMemcpy(&dev.ctx_keys[slot], dev.canon.ctx_keys + slot, 8, cudaMemcpyDeviceToHost));
-            CUDA_CHECK(cudaMemcpy(&dev.ctx_obs[slot], dev.canon.ctx_obs + slot, 4, cudaMemcpyDeviceToHost));
-            CUDA_CHECK(cudaMemcpy(&dev.ctx_emb[(size_t)slot * z.d], dev.canon.ctx_emb + (size_t)slot * z.d, z.d * 4,
-                                  cudaMemcpyDeviceToHost));
-        }
-        uint32_t d = (uint32_t)z.d, total = (uint32_t)slots.size() * (d + 1);
-        if (lane_count > 0)
-            scatter_context_rows_kernel<<<std::max(1u, std::min(total / 256 + 1, 4096u)), 256, 0, dev.stream>>>(
-                rl.st.ctx_list, (uint32_t)slots.size(), dev.canon.ctx_keys, dev.canon.ctx_obs, dev.canon.ctx_emb, d,
-                dev.d_lanes, (int)lane_count);
+        const uint32_t n = rs.ctx_changed, d = (uint32_t)z.d;
+        std::vector<uint32_t> slots(n);
+        std::vector<ContextRow> rows(n);
+        std::vector<float> emb((size_t)n * d);
+        const uint32_t grid = std::max(1u, std::min(n / 128 + 1, 1024u));
+        gather_context_rows_kernel<<<grid, 128, 0, dev.stream>>>(rl.st.ctx_list, n, dev.canon.ctx_keys,
+                                                                dev.canon.ctx_obs, dev.canon.ctx_emb, d,
+                                                                dev.ctx_stage_rows, dev.ctx_stage_emb);
         CUDA_CHECK(cudaGetLastError());
-        clear_marks_kernel<<<std::max(1u, std::min((uint32_t)slots.size() / 256 + 1, 4096u)), 256, 0, dev.stream>>>(
-            rl.st.ctx_list, (uint32_t)slots.size(), rl.st.ctx_mark);
+        CUDA_CHECK(cudaMemcpyAsync(slots.data(), rl.st.ctx_list, n * 4, cudaMemcpyDeviceToHost, dev.stream));
+        CUDA_CHECK(cudaMemcpyAsync(rows.data(), dev.ctx_stage_rows, n * sizeof(ContextRow), cudaMemcpyDeviceToHost,
+                                   dev.stream));
+        CUDA_CHECK(cudaMemcpyAsync(emb.data(), dev.ctx_stage_emb, emb.size() * 4, cudaMemcpyDeviceToHost, dev.stream));
+        const uint32_t total = n * (d + 1);
+        if (lane_count > 0)
+            broadcast_context_rows_kernel<<<std::max(1u, std::min(total / 256 + 1, 4096u)), 256, 0, dev.stream>>>(
+                rl.st.ctx_list, n, dev.canon, d, dev.d_lanes, (int)lane_count);
+        CUDA_CHECK(cudaGetLastError());
+        clear_marks_kernel<<<std::max(1u, std::min(n / 256 + 1, 4096u)), 256, 0, dev.stream>>>(rl.st.ctx_list, n,
+                                                                                              rl.st.ctx_mark);
         CUDA_CHECK(cudaGetLastError());
         CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+        for (uint32_t i = 0; i < n; ++i) {
+            const uint32_t slot = slots[i];
+            dev.ctx_keys[slot] = rows[i].key;
+            dev.ctx_obs[slot] = rows[i].obs;
+            std::copy_n(emb.begin() + (size_t)i * d, d, dev.ctx_emb.begin() + (size_t)slot * d);
+        }
     }
 }
 
@@ -1321,6 +1368,7 @@ void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySu
     } else {
         uint32_t L = dev.batch_lanes;
         std::vector<LaneScalars> scal(L);
+        auto t0 = std::chrono::steady_clock::now();
         for (uint32_t l = 0; l < L; ++l) {
             read_scalars(dev, *dev.lanes[l], scal[l]);
             check_error_flag(scal[l]);
@@ -1335,8 +1383,13 @@ void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySu
         // apply_mean_deltas (parallel.rs:715-798): fixed tensors on the device,
         // keyed context on the host mirror, statistics and revision here.
         double canon_loss = dev.stats.training_loss_sum;
+        dev.perf.collect_ms += ms_since(t0);
+        t0 = std::chrono::steady_clock::now();
         rep.fixed_parameter_updates = merge_fixed(dev, L, scal);
+        dev.perf.merge_fixed_ms += ms_since(t0);
+        t0 = std::chrono::steady_clock::now();
         rep.context_keys = merge_context(dev, L, scal);
+        dev.perf.merge_context_ms += ms_since(t0);
         for (uint32_t l = 0; l < L; ++l) {
             const LaneScalars& sc = scal[l];
             const auto& story = dev.batch_stories[l];
@@ -1374,9 +1427,15 @@ void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySu
         rep.mean_loss = weighted / (double)std::max<size_t>(targets, 1);
         // Serial canonical replay (training.rs:1709-1711), then one sync of the
         // replay's changed rows into every lane (training.rs:1644-1649).
+        t0 = std::chrono::steady_clock::now();
         for (uint32_t l = 0; l < L; ++l)
             replay_story(dev, dev.batch_stories[l], losses[l], dev.batch_permission, replay_changes, &rep);
+        CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+        dev.perf.replay_ms += ms_since(t0);
+        t0 = std::chrono::steady_clock::now();
         sync_replay_changes(dev, replay_changes);
+        CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+        dev.perf.replay_sync_ms += ms_since(t0);
     }
     CUDA_CHECK(cudaEventRecord(dev.batch_stop, dev.stream));
     CUDA_CHECK(cudaEventSynchronize(dev.batch_stop));

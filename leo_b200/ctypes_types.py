@@ -181,4 +181,9 @@ class LeoB200PerfStats(C.Structure):
         ("whole_gpu_launches", C.c_uint64),
         ("fit_clusters", C.c_int32 * 3),
         ("sm_count", C.c_int32),
+        ("collect_ms", C.c_double),
+        ("merge_fixed_ms", C.c_double),
+        ("merge_context_ms", C.c_double),
+        ("replay_ms", C.c_double),
+        ("replay_sync_ms", C.c_double),
     ]
