@@ -363,8 +363,13 @@ __device__ void context_resolve_warp(const LaneState& ln, uint32_t s, const Kern
 // event order: previous actives, then due events from emission ticks s-8,
 // s-4, s-2, s-1 (rank, then slot), then the symbol's input slots; the event
 // index q encodes that order.
-__device__ void phase_deliver(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t worker,
-                              uint32_t workers, bool learn, uint32_t symbol) {
+//
+// `fresh_d1`: the previous step was frozen and its emit phase runs beside this
+// deliver, so its ring values are not written yet; a delay-1 event's value is
+// formed here from the same operands (activation x weight; no learning step
+// separates emission and delivery, so the weight is the one emit reads).
+__device__ uint32_t phase_deliver(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t worker,
+                                  uint32_t workers, bool learn, uint32_t symbol, bool fresh_d1) {
     const uint32_t S = kc.topo.s, F = kc.topo.f, maxa = kc.topo.max_active;
     LaneScalars* sc = ln.sc;
     uint32_t prev = s >= 1 ? sc->ring_count[(s - 1) % LEO_RING] : 0u;
@@ -378,7 +383,6 @@ __device__ void phase_deliver(const LaneState& ln, uint32_t s, const KernelConst
     if (worker == 0) {
         sc->elig_count[cur ^ 1u] = 0;
         sc->in_elig_count[cur ^ 1u] = 0;
-        sc->work_deliver += events + F;
     }
     const uint32_t epoch = s + 1;
     for (uint32_t i = worker; i < total; i += workers) {
@@ -405,7 +409,8 @@ __device__ void phase_deliver(const LaneState& ln, uint32_t s, const KernelConst
             uint32_t word = kc.topo.rec_word[slot];
             if (LEO_WORD_DELAY(word) != d) continue;
             uint32_t n = word & LEO_TARGET_MASK, b = LEO_WORD_BRANCH(word);
-            float value = ln.ring_val[((size_t)entry * maxa + r) * S + j];
+            const float value = (fresh_d1 && d == 1) ? ln.ring_act[entry * maxa + r] * ln.p.rec_weight[slot]
+                                                     : ln.ring_val[((size_t)entry * maxa + r) * S + j];
             touch(ln, n, epoch);
             const int32_t h = kc.topo.hubs ? kc.topo.hub_of[n] : -1;
             if (h >= 0)
@@ -454,6 +459,7 @@ __device__ void phase_deliver(const LaneState& ln, uint32_t s, const KernelConst
             }
         }
     }
+    return events + F;
 }
 
 // ---------------------------------------------------------------------------
@@ -887,7 +893,7 @@ __device__ void phase_blocks(const LaneState& ln, const KernelConsts& kc, uint32
 // assemble (one CTA): active list in block order, the global cap
 // (runtime.rs:998-1064), population inhibition (runtime.rs:1076-1082), the
 // active ring entry, activations, and the actives as learning destinations.
-__device__ void phase_assemble(const LaneState& ln, uint32_t s, const KernelConsts& kc,
+__device__ void phase_assemble(const LaneState& ln, uint32_t s, const KernelConsts& kc, bool learning,
                                unsigned long long* sorted) {
     __shared__ uint32_t s_offset[1025];
     __shared__ uint32_t s_warp_sums[kWarps];
@@ -896,6 +902,13 @@ __device__ void phase_assemble(const LaneState& ln, uint32_t s, const KernelCons
     const uint32_t B = kc.topo.blocks, keep = kc.topo.keep, n_count = kc.topo.n, maxa = kc.topo.max_active;
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
     const uint32_t rotation = (uint32_t)((sc->base_tick + s) % (unsigned long long)n_count);
+    // Thread 0's scalars, loaded now so their latency overlaps the scan.
+    float pop_inh = 0.0f;
+    uint32_t supra = 0;
+    if (tid == 0) {
+        pop_inh = sc->population_inhibition;
+        supra = sc->step_supra;
+    }
     // exclusive scan of block winner counts (B <= 1024, two blocks per thread)
     uint32_t b0 = 2 * tid, b1 = 2 * tid + 1;
     uint32_t v0 = b0 < B ? ln.block_nwin[b0] : 0u, v1 = b1 < B ? ln.block_nwin[b1] : 0u;
@@ -972,17 +985,19 @@ __device__ void phase_assemble(const LaneState& ln, uint32_t s, const KernelCons
         ln.ring_src[entry * maxa + r] = n;
         ln.ring_act[entry * maxa + r] = act;
         ln.hot[n].activation = act;
-        add_destination(ln, n, s + 1);  // every active neuron is a destination (runtime.rs:1240-1245)
+        // Every active neuron is a learning destination (runtime.rs:1240-1245);
+        // the destination list is read only by a learning step's learn phase.
+        if (learning) add_destination(ln, n, s + 1);
     }
     if (tid == 0) {
         sc->ring_count[entry] = active;
         float activity = (float)active / (float)(n_count > 0 ? n_count : 1);
         float error = activity - c.target_activity;
         sc->population_inhibition =
-            clampf(sc->population_inhibition + c.population_inhibition_rate * error, 0.0f, c.population_inhibition_max);
+            clampf(pop_inh + c.population_inhibition_rate * error, 0.0f, c.population_inhibition_max);
         sc->population_cutoff = redundant ? 0.0f : pop_cutoff;
         sc->last_active = active;
-        sc->last_suprathreshold = sc->step_supra;
+        sc->last_suprathreshold = supra;
         sc->last_block_selected = selected;
         sc->last_clipped = clipped;
         sc->step_supra = 0;
@@ -1499,19 +1514,48 @@ __device__ void phase_inhibit(const LaneState& ln, uint32_t s, const KernelConst
     }
 }
 
+// Work counters of one launch, held by the launch's first thread and added to
+// the lane's scalars when the launch ends.
+struct WorkTally {
+    unsigned long long deliver, touched, active, steps, eligible, destinations;
+};
+
 // Step epilogue (one thread): work counters, per-tick counter reset, and the
-// worklist swap after an eligibility phase.
-__device__ void step_epilogue(const LaneState& ln, uint32_t s, bool frozen) {
+// worklist swap after an eligibility phase.  Every load is issued before the
+// stores so the thread's chain is one round trip.
+// A frozen step's touched list is released in its blocks phase (see
+// release_touched), so the next step's deliver may run beside this epilogue.
+__device__ void step_epilogue(const LaneState& ln, uint32_t s, bool frozen, WorkTally& tally) {
     LaneScalars* sc = ln.sc;
-    uint32_t cur = sc->elig_cur;
-    sc->work_touched += sc->touched_count;
-    sc->work_active += sc->ring_count[s % LEO_RING];
-    sc->work_steps += 1;
-    if (!frozen) sc->work_eligible += sc->elig_count[cur] + sc->in_elig_count[cur];
-    if ((sc->step_flags & 3u) == 3u) sc->work_destinations += sc->dst_count;
-    sc->touched_count = 0;
+    const uint32_t cur = sc->elig_cur;
+    const uint32_t touched = frozen ? 0u : sc->touched_count, active = sc->ring_count[s % LEO_RING];
+    const uint32_t flags = sc->step_flags, dsts = sc->dst_count;
+    const uint32_t e0 = sc->elig_count[0] + sc->in_elig_count[0], e1 = sc->elig_count[1] + sc->in_elig_count[1];
+    tally.touched += touched;
+    tally.active += active;
+    tally.steps += 1;
+    if (!frozen) tally.eligible += cur ? e1 : e0;
+    if ((flags & 3u) == 3u) tally.destinations += dsts;
+    if (!frozen) sc->touched_count = 0;
     sc->dst_count = 0;
     if (!frozen) sc->elig_cur = cur ^ 1u;
+}
+
+// After settle, a frozen step reads its touched list no more (no surrogate,
+// eligibility or learning follows): count it and empty it (one thread).
+__device__ __forceinline__ void release_touched(const LaneState& ln, WorkTally& tally) {
+    tally.touched += ln.sc->touched_count;
+    ln.sc->touched_count = 0;
+}
+
+__device__ void flush_tally(const LaneState& ln, const WorkTally& tally) {
+    LaneScalars* sc = ln.sc;
+    sc->work_deliver += tally.deliver;
+    sc->work_touched += tally.touched;
+    sc->work_active += tally.active;
+    sc->work_steps += tally.steps;
+    sc->work_eligible += tally.eligible;
+    sc->work_destinations += tally.destinations;
 }
 
 __device__ __forceinline__ unsigned long long clock_now() { return clock64(); }
@@ -1531,7 +1575,11 @@ __device__ __forceinline__ void wavefront_steps(const LaneState* __restrict__ la
     const uint32_t worker = rank * kThreads + threadIdx.x, workers = C * kThreads;
     const uint32_t gwarp = rank * kWarps + (threadIdx.x >> 5), gwarps = C * kWarps;
     const bool timer = rank == 0 && threadIdx.x == 0;
-    unsigned long long t0 = 0, acc[LEO_PHASES] = {0};
+    // Phase clocks and work counters belong to the first thread alone; they
+    // live in shared memory so they cost the other threads no registers.
+    __shared__ unsigned long long acc[LEO_PHASES];
+    __shared__ WorkTally tally;
+    unsigned long long t0 = 0;
     auto mark = [&](int p) {
         if (timer) {
             unsigned long long t = clock_now();
@@ -1539,7 +1587,16 @@ __device__ __forceinline__ void wavefront_steps(const LaneState* __restrict__ la
             t0 = t;
         }
     };
-    if (timer) t0 = clock_now();
+    if (timer) {
+        for (int p = 0; p < LEO_PHASES; ++p) acc[p] = 0;
+        tally = WorkTally{0, 0, 0, 0, 0, 0};
+        t0 = clock_now();
+    }
+    // `joined`: the previous step was frozen without a forward pass and its
+    // emit phase is still open -- this step's deliver runs in it.  Nothing of
+    // this step before settle reads what that emit writes except the delay-1
+    // ring values, which deliver then forms from their operands.
+    bool joined = false;
     for (uint32_t s = begin; s < end && s < steps; ++s) {
         const uint32_t sched = ln.schedule[s];
         const bool frozen = LEO_SCHED_PERMISSION(sched) == kFrozen;
@@ -1547,7 +1604,8 @@ __device__ __forceinline__ void wavefront_steps(const LaneState* __restrict__ la
         // deliver; the cluster's last warp first resolves the context
         if (rank == C - 1 && (threadIdx.x >> 5) == kWarps - 1)
             context_resolve_warp(ln, s, kc, symbol, frozen, !frozen || LEO_SCHED_TARGET(sched) >= 0);
-        phase_deliver(ln, s, kc, worker, workers, !frozen, symbol);
+        const uint32_t delivered = phase_deliver(ln, s, kc, worker, workers, !frozen, symbol, joined);
+        if (worker == 0) tally.deliver += delivered;
         sync();
         mark(0);
         phase_settle(ln, s, kc, worker, workers, rank, C, reinterpret_cast<uint32_t*>(smem_sorted));
@@ -1556,9 +1614,10 @@ __device__ __forceinline__ void wavefront_steps(const LaneState* __restrict__ la
         for (uint32_t h = worker; h < kc.topo.hubs; h += workers) ln.hub_count[h] = 0;
         if (worker == 0) sc->hub_next = 0;
         phase_blocks(ln, kc, gwarp, gwarps);
+        if (frozen && worker == 0) release_touched(ln, tally);
         sync();
         mark(2);
-        if (rank == 0) phase_assemble(ln, s, kc, smem_sorted);
+        if (rank == 0) phase_assemble(ln, s, kc, !frozen, smem_sorted);
         sync();
         mark(3);
         if (!frozen) {
@@ -1582,10 +1641,13 @@ __device__ __forceinline__ void wavefront_steps(const LaneState* __restrict__ la
         }
         if (frozen && worker == 0) {
             if (!forward) sc->step_flags = 0;
-            step_epilogue(ln, s, true);
+            step_epilogue(ln, s, true, tally);
         }
-        sync();
-        mark(6);
+        joined = !forward && s + 1 < end && s + 1 < steps;
+        if (!joined) {
+            sync();
+            mark(6);
+        }
         if (!frozen) {
             phase_learn(ln, s, kc, worker, workers, gwarp, gwarps, reinterpret_cast<float (*)[32][33]>(smem_sorted));
             sync();
@@ -1594,11 +1656,12 @@ __device__ __forceinline__ void wavefront_steps(const LaneState* __restrict__ la
             sync();
             mark(8);
             phase_inhibit(ln, s, kc, worker, workers);
-            if (worker == 0) step_epilogue(ln, s, false);
+            if (worker == 0) step_epilogue(ln, s, false, tally);
             sync();
             mark(9);
         }
     }
+    if (worker == 0) flush_tally(ln, tally);
     if (timer) {
         for (int p = 0; p < LEO_PHASES; ++p) sc->phase_cycles[p] += acc[p];
         if (ln.load_out) {
