@@ -153,6 +153,16 @@ int leo_b200_set_cluster_sizes(LeoB200Device* device, uint32_t story_cluster, ui
    plays this role statically, crates/leo-core/src/cuda_plan.rs:189-453). */
 int leo_b200_set_story_chunk(LeoB200Device* device, uint32_t steps);
 
+/* Execution geometry only: with `enable`, a replay segment's frozen prefix
+   first runs on one CTA with its per-step lists in shared memory while each
+   step's touched neurons and events fit (a few hundred neurons per step is
+   typical), and the wavefront resumes at the first step that does not fit.
+   Off by default: on a 65,536-neuron model such a step takes about as long on
+   one SM (its issue rate and L2 latency bound it) as on the 16-CTA wavefront.
+   No reference counterpart (the reference runs replay prefixes on its
+   cooperative frozen-advance kernel, crates/leo-core/src/cuda_kernels.cu:4529). */
+int leo_b200_set_quiet_steps(LeoB200Device* device, int enable);
+
 /* Execution geometry only: neurons whose recurrent in-degree is at least
    `min_in_degree` are hubs -- their events per step go to a contiguous buffer
    sorted by event order instead of a per-target linked list, which keeps

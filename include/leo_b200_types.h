@@ -247,6 +247,10 @@ typedef struct LeoB200PerfStats {
     double merge_context_ms;  /* keyed context merge and lane context sync */
     double replay_ms;         /* serial canonical replay, range selection to last segment */
     double replay_sync_ms;    /* replay's changed rows into every lane */
+    uint64_t quiet_launches;  /* replay-prefix launches of the one-CTA quiet-step kernel */
+    uint64_t quiet_steps;     /* steps it ran (the wavefront resumed after them) */
+    double quiet_ms;          /* its device time */
+    uint64_t quiet_cycles[6]; /* its SM cycles: deliver, group, settle, blocks, assemble, emit */
 } LeoB200PerfStats;
 
 #ifdef __cplusplus

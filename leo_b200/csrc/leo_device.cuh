@@ -36,6 +36,10 @@
 #define LEO_MAX_EMBEDDING 256u
 #define LEO_WAVEFRONT_THREADS 512u  // threads per CTA of the persistent wavefront
 #define LEO_PHASES 11
+#define LEO_QUIET_PHASES 6  // quiet-step kernel: deliver, group, settle, blocks, assemble, emit
+// A wavefront launch whose first step is the lane's resume_step (written by
+// the quiet-step kernel launched before it on the same stream).
+#define LEO_RESUME_STEP 0xffffffffu
 
 // Packed topology words.
 #define LEO_TARGET_MASK 0x00ffffffu
@@ -142,6 +146,9 @@ struct LaneScalars {
     unsigned long long phase_cycles[LEO_PHASES];  // SM clock cycles per phase (first CTA, first thread)
     uint32_t step_supra;                          // candidates of the current tick (all blocks)
     uint32_t hub_next;                            // next hub a warp takes in settle (reset after settle)
+    uint32_t resume_step;                         // first step the quiet-step kernel left to the wavefront
+    unsigned long long work_quiet;                // steps run by the quiet-step kernel
+    unsigned long long quiet_cycles[LEO_QUIET_PHASES];  // its SM clock cycles per phase (first thread)
     // last-step metrics
     uint32_t last_active, last_suprathreshold, last_block_selected, last_clipped, last_predicted;
     float last_loss;

@@ -150,6 +150,9 @@ struct LeoB200Device {
     int sm_count = 0;
     int fit16 = 0, fit8 = 0, fit4 = 0;  // co-resident clusters of 16 / 8 / 4 CTAs
     int grid_ctas = 0;                  // CTAs of the whole-GPU replay launch (0: unavailable)
+    bool quiet_steps = false;           // replay prefixes start on the one-CTA quiet-step kernel (opt-in)
+    size_t quiet_smem = 0;              // its shared memory (0: not available for this model)
+    cudaEvent_t quiet_start = nullptr, quiet_stop = nullptr;
     uint32_t replay_load = 0;           // work per step the replay lane reported last
     uint32_t story_chunk = 32;        // steps per story-pass launch while lane loads are skewed
     uint32_t* d_lane_load = nullptr;  // [max_lanes + 1], last entry: replay lane
@@ -295,6 +298,11 @@ void reset_lane(LeoB200Device& dev, Lane& lane, unsigned long long base_tick, ui
     const ModelSizes& z = dev.z;
     cudaStream_t s = dev.stream;
     LaneState& st = lane.st;
+    // The traces (32 B per synapse: 134 MB on a 65,536 x 64 model) are zeroed
+    // first and with evict-first stores, so that zeroing them does not push the
+    // lane's neuron state and the topology the next steps read out of L2.
+    CUDA_CHECK(leo_launch_zero_streaming(reinterpret_cast<float4*>(st.traces), z.synapses * sizeof(Trace) / 16, s));
+    CUDA_CHECK(leo_launch_zero_streaming(reinterpret_cast<float4*>(st.in_traces), z.inputs * sizeof(Trace) / 16, s));
     CUDA_CHECK(cudaMemsetAsync(st.hot, 0, z.n * sizeof(NeuronHot), s));
     CUDA_CHECK(cudaMemsetAsync(st.cold, 0, z.n * sizeof(NeuronCold), s));
     CUDA_CHECK(cudaMemsetAsync(st.branches, 0, z.n * sizeof(float4), s));
@@ -302,8 +310,6 @@ void reset_lane(LeoB200Device& dev, Lane& lane, unsigned long long base_tick, ui
     CUDA_CHECK(cudaMemsetAsync(st.dst_epoch, 0, z.n * 4, s));
     CUDA_CHECK(cudaMemsetAsync(st.ev_head, 0xff, z.n * 16, s));
     CUDA_CHECK(cudaMemsetAsync(st.block_cand_count, 0, dev.cfg.abi.block_count * 4, s));
-    CUDA_CHECK(cudaMemsetAsync(st.traces, 0, z.synapses * sizeof(Trace), s));
-    CUDA_CHECK(cudaMemsetAsync(st.in_traces, 0, z.inputs * sizeof(Trace), s));
     if (st.hub_count) CUDA_CHECK(cudaMemsetAsync(st.hub_count, 0, dev.kc.topo.hubs * 4, s));
     LaneScalars sc{};
     sc.base_tick = base_tick;
@@ -531,9 +537,12 @@ uint32_t pick_cluster(LeoB200Device& dev, uint32_t lanes, uint32_t request, uint
 // more than ~50k units of work (fitted to measured replay steps).
 constexpr uint32_t kWholeGpuLoad = 50000;
 
+// `resume`: the launch starts at the lane's resume_step (left by the quiet-step
+// kernel before it on the stream) instead of `begin`.
 void run_steps(LeoB200Device& dev, const LaneState* d_lanes, int lane_count, uint32_t begin, uint32_t end,
-               bool story) {
+               bool story, bool resume = false) {
     if (end <= begin || lane_count == 0) return;
+    const uint32_t first = resume ? LEO_RESUME_STEP : begin;
     const bool whole_gpu = !story && lane_count == 1 && dev.grid_ctas > 0 &&
                            (dev.replay_cluster_request == LEO_B200_WHOLE_GPU ||
                             (dev.replay_cluster_request == 0 && dev.replay_load > kWholeGpuLoad));
@@ -544,9 +553,9 @@ void run_steps(LeoB200Device& dev, const LaneState* d_lanes, int lane_count, uin
                                                    ? 0u : dev.replay_cluster_request, 16);
     CUDA_CHECK(cudaEventRecord(dev.wave_start, dev.stream));
     if (whole_gpu)
-        CUDA_CHECK(leo_launch_wavefront_grid(d_lanes, (uint32_t)dev.grid_ctas, begin, end, dev.kc, dev.stream));
+        CUDA_CHECK(leo_launch_wavefront_grid(d_lanes, (uint32_t)dev.grid_ctas, first, end, dev.kc, dev.stream));
     else
-        CUDA_CHECK(leo_launch_wavefront(d_lanes, lane_count, cluster, begin, end, dev.kc, dev.stream));
+        CUDA_CHECK(leo_launch_wavefront(d_lanes, lane_count, cluster, first, end, dev.kc, dev.stream));
     CUDA_CHECK(cudaGetLastError());
     CUDA_CHECK(cudaEventRecord(dev.wave_stop, dev.stream));
     CUDA_CHECK(cudaEventSynchronize(dev.wave_stop));
@@ -702,6 +711,8 @@ void add_work(LeoB200Device& dev, const LaneScalars& sc, bool story) {
     dev.perf.work_active += sc.work_active;
     dev.perf.work_plastic += sc.work_plastic;
     dev.perf.work_steps += sc.work_steps;
+    dev.perf.quiet_steps += sc.work_quiet;
+    for (int p = 0; p < LEO_QUIET_PHASES; ++p) dev.perf.quiet_cycles[p] += sc.quiet_cycles[p];
 }
 
 void read_scalars(LeoB200Device& dev, Lane& lane, LaneScalars& out) {
@@ -1184,7 +1195,26 @@ void run_canonical_schedule(LeoB200Device& dev, const std::vector<uint32_t>& sch
     carry.bias_dirty = out.bias_dirty;
     carry.ctx_out_dirty = out.ctx_out_dirty;
     CUDA_CHECK(cudaMemcpyAsync(rl.st.sc, &carry, sizeof(carry), cudaMemcpyHostToDevice, dev.stream));
-    run_steps(dev, dev.d_replay, 1, 0, (uint32_t)schedule.size(), false);
+    // The frozen prefix (leading frozen steps without a target) starts on the
+    // quiet-step kernel; the wavefront resumes where it stopped.
+    size_t prefix = 0;
+    while (prefix < schedule.size() && LEO_SCHED_PERMISSION(schedule[prefix]) == LEO_B200_FROZEN &&
+           LEO_SCHED_TARGET(schedule[prefix]) < 0)
+        ++prefix;
+    const bool quiet = dev.quiet_steps && dev.quiet_smem > 0 && prefix > 0;
+    if (quiet) {
+        CUDA_CHECK(cudaEventRecord(dev.quiet_start, dev.stream));
+        CUDA_CHECK(leo_launch_quiet(dev.d_replay, 0, (uint32_t)prefix, dev.kc, dev.stream));
+        CUDA_CHECK(cudaEventRecord(dev.quiet_stop, dev.stream));
+        dev.perf.launches += 1;
+        dev.perf.quiet_launches += 1;
+    }
+    run_steps(dev, dev.d_replay, 1, 0, (uint32_t)schedule.size(), false, quiet);
+    if (quiet) {
+        float ms = 0.0f;
+        CUDA_CHECK(cudaEventElapsedTime(&ms, dev.quiet_start, dev.quiet_stop));
+        dev.perf.quiet_ms += ms;
+    }
     LaneScalars sc;
     read_scalars(dev, rl, sc);
     check_error_flag(sc);
@@ -1877,6 +1907,9 @@ int leo_b200_open(int device, const LeoB200HostModel* canonical, uint32_t max_la
             cudaGetLastError();
             dev->grid_ctas = 0;
         }
+        dev->quiet_smem = leo_quiet_smem_bytes(dev->kc);
+        CUDA_CHECK(cudaEventCreate(&dev->quiet_start));
+        CUDA_CHECK(cudaEventCreate(&dev->quiet_stop));
         upload_model(*dev, *canonical);
         *out = dev.release();
         return 0;
@@ -1890,6 +1923,8 @@ void leo_b200_close(LeoB200Device* dev) {
     cudaSetDevice(dev->device);
     cudaStreamSynchronize(dev->stream);
     cudaStream_t s = dev->stream;
+    if (dev->quiet_start) cudaEventDestroy(dev->quiet_start);
+    if (dev->quiet_stop) cudaEventDestroy(dev->quiet_stop);
     if (dev->wave_start) cudaEventDestroy(dev->wave_start);
     if (dev->wave_stop) cudaEventDestroy(dev->wave_stop);
     if (dev->batch_start) cudaEventDestroy(dev->batch_start);
@@ -2313,6 +2348,11 @@ int leo_b200_set_cluster_sizes(LeoB200Device* dev, uint32_t story_cluster, uint3
     }
     dev->story_cluster_request = story_cluster;
     dev->replay_cluster_request = replay_cluster;
+    return 0;
+}
+
+int leo_b200_set_quiet_steps(LeoB200Device* dev, int enable) {
+    dev->quiet_steps = enable != 0;
     return 0;
 }
 

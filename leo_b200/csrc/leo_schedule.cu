@@ -11,7 +11,8 @@
 // word, the tick and the configuration, so a word is 4 bytes per step.
 //
 // Work is one byte read and one word written per step: a few microseconds for
-// a batch, bound by launch latency.
+// a batch, bound by launch latency.  The file also holds the lanes' streaming
+// zero fill used when a lane's transient state is reset.
 #include <stdint.h>
 
 #include "../../include/leo_b200_types.h"
@@ -40,7 +41,24 @@ __global__ void __launch_bounds__(kThreads) build_schedules_kernel(const uint8_t
     }
 }
 
+// Grid-stride zero fill with st.global.cs (streaming: evict-first in L2).
+__global__ void __launch_bounds__(kThreads) zero_streaming_kernel(float4* __restrict__ p, size_t n) {
+    const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (size_t i = (size_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += (size_t)gridDim.x * kThreads) __stcs(p + i, z);
+}
+
 }  // namespace
+
+cudaError_t leo_launch_zero_streaming(float4* p, size_t n, cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    int device = 0, sms = 148;
+    cudaGetDevice(&device);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    const size_t want = (n + kThreads - 1) / kThreads;
+    const unsigned grid = (unsigned)(want < (size_t)sms * 8 ? want : (size_t)sms * 8);
+    zero_streaming_kernel<<<grid, kThreads, 0, stream>>>(p, n);
+    return cudaGetLastError();
+}
 
 cudaError_t leo_launch_build_schedules(const uint8_t* bytes, const uint64_t* offsets, const LaneState* lanes,
                                        uint32_t count, uint32_t permission, cudaStream_t stream) {

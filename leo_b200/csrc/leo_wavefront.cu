@@ -120,15 +120,18 @@ __device__ __forceinline__ float leo_logf(const KernelConsts& kc, float x) {
 // Packed selection key: activation bits (positive floats order like their
 // bits) above the complement of the rotated tie key (runtime.rs:99-101); a
 // larger key is a better candidate.
+// neuron, rotation < n < 2^24, so one conditional subtraction is the modulus.
 __device__ __forceinline__ unsigned long long selection_key(float act, uint32_t neuron, uint32_t rotation,
                                                             uint32_t n) {
-    uint32_t rotated = (uint32_t)(((unsigned long long)neuron + n - rotation) % n);
+    uint32_t rotated = neuron + n - rotation;
+    if (rotated >= n) rotated -= n;
     return ((unsigned long long)__float_as_uint(act) << 32) | (unsigned long long)(0xffffffffu - rotated);
 }
 __device__ __forceinline__ float key_value(unsigned long long key) { return __uint_as_float((uint32_t)(key >> 32)); }
 __device__ __forceinline__ uint32_t key_neuron(unsigned long long key, uint32_t rotation, uint32_t n) {
-    uint32_t rotated = 0xffffffffu - (uint32_t)(key & 0xffffffffu);
-    return (uint32_t)(((unsigned long long)rotated + rotation) % n);
+    uint32_t neuron = 0xffffffffu - (uint32_t)(key & 0xffffffffu) + rotation;
+    if (neuron >= n) neuron -= n;
+    return neuron;
 }
 
 __device__ __forceinline__ Trace load_trace(const Trace* p) {
@@ -497,11 +500,12 @@ __device__ __forceinline__ SettlePre settle_preload(const LaneState& ln, const K
     return SettlePre{ln.p.threshold[n], kc.topo.excitability[n], ln.hot[n].refractory_until};
 }
 
-// Integration and block candidate after the branch sums; stores the neuron.
-__device__ __forceinline__ void settle_integrate(const LaneState& ln, const KernelConsts& kc, uint32_t n, uint32_t s,
-                                                 NeuronCold cold, float4 br, float pop_inh, uint32_t rotation,
-                                                 SettlePre pre) {
-    const uint32_t npb = kc.topo.npb, n_count = kc.topo.n;
+// Integration after the branch sums; stores the neuron and returns its block
+// candidate key (0: not a candidate).
+__device__ __forceinline__ unsigned long long settle_integrate_key(const LaneState& ln, const KernelConsts& kc,
+                                                                   uint32_t n, uint32_t s, NeuronCold cold, float4 br,
+                                                                   float pop_inh, uint32_t rotation, SettlePre pre) {
+    unsigned long long key = 0ull;
     ln.hot[n].activation = 0.0f;
     bool refractory = pre.refractory_until > s;
     if (!refractory) {
@@ -512,14 +516,23 @@ __device__ __forceinline__ void settle_integrate(const LaneState& ln, const Kern
         float drive = pre.excitability * net - cold.fatigue - adaptation - pop_inh;
         cold.membrane = cold.membrane + drive;
         float act = clampf(cold.membrane - pre.threshold, 0.0f, 1.0f);
-        if (act > 0.0f) {
-            uint32_t blk = n / npb;
-            uint32_t pos = atomicAdd(&ln.block_cand_count[blk], 1u);
-            ln.block_cand[(size_t)blk * npb + pos] = selection_key(act, n, rotation, n_count);
-        }
+        if (act > 0.0f) key = selection_key(act, n, rotation, kc.topo.n);
     }
     ln.cold[n] = cold;
     ln.branches[n] = br;
+    return key;
+}
+
+// Integration and block candidate after the branch sums; stores the neuron.
+__device__ __forceinline__ void settle_integrate(const LaneState& ln, const KernelConsts& kc, uint32_t n, uint32_t s,
+                                                 NeuronCold cold, float4 br, float pop_inh, uint32_t rotation,
+                                                 SettlePre pre) {
+    const unsigned long long key = settle_integrate_key(ln, kc, n, s, cold, br, pop_inh, rotation, pre);
+    if (key) {
+        const uint32_t npb = kc.topo.npb, blk = n / npb;
+        const uint32_t pos = atomicAdd(&ln.block_cand_count[blk], 1u);
+        ln.block_cand[(size_t)blk * npb + pos] = key;
+    }
 }
 
 // Bounds of one branch in a hub's sorted keys (branch in the top two bits).
@@ -893,8 +906,13 @@ __device__ void phase_blocks(const LaneState& ln, const KernelConsts& kc, uint32
 // assemble (one CTA): active list in block order, the global cap
 // (runtime.rs:998-1064), population inhibition (runtime.rs:1076-1082), the
 // active ring entry, activations, and the actives as learning destinations.
+//
+// `nwin` / `winners`: the blocks phase's winner counts and winners (global in
+// the wavefront, shared memory in the quiet-step kernel); `active_out`, when
+// given, receives the step's active count from thread 0.
 __device__ void phase_assemble(const LaneState& ln, uint32_t s, const KernelConsts& kc, bool learning,
-                               unsigned long long* sorted) {
+                               unsigned long long* sorted, const uint32_t* nwin, const unsigned long long* winners,
+                               uint32_t* active_out) {
     __shared__ uint32_t s_offset[1025];
     __shared__ uint32_t s_warp_sums[kWarps];
     LaneScalars* sc = ln.sc;
@@ -911,7 +929,7 @@ __device__ void phase_assemble(const LaneState& ln, uint32_t s, const KernelCons
     }
     // exclusive scan of block winner counts (B <= 1024, two blocks per thread)
     uint32_t b0 = 2 * tid, b1 = 2 * tid + 1;
-    uint32_t v0 = b0 < B ? ln.block_nwin[b0] : 0u, v1 = b1 < B ? ln.block_nwin[b1] : 0u;
+    uint32_t v0 = b0 < B ? nwin[b0] : 0u, v1 = b1 < B ? nwin[b1] : 0u;
     uint32_t pair = v0 + v1, incl = pair;
     for (int o = 1; o < 32; o <<= 1) {
         uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
@@ -936,7 +954,7 @@ __device__ void phase_assemble(const LaneState& ln, uint32_t s, const KernelCons
     uint32_t selected = s_offset[B];
     for (uint32_t i = tid; i < B * keep; i += kThreads) {
         uint32_t b = i / keep, k = i - b * keep;
-        if (k < ln.block_nwin[b]) sorted[s_offset[b] + k] = ln.block_winners[i];
+        if (k < nwin[b]) sorted[s_offset[b] + k] = winners[i];
     }
     __syncthreads();
     uint32_t cap = c.max_active_global;
@@ -990,6 +1008,7 @@ __device__ void phase_assemble(const LaneState& ln, uint32_t s, const KernelCons
         if (learning) add_destination(ln, n, s + 1);
     }
     if (tid == 0) {
+        if (active_out) *active_out = active;
         sc->ring_count[entry] = active;
         float activity = (float)active / (float)(n_count > 0 ? n_count : 1);
         float error = activity - c.target_activity;
@@ -1572,6 +1591,7 @@ __device__ __forceinline__ void wavefront_steps(const LaneState* __restrict__ la
     const LaneState& ln = lanes[blockIdx.x / C];
     LaneScalars* sc = ln.sc;
     const uint32_t steps = sc->steps;
+    if (begin == LEO_RESUME_STEP) begin = sc->resume_step;
     const uint32_t worker = rank * kThreads + threadIdx.x, workers = C * kThreads;
     const uint32_t gwarp = rank * kWarps + (threadIdx.x >> 5), gwarps = C * kWarps;
     const bool timer = rank == 0 && threadIdx.x == 0;
@@ -1617,7 +1637,7 @@ __device__ __forceinline__ void wavefront_steps(const LaneState* __restrict__ la
         if (frozen && worker == 0) release_touched(ln, tally);
         sync();
         mark(2);
-        if (rank == 0) phase_assemble(ln, s, kc, !frozen, smem_sorted);
+        if (rank == 0) phase_assemble(ln, s, kc, !frozen, smem_sorted, ln.block_nwin, ln.block_winners, nullptr);
         sync();
         mark(3);
         if (!frozen) {
@@ -1673,6 +1693,489 @@ __device__ __forceinline__ void wavefront_steps(const LaneState* __restrict__ la
     }
 }
 
+// ---------------------------------------------------------------------------
+// Quiet frozen steps on one CTA (replay prefixes).
+//
+// A replay segment starts from a fresh transient state and runs a frozen
+// prefix (no target, no learning) before its training steps, and most prefix
+// steps touch a few hundred neurons.  This kernel runs such steps on one CTA
+// with the step's transient lists in shared memory -- touched neurons in a
+// hash table, the step's events grouped by target with a counting sort, block
+// candidates grouped by block, block winners, the active list and the ring
+// counts -- so a step's critical path is four global round trips (deliver's
+// sources and values, their synapse words, the touched neurons' state, the
+// emitters' state) and CTA barriers, where the wavefront pays cluster
+// barriers around lists in global memory.  Each thread issues its deliver
+// items' loads in batches so one round trip covers several items.  Arithmetic
+// and order are the wavefront's: each branch sums its events in ascending
+// event order, then the same integration, block top-k (same rounds), global
+// cap (phase_assemble is shared) and emission.  Persistent state (neurons,
+// rings, scalars) is the wavefront's, so the wavefront resumes where this
+// kernel stops: at the first step that is not frozen without a target, or
+// whose touched neurons, events or per-target events exceed the tables --
+// checked after the step's deliver, before the step changes persistent state.
+namespace {
+
+constexpr uint32_t kQuietSlots = 4096;               // hash slots (power of two)
+constexpr uint32_t kQuietTouched = kQuietSlots / 2;  // touched neurons per step
+constexpr uint32_t kQuietEvents = 8192;              // events per step
+constexpr uint32_t kQuietPerTarget = 64;             // events per touched neuron
+constexpr uint32_t kQuietBlocks = 1024;              // blocks (phase_assemble's limit too)
+constexpr uint32_t kQuietWinners = kQuietTouched;    // blocks x keep
+constexpr uint32_t kQuietThreadCands = 32;           // a block with more candidates is selected by a warp
+
+struct QuietShared {
+    uint32_t key[kQuietSlots];              // neuron + 1; 0 = empty
+    uint32_t start[kQuietSlots];            // events per slot, then the end of its placed run
+    uint16_t touched[kQuietTouched];        // slots in touch order
+    uint16_t tcount[kQuietTouched];         // events of touched[t]
+    uint32_t tneuron[kQuietTouched];        // neuron of touched[t]
+    uint32_t ev_key[kQuietEvents];          // branch << 24 | event order
+    float ev_val[kQuietEvents];             // then: candidates grouped by block
+    uint16_t ev_slot[kQuietEvents];
+    uint16_t placed[kQuietEvents];          // events grouped by slot
+    unsigned long long cand[kQuietTouched];  // candidate key of touched[t] (0: none); then: block winners
+    uint16_t cand_pos[kQuietTouched];       // its position in its block's run
+    uint32_t bcount[kQuietBlocks];
+    uint32_t boff[kQuietBlocks];            // then: winners per block
+    uint32_t wsum[kWarps];
+    uint32_t ring[LEO_RING];                // ring_count mirror
+    uint32_t hist[LEO_MAX_CONTEXT_ORDER];   // context history mirror (runtime.rs:642-646)
+    uint32_t nev, ntouched, overflow, supra, active, hist_len;
+};
+
+__device__ __forceinline__ int quiet_insert(QuietShared& q, uint32_t n) {
+    const uint32_t want = n + 1u;
+    uint32_t h = (n * 0x9E3779B1u) >> 20;  // 12 bits: kQuietSlots == 4096
+    for (uint32_t i = 0; i < kQuietSlots; ++i, h = (h + 1u) & (kQuietSlots - 1u)) {
+        const uint32_t k = *(volatile uint32_t*)&q.key[h];
+        if (k == want) return (int)h;
+        if (k != 0u) continue;
+        const uint32_t old = atomicCAS(&q.key[h], 0u, want);
+        if (old == 0u) {
+            // one counter update per group of converged threads
+            cg::coalesced_group g = cg::coalesced_threads();
+            uint32_t base = 0;
+            if (g.thread_rank() == 0) base = atomicAdd(&q.ntouched, g.size());
+            const uint32_t t = g.shfl(base, 0) + g.thread_rank();
+            if (t < kQuietTouched) q.touched[t] = (uint16_t)h;
+            else q.overflow = 1u;
+            return (int)h;
+        }
+        if (old == want) return (int)h;
+    }
+    q.overflow = 1u;
+    return -1;
+}
+
+__device__ __forceinline__ void quiet_event(QuietShared& q, uint32_t n, uint32_t b, uint32_t qi, float value) {
+    const int h = quiet_insert(q, n);
+    if (h < 0) return;
+    cg::coalesced_group g = cg::coalesced_threads();
+    uint32_t base = 0;
+    if (g.thread_rank() == 0) base = atomicAdd(&q.nev, g.size());
+    const uint32_t e = g.shfl(base, 0) + g.thread_rank();
+    if (e >= kQuietEvents) {
+        q.overflow = 1u;
+        return;
+    }
+    q.ev_key[e] = (b << 24) | qi;
+    q.ev_val[e] = value;
+    q.ev_slot[e] = (uint16_t)h;
+    if (atomicAdd(&q.start[h], 1u) >= kQuietPerTarget) q.overflow = 1u;
+}
+
+// Exclusive scan of one value per thread across the CTA; returns this
+// thread's offset and leaves the total in *total (every thread).
+__device__ __forceinline__ uint32_t quiet_scan(QuietShared& q, uint32_t v, uint32_t* total) {
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    uint32_t incl = v;
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= (uint32_t)o) incl += y;
+    }
+    if (lane == 31) q.wsum[warp] = incl;
+    __syncthreads();
+    uint32_t before = 0, all = 0;
+    for (uint32_t w = 0; w < kWarps; ++w) {
+        const uint32_t x = q.wsum[w];
+        if (w < warp) before += x;
+        all += x;
+    }
+    __syncthreads();
+    *total = all;
+    return before + incl - v;
+}
+
+// Deliver of step s into the shared tables (no global writes); the previous
+// step's active list is `prev_list` (its assemble keys, rank order) when
+// given, else the ring.  The delayed events are enumerated as (delay group in
+// the order 8, 4, 2, 1; source rank r; synapse j), a warp per (group, source)
+// and the warp's lanes over j, so each step's loads are coalesced and issued
+// kQuietPairs sources at a time; an event's order is its item index in the
+// wavefront's numbering (group offset + r * S + j).  Returns the step's deliver
+// work items.
+constexpr uint32_t kQuietPairs = 4;
+
+__device__ uint32_t quiet_deliver(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t symbol,
+                                  QuietShared& q, const unsigned long long* prev_list, uint32_t prev_rotation) {
+    const uint32_t S = kc.topo.s, F = kc.topo.f, maxa = kc.topo.max_active, n_count = kc.topo.n;
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    const uint32_t prev = s >= 1 ? q.ring[(s - 1) % LEO_RING] : 0u;
+    const uint32_t a8 = s >= 8 ? q.ring[(s - 8) % LEO_RING] : 0u;
+    const uint32_t a4 = s >= 4 ? q.ring[(s - 4) % LEO_RING] : 0u;
+    const uint32_t a2 = s >= 2 ? q.ring[(s - 2) % LEO_RING] : 0u;
+    const uint32_t e8 = a8 * S, e4 = a4 * S, e2 = a2 * S, e1 = prev * S;
+    const uint32_t events = e8 + e4 + e2 + e1;
+    if (events + F >= (1u << 24)) {  // event order must fit the 24-bit key field
+        if (threadIdx.x == 0) q.overflow = 1u;
+        return 0u;
+    }
+    // the previous step's actives are touched (runtime.rs:537-548)
+    for (uint32_t i = threadIdx.x; i < prev; i += kThreads)
+        quiet_insert(q, prev_list ? key_neuron(prev_list[i], prev_rotation, n_count)
+                                  : ln.ring_src[((s - 1) % LEO_RING) * maxa + i]);
+    // the symbol's input slots (runtime.rs:620-639)
+    for (uint32_t f = threadIdx.x; f < F; f += kThreads) {
+        const uint32_t slot = symbol * F + f;
+        const uint32_t word = kc.topo.in_word[slot];
+        const float value = ln.p.in_weight[slot];
+        quiet_event(q, word & LEO_TARGET_MASK, LEO_WORD_BRANCH(word), events + f, value);
+    }
+    // delayed events (runtime.rs:549-618)
+    const uint32_t pairs = a8 + a4 + a2 + prev;
+    for (uint32_t p0 = warp * kQuietPairs; p0 < pairs; p0 += kWarps * kQuietPairs) {
+        // lane k < kQuietPairs resolves pair p0 + k: its group, ring entry and source
+        uint32_t my_src = 0, my_info = 0xffffffffu;  // info: d << 28 | entry << 24 | r (r < 2^24)
+        if (lane < kQuietPairs && p0 + lane < pairs) {
+            uint32_t pr = p0 + lane, d;
+            if (pr < a8) {
+                d = 8;
+            } else if (pr < a8 + a4) {
+                d = 4; pr -= a8;
+            } else if (pr < a8 + a4 + a2) {
+                d = 2; pr -= a8 + a4;
+            } else {
+                d = 1; pr -= a8 + a4 + a2;
+            }
+            const uint32_t entry = (s - d) % LEO_RING;
+            my_src = (d == 1 && prev_list) ? key_neuron(prev_list[pr], prev_rotation, n_count)
+                                           : ln.ring_src[entry * maxa + pr];
+            my_info = (d << 28) | (entry << 24) | pr;
+        }
+        for (uint32_t j0 = 0; j0 < S; j0 += 64) {
+            uint32_t word[kQuietPairs][2];
+            float val[kQuietPairs][2];
+#pragma unroll
+            for (uint32_t k = 0; k < kQuietPairs; ++k) {
+                const uint32_t info = __shfl_sync(0xffffffffu, my_info, k);
+                const uint32_t src = __shfl_sync(0xffffffffu, my_src, k);
+#pragma unroll
+                for (uint32_t h = 0; h < 2; ++h) {
+                    const uint32_t j = j0 + h * 32 + lane;
+                    word[k][h] = 0u;
+                    if (info != 0xffffffffu && j < S) {
+                        const uint32_t entry = (info >> 24) & 15u, r = info & 0xffffffu;
+                        word[k][h] = kc.topo.rec_word[src * S + j];
+                        val[k][h] = ln.ring_val[((size_t)entry * maxa + r) * S + j];
+                    }
+                }
+            }
+#pragma unroll
+            for (uint32_t k = 0; k < kQuietPairs; ++k) {
+                const uint32_t info = __shfl_sync(0xffffffffu, my_info, k);
+#pragma unroll
+                for (uint32_t h = 0; h < 2; ++h) {
+                    const uint32_t j = j0 + h * 32 + lane;
+                    if (info == 0xffffffffu || j >= S) continue;
+                    const uint32_t d = info >> 28, r = info & 0xffffffu;
+                    if (LEO_WORD_DELAY(word[k][h]) != d) continue;
+                    const uint32_t off = d == 8 ? 0u : (d == 4 ? e8 : (d == 2 ? e8 + e4 : e8 + e4 + e2));
+                    quiet_event(q, word[k][h] & LEO_TARGET_MASK, LEO_WORD_BRANCH(word[k][h]), off + r * S + j,
+                                val[k][h]);
+                }
+            }
+        }
+    }
+    return events + F;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1)
+    leo_quiet_kernel(const LaneState* __restrict__ lanes, uint32_t begin, uint32_t end, KernelConsts kc) {
+    extern __shared__ __align__(16) unsigned char quiet_smem[];
+    QuietShared& q = *reinterpret_cast<QuietShared*>(quiet_smem);
+    unsigned long long* sorted = reinterpret_cast<unsigned long long*>(quiet_smem + sizeof(QuietShared));
+    const LaneState& ln = lanes[0];
+    LaneScalars* sc = ln.sc;
+    const LeoConfig& c = kc.cfg;
+    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+    const uint32_t B = kc.topo.blocks, S = kc.topo.s, npb = kc.topo.npb, keep = kc.topo.keep, n_count = kc.topo.n;
+    const uint32_t steps = sc->steps;
+    const unsigned long long base_tick = sc->base_tick;
+    for (uint32_t i = tid; i < kQuietSlots; i += kThreads) {
+        q.key[i] = 0u;
+        q.start[i] = 0u;
+    }
+    for (uint32_t i = tid; i < kQuietBlocks; i += kThreads) q.bcount[i] = 0u;
+    if (tid < LEO_RING) q.ring[tid] = sc->ring_count[tid];
+    if (tid < LEO_MAX_CONTEXT_ORDER) q.hist[tid] = sc->ctx_history[tid];
+    __shared__ unsigned long long acc[LEO_QUIET_PHASES];
+    __shared__ WorkTally tally;
+    if (tid == 0) {
+        q.nev = q.ntouched = q.overflow = q.supra = q.active = 0u;
+        q.hist_len = sc->ctx_history_len;
+        for (int p = 0; p < LEO_QUIET_PHASES; ++p) acc[p] = 0ull;
+        tally = WorkTally{0, 0, 0, 0, 0, 0};
+        const uint32_t cur = sc->elig_cur;
+        sc->elig_count[cur ^ 1u] = 0;
+        sc->in_elig_count[cur ^ 1u] = 0;
+    }
+    unsigned long long t0 = tid == 0 ? clock_now() : 0ull;
+    auto mark = [&](int p) {
+        if (tid == 0) {
+            const unsigned long long t = clock_now();
+            acc[p] += t - t0;
+            t0 = t;
+        }
+    };
+    __syncthreads();
+    unsigned long long* winners = q.cand;  // after the candidates are grouped
+    uint32_t* nwin = q.boff;               // after each block's run is read
+    bool have_prev = false;                // `sorted` holds the previous step's active list
+    uint32_t s = begin;
+    for (; s < end && s < steps; ++s) {
+        const uint32_t sched = ln.schedule[s];
+        if (LEO_SCHED_PERMISSION(sched) != kFrozen || LEO_SCHED_TARGET(sched) >= 0) break;
+        const uint32_t symbol = LEO_SCHED_SYMBOL(sched);
+        const uint32_t rotation = (uint32_t)((base_tick + s) % (unsigned long long)n_count);
+        const uint32_t prev_rotation = (uint32_t)((base_tick + s + n_count - 1) % (unsigned long long)n_count);
+        // deliver into the tables; give the step to the wavefront if they overflow
+        const uint32_t delivered = quiet_deliver(ln, s, kc, symbol, q, have_prev ? sorted : nullptr, prev_rotation);
+        __syncthreads();
+        if (q.overflow) break;
+        mark(0);  // deliver
+        // group the events by touched neuron: offsets of the per-slot counts
+        const uint32_t T = q.ntouched, E = q.nev;
+        const float pop_inh = sc->population_inhibition;  // latency overlaps the scan
+        uint32_t mine[4], sum = 0;
+        const uint32_t t_lo = tid * 4u;
+        for (uint32_t k = 0; k < 4; ++k) {
+            const uint32_t t = t_lo + k;
+            mine[k] = t < T ? q.start[q.touched[t]] : 0u;
+            sum += mine[k];
+        }
+        uint32_t grand = 0;
+        uint32_t off = quiet_scan(q, sum, &grand);
+        for (uint32_t k = 0; k < 4; ++k) {
+            const uint32_t t = t_lo + k;
+            if (t < T) {
+                q.tcount[t] = (uint16_t)mine[k];
+                q.start[q.touched[t]] = off;
+            }
+            off += mine[k];
+        }
+        __syncthreads();
+        for (uint32_t e = tid; e < E; e += kThreads) q.placed[atomicAdd(&q.start[q.ev_slot[e]], 1u)] = (uint16_t)e;
+        __syncthreads();
+        mark(1);  // events grouped by target
+        // settle (runtime.rs:576-603, 710-717, 947-962)
+        for (uint32_t t = tid; t < T; t += kThreads) {
+            const uint32_t h = q.touched[t];
+            const uint32_t n = q.key[h] - 1u;
+            const uint32_t cnt = q.tcount[t], hi = q.start[h], lo = hi - cnt;
+            NeuronCold cold = ln.cold[n];
+            float4 br = ln.branches[n];
+            const SettlePre pre = settle_preload(ln, kc, n);
+            for (uint32_t x = lo + 1; x < hi; ++x) {  // insertion sort by (branch, event order)
+                const uint16_t e = q.placed[x];
+                const uint32_t k = q.ev_key[e];
+                uint32_t y = x;
+                while (y > lo && q.ev_key[q.placed[y - 1]] > k) {
+                    q.placed[y] = q.placed[y - 1];
+                    --y;
+                }
+                q.placed[y] = e;
+            }
+            settle_decay(c, s, cold, br);
+            float a[4] = {br.x, br.y, br.z, br.w};
+            for (uint32_t x = lo; x < hi; ++x) {
+                const uint16_t e = q.placed[x];
+                const uint32_t b = q.ev_key[e] >> 24;
+                a[b] = a[b] + q.ev_val[e];
+            }
+            const unsigned long long key = settle_integrate_key(ln, kc, n, s, cold, make_float4(a[0], a[1], a[2], a[3]),
+                                                                pop_inh, rotation, pre);
+            q.tneuron[t] = n;
+            q.cand[t] = key;
+            if (key) q.cand_pos[t] = (uint16_t)atomicAdd(&q.bcount[n / npb], 1u);
+        }
+        __syncthreads();
+        mark(2);  // settle
+        // candidates grouped by block: exclusive scan of the block counts (B <= 1024, two per thread)
+        {
+            const uint32_t b0 = 2u * tid, b1 = b0 + 1u;
+            const uint32_t v0 = b0 < B ? q.bcount[b0] : 0u, v1 = b1 < B ? q.bcount[b1] : 0u;
+            uint32_t all = 0;
+            const uint32_t o = quiet_scan(q, v0 + v1, &all);
+            if (b0 < B) q.boff[b0] = o;
+            if (b1 < B) q.boff[b1] = o + v0;
+        }
+        __syncthreads();
+        unsigned long long* grouped = reinterpret_cast<unsigned long long*>(q.ev_val);  // events are consumed
+        for (uint32_t t = tid; t < T; t += kThreads) {
+            const unsigned long long key = q.cand[t];
+            if (key) grouped[q.boff[q.tneuron[t] / npb] + q.cand_pos[t]] = key;
+            q.key[q.touched[t]] = 0u;  // empty the tables for the next step
+            q.start[q.touched[t]] = 0u;
+        }
+        __syncthreads();
+        // blocks: block-local top-k and the (k+1)-th cutoff (runtime.rs:964-997):
+        // one thread per block with at most kQuietThreadCands candidates, one
+        // warp per larger block; both take the largest key below the previous
+        // winner keep + 1 times.
+        uint32_t supra = 0;
+        for (uint32_t b = tid; b < B; b += kThreads) {
+            const uint32_t count = q.bcount[b];
+            supra += count;
+            if (count > kQuietThreadCands) continue;
+            const unsigned long long* cand = grouped + q.boff[b];
+            unsigned long long prev = ~0ull;
+            const uint32_t rounds = count < keep + 1 ? count : keep + 1;
+            float cutoff = 0.0f;
+            for (uint32_t k = 0; k < rounds; ++k) {
+                unsigned long long best = 0ull;
+                for (uint32_t idx = 0; idx < count; ++idx) {
+                    const unsigned long long key = cand[idx];
+                    if (key < prev && key > best) best = key;
+                }
+                if (k < keep) winners[(size_t)b * keep + k] = best;
+                else cutoff = key_value(best);
+                prev = best;
+            }
+            ln.block_cutoff[b] = count > keep ? cutoff : 0.0f;
+            nwin[b] = count < keep ? count : keep;  // boff[b] is read above: this thread's own slot
+        }
+        for (uint32_t b = warp; b < B; b += kWarps) {
+            const uint32_t count = q.bcount[b];
+            if (count <= kQuietThreadCands) continue;
+            const unsigned long long* cand = grouped + q.boff[b];
+            unsigned long long prev = ~0ull;
+            const uint32_t rounds = count < keep + 1 ? count : keep + 1;
+            float cutoff = 0.0f;
+            for (uint32_t k = 0; k < rounds; ++k) {
+                unsigned long long best = 0ull;
+                for (uint32_t idx = lane; idx < count; idx += 32) {
+                    const unsigned long long key = cand[idx];
+                    if (key < prev && key > best) best = key;
+                }
+                for (int o = 16; o > 0; o >>= 1) {
+                    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+                    best = other > best ? other : best;
+                }
+                if (k < keep) {
+                    if (lane == 0) winners[(size_t)b * keep + k] = best;
+                } else {
+                    cutoff = key_value(best);
+                }
+                prev = best;
+            }
+            __syncwarp();
+            if (lane == 0) {
+                nwin[b] = count < keep ? count : keep;
+                ln.block_cutoff[b] = count > keep ? cutoff : 0.0f;
+            }
+        }
+        // one add per warp of the per-thread counts
+        for (int o = 16; o > 0; o >>= 1) supra += __shfl_xor_sync(0xffffffffu, supra, o);
+        if (lane == 0 && supra) atomicAdd(&q.supra, supra);
+        __syncthreads();
+        for (uint32_t b = tid; b < B; b += kThreads) q.bcount[b] = 0u;
+        if (tid == 0) {
+            sc->step_supra = q.supra;
+            q.supra = 0u;
+        }
+        mark(3);  // blocks
+        // assemble (shared with the wavefront); the active list stays in `sorted`
+        phase_assemble(ln, s, kc, false, sorted, nwin, winners, &q.active);
+        __syncthreads();
+        mark(4);  // assemble
+        // emit (runtime.rs:920-938, 1084-1106) from the active list in shared memory
+        const uint32_t active = q.active;
+        for (uint32_t i = tid; i < active * S; i += kThreads) {
+            const uint32_t r = i / S, j = i - r * S;
+            const unsigned long long k = sorted[r];
+            const uint32_t n = key_neuron(k, rotation, n_count);
+            const float a = key_value(k);
+            if (j == 0) {
+                NeuronCold cold = ln.cold[n];
+                cold.fatigue = cold.fatigue + c.fatigue_gain * a;
+                cold.adaptation[0] = cold.adaptation[0] + c.adaptation_fast_gain * a;
+                cold.adaptation[1] = cold.adaptation[1] + c.adaptation_medium_gain * a;
+                cold.adaptation[2] = cold.adaptation[2] + c.adaptation_slow_gain * a;
+                cold.membrane = cold.membrane - ln.p.threshold[n] * c.membrane_reset_fraction;
+                ln.cold[n] = cold;
+                ln.hot[n].refractory_until = s + c.refractory_ticks + 1u;
+            }
+            ln.ring_val[((size_t)(s % LEO_RING) * kc.topo.max_active + r) * S + j] = a * ln.p.rec_weight[(size_t)n * S + j];
+        }
+        if (tid == 0) {
+            // context history push: a frozen step without a target resolves
+            // nothing else (runtime.rs:641-646; context_resolve_warp)
+            uint32_t len = q.hist_len;
+            if (len == kc.topo.k) {
+                for (uint32_t i = 0; i + 1 < len; ++i) q.hist[i] = q.hist[i + 1];
+                len -= 1;
+            }
+            q.hist[len] = symbol;
+            q.hist_len = len + 1;
+            q.ring[s % LEO_RING] = active;
+            sc->step_flags = 0;
+            sc->dst_count = 0;
+            tally.deliver += delivered;
+            tally.touched += T;
+            tally.active += active;
+            tally.steps += 1;
+            q.nev = 0u;
+            q.ntouched = 0u;
+        }
+        have_prev = true;
+        __syncthreads();
+        mark(5);  // emit
+    }
+    if (tid == 0) {
+        if (s > begin) {  // the context state a frozen step without a target leaves
+            for (uint32_t i = 0; i < q.hist_len; ++i) sc->ctx_history[i] = q.hist[i];
+            sc->ctx_history_len = q.hist_len;
+            sc->ctx_applied = 0u;
+            sc->ctx_count = 0u;
+            sc->ctx_probes = 0u;
+        }
+        sc->resume_step = s;
+        sc->work_quiet += tally.steps;
+        flush_tally(ln, tally);
+        for (int p = 0; p < LEO_QUIET_PHASES; ++p) sc->quiet_cycles[p] += acc[p];
+    }
+}
+
+size_t leo_quiet_smem_bytes(const KernelConsts& kc) {
+    if (kc.topo.blocks > kQuietBlocks || kc.topo.blocks * kc.topo.keep > kQuietWinners || kc.topo.n >= (1u << 31))
+        return 0;
+    uint32_t winners = kc.topo.blocks * kc.topo.keep, span = 1;
+    while (span < winners) span <<= 1;
+    const size_t bytes = sizeof(QuietShared) + (size_t)span * sizeof(unsigned long long);
+    return bytes <= 200u * 1024u ? bytes : 0;
+}
+
+cudaError_t leo_launch_quiet(const LaneState* lane, uint32_t begin, uint32_t end, const KernelConsts& kc,
+                             cudaStream_t stream) {
+    const size_t smem = leo_quiet_smem_bytes(kc);
+    if (smem == 0) return cudaErrorInvalidConfiguration;
+    leo_quiet_kernel<<<1, kThreads, smem, stream>>>(lane, begin, end, kc);
+    return cudaGetLastError();
+}
+
 // A thread-block cluster per lane (phases separated by cluster barriers).
 __global__ void __launch_bounds__(kThreads, 1)
     leo_wavefront_kernel(const LaneState* __restrict__ lanes, uint32_t begin, uint32_t end, KernelConsts kc) {
@@ -1717,6 +2220,8 @@ cudaError_t leo_wavefront_configure() {
     cudaError_t e = cudaFuncSetAttribute(leo_wavefront_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(leo_wavefront_grid_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(leo_quiet_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(leo_wavefront_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
 }

@@ -186,4 +186,8 @@ class LeoB200PerfStats(C.Structure):
         ("merge_context_ms", C.c_double),
         ("replay_ms", C.c_double),
         ("replay_sync_ms", C.c_double),
+        ("quiet_launches", C.c_uint64),
+        ("quiet_steps", C.c_uint64),
+        ("quiet_ms", C.c_double),
+        ("quiet_cycles", C.c_uint64 * 6),
     ]

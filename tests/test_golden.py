@@ -139,3 +139,27 @@ def test_gpu_hub_path_matches_golden(native_lib, case_name, min_in_degree, cta_e
         for i, (rec, batch) in enumerate(zip(case["batches"], batches)):
             backend.training_story_batch(batch, TRAINING)
             assert backend.state_digest().hex() == rec["state_hash"], f"batch {i}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case_name", ["baseline1", "baseline2-short", "baseline3-short", "test-8"])
+@pytest.mark.parametrize("quiet", [True, False], ids=["quiet-steps", "wavefront-only"])
+def test_gpu_replay_prefix_kernel_matches_golden(native_lib, case_name, quiet):
+    """With the opt-in quiet-step kernel, replay prefixes run first on one CTA
+    (shared-memory step lists) and the wavefront resumes where it stops; with
+    it on or off the golden hashes hold, and when on it ran some prefix steps."""
+    from leo_b200.backend import GpuBackend
+    from leo_b200.ctypes_types import TRAINING
+    from leo_b200.model import HostModel
+
+    case = CASES[case_name]
+    w, batches = _stories(case)
+    model = HostModel.initialize(w.config, w.topology)
+    with GpuBackend(model, device=0, max_lanes=case["stories_per_batch"]) as backend:
+        backend.set_quiet_steps(quiet)
+        for i, (rec, batch) in enumerate(zip(case["batches"], batches)):
+            backend.training_story_batch(batch, TRAINING)
+            assert backend.state_digest().hex() == rec["state_hash"], f"batch {i}"
+        perf = backend.perf_stats()
+        assert (perf.quiet_steps > 0) == quiet
+        assert (perf.quiet_launches > 0) == quiet
