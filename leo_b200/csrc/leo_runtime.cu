@@ -303,6 +303,7 @@ void reset_lane(LeoB200Device& dev, Lane& lane, unsigned long long base_tick, ui
     // lane's neuron state and the topology the next steps read out of L2.
     CUDA_CHECK(leo_launch_zero_streaming(reinterpret_cast<float4*>(st.traces), z.synapses * sizeof(Trace) / 16, s));
     CUDA_CHECK(leo_launch_zero_streaming(reinterpret_cast<float4*>(st.in_traces), z.inputs * sizeof(Trace) / 16, s));
+    dev.perf.launches += 2;
     CUDA_CHECK(cudaMemsetAsync(st.hot, 0, z.n * sizeof(NeuronHot), s));
     CUDA_CHECK(cudaMemsetAsync(st.cold, 0, z.n * sizeof(NeuronCold), s));
     CUDA_CHECK(cudaMemsetAsync(st.branches, 0, z.n * sizeof(float4), s));
@@ -848,6 +849,7 @@ std::vector<CtxDelta> collect_lane_context(LeoB200Device& dev, Lane& lane, uint3
     gather_context_rows_kernel<<<std::max(1u, std::min(count / 128 + 1, 1024u)), 128, 0, dev.stream>>>(
         lane.st.ctx_list, count, lane.st.p.ctx_keys, lane.st.p.ctx_obs, lane.st.p.ctx_emb, d, d_rows, d_emb);
     CUDA_CHECK(cudaGetLastError());
+    dev.perf.launches += 2;  // the gather above and the mark clear below
     CUDA_CHECK(cudaMemcpyAsync(slots.data(), lane.st.ctx_list, count * 4, cudaMemcpyDeviceToHost, dev.stream));
     CUDA_CHECK(cudaMemcpyAsync(rows.data(), d_rows, count * sizeof(ContextRow), cudaMemcpyDeviceToHost, dev.stream));
     CUDA_CHECK(cudaMemcpyAsync(emb.data(), d_emb, emb.size() * 4, cudaMemcpyDeviceToHost, dev.stream));
@@ -974,6 +976,7 @@ size_t merge_context_deltas(LeoB200Device& dev, const std::vector<std::vector<Ct
             dev.ctx_sync_slots, n, dev.ctx_stage_rows, dev.ctx_stage_emb, d, dev.canon, dev.d_lanes,
             (int)dev.lanes.size());
         CUDA_CHECK(cudaGetLastError());
+        dev.perf.launches += 1;
         CUDA_CHECK(cudaStreamSynchronize(dev.stream));
     }
     return merged.size();
@@ -1090,6 +1093,7 @@ void sync_replay_changes(LeoB200Device& dev, const LaneScalars& rs) {
         clear_marks_kernel<<<std::max(1u, std::min(it.count / 256 + 1, 4096u)), 256, 0, dev.stream>>>(it.list, it.count,
                                                                                                       it.marks);
         CUDA_CHECK(cudaGetLastError());
+        dev.perf.launches += 2;  // the row scatter and the mark clear
         CUDA_CHECK(cudaStreamSynchronize(dev.stream));
     }
     // Dense tensors: bias and context output weights.
@@ -1125,6 +1129,7 @@ void sync_replay_changes(LeoB200Device& dev, const LaneScalars& rs) {
         clear_marks_kernel<<<std::max(1u, std::min(n / 256 + 1, 4096u)), 256, 0, dev.stream>>>(rl.st.ctx_list, n,
                                                                                               rl.st.ctx_mark);
         CUDA_CHECK(cudaGetLastError());
+        dev.perf.launches += lane_count > 0 ? 3 : 2;
         CUDA_CHECK(cudaStreamSynchronize(dev.stream));
         for (uint32_t i = 0; i < n; ++i) {
             const uint32_t slot = slots[i];
@@ -1288,6 +1293,7 @@ void build_schedules(LeoB200Device& dev, uint32_t first, uint32_t count, int per
     CUDA_CHECK(cudaMemcpyAsync(d, dev.h_stage.data(), need, cudaMemcpyHostToDevice, dev.stream));
     CUDA_CHECK(leo_launch_build_schedules(d + head, reinterpret_cast<const uint64_t*>(d), table, count,
                                           (uint32_t)permission, dev.stream));
+    dev.perf.launches += 1;
 }
 
 // ---------------------------------------------------------------- batch
