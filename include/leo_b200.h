@@ -163,6 +163,12 @@ int leo_b200_set_story_chunk(LeoB200Device* device, uint32_t steps);
    cooperative frozen-advance kernel, crates/leo-core/src/cuda_kernels.cu:4529). */
 int leo_b200_set_quiet_steps(LeoB200Device* device, int enable);
 
+/* Where a one-GPU batch's keyed context merge runs: 1 (the default when a
+   context order's slots fit 200 KB of shared memory at 17 bytes a slot) on the
+   device, 0 on the host mirror.  Results are identical; the reference merges
+   on the host (crates/leo-core/src/parallel.rs:1024-1113, cuda.rs:9230-9260). */
+int leo_b200_set_device_context_merge(LeoB200Device* device, int enable);
+
 /* Execution geometry only: neurons whose recurrent in-degree is at least
    `min_in_degree` are hubs -- their events per step go to a contiguous buffer
    sorted by event order instead of a per-target linked list, which keeps

@@ -116,6 +116,9 @@ class GpuBackend:
     def set_quiet_steps(self, enable: bool) -> None:
         native.check(native.lib().leo_b200_set_quiet_steps(self.handle, 1 if enable else 0))
 
+    def set_device_context_merge(self, enable: bool) -> None:
+        native.check(native.lib().leo_b200_set_device_context_merge(self.handle, 1 if enable else 0))
+
     def perf_stats(self):
         from .ctypes_types import LeoB200PerfStats
 

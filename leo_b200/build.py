@@ -26,7 +26,7 @@ NVCC = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 CU_SOURCES = ["leo_wavefront.cu", "leo_merge_kernels.cu", "leo_shard_kernels.cu", "leo_sparse_apply.cu", "leo_schedule.cu",
-              "leo_runtime.cu"]
+              "leo_context_merge.cu", "leo_runtime.cu"]
 CPP_SOURCES = ["leo_host_model.cpp"]
 
 

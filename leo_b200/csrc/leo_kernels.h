@@ -21,6 +21,55 @@ cudaError_t leo_wavefront_grid_ctas(const KernelConsts& kc, int sms, int* out);
 // Clusters of `cluster` CTAs that can be resident at once.
 cudaError_t leo_wavefront_max_clusters(uint32_t cluster, const KernelConsts& kc, int* out);
 
+// Batch-end keyed context merge on the device (leo_context_merge.cu).
+#define LEO_CTX_MERGE_BAD_DELTA 1u  // a lane's context delta is not finite
+#define LEO_CTX_MERGE_BAD_VALUE 2u  // a merged embedding is not finite after projection
+
+struct CtxMergeArgs {
+    uint32_t slots_per_order, dim, probe_limit, stories;
+    float weight_min, weight_max;
+    // per entry (a lane's changed slot), lane-major
+    uint32_t* lane_slots;
+    uint8_t* valid;
+    unsigned long long* key;
+    uint32_t* order;
+    uint32_t* obs_inc;
+    float* delta;                 // [entries * dim]
+    // per merged (order, key)
+    double* msum;                 // [groups * dim]
+    unsigned long long* mkey;
+    uint32_t* morder;
+    unsigned long long* mobs;
+    // canonical slots the merge wrote
+    uint32_t* canon_slots;
+    uint32_t* canon_slot_count;
+    uint32_t canon_slot_capacity;
+    uint32_t* error;
+};
+
+struct CtxMergeWork {
+    void* temp;
+    size_t temp_bytes;
+    uint32_t *idx_a, *idx_b, *sorted, *gstart, *k32_a, *k32_b, *count;
+    unsigned long long *k64_a, *k64_b;
+    uint8_t* head;
+};
+
+size_t leo_context_apply_smem(uint32_t slots_per_order);
+size_t leo_context_merge_temp_bytes(uint32_t capacity);
+cudaError_t leo_context_merge_configure();
+cudaError_t leo_context_merge_deltas(const LaneState* lanes, const uint32_t* lane_offset, uint32_t lane_count,
+                                     uint32_t max_lane_entries, LaneParams canon, const CtxMergeArgs& a,
+                                     cudaStream_t stream);
+cudaError_t leo_context_merge_group(uint32_t entries, const CtxMergeArgs& a, CtxMergeWork& w, uint32_t* valid_out,
+                                    cudaStream_t stream);
+cudaError_t leo_context_merge_sort(uint32_t valid, const CtxMergeArgs& a, CtxMergeWork& w, uint32_t* groups_out,
+                                   cudaStream_t stream);
+cudaError_t leo_context_merge_apply(uint32_t valid, uint32_t groups, uint32_t orders, LaneParams canon,
+                                    const LaneState* lanes, int lane_count, const uint32_t* lane_slots,
+                                    uint32_t lane_slot_count, const CtxMergeArgs& a, CtxMergeWork& w,
+                                    cudaStream_t stream);
+
 // Zeroes n float4 with evict-first (streaming) stores (leo_schedule.cu).
 cudaError_t leo_launch_zero_streaming(float4* p, size_t n, cudaStream_t stream);
 

@@ -124,6 +124,15 @@ struct LeoB200Device {
     int batch_permission = LEO_B200_TRAINING;
     bool single_story = false;
     std::vector<std::vector<uint8_t>> batch_stories;
+    // Device keyed context merge: buffers for `ctx_capacity` lane entries
+    // (grown on demand; one block of device memory), and whether the
+    // configuration fits its per-order shared-memory tables.
+    bool ctx_device_merge = false;
+    size_t ctx_capacity = 0;
+    std::unique_ptr<DevMem> ctx_mem;
+    CtxMergeArgs ctx_args{};
+    CtxMergeWork ctx_work{};
+    uint32_t* ctx_lane_offset = nullptr;  // [max_lanes + 1]
     // The batch's story bytes staged for the on-device schedule builder.
     std::vector<uint8_t> h_stage;
     std::unique_ptr<DevMem> d_stage;
@@ -982,13 +991,111 @@ size_t merge_context_deltas(LeoB200Device& dev, const std::vector<std::vector<Ct
     return merged.size();
 }
 
-// The single-GPU batch: every story is a resident lane.
+// Device merge buffers for at least `entries` lane entries (one allocation,
+// carved into the per-entry arrays; the canonical slot list is sized by the
+// context table).
+void ensure_ctx_merge(LeoB200Device& dev, size_t entries) {
+    if (dev.ctx_capacity >= entries && dev.ctx_mem) return;
+    const size_t cap = std::max<size_t>({entries, 2 * dev.ctx_capacity, (size_t)1 << 14});
+    const size_t d = dev.z.d, slots = dev.z.ctx;
+    const size_t temp = leo_context_merge_temp_bytes((uint32_t)cap);
+    auto align = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    const size_t u32 = align(cap * 4), u64 = align(cap * 8), u8 = align(cap);
+    const size_t bytes = 10 * u32 + 5 * u64 + 2 * u8 + align(cap * d * 4) + align(cap * d * 8) + align(slots * 4) +
+                         align(64) + align(temp);
+    dev.ctx_mem.reset();
+    auto m = std::make_unique<DevMem>();
+    CUDA_CHECK(cudaMalloc(&m->p, bytes));
+    uint8_t* at = static_cast<uint8_t*>(m->p);
+    auto take = [&](size_t n) {
+        uint8_t* r = at;
+        at += n;
+        return r;
+    };
+    CtxMergeArgs& a = dev.ctx_args;
+    CtxMergeWork& w = dev.ctx_work;
+    a.lane_slots = (uint32_t*)take(u32);
+    a.order = (uint32_t*)take(u32);
+    a.obs_inc = (uint32_t*)take(u32);
+    a.morder = (uint32_t*)take(u32);
+    w.idx_a = (uint32_t*)take(u32);
+    w.idx_b = (uint32_t*)take(u32);
+    w.sorted = (uint32_t*)take(u32);
+    w.gstart = (uint32_t*)take(u32);
+    w.k32_a = (uint32_t*)take(u32);
+    w.k32_b = (uint32_t*)take(u32);
+    a.key = (unsigned long long*)take(u64);
+    a.mkey = (unsigned long long*)take(u64);
+    a.mobs = (unsigned long long*)take(u64);
+    w.k64_a = (unsigned long long*)take(u64);
+    w.k64_b = (unsigned long long*)take(u64);
+    a.valid = take(u8);
+    w.head = take(u8);
+    a.delta = (float*)take(align(cap * d * 4));
+    a.msum = (double*)take(align(cap * d * 8));
+    a.canon_slots = (uint32_t*)take(align(slots * 4));
+    uint32_t* small = (uint32_t*)take(align(64));
+    w.count = small;
+    a.canon_slot_count = small + 1;
+    a.error = small + 2;
+    w.temp = take(align(temp));
+    w.temp_bytes = temp;
+    dev.ctx_mem = std::move(m);
+    dev.ctx_capacity = cap;
+    a.canon_slot_capacity = (uint32_t)slots;
+}
+
+// The single-GPU batch: every story is a resident lane.  The merge runs on the
+// device (leo_context_merge.cu) when the context order's slot partition fits
+// its shared-memory tables; otherwise on the host.
 size_t merge_context(LeoB200Device& dev, uint32_t lane_count, const std::vector<LaneScalars>& scal) {
-    std::vector<std::vector<CtxDelta>> per_lane(lane_count);
-    std::vector<uint32_t> lane_slots;
-    for (uint32_t l = 0; l < lane_count; ++l)
-        per_lane[l] = collect_lane_context(dev, *dev.lanes[l], scal[l].ctx_changed, lane_slots);
-    return merge_context_deltas(dev, per_lane, lane_count, lane_slots);
+    if (!dev.ctx_device_merge) {
+        std::vector<std::vector<CtxDelta>> per_lane(lane_count);
+        std::vector<uint32_t> lane_slots;
+        for (uint32_t l = 0; l < lane_count; ++l)
+            per_lane[l] = collect_lane_context(dev, *dev.lanes[l], scal[l].ctx_changed, lane_slots);
+        return merge_context_deltas(dev, per_lane, lane_count, lane_slots);
+    }
+    std::vector<uint32_t> offset(lane_count + 1, 0);
+    uint32_t widest = 0;
+    for (uint32_t l = 0; l < lane_count; ++l) {
+        offset[l + 1] = offset[l] + scal[l].ctx_changed;
+        widest = std::max(widest, scal[l].ctx_changed);
+    }
+    const uint32_t entries = offset[lane_count];
+    if (entries == 0) return 0;
+    ensure_ctx_merge(dev, entries);
+    CtxMergeArgs& a = dev.ctx_args;
+    a.slots_per_order = dev.cfg.abi.context_slots_per_order;
+    a.dim = (uint32_t)dev.z.d;
+    a.probe_limit = dev.cfg.abi.context_probe_limit;
+    a.stories = lane_count;
+    a.weight_min = dev.cfg.abi.weight_min;
+    a.weight_max = dev.cfg.abi.weight_max;
+    CUDA_CHECK(cudaMemcpyAsync(dev.ctx_lane_offset, offset.data(), offset.size() * 4, cudaMemcpyHostToDevice,
+                               dev.stream));
+    CUDA_CHECK(cudaMemsetAsync(a.error, 0, 4, dev.stream));
+    CUDA_CHECK(leo_context_merge_deltas(dev.d_lanes, dev.ctx_lane_offset, lane_count, widest, dev.canon, a,
+                                        dev.stream));
+    uint32_t valid = 0, groups = 0;
+    CUDA_CHECK(leo_context_merge_group(entries, a, dev.ctx_work, &valid, dev.stream));
+    if (valid) CUDA_CHECK(leo_context_merge_sort(valid, a, dev.ctx_work, &groups, dev.stream));
+    CUDA_CHECK(leo_context_merge_apply(valid, groups, dev.cfg.abi.context_max_order, dev.canon, dev.d_lanes,
+                                       (int)dev.lanes.size(), a.lane_slots, entries, a, dev.ctx_work, dev.stream));
+    dev.perf.launches += 16;
+    uint32_t error = 0;
+    CUDA_CHECK(cudaMemcpyAsync(&error, a.error, 4, cudaMemcpyDeviceToHost, dev.stream));
+    // the host mirror of the canonical context follows the device tables
+    CUDA_CHECK(cudaMemcpyAsync(dev.ctx_keys.data(), dev.canon.ctx_keys, dev.ctx_keys.size() * 8,
+                               cudaMemcpyDeviceToHost, dev.stream));
+    CUDA_CHECK(cudaMemcpyAsync(dev.ctx_obs.data(), dev.canon.ctx_obs, dev.ctx_obs.size() * 4, cudaMemcpyDeviceToHost,
+                               dev.stream));
+    CUDA_CHECK(cudaMemcpyAsync(dev.ctx_emb.data(), dev.canon.ctx_emb, dev.ctx_emb.size() * 4, cudaMemcpyDeviceToHost,
+                               dev.stream));
+    CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+    if (error & LEO_CTX_MERGE_BAD_DELTA) throw LeoFailure("invalid keyed context worker delta");
+    if (error & LEO_CTX_MERGE_BAD_VALUE) throw LeoFailure("merged context embedding violates canonical parameter bounds");
+    return groups;
 }
 
 // ---------------------------------------------------------------- fixed tensor merge
@@ -1914,6 +2021,9 @@ int leo_b200_open(int device, const LeoB200HostModel* canonical, uint32_t max_la
             dev->grid_ctas = 0;
         }
         dev->quiet_smem = leo_quiet_smem_bytes(dev->kc);
+        dev->ctx_lane_offset = dev->mem.alloc<uint32_t>(max_lanes + 1);
+        dev->ctx_device_merge = leo_context_apply_smem(dev->cfg.abi.context_slots_per_order) <= 200u * 1024u &&
+                                leo_context_merge_configure() == cudaSuccess;
         CUDA_CHECK(cudaEventCreate(&dev->quiet_start));
         CUDA_CHECK(cudaEventCreate(&dev->quiet_stop));
         upload_model(*dev, *canonical);
@@ -2354,6 +2464,13 @@ int leo_b200_set_cluster_sizes(LeoB200Device* dev, uint32_t story_cluster, uint3
     }
     dev->story_cluster_request = story_cluster;
     dev->replay_cluster_request = replay_cluster;
+    return 0;
+}
+
+int leo_b200_set_device_context_merge(LeoB200Device* dev, int enable) {
+    if (enable && leo_context_apply_smem(dev->cfg.abi.context_slots_per_order) > 200u * 1024u)
+        return fail(LeoFailure("context slots per order exceed the device merge's shared-memory tables"));
+    dev->ctx_device_merge = enable != 0;
     return 0;
 }
 

@@ -163,3 +163,25 @@ def test_gpu_replay_prefix_kernel_matches_golden(native_lib, case_name, quiet):
         perf = backend.perf_stats()
         assert (perf.quiet_steps > 0) == quiet
         assert (perf.quiet_launches > 0) == quiet
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case_name", ["test", "baseline1", "baseline2-short", "baseline3-short", "test-8"])
+@pytest.mark.parametrize("device_merge", [True, False], ids=["device-context-merge", "host-context-merge"])
+def test_gpu_context_merge_site_matches_golden(native_lib, case_name, device_merge):
+    """The batch-end keyed context merge gives the golden hashes whether it
+    runs on the device (per-order slot tables in shared memory) or on the host
+    mirror, and the merged key count in the report is the same."""
+    from leo_b200.backend import GpuBackend
+    from leo_b200.ctypes_types import TRAINING
+    from leo_b200.model import HostModel
+
+    case = CASES[case_name]
+    w, batches = _stories(case)
+    model = HostModel.initialize(w.config, w.topology)
+    with GpuBackend(model, device=0, max_lanes=case["stories_per_batch"]) as backend:
+        backend.set_device_context_merge(device_merge)
+        for i, (rec, batch) in enumerate(zip(case["batches"], batches)):
+            result = backend.training_story_batch(batch, TRAINING)
+            assert backend.state_digest().hex() == rec["state_hash"], f"batch {i}"
+            assert int(result.report.context_keys) == rec["report"]["context_keys"], f"batch {i}"
