@@ -301,6 +301,38 @@ def run_sparse_apply_micro(args) -> None:
         dist.destroy_process_group()
 
 
+def measure_replay_off(backend, workload, args, device: int) -> dict:
+    """The same model with replay fraction 0 (the reference's replay-off
+    figure): one warm-up and `--steps` timed batches of fresh stories, CUDA-event
+    batch time.  The main backend is closed first so both never hold the device."""
+    from dataclasses import replace
+
+    from leo_b200.backend import GpuBackend
+    from leo_b200.ctypes_types import TRAINING
+    from leo_b200.model import HostModel
+    from leo_b200.synthetic import story_stream
+
+    trained = backend.synchronize_model()
+    model = HostModel(replace(workload.config, replay_fraction=0.0), trained.arrays)
+    model.generation, model.parameter_revision, model.statistics = (trained.generation, trained.parameter_revision,
+                                                                    trained.statistics)
+    backend.close()
+    n = workload.workers
+    stories = story_stream(workload.story_seed + 1, n * (args.steps + 1), workload.min_story_bytes,
+                           workload.max_story_bytes)
+    with GpuBackend(model, device=device, max_lanes=2 * n) as off:
+        off.training_story_batch(stories[:n], TRAINING)
+        off.reset_perf_stats()
+        nbytes = 0
+        for b in range(1, args.steps + 1):
+            batch = stories[b * n:(b + 1) * n]
+            off.training_story_batch(batch, TRAINING)
+            nbytes += sum(len(s) for s in batch)
+        ms = off.perf_stats().batch_ms
+    return {"value": round(nbytes / (ms / 1000.0), 3), "unit": UNIT, "ms_per_step": round(ms / args.steps, 3),
+            "batches": args.steps, "note": "same model, replay fraction 0, fresh stories"}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -311,6 +343,8 @@ def main() -> None:
     ap.add_argument("--cpu-stories", type=int, default=16)
     ap.add_argument("--cpu-bytes", type=int, default=0, help="fixed CPU sample story length (0: workload's range)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-replay-off", action="store_true",
+                    help="skip the replay-off figure (same model, replay fraction 0) that follows the timed batches")
     ap.add_argument("--micro", choices=["sparse-apply"], default=None,
                     help="run a microbenchmark instead of the training step (config 5)")
     ap.add_argument("--densities", default="0.001,0.01,0.1")
@@ -382,6 +416,7 @@ def main() -> None:
     wall = 0.0
     nbytes = 0
     h2d = d2h = 0
+    story_steps = replay_steps = 0
     for b in range(args.warmup, total_batches):
         batch = batches[b]
         t0 = time.perf_counter()
@@ -390,9 +425,15 @@ def main() -> None:
         nbytes += sum(len(s) for s in batch)
         h2d += sum(len(s) for s in batch) + 8 * (len(batch) + 1)
         d2h += 4 * sum(len(x) for x in result.losses) + 48 * len(batch) + 80
+        story_steps += sum(len(s) + 1 for s in batch if s)
+        replay_steps += int(result.report.replay_steps) + int(result.report.replay_prefix_steps)
     perf = backend.perf_stats()
     clk = clocks.stop()
     device_s = perf.batch_ms / 1000.0
+    device_gb = round(backend.device_bytes() / 1e9, 3)
+    replay_off = None
+    if world == 1 and cfg.replay_fraction > 0 and not args.no_replay_off:
+        replay_off = measure_replay_off(backend, workload, args, local)
     times = np.array([device_s, wall, float(nbytes)], dtype=np.float64)
     if dist is not None:
         import torch
@@ -417,6 +458,7 @@ def main() -> None:
                     "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 6), "peak_source": peak_kind,
                     "traffic": traffic, "traffic_source": traffic_source,
                     "algorithmic_bytes_per_launch": round(per_launch_bytes, 1),
+                    "frac_of_nominal_8tbs": round(achieved / 8000.0, 6),
                     "launch_ms": round(per_launch_ms, 4), "launches": int(perf.wavefront_launches),
                     "share_of_step_time": round(perf.wavefront_ms / max(perf.batch_ms, 1e-9), 4),
                     "story_pass_launch_ms": round(perf.story_wavefront_ms / story_launches, 3),
@@ -438,10 +480,13 @@ def main() -> None:
             "e2e": {"value": round(total_bytes / wall, 3), "unit": UNIT, "h2d_bytes_per_step": h2d // args.steps,
                     "d2h_bytes_per_step": d2h // args.steps},
             "roofline": roofline, "clocks": clk, "gpu_launches": int(perf.launches),
+            "steps_per_second": round(story_steps / device_s, 1),
+            "execution_steps_per_second": round((story_steps + replay_steps) / device_s, 1),
+            "replay_off": replay_off,
             "batch_end_ms_per_step": {k: round(getattr(perf, k) / args.steps, 2)
                                       for k in ("collect_ms", "merge_fixed_ms", "merge_context_ms", "replay_ms",
                                                 "replay_sync_ms")},
-            "device_gb": round(backend.device_bytes() / 1e9, 3),
+            "device_gb": device_gb,
         }
         if not args.no_cpu_baseline:
             res = cpu_sample(workload, min(args.cpu_stories, os.cpu_count() or 1), args.cpu_stories,

@@ -47,3 +47,5 @@ def test_gpu_arm_prints_the_contract_line(native_lib, oracle_lib):
     assert d["gpu_launches"] > 0
     assert {"sm_mhz", "sm_max_mhz", "reasons"} <= set(d["clocks"])
     assert set(d["cpu_baseline"]) >= {"value", "unit", "cores", "kind", "sample"}
+    assert d["replay_off"]["value"] > 0 and d["replay_off"]["unit"] == d["unit"]
+    assert d["execution_steps_per_second"] >= d["steps_per_second"] > 0
