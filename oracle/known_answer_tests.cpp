@@ -142,12 +142,23 @@ static size_t configure_chain(Model& m, size_t source, size_t links, uint8_t del
 
 int main() {
     // ---------------------------------------------------------------- learning.rs:83-108
-    run("learning.rs:84 analog_surrogate_preserves_selected_unsaturated_gradient", [] {
-        // analog_rank_surrogate is file-local in the oracle; exercise it through the runtime's formula.
-        float margin = 0.5f, cutoff = 0.4f, width = 0.25f, gain = 0.1f;
-        float direct = 1.0f;
-        float boundary = std::fmin(std::fmax(1.0f - std::fabs(margin - cutoff) / width, 0.0f), 1.0f);
-        CHECK(std::fabs(direct + gain * boundary - 1.06f) <= 1.0e-6f);
+    run("learning.rs:85 analog_surrogate_preserves_selected_unsaturated_gradient", [] {
+        CHECK(std::fabs(analog_rank_surrogate(0.5f, 0.4f, true, 0.25f, 0.1f) - 1.06f) <= 1.0e-6f);
+        CHECK(analog_rank_surrogate(1.0f, 0.4f, true, 0.25f, 0.1f) == 0.0f);
+    });
+    run("learning.rs:91 branch_jacobian_matches_integrated_branch_semantics", [] {
+        CHECK(branch_jacobian(BRANCH_EXCITATORY, 1.0f, 0.5f, 0.5f) == 1.0f);
+        CHECK(branch_jacobian(BRANCH_TEMPORAL, 1.0f, 0.5f, 0.5f) == 0.5f);
+        CHECK(branch_jacobian(BRANCH_INHIBITORY, 1.0f, 0.5f, 0.5f) == 1.0f);
+        CHECK(branch_jacobian(BRANCH_CONTEXT_GATE, 1.0f, 0.5f, 0.5f) == 0.5f);
+    });
+    run("learning.rs:99 inhibitory_homeostasis_pushes_in_the_correct_direction", [] {
+        CHECK(inhibitory_homeostasis_delta(1.0f, 0.10f, 0.02f, 0.01f, 1.0f, 0.1f) < 0.0f);
+        CHECK(inhibitory_homeostasis_delta(1.0f, 0.00f, 0.02f, 0.01f, 1.0f, 0.1f) > 0.0f);
+    });
+    run("learning.rs:105 update_clipping_is_symmetric", [] {
+        CHECK(bounded_delta(1.0f, 0.1f) == 0.1f);
+        CHECK(bounded_delta(-1.0f, 0.1f) == -0.1f);
     });
 
     // ---------------------------------------------------------------- runtime.rs tests

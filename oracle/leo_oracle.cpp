@@ -69,15 +69,28 @@ inline bool context_survives_dropout(uint64_t seed, uint64_t tick, uint32_t symb
     return draw >= rate;
 }
 
+
+// Rust's f32 Sum folds from -0.0 (Rust >= 1.83; the reference pins 1.85).
+inline float sum3(float a, float b, float c) {
+    float s = -0.0f;
+    s += a;
+    s += b;
+    s += c;
+    return s;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- learning.rs (declared in leo_oracle.hpp)
 // learning.rs:6-24
-inline float analog_rank_surrogate(float margin, float cutoff, bool selected, float width, float gain) {
+float analog_rank_surrogate(float margin, float cutoff, bool selected, float width, float gain) {
     float direct = (selected && margin > 0.0f && margin < 1.0f) ? 1.0f : 0.0f;
     if (width <= 0.0f || gain <= 0.0f) return direct;
     float boundary = clampf(1.0f - std::fabs(margin - cutoff) / width, 0.0f, 1.0f);
     return direct + gain * boundary;
 }
 // learning.rs:28-50
-inline float branch_jacobian(uint8_t branch, float exc, float temporal, float gate_acc) {
+float branch_jacobian(uint8_t branch, float exc, float temporal, float gate_acc) {
     float gate = clampf(gate_acc, 0.0f, 1.0f);
     switch (branch) {
         case BRANCH_EXCITATORY: return exc;
@@ -91,24 +104,13 @@ inline float branch_jacobian(uint8_t branch, float exc, float temporal, float ga
     }
 }
 // learning.rs:52-55
-inline float bounded_delta(float v, float maximum) { return clampf(v, -maximum, maximum); }
+float bounded_delta(float v, float maximum) { return clampf(v, -maximum, maximum); }
 // learning.rs:59-73
-inline float inhibitory_homeostasis_delta(float src_act, float tgt_act, float desired, float lr, float strength,
+float inhibitory_homeostasis_delta(float src_act, float tgt_act, float desired, float lr, float strength,
                                           float maximum) {
     float err = tgt_act - desired;
     return bounded_delta(-lr * strength * src_act * err, maximum);
 }
-
-// Rust's f32 Sum folds from -0.0 (Rust >= 1.83; the reference pins 1.85).
-inline float sum3(float a, float b, float c) {
-    float s = -0.0f;
-    s += a;
-    s += b;
-    s += c;
-    return s;
-}
-
-}  // namespace
 
 // ---------------------------------------------------------------- rng.rs:13-36
 uint64_t SplitMix64::next_u64() {

@@ -34,6 +34,13 @@ constexpr uint8_t BRANCH_INHIBITORY = 1;
 constexpr uint8_t BRANCH_TEMPORAL = 2;
 constexpr uint8_t BRANCH_CONTEXT_GATE = 3;
 
+// crates/leo-core/src/learning.rs:6-73
+float analog_rank_surrogate(float margin, float cutoff, bool selected, float width, float gain);
+float branch_jacobian(uint8_t branch, float exc, float temporal, float gate_acc);
+float bounded_delta(float v, float maximum);
+float inhibitory_homeostasis_delta(float src_act, float tgt_act, float desired, float lr, float strength,
+                                   float maximum);
+
 struct LeoError : std::runtime_error {
     enum Kind { Internal, Configuration, Numerical };
     Kind kind;
