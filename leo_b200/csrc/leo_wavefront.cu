@@ -857,7 +857,12 @@ __device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts
 // blocks: block-local top-k and the exact (k+1)-th cutoff (runtime.rs:964-997),
 // one warp per block; keys are unique, so "largest key below the previous
 // winner" enumerates the block in rank order.
-__device__ void phase_blocks(const LaneState& ln, const KernelConsts& kc, uint32_t gwarp, uint32_t gwarps) {
+//
+// `winners` / `nwin` receive each block's winners and their count: the first
+// CTA's shared memory (through the cluster's distributed shared memory) in
+// the cluster wavefront, global memory in the whole-GPU launch.
+__device__ void phase_blocks(const LaneState& ln, const KernelConsts& kc, uint32_t gwarp, uint32_t gwarps,
+                             unsigned long long* winners, uint32_t* nwin) {
     const uint32_t B = kc.topo.blocks, npb = kc.topo.npb, keep = kc.topo.keep;
     const uint32_t lane = threadIdx.x & 31u;
     uint32_t supra = 0;
@@ -886,14 +891,14 @@ __device__ void phase_blocks(const LaneState& ln, const KernelConsts& kc, uint32
                 best = other > best ? other : best;
             }
             if (k < keep) {
-                if (lane == 0) ln.block_winners[(size_t)b * keep + k] = best;
+                if (lane == 0) winners[(size_t)b * keep + k] = best;
             } else {
                 cutoff = key_value(best);
             }
             prev = best;
         }
         if (lane == 0) {
-            ln.block_nwin[b] = count < keep ? count : keep;
+            nwin[b] = count < keep ? count : keep;
             ln.block_cutoff[b] = count > keep ? cutoff : 0.0f;
             ln.block_cand_count[b] = 0;
             supra += count;
@@ -1584,11 +1589,23 @@ __device__ __forceinline__ unsigned long long clock_now() { return clock64(); }
 // ---------------------------------------------------------------------------
 // The persistent wavefront: the C CTAs of group blockIdx.x / C run that lane
 // through steps [begin, end) of its schedule, `sync` separating the phases.
+//
+// `win_write` / `nwin_write`: where the blocks phase of every CTA puts the
+// block winners; `win_read` / `nwin_read`: where the first CTA's assemble
+// reads them (null: the lane's global arrays for both).
 template <typename Sync>
 __device__ __forceinline__ void wavefront_steps(const LaneState* __restrict__ lanes, uint32_t begin, uint32_t end,
                                                 const KernelConsts& kc, uint32_t C, uint32_t rank, Sync sync,
-                                                unsigned long long* smem_sorted) {
+                                                unsigned long long* smem_sorted, unsigned long long* win_write,
+                                                uint32_t* nwin_write, const unsigned long long* win_read,
+                                                const uint32_t* nwin_read) {
     const LaneState& ln = lanes[blockIdx.x / C];
+    if (!win_write) {
+        win_write = ln.block_winners;
+        nwin_write = ln.block_nwin;
+        win_read = ln.block_winners;
+        nwin_read = ln.block_nwin;
+    }
     LaneScalars* sc = ln.sc;
     const uint32_t steps = sc->steps;
     if (begin == LEO_RESUME_STEP) begin = sc->resume_step;
@@ -1633,11 +1650,11 @@ __device__ __forceinline__ void wavefront_steps(const LaneState* __restrict__ la
         mark(1);
         for (uint32_t h = worker; h < kc.topo.hubs; h += workers) ln.hub_count[h] = 0;
         if (worker == 0) sc->hub_next = 0;
-        phase_blocks(ln, kc, gwarp, gwarps);
+        phase_blocks(ln, kc, gwarp, gwarps, win_write, nwin_write);
         if (frozen && worker == 0) release_touched(ln, tally);
         sync();
         mark(2);
-        if (rank == 0) phase_assemble(ln, s, kc, !frozen, smem_sorted, ln.block_nwin, ln.block_winners, nullptr);
+        if (rank == 0) phase_assemble(ln, s, kc, !frozen, smem_sorted, nwin_read, win_read, nullptr);
         sync();
         mark(3);
         if (!frozen) {
@@ -2176,13 +2193,19 @@ cudaError_t leo_launch_quiet(const LaneState* lane, uint32_t begin, uint32_t end
     return cudaGetLastError();
 }
 
+__host__ __device__ size_t wavefront_scratch_bytes(const KernelConsts& kc);
+
 // A thread-block cluster per lane (phases separated by cluster barriers).
 __global__ void __launch_bounds__(kThreads, 1)
     leo_wavefront_kernel(const LaneState* __restrict__ lanes, uint32_t begin, uint32_t end, KernelConsts kc) {
     extern __shared__ unsigned long long smem_sorted[];
     cg::cluster_group cluster = cg::this_cluster();
+    // Block winners go straight to the first CTA's shared memory (distributed
+    // shared memory), where its assemble reads them after the phase barrier.
+    unsigned long long* win = smem_sorted + wavefront_scratch_bytes(kc) / sizeof(unsigned long long);
+    uint32_t* nwin = reinterpret_cast<uint32_t*>(win + (size_t)kc.topo.blocks * kc.topo.keep);
     wavefront_steps(lanes, begin, end, kc, cluster.num_blocks(), cluster.block_rank(), [&] { cluster.sync(); },
-                    smem_sorted);
+                    smem_sorted, cluster.map_shared_rank(win, 0), cluster.map_shared_rank(nwin, 0), win, nwin);
 }
 
 // One lane over the whole GPU: one CTA per SM in a cooperative launch, phases
@@ -2192,12 +2215,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     leo_wavefront_grid_kernel(const LaneState* __restrict__ lanes, uint32_t begin, uint32_t end, KernelConsts kc) {
     extern __shared__ unsigned long long smem_sorted[];
     cg::grid_group grid = cg::this_grid();
-    wavefront_steps(lanes, begin, end, kc, gridDim.x, blockIdx.x, [&] { grid.sync(); }, smem_sorted);
+    wavefront_steps(lanes, begin, end, kc, gridDim.x, blockIdx.x, [&] { grid.sync(); }, smem_sorted, nullptr, nullptr,
+                    nullptr, nullptr);
 }
 
 // Dynamic shared memory: the assemble phase's sort buffer and the learn
 // phase's transpose tiles share one region (the phases never overlap).
-size_t leo_wavefront_smem_bytes(const KernelConsts& kc) {
+// Bytes of the phases' shared scratch (sort buffer, transpose tiles, hub
+// sorts), a multiple of 16.
+__host__ __device__ size_t wavefront_scratch_bytes(const KernelConsts& kc) {
     uint32_t winners = kc.topo.blocks * kc.topo.keep, span = 1;
     while (span < winners) span <<= 1;
     size_t sort = (size_t)span * sizeof(unsigned long long);
@@ -2211,7 +2237,13 @@ size_t leo_wavefront_smem_bytes(const KernelConsts& kc) {
         size_t hub = warps > cta ? warps : cta;
         bytes = bytes > hub ? bytes : hub;
     }
-    return bytes;
+    return (bytes + 15) & ~(size_t)15;
+}
+
+// The scratch, then the block winners (blocks x keep keys) and their counts.
+size_t leo_wavefront_smem_bytes(const KernelConsts& kc) {
+    const size_t winners = (size_t)kc.topo.blocks * kc.topo.keep;
+    return wavefront_scratch_bytes(kc) + winners * sizeof(unsigned long long) + (size_t)kc.topo.blocks * sizeof(uint32_t);
 }
 
 // Function attributes the launches and occupancy queries rely on; called
