@@ -36,7 +36,10 @@
 //   plasticity recurrent / input weight updates (runtime.rs:1451-1523)
 //   inhibit    inhibitory homeostasis (runtime.rs:1525-1565) + step epilogue
 // Frozen steps (replay prefixes) run deliver, settle, blocks, assemble and
-// emit only: nothing else can change state on a frozen step.
+// emit only: nothing else can change state on a frozen step; a frozen step
+// without a target shares its emit phase with the next step's deliver.  The
+// blocks phase writes each block's winners into the first CTA's shared memory
+// through the cluster's distributed shared memory, where assemble reads them.
 //
 // Exactness: every floating-point sum that the CPU forms sequentially is
 // formed sequentially here in the same order (branch inputs in event order,
