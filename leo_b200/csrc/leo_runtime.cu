@@ -1481,7 +1481,10 @@ void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySu
             dev.canonical_tick += story.size() + 1;
             dev.revision += sc.revision_increment;
             dev.stats.processed_bytes += sc.processed_bytes;
-            dev.stats.processed_stories += 1;
+            // finish_document counts a story only after a non-frozen step
+            // (runtime.rs:357-362, 492-496): every step of a story pass has
+            // the batch's permission.
+            dev.stats.processed_stories += dev.batch_permission != LEO_B200_FROZEN ? 1 : 0;
             dev.stats.training_loss_sum = sc.loss_sum;
             dev.stats.training_targets += sc.targets;
             dev.stats.active_neurons_sum += sc.active_sum;
@@ -1537,7 +1540,7 @@ void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySu
             const LaneScalars& sc = scal[l];
             const auto& story = dev.batch_stories[l];
             dev.stats.processed_bytes += sc.processed_bytes;
-            dev.stats.processed_stories += story.empty() ? 0 : 1;
+            dev.stats.processed_stories += (story.empty() || dev.batch_permission == LEO_B200_FROZEN) ? 0 : 1;
             dev.stats.training_loss_sum += sc.loss_sum - canon_loss;
             dev.stats.training_targets += sc.targets;
             dev.stats.active_neurons_sum += sc.active_sum;
@@ -1800,7 +1803,7 @@ void shard_finish(LeoB200Device& dev, const LeoB200ShardStory* all, const float*
     for (uint32_t i = 0; i < stories; ++i) {
         const LeoB200ShardStory& sc = all[i];
         dev.stats.processed_bytes += sc.processed_bytes;
-        dev.stats.processed_stories += sc.story_bytes == 0 ? 0 : 1;
+        dev.stats.processed_stories += (sc.story_bytes == 0 || dev.batch_permission == LEO_B200_FROZEN) ? 0 : 1;
         dev.stats.training_loss_sum += sc.loss_sum - canon_loss;
         dev.stats.training_targets += sc.targets;
         dev.stats.active_neurons_sum += sc.active_sum;

@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 
 from leo_b200.configs import WORKLOADS
-from leo_b200.ctypes_types import TRAINING
+from leo_b200.ctypes_types import FROZEN, PROVISIONAL, TRAINING, VERIFIED
 from leo_b200.synthetic import story_stream
 from parity_helpers import compare_lane, story_steps
 
@@ -87,5 +87,30 @@ def test_single_story_batch_trains_canonical_directly(native_lib, oracle_lib):
         backend.training_story_batch(story, TRAINING)
         canonical.train_story_batch(story, TRAINING)
         assert backend.state_digest() == canonical.model.training_state_hash()
+        assert backend.canonical_tick == canonical.tick
+    backend.close()
+
+
+@pytest.mark.parametrize("permission", [FROZEN, PROVISIONAL, VERIFIED], ids=["frozen", "provisional", "verified"])
+def test_story_batch_permissions_match_oracle(permission, native_lib, oracle_lib):
+    """Non-training permissions (permission.rs:24-31): frozen batches learn
+    nothing and count no story; provisional and verified scale learning by
+    their strength.  Losses, report, tensors, digest and tick against the oracle."""
+    wl, hm, om = _models("test", oracle_lib)
+    stories = story_stream(5, 4, 8, 40)
+    backend = _backend(hm, 4)
+    canonical = oracle_lib.OracleRuntime(om)
+    for batch in range(2):
+        result = backend.training_story_batch(stories, permission)
+        report, losses, ranges = canonical.train_story_batch(stories, permission)
+        got = np.concatenate(result.losses)
+        assert np.array_equal(got.view(np.uint32), losses.view(np.uint32)), f"batch {batch}: losses differ"
+        assert result.report.replay_steps == report.replay_steps
+        assert result.report.fixed_parameter_updates == report.fixed_parameter_updates
+        gm = backend.synchronize_model()
+        cm = canonical.model.arrays()
+        bad = [k for k in gm.arrays if not np.array_equal(gm.arrays[k].view(np.uint8), cm[k].view(np.uint8))]
+        assert not bad, f"batch {batch}: canonical tensors differ: {bad}"
+        assert backend.state_digest() == canonical.model.training_state_hash(), f"batch {batch}: digest differs"
         assert backend.canonical_tick == canonical.tick
     backend.close()
