@@ -248,7 +248,7 @@ class OracleRuntime:
         offsets = np.zeros(len(stories) + 1, dtype=np.uint64)
         offsets[1:] = np.cumsum([len(s) for s in stories])
         report = LeoB200BatchReport()
-        total_targets = sum(len(s) + 1 for s in stories)
+        total_targets = sum(len(s) + 1 for s in stories if s)  # an empty story has no steps
         losses = np.zeros(max(total_targets, 1), dtype=np.float32)
         max_ranges = total_targets + len(stories)
         ranges = np.zeros(2 * max(max_ranges, 1), dtype=np.uint64)

@@ -114,3 +114,29 @@ def test_story_batch_permissions_match_oracle(permission, native_lib, oracle_lib
         assert backend.state_digest() == canonical.model.training_state_hash(), f"batch {batch}: digest differs"
         assert backend.canonical_tick == canonical.tick
     backend.close()
+
+
+def test_edge_case_stories_match_oracle(native_lib, oracle_lib):
+    """An empty story, a one-byte story, arbitrary bytes 0-255 and a story
+    longer than 4,096 steps in one batch, then a single-story frozen batch:
+    losses, report, tensors, digest and tick against the oracle."""
+    wl, hm, om = _models("test", oracle_lib)
+    rng = np.random.default_rng(7)
+    stories = [b"", b"x", bytes(rng.integers(0, 256, 300, dtype=np.uint8)),
+               bytes(rng.integers(32, 127, 5000, dtype=np.uint8))]
+    backend = _backend(hm, 4)
+    canonical = oracle_lib.OracleRuntime(om)
+    for batch, permission in ((stories, TRAINING), ([stories[2]], FROZEN)):
+        result = backend.training_story_batch(batch, permission)
+        report, losses, ranges = canonical.train_story_batch(batch, permission)
+        got = np.concatenate(result.losses) if result.losses else np.zeros(0, np.float32)
+        assert np.array_equal(got.view(np.uint32), losses.view(np.uint32)), "losses differ"
+        assert result.report.replay_steps == report.replay_steps
+        assert result.report.replay_prefix_steps == report.replay_prefix_steps
+        gm = backend.synchronize_model()
+        cm = canonical.model.arrays()
+        bad = [k for k in gm.arrays if not np.array_equal(gm.arrays[k].view(np.uint8), cm[k].view(np.uint8))]
+        assert not bad, f"canonical tensors differ: {bad}"
+        assert backend.state_digest() == canonical.model.training_state_hash()
+        assert backend.canonical_tick == canonical.tick
+    backend.close()
