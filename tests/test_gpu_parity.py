@@ -140,3 +140,26 @@ def test_edge_case_stories_match_oracle(native_lib, oracle_lib):
         assert backend.state_digest() == canonical.model.training_state_hash()
         assert backend.canonical_tick == canonical.tick
     backend.close()
+
+
+def test_replace_model_restarts_from_the_given_model(native_lib, oracle_lib):
+    """replace_model (leo_b200_upload_canonical: the trait's model_mut /
+    synchronize flow) puts a host model back on the device and into every
+    lane: training the same batch again from the initial model and tick gives
+    the same digest; a batch wider than the lanes reserved at open is refused."""
+    from leo_b200.native import LeoError
+
+    wl, hm, om = _models("test", oracle_lib)
+    stories = story_stream(9, 4, 8, 40)
+    backend = _backend(hm, 4)
+    backend.training_story_batch(stories, TRAINING)
+    first = backend.state_digest()
+    backend.training_story_batch(stories, TRAINING)  # moves the lanes and canonical model on
+    assert backend.state_digest() != first
+    backend.replace_model(hm)
+    backend.canonical_tick = 0
+    backend.training_story_batch(stories, TRAINING)
+    assert backend.state_digest() == first
+    with pytest.raises(LeoError, match="lanes"):
+        backend.training_story_batch(stories + stories, TRAINING)
+    backend.close()
