@@ -153,16 +153,6 @@ int leo_b200_set_cluster_sizes(LeoB200Device* device, uint32_t story_cluster, ui
    plays this role statically, crates/leo-core/src/cuda_plan.rs:189-453). */
 int leo_b200_set_story_chunk(LeoB200Device* device, uint32_t steps);
 
-/* Execution geometry only: with `enable`, a replay segment's frozen prefix
-   first runs on one CTA with its per-step lists in shared memory while each
-   step's touched neurons and events fit (a few hundred neurons per step is
-   typical), and the wavefront resumes at the first step that does not fit.
-   Off by default: on a 65,536-neuron model such a step takes about as long on
-   one SM (its issue rate and L2 latency bound it) as on the 16-CTA wavefront.
-   No reference counterpart (the reference runs replay prefixes on its
-   cooperative frozen-advance kernel, crates/leo-core/src/cuda_kernels.cu:4529). */
-int leo_b200_set_quiet_steps(LeoB200Device* device, int enable);
-
 /* Where a one-GPU batch's keyed context merge runs: 1 (the default when a
    context order's slots fit 200 KB of shared memory at 17 bytes a slot) on the
    device, 0 on the host mirror.  Results are identical; the reference merges
@@ -195,7 +185,11 @@ size_t leo_b200_device_bytes(LeoB200Device* device);
    Story s owns entries story_offsets[s] .. story_offsets[s + 1] of `indices`
    (sorted, strictly increasing, < length) and `deltas` (finite); the offsets
    and the replica pointer table are HOST arrays, everything else is device
-   memory on `device`.  Invalid input is rejected before anything is written.
+   memory on `device`.  Invalid input (an index out of range or out of order,
+   a non-finite delta) is rejected before anything is written.  A merged value
+   that becomes non-finite is reported only after the merge pass: by then the
+   target and the replicas may be partly updated (clamped values written for
+   some tiles), as the reference's apply also fails after partial writes.
    At most 256 stories and 64 replicas per call.  `stream` is a cudaStream_t
    (NULL: the legacy default stream); the call waits for it and stores the
    number of merged indices in *updates.  Scratch (a tile table of
@@ -214,11 +208,13 @@ int leo_b200_sparse_mean_apply(int device, float* target, uint32_t length, const
    a small scratch, and latency-bounded loops must not enter the allocator.
    Scratch is a fixed 1 MiB device array compiled into the library: the call
    accepts stories * (ceil(length / 4096) + 1) <= 262080 (for example 63
-   stories at length 2^24, or 256 stories up to length 4,165,632) and rejects
-   larger inputs with an error before any device work; the other limits and
-   the results are those of leo_b200_sparse_mean_apply.  The first call on a
-   device resolves the array's address (cudaGetSymbolAddress); make that first
-   call before any stream capture begins.  Every call zeroes the counters at
+   stories at length 2^24, or 256 stories up to length 4,186,112 = 1022
+   tiles) and rejects larger inputs with an error before any device work; the
+   other limits, the results and the error behaviour (including the partial
+   writes before a non-finite merged value is reported) are those of
+   leo_b200_sparse_mean_apply.  The first call on a device resolves the
+   array's address (cudaGetSymbolAddress); make that first call before any
+   stream capture begins.  Every call zeroes the counters at
    the head of the array on `stream` before its kernels run.  All calls on one
    device share the array: calls that overlap in time race, so the caller
    serialises them. */

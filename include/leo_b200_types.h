@@ -247,10 +247,15 @@ typedef struct LeoB200PerfStats {
     double merge_context_ms;  /* keyed context merge and lane context sync */
     double replay_ms;         /* serial canonical replay, range selection to last segment */
     double replay_sync_ms;    /* replay's changed rows into every lane */
-    uint64_t quiet_launches;  /* replay-prefix launches of the one-CTA quiet-step kernel */
-    uint64_t quiet_steps;     /* steps it ran (the wavefront resumed after them) */
-    double quiet_ms;          /* its device time */
-    uint64_t quiet_cycles[6]; /* its SM cycles: deliver, group, settle, blocks, assemble, emit */
+    /* The replay lane alone (serial canonical replay): phase cycles of its
+       first CTA's first thread (wall time of the launch, barrier waits
+       included), and its work counters. */
+    uint64_t replay_phase_cycles[LEO_B200_PHASES];
+    uint64_t replay_work_steps;
+    uint64_t replay_work_touched;
+    uint64_t replay_work_active;
+    uint64_t replay_work_deliver;
+    uint64_t replay_work_eligible;
 } LeoB200PerfStats;
 
 #ifdef __cplusplus

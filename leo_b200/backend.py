@@ -113,9 +113,6 @@ class GpuBackend:
     def set_story_chunk(self, steps: int) -> None:
         native.check(native.lib().leo_b200_set_story_chunk(self.handle, steps))
 
-    def set_quiet_steps(self, enable: bool) -> None:
-        native.check(native.lib().leo_b200_set_quiet_steps(self.handle, 1 if enable else 0))
-
     def set_device_context_merge(self, enable: bool) -> None:
         native.check(native.lib().leo_b200_set_device_context_merge(self.handle, 1 if enable else 0))
 

@@ -36,10 +36,9 @@
 #define LEO_MAX_EMBEDDING 256u
 #define LEO_WAVEFRONT_THREADS 512u  // threads per CTA of the persistent wavefront
 #define LEO_PHASES 11
-#define LEO_QUIET_PHASES 6  // quiet-step kernel: deliver, group, settle, blocks, assemble, emit
-// A wavefront launch whose first step is the lane's resume_step (written by
-// the quiet-step kernel launched before it on the same stream).
-#define LEO_RESUME_STEP 0xffffffffu
+// Capacity bits of DeviceTopology::seg[n].y (bit 31: listed for the CTA tier).
+#define LEO_SEG_CAPACITY 0x7fffffffu
+#define LEO_SEG_LISTED 0x80000000u
 
 // Packed topology words.
 #define LEO_TARGET_MASK 0x00ffffffu
@@ -145,10 +144,6 @@ struct LaneScalars {
         work_steps;
     unsigned long long phase_cycles[LEO_PHASES];  // SM clock cycles per phase (first CTA, first thread)
     uint32_t step_supra;                          // candidates of the current tick (all blocks)
-    uint32_t hub_next;                            // next hub a warp takes in settle (reset after settle)
-    uint32_t resume_step;                         // first step the quiet-step kernel left to the wavefront
-    unsigned long long work_quiet;                // steps run by the quiet-step kernel
-    unsigned long long quiet_cycles[LEO_QUIET_PHASES];  // its SM clock cycles per phase (first thread)
     // last-step metrics
     uint32_t last_active, last_suprathreshold, last_block_selected, last_clipped, last_predicted;
     float last_loss;
@@ -160,17 +155,16 @@ struct DeviceTopology {
     const uint32_t* in_word;       // [258*F]
     const uint8_t* neuron_type;    // [N]
     const float* excitability;     // [N]
-    // Hub targets: neurons whose in-degree makes long event lists per step
-    // (power-law topologies).  Their events go to a contiguous per-hub buffer
-    // that one CTA sorts by event order, instead of a linked list.
-    uint32_t hubs;                 // number of hubs (0: none)
-    uint32_t hub_sort_capacity;    // largest power of two a hub's events may need when sorted
-    uint32_t hub_cta_events;       // hubs with more events than this in a step are settled by a whole CTA
-    uint32_t hub_thread_events;    // hubs with at most this many events are settled by one thread
-    const int32_t* hub_of;         // [N] hub index or -1
-    const uint32_t* hub_offset;    // [hubs] start of the hub's segment in a lane's hub_events
-    const uint32_t* hub_capacity;  // [hubs] events the hub can receive in one step
-    const uint32_t* hub_neuron;    // [hubs] neuron of each hub
+    // Per-target event segments: every target n owns entries
+    // seg[n].x .. seg[n].x + (seg[n].y & LEO_SEG_CAPACITY) of a lane's
+    // seg_events, where its events of a step are appended as keys
+    // (branch << 30 | event order) and sorted in settle.  Bit 31 of seg[n].y
+    // marks the listed targets (cta_targets) that the CTA tier settles.
+    const uint2* seg;               // [N] (offset, capacity | listed << 31)
+    const uint32_t* cta_targets;    // [cta_count] listed targets in descending capacity
+    uint32_t cta_count;
+    uint32_t cta_events;            // a listed target with more events than this is sorted by a whole CTA
+    uint32_t thread_events;         // an unlisted target with at most this many is settled by one thread
 };
 
 struct LaneState {
@@ -197,9 +191,9 @@ struct LaneState {
     uint32_t* ring_src;         // [9 * max_active]
     float* ring_act;            // [9 * max_active]
     float* ring_val;            // [9 * max_active * S] emitted a * w snapshots
-    uint32_t* ev_head;          // [N * 4]
-    uint32_t* ev_next;          // [event capacity]
-    float* ev_val;              // [event capacity]
+    float* ev_val;              // [event capacity] event values by event order
+    uint32_t* seg_count;        // [N] events each target received this step
+    uint32_t* seg_events;       // [sum of segment capacities] keys: branch << 30 | event order
     uint2* elig[2];             // recurrent worklists {slot, eligibility bits}
     uint2* in_elig[2];          // input worklists
     Trace* traces;              // [N*S]
@@ -214,11 +208,6 @@ struct LaneState {
     uint8_t* in_mark;   uint32_t* in_list;    // [258*F]
     uint8_t* out_mark;  uint32_t* out_list;   // [N]
     uint8_t* ctx_mark;  uint32_t* ctx_list;   // [C]
-    // Hub events of the current step: per-hub counts and keys (the values
-    // are stored by event order in ev_val, like listed events).
-    uint32_t* hub_count;                // [hubs]
-    uint32_t* hub_events;               // [sum of hub capacities] keys: branch << 30 | event order
-    uint32_t* hub_sort;                 // [hub_sort_capacity] when a hub's keys exceed the shared-memory sort
     // Where the first CTA reports the lane's work per step (eligible slots +
     // events emitted + touched neurons) at the end of each launch; the host
     // sizes the next launch's clusters from it.  Null: not reported.

@@ -78,15 +78,6 @@ cudaError_t leo_launch_zero_streaming(float4* p, size_t n, cudaStream_t stream);
 cudaError_t leo_launch_build_schedules(const uint8_t* bytes, const uint64_t* offsets, const LaneState* lanes,
                                        uint32_t count, uint32_t permission, cudaStream_t stream);
 
-// Quiet frozen steps of the replay lane on one CTA (leo_wavefront.cu): runs
-// frozen steps without a target from `begin` while each step's touched
-// neurons and events fit its shared-memory tables, and records the first step
-// it leaves in the lane's resume_step.  smem_bytes 0: not available for this
-// configuration.
-size_t leo_quiet_smem_bytes(const KernelConsts& kc);
-cudaError_t leo_launch_quiet(const LaneState* lane, uint32_t begin, uint32_t end, const KernelConsts& kc,
-                             cudaStream_t stream);
-
 // Batch-end sparse merge of one fixed f32 tensor (threshold, recurrent, input,
 // output rows, bias, context output): see leo_merge_kernels.cu.
 struct MergeTensor {

@@ -159,20 +159,17 @@ struct LeoB200Device {
     int sm_count = 0;
     int fit16 = 0, fit8 = 0, fit4 = 0;  // co-resident clusters of 16 / 8 / 4 CTAs
     int grid_ctas = 0;                  // CTAs of the whole-GPU replay launch (0: unavailable)
-    bool quiet_steps = false;           // replay prefixes start on the one-CTA quiet-step kernel (opt-in)
-    size_t quiet_smem = 0;              // its shared memory (0: not available for this model)
-    cudaEvent_t quiet_start = nullptr, quiet_stop = nullptr;
     uint32_t replay_load = 0;           // work per step the replay lane reported last
     uint32_t story_chunk = 32;        // steps per story-pass launch while lane loads are skewed
     uint32_t* d_lane_load = nullptr;  // [max_lanes + 1], last entry: replay lane
     LaneState* d_group_table = nullptr;
     std::vector<uint32_t> lane_steps;
-    // Hub targets (see DeviceTopology): the plan and the threshold it used.
-    uint32_t hub_min_in_degree = 0;   // 0: default, max(4 S, 8 N / max_active_global)
-    uint32_t hub_cta_events = 256;    // more events than this per step: the hub is settled by a CTA
-    uint32_t hub_thread_events = 16;  // at most this many: by one thread; in between: by one warp
-    uint64_t hub_events_total = 0;    // sum of hub capacities (entries per lane)
-    std::vector<int32_t> hub_of_host;
+    // Per-target event segments (see DeviceTopology) and the settle tiers.
+    uint32_t cta_min_in_degree = 0;   // listed for the CTA tier from this in-degree (0: default, see plan_segments)
+    uint32_t cta_events = 256;        // a listed target with more events than this per step is sorted by a CTA
+    uint32_t thread_events = 16;      // at most this many: one thread; otherwise one warp
+    uint64_t seg_events_total = 0;    // sum of segment capacities (entries per lane)
+    std::vector<uint2> seg_host;      // the plan, to detect a changed topology
     cudaStream_t aux[4] = {nullptr, nullptr, nullptr, nullptr};
     cudaEvent_t fork = nullptr, join[4] = {nullptr, nullptr, nullptr, nullptr};
     cudaEvent_t batch_start = nullptr, batch_stop = nullptr;
@@ -211,17 +208,11 @@ KernelConsts make_consts(LeoB200Device& dev) {
     return kc;
 }
 
-// Per-lane hub buffers for the current hub plan (none without hubs).
-void allocate_lane_hubs(LeoB200Device& dev, Lane& lane) {
-    const DeviceTopology& t = dev.kc.topo;
+// Per-lane event segments for the current plan.
+void allocate_lane_segments(LeoB200Device& dev, Lane& lane) {
     LaneState& st = lane.st;
-    st.hub_count = nullptr;
-    st.hub_events = nullptr;
-    st.hub_sort = nullptr;
-    if (t.hubs == 0) return;
-    st.hub_count = lane.mem.alloc<uint32_t>(t.hubs);
-    st.hub_events = lane.mem.alloc<uint32_t>(std::max<uint64_t>(dev.hub_events_total, 1));
-    if (t.hub_sort_capacity > 32768) st.hub_sort = lane.mem.alloc<uint32_t>(t.hub_sort_capacity);
+    st.seg_count = lane.mem.alloc<uint32_t>(dev.z.n);
+    st.seg_events = lane.mem.alloc<uint32_t>(std::max<uint64_t>(dev.seg_events_total, 1));
 }
 
 void allocate_lane_transient(LeoB200Device& dev, Lane& lane) {
@@ -244,8 +235,6 @@ void allocate_lane_transient(LeoB200Device& dev, Lane& lane) {
     st.ring_src = m.alloc<uint32_t>((size_t)LEO_RING * maxa);
     st.ring_act = m.alloc<float>((size_t)LEO_RING * maxa);
     st.ring_val = m.alloc<float>((size_t)LEO_RING * maxa * z.s);
-    st.ev_head = m.alloc<uint32_t>(z.n * 4, 0xff);
-    st.ev_next = m.alloc<uint32_t>(dev.kc.event_capacity);
     st.ev_val = m.alloc<float>(dev.kc.event_capacity);
     for (int i = 0; i < 2; ++i) {
         st.elig[i] = m.alloc<uint2>(z.synapses);
@@ -268,7 +257,7 @@ void allocate_lane_transient(LeoB200Device& dev, Lane& lane) {
     st.out_list = m.alloc<uint32_t>(z.n);
     st.ctx_mark = m.alloc<uint8_t>((z.ctx + 3) & ~(size_t)3);
     st.ctx_list = m.alloc<uint32_t>(z.ctx);
-    allocate_lane_hubs(dev, lane);
+    allocate_lane_segments(dev, lane);
 }
 
 void allocate_lane_params(LeoB200Device& dev, Lane& lane) {
@@ -318,9 +307,8 @@ void reset_lane(LeoB200Device& dev, Lane& lane, unsigned long long base_tick, ui
     CUDA_CHECK(cudaMemsetAsync(st.branches, 0, z.n * sizeof(float4), s));
     CUDA_CHECK(cudaMemsetAsync(st.touch_epoch, 0, z.n * 4, s));
     CUDA_CHECK(cudaMemsetAsync(st.dst_epoch, 0, z.n * 4, s));
-    CUDA_CHECK(cudaMemsetAsync(st.ev_head, 0xff, z.n * 16, s));
+    CUDA_CHECK(cudaMemsetAsync(st.seg_count, 0, z.n * 4, s));
     CUDA_CHECK(cudaMemsetAsync(st.block_cand_count, 0, dev.cfg.abi.block_count * 4, s));
-    if (st.hub_count) CUDA_CHECK(cudaMemsetAsync(st.hub_count, 0, dev.kc.topo.hubs * 4, s));
     LaneScalars sc{};
     sc.base_tick = base_tick;
     sc.steps = steps;
@@ -361,19 +349,28 @@ void upload_lane_table(LeoB200Device& dev) {
     CUDA_CHECK(cudaMemcpyAsync(dev.d_replay, &dev.replay->st, sizeof(LaneState), cudaMemcpyHostToDevice, dev.stream));
 }
 
-// ---------------------------------------------------------------- hub targets
-// Targets whose recurrent in-degree is at least the threshold become hubs.
-// A hub's capacity per step: every slot delivers at most once per step (a
-// slot has one delay), so at most min(in-degree, max_active_global x the
-// largest number of slots one source has to the hub) recurrent events, plus
-// the most input slots one symbol has to it.
-std::vector<int32_t> plan_hubs(LeoB200Device& dev, const uint32_t* recurrent_target, const uint32_t* input_target,
-                               bool upload) {
+// ---------------------------------------------------------------- event segments
+// Every target owns a segment of each lane's seg_events sized for the most
+// events it can receive in one step: a recurrent slot delivers at most once
+// per step, and in each of the four delay classes at most max_active_global
+// sources fire, each with at most mult(n) slots to n -- so at most
+// min(in-degree, 4 x max_active_global x mult(n)) recurrent events -- plus the
+// most input slots one symbol has to n.  Targets whose recurrent in-degree is
+// at least the threshold are listed in descending capacity, and CTA r of a
+// lane settles listed targets r, r + C, ... whatever their count, which
+// spreads the high in-degree targets (the ones with many events per step)
+// evenly over the lane's CTAs; every other target is settled where the
+// touched list puts it.  The default threshold is the in-degree at which
+// max_active_global / N of the sources, firing, would deliver thread_events / 4
+// events (power-law hubs; none on uniform topologies).
+std::vector<uint2> plan_segments(LeoB200Device& dev, const uint32_t* recurrent_target, const uint32_t* input_target,
+                                 bool upload) {
     const ModelSizes& z = dev.z;
     const uint32_t N = (uint32_t)z.n, S = (uint32_t)z.s, F = (uint32_t)z.f;
     const uint32_t maxa = dev.cfg.abi.max_active_global;
-    uint32_t threshold = dev.hub_min_in_degree;
-    if (threshold == 0) threshold = std::max<uint32_t>(4 * S, (uint32_t)((8ull * N + maxa - 1) / maxa));
+    uint64_t threshold = dev.cta_min_in_degree;
+    if (threshold == 0)
+        threshold = std::max<uint64_t>(1, ((uint64_t)dev.thread_events * N + 4ull * maxa - 1) / (4ull * maxa));
     std::vector<uint32_t> degree(N, 0), mult(N, 0), in_max(N, 0);
     std::vector<uint32_t> row(S);
     for (uint32_t src = 0; src < N; ++src) {
@@ -398,59 +395,42 @@ std::vector<int32_t> plan_hubs(LeoB200Device& dev, const uint32_t* recurrent_tar
             f = e;
         }
     }
-    // Hubs in descending capacity (ties by neuron): the CTA tier deals them
-    // round-robin over the cluster and the warp tier takes the largest first.
-    std::vector<std::pair<uint64_t, uint32_t>> ranked;
+    std::vector<uint2> seg(N);
+    std::vector<std::pair<uint64_t, uint32_t>> listed;
+    uint64_t total = 0;
     for (uint32_t n = 0; n < N; ++n) {
-        if (degree[n] < threshold) continue;
-        const uint64_t cap = std::min<uint64_t>(degree[n], (uint64_t)maxa * mult[n]) + in_max[n];
-        ranked.push_back({cap, n});
+        const uint64_t cap = std::min<uint64_t>(degree[n], 4ull * maxa * mult[n]) + in_max[n];
+        // Every segment sorts in shared memory (32,768 keys): the device limits
+        // (max_active_global <= 1024, four branches) keep capacities below that.
+        if (cap > 32768) throw LeoFailure("a target's events per step exceed the settle sort (32768)");
+        seg[n] = make_uint2((uint32_t)total, (uint32_t)cap);
+        if (degree[n] >= threshold && cap > 0) {
+            seg[n].y |= LEO_SEG_LISTED;
+            listed.push_back({cap, n});
+        }
+        total += cap;
+        if (total >= 0xffffffffull) throw LeoFailure("event segment capacity exceeds 32-bit offsets");
     }
-    std::sort(ranked.begin(), ranked.end(), [](const auto& a, const auto& b) {
+    std::sort(listed.begin(), listed.end(), [](const auto& a, const auto& b) {
         return a.first != b.first ? a.first > b.first : a.second < b.second;
     });
-    std::vector<int32_t> hub_of(N, -1);
-    std::vector<uint32_t> offset, capacity, neuron;
-    uint64_t total = 0, largest = 0;
-    for (const auto& [cap, n] : ranked) {
-        hub_of[n] = (int32_t)neuron.size();
-        offset.push_back((uint32_t)total);
-        capacity.push_back((uint32_t)cap);
-        neuron.push_back(n);
-        total += cap;
-        largest = std::max(largest, cap);
-        if (total >= 0xffffffffull) throw LeoFailure("hub event capacity exceeds 32-bit offsets");
-    }
-    if (!upload) return hub_of;
+    if (!upload) return seg;
     DeviceTopology& t = dev.kc.topo;
-    t.hubs = (uint32_t)neuron.size();
-    t.hub_cta_events = dev.hub_cta_events;
-    t.hub_thread_events = std::min(dev.hub_thread_events, dev.hub_cta_events);
-    uint32_t sort_cap = 1;
-    while (sort_cap < largest) sort_cap <<= 1;
-    t.hub_sort_capacity = t.hubs ? sort_cap : 0;
-    dev.hub_events_total = total;
-    dev.hub_of_host = hub_of;
-    if (t.hubs) {
-        int32_t* d_of = dev.mem.alloc<int32_t>(N);
-        uint32_t* d_off = dev.mem.alloc<uint32_t>(t.hubs);
-        uint32_t* d_cap = dev.mem.alloc<uint32_t>(t.hubs);
-        uint32_t* d_neuron = dev.mem.alloc<uint32_t>(t.hubs);
-        CUDA_CHECK(cudaMemcpy(d_of, hub_of.data(), N * 4, cudaMemcpyHostToDevice));
-        CUDA_CHECK(cudaMemcpy(d_off, offset.data(), t.hubs * 4, cudaMemcpyHostToDevice));
-        CUDA_CHECK(cudaMemcpy(d_cap, capacity.data(), t.hubs * 4, cudaMemcpyHostToDevice));
-        CUDA_CHECK(cudaMemcpy(d_neuron, neuron.data(), t.hubs * 4, cudaMemcpyHostToDevice));
-        t.hub_of = d_of;
-        t.hub_offset = d_off;
-        t.hub_capacity = d_cap;
-        t.hub_neuron = d_neuron;
-    } else {
-        t.hub_of = nullptr;
-        t.hub_offset = nullptr;
-        t.hub_capacity = nullptr;
-        t.hub_neuron = nullptr;
-    }
-    return hub_of;
+    t.cta_count = (uint32_t)listed.size();
+    t.cta_events = dev.cta_events;
+    t.thread_events = std::min(dev.thread_events, dev.cta_events);
+    dev.seg_events_total = total;
+    dev.seg_host = seg;
+    std::vector<uint32_t> targets(listed.size());
+    for (size_t i = 0; i < listed.size(); ++i) targets[i] = listed[i].second;
+    uint2* d_seg = t.seg ? const_cast<uint2*>(t.seg) : dev.mem.alloc<uint2>(N);
+    CUDA_CHECK(cudaMemcpy(d_seg, seg.data(), N * sizeof(uint2), cudaMemcpyHostToDevice));
+    t.seg = d_seg;
+    uint32_t* d_targets = dev.mem.alloc<uint32_t>(std::max<size_t>(targets.size(), 1));
+    if (!targets.empty())
+        CUDA_CHECK(cudaMemcpy(d_targets, targets.data(), targets.size() * 4, cudaMemcpyHostToDevice));
+    t.cta_targets = d_targets;
+    return seg;
 }
 
 // ---------------------------------------------------------------- model I/O
@@ -547,12 +527,10 @@ uint32_t pick_cluster(LeoB200Device& dev, uint32_t lanes, uint32_t request, uint
 // more than ~50k units of work (fitted to measured replay steps).
 constexpr uint32_t kWholeGpuLoad = 50000;
 
-// `resume`: the launch starts at the lane's resume_step (left by the quiet-step
-// kernel before it on the stream) instead of `begin`.
 void run_steps(LeoB200Device& dev, const LaneState* d_lanes, int lane_count, uint32_t begin, uint32_t end,
-               bool story, bool resume = false) {
+               bool story) {
     if (end <= begin || lane_count == 0) return;
-    const uint32_t first = resume ? LEO_RESUME_STEP : begin;
+    const uint32_t first = begin;
     const bool whole_gpu = !story && lane_count == 1 && dev.grid_ctas > 0 &&
                            (dev.replay_cluster_request == LEO_B200_WHOLE_GPU ||
                             (dev.replay_cluster_request == 0 && dev.replay_load > kWholeGpuLoad));
@@ -721,8 +699,14 @@ void add_work(LeoB200Device& dev, const LaneScalars& sc, bool story) {
     dev.perf.work_active += sc.work_active;
     dev.perf.work_plastic += sc.work_plastic;
     dev.perf.work_steps += sc.work_steps;
-    dev.perf.quiet_steps += sc.work_quiet;
-    for (int p = 0; p < LEO_QUIET_PHASES; ++p) dev.perf.quiet_cycles[p] += sc.quiet_cycles[p];
+    if (!story) {
+        for (int p = 0; p < LEO_PHASES; ++p) dev.perf.replay_phase_cycles[p] += sc.phase_cycles[p];
+        dev.perf.replay_work_steps += sc.work_steps;
+        dev.perf.replay_work_touched += sc.work_touched;
+        dev.perf.replay_work_active += sc.work_active;
+        dev.perf.replay_work_deliver += sc.work_deliver;
+        dev.perf.replay_work_eligible += sc.work_eligible;
+    }
 }
 
 void read_scalars(LeoB200Device& dev, Lane& lane, LaneScalars& out) {
@@ -1307,26 +1291,7 @@ void run_canonical_schedule(LeoB200Device& dev, const std::vector<uint32_t>& sch
     carry.bias_dirty = out.bias_dirty;
     carry.ctx_out_dirty = out.ctx_out_dirty;
     CUDA_CHECK(cudaMemcpyAsync(rl.st.sc, &carry, sizeof(carry), cudaMemcpyHostToDevice, dev.stream));
-    // The frozen prefix (leading frozen steps without a target) starts on the
-    // quiet-step kernel; the wavefront resumes where it stopped.
-    size_t prefix = 0;
-    while (prefix < schedule.size() && LEO_SCHED_PERMISSION(schedule[prefix]) == LEO_B200_FROZEN &&
-           LEO_SCHED_TARGET(schedule[prefix]) < 0)
-        ++prefix;
-    const bool quiet = dev.quiet_steps && dev.quiet_smem > 0 && prefix > 0;
-    if (quiet) {
-        CUDA_CHECK(cudaEventRecord(dev.quiet_start, dev.stream));
-        CUDA_CHECK(leo_launch_quiet(dev.d_replay, 0, (uint32_t)prefix, dev.kc, dev.stream));
-        CUDA_CHECK(cudaEventRecord(dev.quiet_stop, dev.stream));
-        dev.perf.launches += 1;
-        dev.perf.quiet_launches += 1;
-    }
-    run_steps(dev, dev.d_replay, 1, 0, (uint32_t)schedule.size(), false, quiet);
-    if (quiet) {
-        float ms = 0.0f;
-        CUDA_CHECK(cudaEventElapsedTime(&ms, dev.quiet_start, dev.quiet_stop));
-        dev.perf.quiet_ms += ms;
-    }
+    run_steps(dev, dev.d_replay, 1, 0, (uint32_t)schedule.size(), false);
     LaneScalars sc;
     read_scalars(dev, rl, sc);
     check_error_flag(sc);
@@ -1999,7 +1964,7 @@ int leo_b200_open(int device, const LeoB200HostModel* canonical, uint32_t max_la
         for (cudaEvent_t& ev : dev->join) CUDA_CHECK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
         dev->sm_count = prop.multiProcessorCount;
         // replay lane: canonical parameters, private transient state
-        plan_hubs(*dev, canonical->recurrent_target, canonical->input_target, true);
+        plan_segments(*dev, canonical->recurrent_target, canonical->input_target, true);
         dev->replay = std::make_unique<Lane>();
         dev->replay->st.p = dev->canon;
         allocate_lane_transient(*dev, *dev->replay);
@@ -2023,12 +1988,9 @@ int leo_b200_open(int device, const LeoB200HostModel* canonical, uint32_t max_la
             cudaGetLastError();
             dev->grid_ctas = 0;
         }
-        dev->quiet_smem = leo_quiet_smem_bytes(dev->kc);
         dev->ctx_lane_offset = dev->mem.alloc<uint32_t>(max_lanes + 1);
         dev->ctx_device_merge = leo_context_apply_smem(dev->cfg.abi.context_slots_per_order) <= 200u * 1024u &&
                                 leo_context_merge_configure() == cudaSuccess;
-        CUDA_CHECK(cudaEventCreate(&dev->quiet_start));
-        CUDA_CHECK(cudaEventCreate(&dev->quiet_stop));
         upload_model(*dev, *canonical);
         *out = dev.release();
         return 0;
@@ -2042,8 +2004,6 @@ void leo_b200_close(LeoB200Device* dev) {
     cudaSetDevice(dev->device);
     cudaStreamSynchronize(dev->stream);
     cudaStream_t s = dev->stream;
-    if (dev->quiet_start) cudaEventDestroy(dev->quiet_start);
-    if (dev->quiet_stop) cudaEventDestroy(dev->quiet_stop);
     if (dev->wave_start) cudaEventDestroy(dev->wave_start);
     if (dev->wave_stop) cudaEventDestroy(dev->wave_stop);
     if (dev->batch_start) cudaEventDestroy(dev->batch_start);
@@ -2062,8 +2022,11 @@ int leo_b200_upload_canonical(LeoB200Device* dev, const LeoB200HostModel* model)
         const char* e = leo_host::validate_model(*model);
         if (*e) throw LeoFailure(e);
         CUDA_CHECK(cudaSetDevice(dev->device));
-        if (plan_hubs(*dev, model->recurrent_target, model->input_target, false) != dev->hub_of_host)
-            throw LeoFailure("the recurrent topology changed: open a new backend for it");
+        const std::vector<uint2> seg = plan_segments(*dev, model->recurrent_target, model->input_target, false);
+        bool same = seg.size() == dev->seg_host.size();
+        for (size_t n = 0; same && n < seg.size(); ++n)
+            same = seg[n].x == dev->seg_host[n].x && (seg[n].y & LEO_SEG_CAPACITY) == (dev->seg_host[n].y & LEO_SEG_CAPACITY);
+        if (!same) throw LeoFailure("the recurrent topology changed: open a new backend for it");
         upload_model(*dev, *model);
         return 0;
     } catch (const std::exception& e) {
@@ -2477,11 +2440,6 @@ int leo_b200_set_device_context_merge(LeoB200Device* dev, int enable) {
     return 0;
 }
 
-int leo_b200_set_quiet_steps(LeoB200Device* dev, int enable) {
-    dev->quiet_steps = enable != 0;
-    return 0;
-}
-
 int leo_b200_set_story_chunk(LeoB200Device* dev, uint32_t steps) {
     if (steps == 0) return fail(LeoFailure("story chunk must be at least one step"));
     dev->story_chunk = steps;
@@ -2502,12 +2460,10 @@ int leo_b200_set_hub_threshold(LeoB200Device* dev, uint32_t min_in_degree, uint3
         CUDA_CHECK(cudaMemcpy(in.data(), dev->kc.topo.in_word, z.inputs * 4, cudaMemcpyDeviceToHost));
         for (auto& w : rec) w &= LEO_TARGET_MASK;
         for (auto& w : in) w &= LEO_TARGET_MASK;
-        dev->hub_min_in_degree = min_in_degree;
-        dev->hub_cta_events = cta_events ? cta_events : 256;
-        dev->hub_thread_events = thread_events ? thread_events : 16;
-        plan_hubs(*dev, rec.data(), in.data(), true);
-        if (leo_wavefront_smem_bytes(dev->kc) > 160 * 1024) throw LeoFailure("hub sort exceeds shared memory");
-        allocate_lane_hubs(*dev, *dev->replay);
+        dev->cta_min_in_degree = min_in_degree;
+        dev->cta_events = cta_events ? cta_events : 256;
+        dev->thread_events = thread_events ? thread_events : 16;
+        plan_segments(*dev, rec.data(), in.data(), true);  // capacities are unchanged: lane buffers stay valid
         return 0;
     } catch (const std::exception& e) {
         return fail(e);
@@ -2515,8 +2471,8 @@ int leo_b200_set_hub_threshold(LeoB200Device* dev, uint32_t min_in_degree, uint3
 }
 
 int leo_b200_hub_count(LeoB200Device* dev, uint32_t* hubs, uint64_t* events_per_lane) {
-    if (hubs) *hubs = dev->kc.topo.hubs;
-    if (events_per_lane) *events_per_lane = dev->hub_events_total;
+    if (hubs) *hubs = dev->kc.topo.cta_count;
+    if (events_per_lane) *events_per_lane = dev->seg_events_total;
     return 0;
 }
 

@@ -55,10 +55,9 @@
 
 namespace cg = cooperative_groups;
 
-// Hub event keys sorted in shared memory when their padded count fits (128 KB of 4-byte keys).
+// Most event keys one target's segment holds, all sorted in shared memory by
+// one CTA (128 KB; the host rejects larger segment capacities).
 constexpr uint32_t kHubSortShared = 32768;
-// Largest event count a hub's thread-level sort handles (kc.topo.hub_thread_events <= this).
-constexpr uint32_t kHubThreadEvents = 16;
 // Largest event count a warp sorts in its slice of shared memory (16 warps x 2048 x 4 B = 128 KB).
 constexpr uint32_t kHubWarpEvents = 2048;
 
@@ -200,29 +199,24 @@ __device__ __forceinline__ void touch(const LaneState& ln, uint32_t n, uint32_t 
     if (atomicExch(&ln.touch_epoch[n], epoch) != epoch) append_coalesced(ln.touched, &ln.sc->touched_count, n);
 }
 
-__device__ __forceinline__ void push_event(const LaneState& ln, uint32_t tb, uint32_t q, float value) {
-    uint32_t old = atomicExch(&ln.ev_head[tb], q);
-    ln.ev_next[q] = old;
-    ln.ev_val[q] = value;
-}
-
-// A hub target's event: its value is stored by event order (as for listed
-// events) and its key (branch << 30 | event order) appended to the hub's
-// segment, one atomic per group of converged threads with the same hub; the
-// order is restored by sorting the keys in settle.  Capacity is an upper
-// bound computed from the topology.
+// An event: its value is stored by event order, and its key (branch << 30 |
+// event order) appended to the target's segment, one atomic per group of
+// converged threads with the same target; settle restores the order by
+// sorting the keys.  A segment holds every event the target can receive in
+// one step (the bound is computed from the topology); an overrun is reported.
 constexpr uint32_t kEventOrderMask = 0x3fffffffu;
-__device__ __forceinline__ void hub_push(const LaneState& ln, const KernelConsts& kc, int32_t h, uint32_t key,
+__device__ __forceinline__ void seg_push(const LaneState& ln, const KernelConsts& kc, uint32_t n, uint32_t key,
                                          float value) {
     cg::coalesced_group g = cg::coalesced_threads();
-    cg::coalesced_group peers = cg::labeled_partition(g, h);
+    cg::coalesced_group peers = cg::labeled_partition(g, n);
     uint32_t base = 0;
-    if (peers.thread_rank() == 0) base = atomicAdd(&ln.hub_count[h], peers.size());
+    if (peers.thread_rank() == 0) base = atomicAdd(&ln.seg_count[n], peers.size());
     base = peers.shfl(base, 0);
     const uint32_t pos = base + peers.thread_rank();
     ln.ev_val[key & kEventOrderMask] = value;
-    if (pos < kc.topo.hub_capacity[h])
-        ln.hub_events[kc.topo.hub_offset[h] + pos] = key;
+    const uint2 seg = kc.topo.seg[n];
+    if (pos < (seg.y & LEO_SEG_CAPACITY))
+        ln.seg_events[seg.x + pos] = key;
     else
         atomicOr(&ln.sc->error_flag, LEO_ERR_CAPACITY);
 }
@@ -418,11 +412,7 @@ __device__ uint32_t phase_deliver(const LaneState& ln, uint32_t s, const KernelC
             const float value = (fresh_d1 && d == 1) ? ln.ring_act[entry * maxa + r] * ln.p.rec_weight[slot]
                                                      : ln.ring_val[((size_t)entry * maxa + r) * S + j];
             touch(ln, n, epoch);
-            const int32_t h = kc.topo.hubs ? kc.topo.hub_of[n] : -1;
-            if (h >= 0)
-                hub_push(ln, kc, h, (b << 30) | q, value);
-            else
-                push_event(ln, n * 4 + b, q, value);
+            seg_push(ln, kc, n, (b << 30) | q, value);
             if (learn) {  // activate_recurrent_trace (runtime.rs:719-726); one event per slot per tick
                 float a = ln.ring_act[entry * maxa + r];
                 Trace t = load_trace(&ln.traces[slot]);
@@ -444,11 +434,7 @@ __device__ uint32_t phase_deliver(const LaneState& ln, uint32_t s, const KernelC
             uint32_t word = kc.topo.in_word[slot];
             uint32_t n = word & LEO_TARGET_MASK, b = LEO_WORD_BRANCH(word);
             touch(ln, n, epoch);
-            const int32_t h = kc.topo.hubs ? kc.topo.hub_of[n] : -1;
-            if (h >= 0)
-                hub_push(ln, kc, h, (b << 30) | q, ln.p.in_weight[slot]);
-            else
-                push_event(ln, n * 4 + b, q, ln.p.in_weight[slot]);
+            seg_push(ln, kc, n, (b << 30) | q, ln.p.in_weight[slot]);
             if (learn) {
                 Trace t = load_trace(&ln.in_traces[slot]);
                 advance_trace(kc.cfg, t, s);
@@ -632,63 +618,331 @@ __device__ __forceinline__ void bitonic_sort_keys(uint32_t* keys, uint32_t P, ui
     }
 }
 
-// Hubs by event count this step: more than hub_cta_events -> one CTA per hub
-// (hubs h = rank, rank + C, ...); more than hub_thread_events -> one warp per
-// hub; the rest are settled by one thread in phase_settle.  A tier sorts the
-// hub's keys (branch << 30 | event order), replaces each key by its event's
-// value in place, and sums each branch's values in ascending event order.
-__device__ void settle_hubs(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t rank, uint32_t C,
-                            uint32_t* smem, float pop_inh, uint32_t rotation) {
+// ---------------------------------------------------------------------------
+// Register-resident bitonic sort of P keys per thread in blocked layout
+// (thread t holds elements Pt .. Pt+P-1): strides below P exchange registers,
+// strides P..16P exchange with the partner lane by shuffle, and strides of
+// 32P and more (the CTA sort only) exchange through shared memory, one
+// barrier per such stage.  A warp sorts 256 keys (P = 8); a CTA sorts up to
+// 4096, with P = 2, 4 or 8 so that every warp takes part from 1024 keys up.
+constexpr uint32_t kSortPer = 8;
+constexpr uint32_t kWarpSortKeys = 32 * kSortPer;
+constexpr uint32_t kCtaSortKeys = kThreads * kSortPer;
+
+template <int P, int S>
+__device__ __forceinline__ void sort_regs(uint32_t (&v)[P], uint32_t e0, uint32_t w) {
+#pragma unroll
+    for (int r = 0; r < P; ++r) {
+        if ((r & S) == 0) {
+            const bool asc = ((e0 + (uint32_t)r) & w) == 0u;
+            const uint32_t a = v[r], b = v[r | S];
+            const uint32_t lo = a < b ? a : b, hi = a < b ? b : a;
+            v[r] = asc ? lo : hi;
+            v[r | S] = asc ? hi : lo;
+        }
+    }
+}
+
+template <int P>
+__device__ __forceinline__ void sort_shfl(uint32_t (&v)[P], uint32_t e0, uint32_t w, uint32_t stride) {
+    const bool keep_min = ((e0 & stride) == 0u) == ((e0 & w) == 0u);
+    const int lane_mask = (int)(stride / P);
+#pragma unroll
+    for (int r = 0; r < P; ++r) {
+        const uint32_t o = __shfl_xor_sync(0xffffffffu, v[r], lane_mask);
+        v[r] = keep_min ? (v[r] < o ? v[r] : o) : (v[r] < o ? o : v[r]);
+    }
+}
+
+// Thread t's P keys to / from words Pt .. Pt+P-1 of shared memory (16-byte aligned).
+template <int P>
+__device__ __forceinline__ void store_keys(uint32_t* buf, uint32_t t, const uint32_t (&v)[P]) {
+    if constexpr (P == 2) {
+        reinterpret_cast<uint2*>(buf)[t] = make_uint2(v[0], v[1]);
+    } else {
+#pragma unroll
+        for (int r = 0; r < P; r += 4) reinterpret_cast<uint4*>(buf)[(P / 4) * t + r / 4] = make_uint4(v[r], v[r + 1], v[r + 2], v[r + 3]);
+    }
+}
+template <int P>
+__device__ __forceinline__ void fetch_keys(const uint32_t* buf, uint32_t t, uint32_t (&v)[P]) {
+    if constexpr (P == 2) {
+        const uint2 x = reinterpret_cast<const uint2*>(buf)[t];
+        v[0] = x.x;
+        v[1] = x.y;
+    } else {
+#pragma unroll
+        for (int r = 0; r < P; r += 4) {
+            const uint4 x = reinterpret_cast<const uint4*>(buf)[(P / 4) * t + r / 4];
+            v[r] = x.x;
+            v[r + 1] = x.y;
+            v[r + 2] = x.z;
+            v[r + 3] = x.w;
+        }
+    }
+}
+
+template <int P>
+__device__ __forceinline__ void sort_smem(uint32_t (&v)[P], uint32_t* buf, uint32_t t, uint32_t w, uint32_t stride,
+                                          bool active) {
+    if (active) store_keys<P>(buf, t, v);
+    __syncthreads();
+    if (!active) return;
+    uint32_t o[P];
+    fetch_keys<P>(buf, t ^ (stride / P), o);
+    const uint32_t e0 = t * P;
+    const bool keep_min = ((e0 & stride) == 0u) == ((e0 & w) == 0u);
+#pragma unroll
+    for (int r = 0; r < P; ++r) v[r] = keep_min ? (v[r] < o[r] ? v[r] : o[r]) : (v[r] < o[r] ? o[r] : v[r]);
+}
+
+// Ascending sort of the n keys (a power of two, P per thread) held by threads
+// t < n / P: a warp (kCta false: n = 32 P, no shared memory), or some or all of
+// the CTA's threads (kCta true: `buf` holds 2 x n keys, 16-byte aligned, and
+// every thread of the CTA calls this, the others only meeting the barriers).
+template <bool kCta, int P>
+__device__ __forceinline__ void bitonic_sort_regs(uint32_t (&v)[P], uint32_t t, uint32_t n, uint32_t* buf) {
+    const uint32_t e0 = t * P;
+    const bool active = e0 < n;
+    uint32_t half = 0;
+    for (uint32_t w = 2; w <= n; w <<= 1) {
+        for (uint32_t stride = w >> 1; stride >= (uint32_t)P; stride >>= 1) {
+            if (kCta && stride >= (uint32_t)P * 32u) {
+                sort_smem<P>(v, buf + (half ? n : 0u), t, w, stride, active);
+                half ^= 1u;
+            } else if (active) {
+                sort_shfl<P>(v, e0, w, stride);
+            }
+        }
+        if (active) {
+            if constexpr (P >= 8) {
+                if (w >= 8) sort_regs<P, 4>(v, e0, w);
+            }
+            if constexpr (P >= 4) {
+                if (w >= 4) sort_regs<P, 2>(v, e0, w);
+            }
+            sort_regs<P, 1>(v, e0, w);
+        }
+    }
+}
+
+// Strictly sequential sum of shared vals[lo, hi) onto `a`, the next eight
+// loads issued before the current eight adds.
+__device__ __forceinline__ float ordered_sum_pipelined(const float* vals, uint32_t lo, uint32_t hi, float a) {
+    uint32_t i = lo;
+    if (i + 8 <= hi) {
+        float nxt[8];
+#pragma unroll
+        for (int x = 0; x < 8; ++x) nxt[x] = vals[i + x];
+        for (;;) {
+            float cur[8];
+#pragma unroll
+            for (int x = 0; x < 8; ++x) cur[x] = nxt[x];
+            i += 8;
+            const bool more = i + 8 <= hi;
+            if (more) {
+#pragma unroll
+                for (int x = 0; x < 8; ++x) nxt[x] = vals[i + x];
+            }
+#pragma unroll
+            for (int x = 0; x < 8; ++x) a = a + cur[x];
+            if (!more) break;
+        }
+    }
+    for (; i < hi; ++i) a = a + vals[i];
+    return a;
+}
+
+// Per-branch counts of the sorted keys e < k held in v (blocked layout).
+template <int P>
+__device__ __forceinline__ void branch_counts(const uint32_t (&v)[P], uint32_t e0, uint32_t k, uint32_t (&cnt)[4]) {
+#pragma unroll
+    for (int b = 0; b < 4; ++b) cnt[b] = 0u;
+#pragma unroll
+    for (int r = 0; r < P; ++r) {
+        const uint32_t b = e0 + (uint32_t)r < k ? v[r] >> 30 : 4u;
+#pragma unroll
+        for (int x = 0; x < 4; ++x) cnt[x] += b == (uint32_t)x ? 1u : 0u;
+    }
+}
+
+// The CTA's sort of one target's n keys (loaded in smem[0, n)): threads
+// t < n / P sort them (exchange buffers after the first kCtaSortKeys words),
+// gather each key's event value, write the values back to smem[0, k) in
+// sorted order and add their per-branch counts to s_cnt.
+template <int P>
+__device__ __forceinline__ void cta_sort_values(const LaneState& ln, uint32_t* smem, uint32_t n, uint32_t k,
+                                                uint32_t* s_cnt) {
+    const uint32_t tid = threadIdx.x, e0 = tid * P;
+    const bool active = e0 < n;
+    uint32_t v[P];
+    if (active) fetch_keys<P>(smem, tid, v);
+    bitonic_sort_regs<true, P>(v, tid, n, smem + kCtaSortKeys);
+    if (!active) return;
+    uint32_t val[P];
+#pragma unroll
+    for (int r = 0; r < P; ++r)
+        val[r] = e0 + (uint32_t)r < k ? __float_as_uint(ln.ev_val[v[r] & kEventOrderMask]) : 0u;
+    uint32_t cnt[4];
+    branch_counts<P>(v, e0, k, cnt);
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        const uint32_t c = __reduce_add_sync(0xffffffffu, cnt[b]);  // whole warps are active
+        if ((tid & 31u) == 0u && c) atomicAdd(&s_cnt[b], c);
+    }
+    store_keys<P>(smem, tid, val);
+}
+
+// Bitonic sorting network over the first N of 16 keys in registers (N a
+// power of two; entries past the target's count hold the 0xffffffff padding).
+template <int N>
+__device__ __forceinline__ void sort_network(uint32_t (&e)[16]) {
+#pragma unroll
+    for (int w = 2; w <= N; w <<= 1) {
+#pragma unroll
+        for (int st = w >> 1; st > 0; st >>= 1) {
+#pragma unroll
+            for (int i = 0; i < N; ++i) {
+                const int j = i ^ st;
+                if (j > i) {
+                    const bool asc = (i & w) == 0;
+                    const uint32_t a = e[i], b = e[j];
+                    const uint32_t lo = a < b ? a : b, hi = a < b ? b : a;
+                    e[i] = asc ? lo : hi;
+                    e[j] = asc ? hi : lo;
+                }
+            }
+        }
+    }
+}
+
+// Adds `v` to the accumulator of `branch` (registers, no indexed array).
+__device__ __forceinline__ void add_branch(float4& acc, uint32_t branch, float v) {
+    if (branch == 0u)
+        acc.x = acc.x + v;
+    else if (branch == 1u)
+        acc.y = acc.y + v;
+    else if (branch == 2u)
+        acc.z = acc.z + v;
+    else
+        acc.w = acc.w + v;
+}
+
+// One target settled by the whole CTA (every thread calls it): its k keys
+// sorted (registers up to 4096, shared memory above), each key's event
+// value gathered, and each branch summed in ascending event order onto the
+// decayed branch value by one thread per branch; then integration.  Resets
+// the target's count.
+__device__ __noinline__ void settle_target_cta(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t n, uint32_t k,
+                                  uint32_t offset, uint32_t* smem, float pop_inh, uint32_t rotation) {
     __shared__ float s_acc[4];
+    __shared__ uint32_t s_cnt[4];
     __shared__ uint32_t s_bound[5];
     __shared__ NeuronCold s_cold;
-    const uint32_t H = kc.topo.hubs, tid = threadIdx.x;
-    for (uint32_t h = rank; h < H; h += C) {
-        const uint32_t k = ln.hub_count[h];
-        if (k <= kc.topo.hub_cta_events) continue;  // none, or few: a warp or a thread settles it
-        const uint32_t n = kc.topo.hub_neuron[h];
-        const uint32_t* ev = ln.hub_events + kc.topo.hub_offset[h];
-        uint32_t P = 1;
-        while (P < k) P <<= 1;
-        uint32_t* keys = P <= kHubSortShared ? smem : ln.hub_sort;
-        load_keys(keys, ev, k, P, tid, kThreads);
+    __shared__ SettlePre s_pre;
+    const uint32_t tid = threadIdx.x;
+    const uint32_t* ev = ln.seg_events + offset;
+    if (tid == 0) {
+        NeuronCold cold = ln.cold[n];
+        float4 br = ln.branches[n];
+        s_pre = settle_preload(ln, kc, n);
+        settle_decay(kc.cfg, s, cold, br);
+        s_cold = cold;
+        s_acc[0] = br.x;
+        s_acc[1] = br.y;
+        s_acc[2] = br.z;
+        s_acc[3] = br.w;
+    }
+    if (tid < 4) s_cnt[tid] = 0u;
+    if (k <= kCtaSortKeys) {
+        // The smallest power of two >= k (at least 256), P keys per thread
+        // with P as small as lets every warp take part.
+        uint32_t n = kWarpSortKeys;
+        while (n < k) n <<= 1;
+        load_keys(smem, ev, k, n, tid, kThreads);
+        __syncthreads();
+        if (n <= 2 * kThreads)
+            cta_sort_values<2>(ln, smem, n, k, s_cnt);
+        else if (n <= 4 * kThreads)
+            cta_sort_values<4>(ln, smem, n, k, s_cnt);
+        else
+            cta_sort_values<8>(ln, smem, n, k, s_cnt);
+        __syncthreads();
         if (tid == 0) {
-            NeuronCold cold = ln.cold[n];
-            float4 br = ln.branches[n];
-            settle_decay(kc.cfg, s, cold, br);
-            s_cold = cold;
-            s_acc[0] = br.x;
-            s_acc[1] = br.y;
-            s_acc[2] = br.z;
-            s_acc[3] = br.w;
+            s_bound[0] = 0u;
+            for (int b = 0; b < 4; ++b) s_bound[b + 1] = s_bound[b] + s_cnt[b];
         }
         __syncthreads();
-        bitonic_sort_keys(keys, P, tid, kThreads, BlockSync{});
-        if (tid <= 4) s_bound[tid] = tid == 4 ? k : hub_branch_begin(keys, k, tid);
+        const float* vals = reinterpret_cast<const float*>(smem);
+        if (tid < 4) s_acc[tid] = ordered_sum_pipelined(vals, s_bound[tid], s_bound[tid + 1], s_acc[tid]);
+    } else {
+        // More keys than one register sort: bitonic sort in shared memory
+        // (segment capacities are at most kHubSortShared keys).
+        uint32_t P = 1;
+        while (P < k) P <<= 1;
+        load_keys(smem, ev, k, P, tid, kThreads);
         __syncthreads();
-        gather_values(keys, ln.ev_val, k, tid, kThreads);
+        bitonic_sort_keys(smem, P, tid, kThreads, BlockSync{});
+        if (tid <= 4) s_bound[tid] = tid == 4 ? k : hub_branch_begin(smem, k, tid);
         __syncthreads();
-        const float* vals = reinterpret_cast<const float*>(keys);
+        gather_values(smem, ln.ev_val, k, tid, kThreads);
+        __syncthreads();
+        const float* vals = reinterpret_cast<const float*>(smem);
         if (tid < 4) s_acc[tid] = ordered_sum(vals, s_bound[tid], s_bound[tid + 1], s_acc[tid]);
-        __syncthreads();
-        if (tid == 0) settle_integrate(ln, kc, n, s, s_cold, make_float4(s_acc[0], s_acc[1], s_acc[2], s_acc[3]),
-                                       pop_inh, rotation, settle_preload(ln, kc, n));
-        __syncthreads();
     }
-    // Medium hubs: one warp each, sorted in the warp's slice of shared memory.
-    // Warps take hubs one at a time from a shared counter, largest capacity
-    // first, and stop at the first hub whose capacity fits the thread tier.
-    const uint32_t lane = tid & 31u, warp = tid >> 5;
-    uint32_t* wkeys = smem + (size_t)warp * kHubWarpEvents;
-    for (;;) {
-        uint32_t h = 0;
-        if (lane == 0) h = atomicAdd(&ln.sc->hub_next, 1u);
-        h = __shfl_sync(0xffffffffu, h, 0);
-        if (h >= H || kc.topo.hub_capacity[h] <= kc.topo.hub_thread_events) break;
-        const uint32_t k = ln.hub_count[h];
-        if (k <= kc.topo.hub_thread_events || k > kc.topo.hub_cta_events) continue;
-        const uint32_t n = kc.topo.hub_neuron[h];
-        const uint32_t* ev = ln.hub_events + kc.topo.hub_offset[h];
+    __syncthreads();
+    if (tid == 0) {
+        settle_integrate(ln, kc, n, s, s_cold, make_float4(s_acc[0], s_acc[1], s_acc[2], s_acc[3]), pop_inh, rotation,
+                         s_pre);
+        ln.seg_count[n] = 0u;
+    }
+    __syncthreads();
+}
+
+// One target settled by one warp (every lane calls it; k <= kHubWarpEvents):
+// registers up to 256 keys, the warp's shared-memory slice above.  Resets
+// the target's count.
+__device__ __noinline__ void settle_target_warp(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t n, uint32_t k,
+                                   uint32_t offset, uint32_t* wkeys, float pop_inh, uint32_t rotation) {
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t* ev = ln.seg_events + offset;
+    NeuronCold cold;
+    float4 br = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    SettlePre pre{};
+    if (lane == 0) {
+        cold = ln.cold[n];
+        br = ln.branches[n];
+        pre = settle_preload(ln, kc, n);
+        settle_decay(kc.cfg, s, cold, br);
+    }
+    uint32_t lo = 0, hi = 0;  // this lane's branch range (lanes 0..3)
+    const float* wvals = reinterpret_cast<const float*>(wkeys);
+    if (k <= kWarpSortKeys) {
+        const uint32_t e0 = lane * kSortPer;
+        uint32_t v[kSortPer];
+#pragma unroll
+        for (int r = 0; r < (int)kSortPer; ++r) v[r] = e0 + (uint32_t)r < k ? ev[e0 + r] : 0xffffffffu;
+        bitonic_sort_regs<false, kSortPer>(v, lane, kWarpSortKeys, nullptr);
+        float val[kSortPer];
+#pragma unroll
+        for (int r = 0; r < (int)kSortPer; ++r) val[r] = e0 + (uint32_t)r < k ? ln.ev_val[v[r] & kEventOrderMask] : 0.0f;
+        uint32_t cnt[4];
+        branch_counts<kSortPer>(v, e0, k, cnt);
+        uint32_t acc_c = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const uint32_t c = __reduce_add_sync(0xffffffffu, cnt[b]);
+            if ((uint32_t)b == lane) {
+                lo = acc_c;
+                hi = acc_c + c;
+            }
+            acc_c += c;
+        }
+        float4* vb = reinterpret_cast<float4*>(wkeys);
+        vb[2 * lane] = make_float4(val[0], val[1], val[2], val[3]);
+        vb[2 * lane + 1] = make_float4(val[4], val[5], val[6], val[7]);
+        __syncwarp();
+    } else {
         uint32_t P = 32;
         while (P < k) P <<= 1;
         load_keys(wkeys, ev, k, P, lane, 32u);
@@ -697,163 +951,161 @@ __device__ void settle_hubs(const LaneState& ln, uint32_t s, const KernelConsts&
         const uint32_t bound = lane <= 4 ? (lane == 4 ? k : hub_branch_begin(wkeys, k, lane)) : 0u;
         __syncwarp();
         gather_values(wkeys, ln.ev_val, k, lane, 32u);
-        const float* wvals = reinterpret_cast<const float*>(wkeys);
-        NeuronCold cold;
-        float4 br = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (lane == 0) {
-            cold = ln.cold[n];
-            br = ln.branches[n];
-            settle_decay(kc.cfg, s, cold, br);
-        }
-        br.x = __shfl_sync(0xffffffffu, br.x, 0);
-        br.y = __shfl_sync(0xffffffffu, br.y, 0);
-        br.z = __shfl_sync(0xffffffffu, br.z, 0);
-        br.w = __shfl_sync(0xffffffffu, br.w, 0);
-        const uint32_t next_bound = __shfl_down_sync(0xffffffffu, bound, 1);
-        __syncwarp();
-        float a = 0.0f;
-        if (lane < 4) a = ordered_sum(wvals, bound, next_bound, lane == 0 ? br.x : (lane == 1 ? br.y : (lane == 2 ? br.z : br.w)));
-        const float a1 = __shfl_sync(0xffffffffu, a, 1), a2 = __shfl_sync(0xffffffffu, a, 2),
-                    a3 = __shfl_sync(0xffffffffu, a, 3);
-        if (lane == 0)
-            settle_integrate(ln, kc, n, s, cold, make_float4(a, a1, a2, a3), pop_inh, rotation, settle_preload(ln, kc, n));
+        lo = bound;
+        hi = __shfl_down_sync(0xffffffffu, bound, 1);
         __syncwarp();
     }
+    br.x = __shfl_sync(0xffffffffu, br.x, 0);
+    br.y = __shfl_sync(0xffffffffu, br.y, 0);
+    br.z = __shfl_sync(0xffffffffu, br.z, 0);
+    br.w = __shfl_sync(0xffffffffu, br.w, 0);
+    float a = 0.0f;
+    if (lane < 4) a = ordered_sum_pipelined(wvals, lo, hi, lane == 0 ? br.x : (lane == 1 ? br.y : (lane == 2 ? br.z : br.w)));
+    const float a1 = __shfl_sync(0xffffffffu, a, 1), a2 = __shfl_sync(0xffffffffu, a, 2),
+                a3 = __shfl_sync(0xffffffffu, a, 3);
+    if (lane == 0) {
+        settle_integrate(ln, kc, n, s, cold, make_float4(a, a1, a2, a3), pop_inh, rotation, pre);
+        ln.seg_count[n] = 0u;
+    }
+    __syncwarp();
 }
 
+// One target settled by one thread (k <= 16): its keys, state and preloads
+// all in flight at once, a sorting network in registers, the values, the
+// ordered per-branch sums, integration.  Resets the target's count.
+__device__ __forceinline__ void settle_target_thread(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t n,
+                                                     uint32_t k, uint32_t offset, float pop_inh, uint32_t rotation) {
+    uint32_t e[16];
+#pragma unroll
+    for (int x = 0; x < 16; ++x) e[x] = (uint32_t)x < k ? ln.seg_events[offset + x] : 0xffffffffu;
+    NeuronCold cold = ln.cold[n];
+    float4 br = ln.branches[n];
+    const SettlePre pre = settle_preload(ln, kc, n);
+    if (k > 8u)
+        sort_network<16>(e);
+    else if (k > 4u)
+        sort_network<8>(e);
+    else if (k > 1u)
+        sort_network<4>(e);
+    float v[16];
+#pragma unroll
+    for (int x = 0; x < 16; ++x) v[x] = (uint32_t)x < k ? ln.ev_val[e[x] & kEventOrderMask] : 0.0f;
+    settle_decay(kc.cfg, s, cold, br);
+#pragma unroll
+    for (int x = 0; x < 16; ++x)
+        if ((uint32_t)x < k) add_branch(br, e[x] >> 30, v[x]);
+    settle_integrate(ln, kc, n, s, cold, br, pop_inh, rotation, pre);
+    if (k) ln.seg_count[n] = 0u;
+}
+
+// Unlisted targets with more events than a warp sorts: queued per CTA during
+// the touched loop and settled by the CTA after it.
+constexpr uint32_t kCtaQueue = 32;
+// Listed targets classified per chunk of the CTA's share of the list.
+constexpr uint32_t kListedChunk = kThreads;
+
+// ---------------------------------------------------------------------------
+// settle (runtime.rs:576-603, 710-717, 541-548, 947-962): every touched
+// neuron adds its events per branch in ascending event order onto its decayed
+// branches, then integrates (membrane, drive, block candidate).  A target's
+// events of the step are the keys in its segment (seg_count[n] of them).
+//   listed targets (high in-degree, descending capacity): CTA r settles listed
+//     targets r, r + C, ...: those with more than cta_events events by the
+//     whole CTA, more than thread_events by one of its warps, the rest (when
+//     touched this step) by one of its threads;
+//   every other touched neuron, in the warp that holds it in the touched list:
+//     at most thread_events events by its own thread, at most kHubWarpEvents
+//     by the warp, more by the CTA after the loop.
+// Whoever settles a target resets its count for the next step's deliver.
 __device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t worker,
                              uint32_t workers, uint32_t rank, uint32_t C, uint32_t* smem) {
-    const LeoConfig& c = kc.cfg;
+    __shared__ uint32_t s_list[3][kListedChunk];
+    __shared__ uint32_t s_list_k[3][kListedChunk];
+    __shared__ uint32_t s_queue[kCtaQueue], s_queue_k[kCtaQueue];
+    __shared__ uint32_t s_nlist[3], s_nqueue;
     const uint32_t n_count = kc.topo.n;
-    constexpr int kCap = 24;
     LaneScalars* sc = ln.sc;
-    uint32_t count = sc->touched_count;
-    float pop_inh = sc->population_inhibition;
-    uint32_t rotation = (uint32_t)((sc->base_tick + s) % (unsigned long long)n_count);
-    if (kc.topo.hubs) {
-        const unsigned long long t0 = clock64();
-        settle_hubs(ln, s, kc, rank, C, smem, pop_inh, rotation);
-        // Hub share of settle (first CTA), reported as the last phase counter.
-        if (rank == 0 && threadIdx.x == 0) sc->phase_cycles[LEO_PHASES - 1] += clock64() - t0;
+    const uint32_t count = sc->touched_count;
+    const float pop_inh = sc->population_inhibition;
+    const uint32_t rotation = (uint32_t)((sc->base_tick + s) % (unsigned long long)n_count);
+    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+    const uint32_t epoch = s + 1;
+    uint32_t* wkeys = smem + (size_t)warp * kHubWarpEvents;
+    if (tid == 0) s_nqueue = 0u;
+    // Listed targets, one chunk of this CTA's share at a time: classified by
+    // the step's event count into CTA / warp / thread work.
+    const unsigned long long t0 = clock64();
+    for (uint32_t round0 = 0; round0 * C < kc.topo.cta_count; round0 += kListedChunk) {
+        if (tid < 3) s_nlist[tid] = 0u;
+        __syncthreads();
+        // Round r of the list goes to the CTAs in alternating directions, so
+        // the CTA with the largest target of one round gets the smallest of
+        // the next.
+        const uint32_t round = round0 + tid;
+        const uint32_t i = round * C + ((round & 1u) ? C - 1u - rank : rank);
+        if (i < kc.topo.cta_count) {
+            const uint32_t n = kc.topo.cta_targets[i];
+            const uint32_t k = ln.seg_count[n];
+            const int tier = k > kc.topo.cta_events ? 0 : (k > kc.topo.thread_events ? 1 : 2);
+            if (tier < 2 || k > 0u || ln.touch_epoch[n] == epoch) {
+                const uint32_t pos = atomicAdd(&s_nlist[tier], 1u);
+                s_list[tier][pos] = n;
+                s_list_k[tier][pos] = k;
+            }
+        }
+        __syncthreads();
+        const uint32_t nbig = s_nlist[0], nmid = s_nlist[1], nsmall = s_nlist[2];
+        for (uint32_t j = 0; j < nbig; ++j)
+            settle_target_cta(ln, s, kc, s_list[0][j], s_list_k[0][j], kc.topo.seg[s_list[0][j]].x, smem, pop_inh,
+                              rotation);
+        if (tid < nsmall)
+            settle_target_thread(ln, s, kc, s_list[2][tid], s_list_k[2][tid], kc.topo.seg[s_list[2][tid]].x, pop_inh,
+                                 rotation);
+        for (uint32_t j = warp; j < nmid; j += kWarps)
+            settle_target_warp(ln, s, kc, s_list[1][j], s_list_k[1][j], kc.topo.seg[s_list[1][j]].x, wkeys, pop_inh,
+                               rotation);
+        __syncthreads();
     }
-    for (uint32_t i = worker; i < count; i += workers) {
-        uint32_t n = ln.touched[i];
-        NeuronCold cold;
-        float4 br;
-        if (kc.topo.hubs) {
-            const int32_t h = kc.topo.hub_of[n];
-            const uint32_t k = h >= 0 ? ln.hub_count[h] : 0u;
-            if (k > kc.topo.hub_thread_events) continue;  // settled by a warp or a CTA above
-            if (k > 0) {
-                // A hub with few events: sort its keys (branch, event order) here.
-                const uint32_t* ev = ln.hub_events + kc.topo.hub_offset[h];
-                uint32_t e[kHubThreadEvents];
-                for (uint32_t x = 0; x < k; ++x) e[x] = ev[x];
-                for (uint32_t x = 1; x < k; ++x) {
-                    const uint32_t v = e[x];
-                    int y = (int)x - 1;
-                    while (y >= 0 && e[y] > v) {
-                        e[y + 1] = e[y];
-                        --y;
-                    }
-                    e[y + 1] = v;
-                }
-                float vals[kHubThreadEvents];
-                for (uint32_t x = 0; x < k; ++x) vals[x] = ln.ev_val[e[x] & kEventOrderMask];
-                cold = ln.cold[n];
-                br = ln.branches[n];
-                settle_decay(c, s, cold, br);
-                float acc[4] = {br.x, br.y, br.z, br.w};
-                for (uint32_t x = 0; x < k; ++x) acc[e[x] >> 30] = acc[e[x] >> 30] + vals[x];
-                settle_integrate(ln, kc, n, s, cold, make_float4(acc[0], acc[1], acc[2], acc[3]), pop_inh, rotation,
-                                 settle_preload(ln, kc, n));
-                continue;
+    // Listed share of settle (first CTA), reported as the last phase counter.
+    if (rank == 0 && tid == 0 && kc.topo.cta_count) sc->phase_cycles[LEO_PHASES - 1] += clock64() - t0;
+    __syncthreads();
+    // The touched list, in warp-aligned ranges.
+    for (uint32_t base = worker - lane; base < count; base += workers) {
+        const uint32_t i = base + lane;
+        const bool valid = i < count;
+        const uint32_t n = valid ? ln.touched[i] : 0u;
+        uint2 seg = make_uint2(0u, LEO_SEG_LISTED);
+        uint32_t k = 0;
+        if (valid) {
+            seg = kc.topo.seg[n];
+            k = ln.seg_count[n];
+        }
+        const bool listed = (seg.y & LEO_SEG_LISTED) != 0u;
+        const bool alone = !listed && k <= kc.topo.thread_events;
+        if (alone) settle_target_thread(ln, s, kc, n, k, seg.x, pop_inh, rotation);
+        const bool by_warp = !listed && !alone && k <= kHubWarpEvents;
+        if (!listed && !alone && !by_warp) {
+            const uint32_t pos = atomicAdd(&s_nqueue, 1u);
+            if (pos < kCtaQueue) {
+                s_queue[pos] = n;
+                s_queue_k[pos] = k;
+            } else {
+                atomicOr(&sc->error_flag, LEO_ERR_CAPACITY);
             }
         }
-        cold = ln.cold[n];
-        br = ln.branches[n];
-        const SettlePre pre = settle_preload(ln, kc, n);
-        settle_decay(c, s, cold, br);
-        float acc[4] = {br.x, br.y, br.z, br.w};
-        // The four (target, branch) event lists, walked in lockstep so their
-        // hops overlap; events are summed per branch in ascending event order.
-        const uint4 heads = *reinterpret_cast<const uint4*>(&ln.ev_head[n * 4]);
-        if ((heads.x & heads.y & heads.z & heads.w) != LEO_EMPTY)
-            *reinterpret_cast<uint4*>(&ln.ev_head[n * 4]) = make_uint4(LEO_EMPTY, LEO_EMPTY, LEO_EMPTY, LEO_EMPTY);
-        uint32_t p[4] = {heads.x, heads.y, heads.z, heads.w};
-        uint32_t keys[kCap];
-        float vals[kCap];
-        int k = 0;
-        bool overflow = false;
-        while ((p[0] & p[1] & p[2] & p[3]) != LEO_EMPTY) {
-            uint32_t nxt[4];
-            float v[4];
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                nxt[b] = LEO_EMPTY;
-                if (p[b] != LEO_EMPTY) {
-                    nxt[b] = ln.ev_next[p[b]];
-                    v[b] = ln.ev_val[p[b]];
-                }
-            }
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                if (p[b] == LEO_EMPTY) continue;
-                if (k == kCap) {
-                    overflow = true;
-                    break;
-                }
-                keys[k] = ((uint32_t)b << 24) | p[b];
-                vals[k] = v[b];
-                ++k;
-            }
-            if (overflow) break;
-#pragma unroll
-            for (int b = 0; b < 4; ++b) p[b] = nxt[b];
+        unsigned int mask = __ballot_sync(0xffffffffu, by_warp);
+        while (mask) {
+            const int j = __ffs(mask) - 1;
+            mask &= mask - 1u;
+            const uint32_t nj = __shfl_sync(0xffffffffu, n, j), kj = __shfl_sync(0xffffffffu, k, j),
+                           oj = __shfl_sync(0xffffffffu, seg.x, j);
+            settle_target_warp(ln, s, kc, nj, kj, oj, wkeys, pop_inh, rotation);
         }
-        if (!overflow) {
-            for (int x = 1; x < k; ++x) {  // insertion sort by (branch, event order)
-                uint32_t kk = keys[x];
-                float vk = vals[x];
-                int y = x - 1;
-                while (y >= 0 && keys[y] > kk) {
-                    keys[y + 1] = keys[y];
-                    vals[y + 1] = vals[y];
-                    --y;
-                }
-                keys[y + 1] = kk;
-                vals[y + 1] = vk;
-            }
-            for (int x = 0; x < k; ++x) acc[keys[x] >> 24] = acc[keys[x] >> 24] + vals[x];
-        } else {
-            // A long list (hot target): per branch, add in ascending event
-            // order by repeated scans of the list.
-            const uint32_t head4[4] = {heads.x, heads.y, heads.z, heads.w};
-            for (int b = 0; b < 4; ++b) {
-                const uint32_t head = head4[b];
-                float a = acc[b];
-                uint32_t last = 0u;
-                bool first = true;
-                for (;;) {
-                    uint32_t best = LEO_EMPTY;
-                    float bv = 0.0f;
-                    for (uint32_t it = head; it != LEO_EMPTY; it = ln.ev_next[it]) {
-                        if ((first || it > last) && (best == LEO_EMPTY || it < best)) {
-                            best = it;
-                            bv = ln.ev_val[it];
-                        }
-                    }
-                    if (best == LEO_EMPTY) break;
-                    a = a + bv;
-                    last = best;
-                    first = false;
-                }
-                acc[b] = a;
-            }
-        }
-        br = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        settle_integrate(ln, kc, n, s, cold, br, pop_inh, rotation, pre);
     }
+    __syncthreads();
+    const uint32_t nqueue = s_nqueue < kCtaQueue ? s_nqueue : kCtaQueue;
+    for (uint32_t j = 0; j < nqueue; ++j)
+        settle_target_cta(ln, s, kc, s_queue[j], s_queue_k[j], kc.topo.seg[s_queue[j]].x, smem, pop_inh, rotation);
 }
 
 // ---------------------------------------------------------------------------
@@ -916,7 +1168,7 @@ __device__ void phase_blocks(const LaneState& ln, const KernelConsts& kc, uint32
 // active ring entry, activations, and the actives as learning destinations.
 //
 // `nwin` / `winners`: the blocks phase's winner counts and winners (global in
-// the wavefront, shared memory in the quiet-step kernel); `active_out`, when
+// the wavefront's global arrays or the first CTA's shared memory); `active_out`, when
 // given, receives the step's active count from thread 0.
 __device__ void phase_assemble(const LaneState& ln, uint32_t s, const KernelConsts& kc, bool learning,
                                unsigned long long* sorted, const uint32_t* nwin, const unsigned long long* winners,
@@ -1611,7 +1863,6 @@ __device__ __forceinline__ void wavefront_steps(const LaneState* __restrict__ la
     }
     LaneScalars* sc = ln.sc;
     const uint32_t steps = sc->steps;
-    if (begin == LEO_RESUME_STEP) begin = sc->resume_step;
     const uint32_t worker = rank * kThreads + threadIdx.x, workers = C * kThreads;
     const uint32_t gwarp = rank * kWarps + (threadIdx.x >> 5), gwarps = C * kWarps;
     const bool timer = rank == 0 && threadIdx.x == 0;
@@ -1651,8 +1902,6 @@ __device__ __forceinline__ void wavefront_steps(const LaneState* __restrict__ la
         phase_settle(ln, s, kc, worker, workers, rank, C, reinterpret_cast<uint32_t*>(smem_sorted));
         sync();
         mark(1);
-        for (uint32_t h = worker; h < kc.topo.hubs; h += workers) ln.hub_count[h] = 0;
-        if (worker == 0) sc->hub_next = 0;
         phase_blocks(ln, kc, gwarp, gwarps, win_write, nwin_write);
         if (frozen && worker == 0) release_touched(ln, tally);
         sync();
@@ -1713,495 +1962,12 @@ __device__ __forceinline__ void wavefront_steps(const LaneState* __restrict__ la
     }
 }
 
-// ---------------------------------------------------------------------------
-// Quiet frozen steps on one CTA (replay prefixes).
-//
-// A replay segment starts from a fresh transient state and runs a frozen
-// prefix (no target, no learning) before its training steps, and most prefix
-// steps touch a few hundred neurons.  This kernel runs such steps on one CTA
-// with the step's transient lists in shared memory -- touched neurons in a
-// hash table, the step's events grouped by target with a counting sort, block
-// candidates grouped by block, block winners, the active list and the ring
-// counts -- so a step's critical path is four global round trips (deliver's
-// sources and values, their synapse words, the touched neurons' state, the
-// emitters' state) and CTA barriers, where the wavefront pays cluster
-// barriers around lists in global memory.  Each thread issues its deliver
-// items' loads in batches so one round trip covers several items.  Arithmetic
-// and order are the wavefront's: each branch sums its events in ascending
-// event order, then the same integration, block top-k (same rounds), global
-// cap (phase_assemble is shared) and emission.  Persistent state (neurons,
-// rings, scalars) is the wavefront's, so the wavefront resumes where this
-// kernel stops: at the first step that is not frozen without a target, or
-// whose touched neurons, events or per-target events exceed the tables --
-// checked after the step's deliver, before the step changes persistent state.
-namespace {
-
-constexpr uint32_t kQuietSlots = 4096;               // hash slots (power of two)
-constexpr uint32_t kQuietTouched = kQuietSlots / 2;  // touched neurons per step
-constexpr uint32_t kQuietEvents = 8192;              // events per step
-constexpr uint32_t kQuietPerTarget = 64;             // events per touched neuron
-constexpr uint32_t kQuietBlocks = 1024;              // blocks (phase_assemble's limit too)
-constexpr uint32_t kQuietWinners = kQuietTouched;    // blocks x keep
-constexpr uint32_t kQuietThreadCands = 32;           // a block with more candidates is selected by a warp
-
-struct QuietShared {
-    uint32_t key[kQuietSlots];              // neuron + 1; 0 = empty
-    uint32_t start[kQuietSlots];            // events per slot, then the end of its placed run
-    uint16_t touched[kQuietTouched];        // slots in touch order
-    uint16_t tcount[kQuietTouched];         // events of touched[t]
-    uint32_t tneuron[kQuietTouched];        // neuron of touched[t]
-    uint32_t ev_key[kQuietEvents];          // branch << 24 | event order
-    float ev_val[kQuietEvents];             // then: candidates grouped by block
-    uint16_t ev_slot[kQuietEvents];
-    uint16_t placed[kQuietEvents];          // events grouped by slot
-    unsigned long long cand[kQuietTouched];  // candidate key of touched[t] (0: none); then: block winners
-    uint16_t cand_pos[kQuietTouched];       // its position in its block's run
-    uint32_t bcount[kQuietBlocks];
-    uint32_t boff[kQuietBlocks];            // then: winners per block
-    uint32_t wsum[kWarps];
-    uint32_t ring[LEO_RING];                // ring_count mirror
-    uint32_t hist[LEO_MAX_CONTEXT_ORDER];   // context history mirror (runtime.rs:642-646)
-    uint32_t nev, ntouched, overflow, supra, active, hist_len;
-};
-
-__device__ __forceinline__ int quiet_insert(QuietShared& q, uint32_t n) {
-    const uint32_t want = n + 1u;
-    uint32_t h = (n * 0x9E3779B1u) >> 20;  // 12 bits: kQuietSlots == 4096
-    for (uint32_t i = 0; i < kQuietSlots; ++i, h = (h + 1u) & (kQuietSlots - 1u)) {
-        const uint32_t k = *(volatile uint32_t*)&q.key[h];
-        if (k == want) return (int)h;
-        if (k != 0u) continue;
-        const uint32_t old = atomicCAS(&q.key[h], 0u, want);
-        if (old == 0u) {
-            // one counter update per group of converged threads
-            cg::coalesced_group g = cg::coalesced_threads();
-            uint32_t base = 0;
-            if (g.thread_rank() == 0) base = atomicAdd(&q.ntouched, g.size());
-            const uint32_t t = g.shfl(base, 0) + g.thread_rank();
-            if (t < kQuietTouched) q.touched[t] = (uint16_t)h;
-            else q.overflow = 1u;
-            return (int)h;
-        }
-        if (old == want) return (int)h;
-    }
-    q.overflow = 1u;
-    return -1;
-}
-
-__device__ __forceinline__ void quiet_event(QuietShared& q, uint32_t n, uint32_t b, uint32_t qi, float value) {
-    const int h = quiet_insert(q, n);
-    if (h < 0) return;
-    cg::coalesced_group g = cg::coalesced_threads();
-    uint32_t base = 0;
-    if (g.thread_rank() == 0) base = atomicAdd(&q.nev, g.size());
-    const uint32_t e = g.shfl(base, 0) + g.thread_rank();
-    if (e >= kQuietEvents) {
-        q.overflow = 1u;
-        return;
-    }
-    q.ev_key[e] = (b << 24) | qi;
-    q.ev_val[e] = value;
-    q.ev_slot[e] = (uint16_t)h;
-    if (atomicAdd(&q.start[h], 1u) >= kQuietPerTarget) q.overflow = 1u;
-}
-
-// Exclusive scan of one value per thread across the CTA; returns this
-// thread's offset and leaves the total in *total (every thread).
-__device__ __forceinline__ uint32_t quiet_scan(QuietShared& q, uint32_t v, uint32_t* total) {
-    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
-    uint32_t incl = v;
-    for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= (uint32_t)o) incl += y;
-    }
-    if (lane == 31) q.wsum[warp] = incl;
-    __syncthreads();
-    uint32_t before = 0, all = 0;
-    for (uint32_t w = 0; w < kWarps; ++w) {
-        const uint32_t x = q.wsum[w];
-        if (w < warp) before += x;
-        all += x;
-    }
-    __syncthreads();
-    *total = all;
-    return before + incl - v;
-}
-
-// Deliver of step s into the shared tables (no global writes); the previous
-// step's active list is `prev_list` (its assemble keys, rank order) when
-// given, else the ring.  The delayed events are enumerated as (delay group in
-// the order 8, 4, 2, 1; source rank r; synapse j), a warp per (group, source)
-// and the warp's lanes over j, so each step's loads are coalesced and issued
-// kQuietPairs sources at a time; an event's order is its item index in the
-// wavefront's numbering (group offset + r * S + j).  Returns the step's deliver
-// work items.
-constexpr uint32_t kQuietPairs = 4;
-
-__device__ uint32_t quiet_deliver(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t symbol,
-                                  QuietShared& q, const unsigned long long* prev_list, uint32_t prev_rotation) {
-    const uint32_t S = kc.topo.s, F = kc.topo.f, maxa = kc.topo.max_active, n_count = kc.topo.n;
-    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
-    const uint32_t prev = s >= 1 ? q.ring[(s - 1) % LEO_RING] : 0u;
-    const uint32_t a8 = s >= 8 ? q.ring[(s - 8) % LEO_RING] : 0u;
-    const uint32_t a4 = s >= 4 ? q.ring[(s - 4) % LEO_RING] : 0u;
-    const uint32_t a2 = s >= 2 ? q.ring[(s - 2) % LEO_RING] : 0u;
-    const uint32_t e8 = a8 * S, e4 = a4 * S, e2 = a2 * S, e1 = prev * S;
-    const uint32_t events = e8 + e4 + e2 + e1;
-    if (events + F >= (1u << 24)) {  // event order must fit the 24-bit key field
-        if (threadIdx.x == 0) q.overflow = 1u;
-        return 0u;
-    }
-    // the previous step's actives are touched (runtime.rs:537-548)
-    for (uint32_t i = threadIdx.x; i < prev; i += kThreads)
-        quiet_insert(q, prev_list ? key_neuron(prev_list[i], prev_rotation, n_count)
-                                  : ln.ring_src[((s - 1) % LEO_RING) * maxa + i]);
-    // the symbol's input slots (runtime.rs:620-639)
-    for (uint32_t f = threadIdx.x; f < F; f += kThreads) {
-        const uint32_t slot = symbol * F + f;
-        const uint32_t word = kc.topo.in_word[slot];
-        const float value = ln.p.in_weight[slot];
-        quiet_event(q, word & LEO_TARGET_MASK, LEO_WORD_BRANCH(word), events + f, value);
-    }
-    // delayed events (runtime.rs:549-618)
-    const uint32_t pairs = a8 + a4 + a2 + prev;
-    for (uint32_t p0 = warp * kQuietPairs; p0 < pairs; p0 += kWarps * kQuietPairs) {
-        // lane k < kQuietPairs resolves pair p0 + k: its group, ring entry and source
-        uint32_t my_src = 0, my_info = 0xffffffffu;  // info: d << 28 | entry << 24 | r (r < 2^24)
-        if (lane < kQuietPairs && p0 + lane < pairs) {
-            uint32_t pr = p0 + lane, d;
-            if (pr < a8) {
-                d = 8;
-            } else if (pr < a8 + a4) {
-                d = 4; pr -= a8;
-            } else if (pr < a8 + a4 + a2) {
-                d = 2; pr -= a8 + a4;
-            } else {
-                d = 1; pr -= a8 + a4 + a2;
-            }
-            const uint32_t entry = (s - d) % LEO_RING;
-            my_src = (d == 1 && prev_list) ? key_neuron(prev_list[pr], prev_rotation, n_count)
-                                           : ln.ring_src[entry * maxa + pr];
-            my_info = (d << 28) | (entry << 24) | pr;
-        }
-        for (uint32_t j0 = 0; j0 < S; j0 += 64) {
-            uint32_t word[kQuietPairs][2];
-            float val[kQuietPairs][2];
-#pragma unroll
-            for (uint32_t k = 0; k < kQuietPairs; ++k) {
-                const uint32_t info = __shfl_sync(0xffffffffu, my_info, k);
-                const uint32_t src = __shfl_sync(0xffffffffu, my_src, k);
-#pragma unroll
-                for (uint32_t h = 0; h < 2; ++h) {
-                    const uint32_t j = j0 + h * 32 + lane;
-                    word[k][h] = 0u;
-                    if (info != 0xffffffffu && j < S) {
-                        const uint32_t entry = (info >> 24) & 15u, r = info & 0xffffffu;
-                        word[k][h] = kc.topo.rec_word[src * S + j];
-                        val[k][h] = ln.ring_val[((size_t)entry * maxa + r) * S + j];
-                    }
-                }
-            }
-#pragma unroll
-            for (uint32_t k = 0; k < kQuietPairs; ++k) {
-                const uint32_t info = __shfl_sync(0xffffffffu, my_info, k);
-#pragma unroll
-                for (uint32_t h = 0; h < 2; ++h) {
-                    const uint32_t j = j0 + h * 32 + lane;
-                    if (info == 0xffffffffu || j >= S) continue;
-                    const uint32_t d = info >> 28, r = info & 0xffffffu;
-                    if (LEO_WORD_DELAY(word[k][h]) != d) continue;
-                    const uint32_t off = d == 8 ? 0u : (d == 4 ? e8 : (d == 2 ? e8 + e4 : e8 + e4 + e2));
-                    quiet_event(q, word[k][h] & LEO_TARGET_MASK, LEO_WORD_BRANCH(word[k][h]), off + r * S + j,
-                                val[k][h]);
-                }
-            }
-        }
-    }
-    return events + F;
-}
-
-}  // namespace
-
-__global__ void __launch_bounds__(kThreads, 1)
-    leo_quiet_kernel(const LaneState* __restrict__ lanes, uint32_t begin, uint32_t end, KernelConsts kc) {
-    extern __shared__ __align__(16) unsigned char quiet_smem[];
-    QuietShared& q = *reinterpret_cast<QuietShared*>(quiet_smem);
-    unsigned long long* sorted = reinterpret_cast<unsigned long long*>(quiet_smem + sizeof(QuietShared));
-    const LaneState& ln = lanes[0];
-    LaneScalars* sc = ln.sc;
-    const LeoConfig& c = kc.cfg;
-    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
-    const uint32_t B = kc.topo.blocks, S = kc.topo.s, npb = kc.topo.npb, keep = kc.topo.keep, n_count = kc.topo.n;
-    const uint32_t steps = sc->steps;
-    const unsigned long long base_tick = sc->base_tick;
-    for (uint32_t i = tid; i < kQuietSlots; i += kThreads) {
-        q.key[i] = 0u;
-        q.start[i] = 0u;
-    }
-    for (uint32_t i = tid; i < kQuietBlocks; i += kThreads) q.bcount[i] = 0u;
-    if (tid < LEO_RING) q.ring[tid] = sc->ring_count[tid];
-    if (tid < LEO_MAX_CONTEXT_ORDER) q.hist[tid] = sc->ctx_history[tid];
-    __shared__ unsigned long long acc[LEO_QUIET_PHASES];
-    __shared__ WorkTally tally;
-    if (tid == 0) {
-        q.nev = q.ntouched = q.overflow = q.supra = q.active = 0u;
-        q.hist_len = sc->ctx_history_len;
-        for (int p = 0; p < LEO_QUIET_PHASES; ++p) acc[p] = 0ull;
-        tally = WorkTally{0, 0, 0, 0, 0, 0};
-        const uint32_t cur = sc->elig_cur;
-        sc->elig_count[cur ^ 1u] = 0;
-        sc->in_elig_count[cur ^ 1u] = 0;
-    }
-    unsigned long long t0 = tid == 0 ? clock_now() : 0ull;
-    auto mark = [&](int p) {
-        if (tid == 0) {
-            const unsigned long long t = clock_now();
-            acc[p] += t - t0;
-            t0 = t;
-        }
-    };
-    __syncthreads();
-    unsigned long long* winners = q.cand;  // after the candidates are grouped
-    uint32_t* nwin = q.boff;               // after each block's run is read
-    bool have_prev = false;                // `sorted` holds the previous step's active list
-    uint32_t s = begin;
-    for (; s < end && s < steps; ++s) {
-        const uint32_t sched = ln.schedule[s];
-        if (LEO_SCHED_PERMISSION(sched) != kFrozen || LEO_SCHED_TARGET(sched) >= 0) break;
-        const uint32_t symbol = LEO_SCHED_SYMBOL(sched);
-        const uint32_t rotation = (uint32_t)((base_tick + s) % (unsigned long long)n_count);
-        const uint32_t prev_rotation = (uint32_t)((base_tick + s + n_count - 1) % (unsigned long long)n_count);
-        // deliver into the tables; give the step to the wavefront if they overflow
-        const uint32_t delivered = quiet_deliver(ln, s, kc, symbol, q, have_prev ? sorted : nullptr, prev_rotation);
-        __syncthreads();
-        if (q.overflow) break;
-        mark(0);  // deliver
-        // group the events by touched neuron: offsets of the per-slot counts
-        const uint32_t T = q.ntouched, E = q.nev;
-        const float pop_inh = sc->population_inhibition;  // latency overlaps the scan
-        uint32_t mine[4], sum = 0;
-        const uint32_t t_lo = tid * 4u;
-        for (uint32_t k = 0; k < 4; ++k) {
-            const uint32_t t = t_lo + k;
-            mine[k] = t < T ? q.start[q.touched[t]] : 0u;
-            sum += mine[k];
-        }
-        uint32_t grand = 0;
-        uint32_t off = quiet_scan(q, sum, &grand);
-        for (uint32_t k = 0; k < 4; ++k) {
-            const uint32_t t = t_lo + k;
-            if (t < T) {
-                q.tcount[t] = (uint16_t)mine[k];
-                q.start[q.touched[t]] = off;
-            }
-            off += mine[k];
-        }
-        __syncthreads();
-        for (uint32_t e = tid; e < E; e += kThreads) q.placed[atomicAdd(&q.start[q.ev_slot[e]], 1u)] = (uint16_t)e;
-        __syncthreads();
-        mark(1);  // events grouped by target
-        // settle (runtime.rs:576-603, 710-717, 947-962)
-        for (uint32_t t = tid; t < T; t += kThreads) {
-            const uint32_t h = q.touched[t];
-            const uint32_t n = q.key[h] - 1u;
-            const uint32_t cnt = q.tcount[t], hi = q.start[h], lo = hi - cnt;
-            NeuronCold cold = ln.cold[n];
-            float4 br = ln.branches[n];
-            const SettlePre pre = settle_preload(ln, kc, n);
-            for (uint32_t x = lo + 1; x < hi; ++x) {  // insertion sort by (branch, event order)
-                const uint16_t e = q.placed[x];
-                const uint32_t k = q.ev_key[e];
-                uint32_t y = x;
-                while (y > lo && q.ev_key[q.placed[y - 1]] > k) {
-                    q.placed[y] = q.placed[y - 1];
-                    --y;
-                }
-                q.placed[y] = e;
-            }
-            settle_decay(c, s, cold, br);
-            float a[4] = {br.x, br.y, br.z, br.w};
-            for (uint32_t x = lo; x < hi; ++x) {
-                const uint16_t e = q.placed[x];
-                const uint32_t b = q.ev_key[e] >> 24;
-                a[b] = a[b] + q.ev_val[e];
-            }
-            const unsigned long long key = settle_integrate_key(ln, kc, n, s, cold, make_float4(a[0], a[1], a[2], a[3]),
-                                                                pop_inh, rotation, pre);
-            q.tneuron[t] = n;
-            q.cand[t] = key;
-            if (key) q.cand_pos[t] = (uint16_t)atomicAdd(&q.bcount[n / npb], 1u);
-        }
-        __syncthreads();
-        mark(2);  // settle
-        // candidates grouped by block: exclusive scan of the block counts (B <= 1024, two per thread)
-        {
-            const uint32_t b0 = 2u * tid, b1 = b0 + 1u;
-            const uint32_t v0 = b0 < B ? q.bcount[b0] : 0u, v1 = b1 < B ? q.bcount[b1] : 0u;
-            uint32_t all = 0;
-            const uint32_t o = quiet_scan(q, v0 + v1, &all);
-            if (b0 < B) q.boff[b0] = o;
-            if (b1 < B) q.boff[b1] = o + v0;
-        }
-        __syncthreads();
-        unsigned long long* grouped = reinterpret_cast<unsigned long long*>(q.ev_val);  // events are consumed
-        for (uint32_t t = tid; t < T; t += kThreads) {
-            const unsigned long long key = q.cand[t];
-            if (key) grouped[q.boff[q.tneuron[t] / npb] + q.cand_pos[t]] = key;
-            q.key[q.touched[t]] = 0u;  // empty the tables for the next step
-            q.start[q.touched[t]] = 0u;
-        }
-        __syncthreads();
-        // blocks: block-local top-k and the (k+1)-th cutoff (runtime.rs:964-997):
-        // one thread per block with at most kQuietThreadCands candidates, one
-        // warp per larger block; both take the largest key below the previous
-        // winner keep + 1 times.
-        uint32_t supra = 0;
-        for (uint32_t b = tid; b < B; b += kThreads) {
-            const uint32_t count = q.bcount[b];
-            supra += count;
-            if (count > kQuietThreadCands) continue;
-            const unsigned long long* cand = grouped + q.boff[b];
-            unsigned long long prev = ~0ull;
-            const uint32_t rounds = count < keep + 1 ? count : keep + 1;
-            float cutoff = 0.0f;
-            for (uint32_t k = 0; k < rounds; ++k) {
-                unsigned long long best = 0ull;
-                for (uint32_t idx = 0; idx < count; ++idx) {
-                    const unsigned long long key = cand[idx];
-                    if (key < prev && key > best) best = key;
-                }
-                if (k < keep) winners[(size_t)b * keep + k] = best;
-                else cutoff = key_value(best);
-                prev = best;
-            }
-            ln.block_cutoff[b] = count > keep ? cutoff : 0.0f;
-            nwin[b] = count < keep ? count : keep;  // boff[b] is read above: this thread's own slot
-        }
-        for (uint32_t b = warp; b < B; b += kWarps) {
-            const uint32_t count = q.bcount[b];
-            if (count <= kQuietThreadCands) continue;
-            const unsigned long long* cand = grouped + q.boff[b];
-            unsigned long long prev = ~0ull;
-            const uint32_t rounds = count < keep + 1 ? count : keep + 1;
-            float cutoff = 0.0f;
-            for (uint32_t k = 0; k < rounds; ++k) {
-                unsigned long long best = 0ull;
-                for (uint32_t idx = lane; idx < count; idx += 32) {
-                    const unsigned long long key = cand[idx];
-                    if (key < prev && key > best) best = key;
-                }
-                for (int o = 16; o > 0; o >>= 1) {
-                    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-                    best = other > best ? other : best;
-                }
-                if (k < keep) {
-                    if (lane == 0) winners[(size_t)b * keep + k] = best;
-                } else {
-                    cutoff = key_value(best);
-                }
-                prev = best;
-            }
-            __syncwarp();
-            if (lane == 0) {
-                nwin[b] = count < keep ? count : keep;
-                ln.block_cutoff[b] = count > keep ? cutoff : 0.0f;
-            }
-        }
-        // one add per warp of the per-thread counts
-        for (int o = 16; o > 0; o >>= 1) supra += __shfl_xor_sync(0xffffffffu, supra, o);
-        if (lane == 0 && supra) atomicAdd(&q.supra, supra);
-        __syncthreads();
-        for (uint32_t b = tid; b < B; b += kThreads) q.bcount[b] = 0u;
-        if (tid == 0) {
-            sc->step_supra = q.supra;
-            q.supra = 0u;
-        }
-        mark(3);  // blocks
-        // assemble (shared with the wavefront); the active list stays in `sorted`
-        phase_assemble(ln, s, kc, false, sorted, nwin, winners, &q.active);
-        __syncthreads();
-        mark(4);  // assemble
-        // emit (runtime.rs:920-938, 1084-1106) from the active list in shared memory
-        const uint32_t active = q.active;
-        for (uint32_t i = tid; i < active * S; i += kThreads) {
-            const uint32_t r = i / S, j = i - r * S;
-            const unsigned long long k = sorted[r];
-            const uint32_t n = key_neuron(k, rotation, n_count);
-            const float a = key_value(k);
-            if (j == 0) {
-                NeuronCold cold = ln.cold[n];
-                cold.fatigue = cold.fatigue + c.fatigue_gain * a;
-                cold.adaptation[0] = cold.adaptation[0] + c.adaptation_fast_gain * a;
-                cold.adaptation[1] = cold.adaptation[1] + c.adaptation_medium_gain * a;
-                cold.adaptation[2] = cold.adaptation[2] + c.adaptation_slow_gain * a;
-                cold.membrane = cold.membrane - ln.p.threshold[n] * c.membrane_reset_fraction;
-                ln.cold[n] = cold;
-                ln.hot[n].refractory_until = s + c.refractory_ticks + 1u;
-            }
-            ln.ring_val[((size_t)(s % LEO_RING) * kc.topo.max_active + r) * S + j] = a * ln.p.rec_weight[(size_t)n * S + j];
-        }
-        if (tid == 0) {
-            // context history push: a frozen step without a target resolves
-            // nothing else (runtime.rs:641-646; context_resolve_warp)
-            uint32_t len = q.hist_len;
-            if (len == kc.topo.k) {
-                for (uint32_t i = 0; i + 1 < len; ++i) q.hist[i] = q.hist[i + 1];
-                len -= 1;
-            }
-            q.hist[len] = symbol;
-            q.hist_len = len + 1;
-            q.ring[s % LEO_RING] = active;
-            sc->step_flags = 0;
-            sc->dst_count = 0;
-            tally.deliver += delivered;
-            tally.touched += T;
-            tally.active += active;
-            tally.steps += 1;
-            q.nev = 0u;
-            q.ntouched = 0u;
-        }
-        have_prev = true;
-        __syncthreads();
-        mark(5);  // emit
-    }
-    if (tid == 0) {
-        if (s > begin) {  // the context state a frozen step without a target leaves
-            for (uint32_t i = 0; i < q.hist_len; ++i) sc->ctx_history[i] = q.hist[i];
-            sc->ctx_history_len = q.hist_len;
-            sc->ctx_applied = 0u;
-            sc->ctx_count = 0u;
-            sc->ctx_probes = 0u;
-        }
-        sc->resume_step = s;
-        sc->work_quiet += tally.steps;
-        flush_tally(ln, tally);
-        for (int p = 0; p < LEO_QUIET_PHASES; ++p) sc->quiet_cycles[p] += acc[p];
-    }
-}
-
-size_t leo_quiet_smem_bytes(const KernelConsts& kc) {
-    if (kc.topo.blocks > kQuietBlocks || kc.topo.blocks * kc.topo.keep > kQuietWinners || kc.topo.n >= (1u << 31))
-        return 0;
-    uint32_t winners = kc.topo.blocks * kc.topo.keep, span = 1;
-    while (span < winners) span <<= 1;
-    const size_t bytes = sizeof(QuietShared) + (size_t)span * sizeof(unsigned long long);
-    return bytes <= 200u * 1024u ? bytes : 0;
-}
-
-cudaError_t leo_launch_quiet(const LaneState* lane, uint32_t begin, uint32_t end, const KernelConsts& kc,
-                             cudaStream_t stream) {
-    const size_t smem = leo_quiet_smem_bytes(kc);
-    if (smem == 0) return cudaErrorInvalidConfiguration;
-    leo_quiet_kernel<<<1, kThreads, smem, stream>>>(lane, begin, end, kc);
-    return cudaGetLastError();
-}
-
 __host__ __device__ size_t wavefront_scratch_bytes(const KernelConsts& kc);
 
 // A thread-block cluster per lane (phases separated by cluster barriers).
 __global__ void __launch_bounds__(kThreads, 1)
     leo_wavefront_kernel(const LaneState* __restrict__ lanes, uint32_t begin, uint32_t end, KernelConsts kc) {
-    extern __shared__ unsigned long long smem_sorted[];
+    extern __shared__ __align__(16) unsigned long long smem_sorted[];
     cg::cluster_group cluster = cg::this_cluster();
     // Block winners go straight to the first CTA's shared memory (distributed
     // shared memory), where its assemble reads them after the phase barrier.
@@ -2216,7 +1982,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // eligible slots on large models) needs more bandwidth than one cluster's SMs.
 __global__ void __launch_bounds__(kThreads, 1)
     leo_wavefront_grid_kernel(const LaneState* __restrict__ lanes, uint32_t begin, uint32_t end, KernelConsts kc) {
-    extern __shared__ unsigned long long smem_sorted[];
+    extern __shared__ __align__(16) unsigned long long smem_sorted[];
     cg::grid_group grid = cg::this_grid();
     wavefront_steps(lanes, begin, end, kc, gridDim.x, blockIdx.x, [&] { grid.sync(); }, smem_sorted, nullptr, nullptr,
                     nullptr, nullptr);
@@ -2232,14 +1998,11 @@ __host__ __device__ size_t wavefront_scratch_bytes(const KernelConsts& kc) {
     size_t sort = (size_t)span * sizeof(unsigned long long);
     size_t tiles = (size_t)kWarps * 32 * 33 * sizeof(float);
     size_t bytes = sort > tiles ? sort : tiles;
-    if (kc.topo.hubs) {
-        // the warps' sort slices, or one CTA's sort, whichever is larger
-        size_t warps = (size_t)kWarps * kHubWarpEvents * sizeof(uint32_t);
-        size_t cta = (size_t)(kc.topo.hub_sort_capacity < kHubSortShared ? kc.topo.hub_sort_capacity : kHubSortShared) *
-                     sizeof(uint32_t);
-        size_t hub = warps > cta ? warps : cta;
-        bytes = bytes > hub ? bytes : hub;
-    }
+    // settle's sorts: the warps' slices, or one CTA's sort, whichever is larger
+    const size_t warps = (size_t)kWarps * kHubWarpEvents * sizeof(uint32_t);
+    const size_t cta = (size_t)kHubSortShared * sizeof(uint32_t);
+    const size_t sorts = warps > cta ? warps : cta;
+    bytes = bytes > sorts ? bytes : sorts;
     return (bytes + 15) & ~(size_t)15;
 }
 
@@ -2255,8 +2018,6 @@ cudaError_t leo_wavefront_configure() {
     cudaError_t e = cudaFuncSetAttribute(leo_wavefront_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(leo_wavefront_grid_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(leo_quiet_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(leo_wavefront_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
 }

@@ -186,8 +186,10 @@ class LeoB200PerfStats(C.Structure):
         ("merge_context_ms", C.c_double),
         ("replay_ms", C.c_double),
         ("replay_sync_ms", C.c_double),
-        ("quiet_launches", C.c_uint64),
-        ("quiet_steps", C.c_uint64),
-        ("quiet_ms", C.c_double),
-        ("quiet_cycles", C.c_uint64 * 6),
+        ("replay_phase_cycles", C.c_uint64 * 11),
+        ("replay_work_steps", C.c_uint64),
+        ("replay_work_touched", C.c_uint64),
+        ("replay_work_active", C.c_uint64),
+        ("replay_work_deliver", C.c_uint64),
+        ("replay_work_eligible", C.c_uint64),
     ]

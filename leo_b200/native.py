@@ -58,7 +58,6 @@ def lib() -> C.CDLL:
     L.leo_b200_canonical_tick.restype = u64
     L.leo_b200_set_canonical_tick.argtypes = [vp, u64]
     L.leo_b200_set_story_chunk.argtypes = [vp, u32]
-    L.leo_b200_set_quiet_steps.argtypes = [vp, C.c_int]
     L.leo_b200_set_device_context_merge.argtypes = [vp, C.c_int]
     L.leo_b200_shard_begin.argtypes = [vp, vp, vp, u32, u32, u32, C.c_int]
     L.leo_b200_shard_local.argtypes = [vp, P(LeoB200ShardStory), vp, P(sz)]

@@ -119,12 +119,14 @@ def test_gpu_result_does_not_depend_on_geometry(native_lib, geometry, case_name)
 @pytest.mark.parametrize("case_name,min_in_degree,cta_events,thread_events", [
     ("baseline1", 1, 0, 0), ("baseline1", 1, 1, 1), ("baseline1", 1, 0, 1), ("test-8", 1, 1, 1),
     ("baseline2-short", 32, 2, 1), ("baseline3-short", 0, 1, 1), ("baseline3-short", 0, 0, 0),
+    ("baseline3-short", 0, 2048, 1), ("baseline2-short", 32, 2048, 2),
 ], ids=["baseline1-all-hubs-default", "baseline1-all-hubs-cta", "baseline1-all-hubs-warp", "test8-all-hubs-cta",
-        "baseline2-hubs", "baseline3-cta", "baseline3-default"])
+        "baseline2-hubs", "baseline3-cta", "baseline3-default", "baseline3-warp-wide", "baseline2-warp-wide"])
 def test_gpu_hub_path_matches_golden(native_lib, case_name, min_in_degree, cta_events, thread_events):
     """Hub targets (contiguous per-hub event buffers sorted by event order)
-    give the same results as per-target event lists, on the thread-level and
-    the CTA-level sort, whichever neurons are hubs."""
+    give the same results as per-target event lists, on the thread-level,
+    warp-level (register sort up to 256 keys, shared-memory sort above) and
+    CTA-level sort, whichever neurons are hubs."""
     from leo_b200.backend import GpuBackend
     from leo_b200.ctypes_types import TRAINING
     from leo_b200.model import HostModel
@@ -139,30 +141,6 @@ def test_gpu_hub_path_matches_golden(native_lib, case_name, min_in_degree, cta_e
         for i, (rec, batch) in enumerate(zip(case["batches"], batches)):
             backend.training_story_batch(batch, TRAINING)
             assert backend.state_digest().hex() == rec["state_hash"], f"batch {i}"
-
-
-@pytest.mark.gpu
-@pytest.mark.parametrize("case_name", ["baseline1", "baseline2-short", "baseline3-short", "test-8"])
-@pytest.mark.parametrize("quiet", [True, False], ids=["quiet-steps", "wavefront-only"])
-def test_gpu_replay_prefix_kernel_matches_golden(native_lib, case_name, quiet):
-    """With the opt-in quiet-step kernel, replay prefixes run first on one CTA
-    (shared-memory step lists) and the wavefront resumes where it stops; with
-    it on or off the golden hashes hold, and when on it ran some prefix steps."""
-    from leo_b200.backend import GpuBackend
-    from leo_b200.ctypes_types import TRAINING
-    from leo_b200.model import HostModel
-
-    case = CASES[case_name]
-    w, batches = _stories(case)
-    model = HostModel.initialize(w.config, w.topology)
-    with GpuBackend(model, device=0, max_lanes=case["stories_per_batch"]) as backend:
-        backend.set_quiet_steps(quiet)
-        for i, (rec, batch) in enumerate(zip(case["batches"], batches)):
-            backend.training_story_batch(batch, TRAINING)
-            assert backend.state_digest().hex() == rec["state_hash"], f"batch {i}"
-        perf = backend.perf_stats()
-        assert (perf.quiet_steps > 0) == quiet
-        assert (perf.quiet_launches > 0) == quiet
 
 
 @pytest.mark.gpu
