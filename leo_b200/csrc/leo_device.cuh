@@ -228,4 +228,5 @@ struct KernelConsts {
     uint32_t exp_mask;        // capacity - 1 (power of two)
     uint32_t log_mask;
     uint32_t event_capacity;
+    uint32_t event_bits;      // bits of the largest event order (event_capacity - 1)
 };

@@ -1908,6 +1908,9 @@ int leo_b200_open(int device, const LeoB200HostModel* canonical, uint32_t max_la
         t.neuron_type = dev->mem.alloc<uint8_t>(z.n);
         t.excitability = dev->mem.alloc<float>(z.n);
         dev->kc.event_capacity = 4u * t.max_active * t.s + t.f;
+        dev->kc.event_bits = 1;
+        while ((1u << dev->kc.event_bits) < dev->kc.event_capacity) ++dev->kc.event_bits;
+        if (dev->kc.event_bits > 29) throw LeoFailure("event order exceeds 29 bits");
         // libm exception tables (leo_math.cuh) as open-addressing hash tables
         auto build_table = [&](const uint32_t* keys, const uint32_t* values, size_t count, uint32_t* mask_out) {
             size_t cap = 1024;

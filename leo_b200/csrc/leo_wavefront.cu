@@ -47,6 +47,7 @@
 // signals over the 257 outputs), no multiply-add is fused (-fmad=false), and
 // exp/ln reproduce the platform libm (leo_math.cuh plus exception tables).
 #include <cooperative_groups.h>
+#include <cub/block/block_radix_sort.cuh>
 #include <stdint.h>
 
 #include "leo_device.cuh"
@@ -54,6 +55,8 @@
 #include "leo_math.cuh"
 
 namespace cg = cooperative_groups;
+
+
 
 // Most event keys one target's segment holds, all sorted in shared memory by
 // one CTA (128 KB; the host rejects larger segment capacities).
@@ -192,29 +195,55 @@ __device__ __forceinline__ void append_coalesced(uint32_t* list, uint32_t* count
     list[base + g.thread_rank()] = item;
 }
 
-__device__ __forceinline__ void touch(const LaneState& ln, uint32_t n, uint32_t epoch) {
-    // A plain read skips the atomic for targets already touched this step
-    // (hub targets receive thousands of events per step).
+
+// Neurons a CTA touches in one deliver phase, gathered in shared memory and
+// appended to the lane's touched list with one reservation per CTA (one
+// atomic per neuron on the lane's single counter serialises at that address).
+constexpr uint32_t kTouchBuffer = 2048;
+struct TouchBuffer {
+    uint32_t count;
+    uint32_t base;
+    uint32_t items[kTouchBuffer];
+};
+
+__device__ __forceinline__ void touch_buffered(const LaneState& ln, uint32_t n, uint32_t epoch, TouchBuffer& tb) {
     if (*(volatile uint32_t*)&ln.touch_epoch[n] == epoch) return;
-    if (atomicExch(&ln.touch_epoch[n], epoch) != epoch) append_coalesced(ln.touched, &ln.sc->touched_count, n);
+    if (atomicExch(&ln.touch_epoch[n], epoch) == epoch) return;
+    const uint32_t pos = atomicAdd(&tb.count, 1u);
+    if (pos < kTouchBuffer)
+        tb.items[pos] = n;
+    else
+        append_coalesced(ln.touched, &ln.sc->touched_count, n);
+}
+
+// Appends the CTA's buffered touches to the lane's touched list; every thread
+// of the CTA calls it at the end of its deliver phase.
+__device__ __forceinline__ void flush_touches(const LaneState& ln, TouchBuffer& tb) {
+    __syncthreads();
+    const uint32_t count = tb.count < kTouchBuffer ? tb.count : kTouchBuffer;
+    if (threadIdx.x == 0 && count) tb.base = atomicAdd(&ln.sc->touched_count, count);
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < count; i += kThreads) ln.touched[tb.base + i] = tb.items[i];
 }
 
 // An event: its value is stored by event order, and its key (branch << 30 |
 // event order) appended to the target's segment, one atomic per group of
 // converged threads with the same target; settle restores the order by
-// sorting the keys.  A segment holds every event the target can receive in
-// one step (the bound is computed from the topology); an overrun is reported.
+// sorting the keys.  The first event a target receives in the step also
+// touches it.  A segment holds every event the target can receive in one step
+// (the bound is computed from the topology); an overrun is reported.
 constexpr uint32_t kEventOrderMask = 0x3fffffffu;
-__device__ __forceinline__ void seg_push(const LaneState& ln, const KernelConsts& kc, uint32_t n, uint32_t key,
-                                         float value) {
+__device__ __forceinline__ void push_event(const LaneState& ln, const KernelConsts& kc, uint32_t n, uint32_t key,
+                                           float value, uint32_t epoch, TouchBuffer& tb) {
+    const uint2 seg = kc.topo.seg[n];
     cg::coalesced_group g = cg::coalesced_threads();
     cg::coalesced_group peers = cg::labeled_partition(g, n);
     uint32_t base = 0;
     if (peers.thread_rank() == 0) base = atomicAdd(&ln.seg_count[n], peers.size());
     base = peers.shfl(base, 0);
+    if (base == 0u && peers.thread_rank() == 0) touch_buffered(ln, n, epoch, tb);
     const uint32_t pos = base + peers.thread_rank();
     ln.ev_val[key & kEventOrderMask] = value;
-    const uint2 seg = kc.topo.seg[n];
     if (pos < (seg.y & LEO_SEG_CAPACITY))
         ln.seg_events[seg.x + pos] = key;
     else
@@ -359,98 +388,108 @@ __device__ void context_resolve_warp(const LaneState& ln, uint32_t s, const Kern
 }
 
 // ---------------------------------------------------------------------------
-// deliver (runtime.rs:537-639).  Work item order within a lane is the CPU's
-// event order: previous actives, then due events from emission ticks s-8,
-// s-4, s-2, s-1 (rank, then slot), then the symbol's input slots; the event
-// index q encodes that order.
+// deliver (runtime.rs:537-639).  Event order within a lane is the CPU's:
+// previous actives, then due events from emission ticks s-8, s-4, s-2, s-1
+// (rank, then slot), then the symbol's input slots; the event index q (the
+// position among all scanned slots, then the input slots) encodes it.  A due
+// source is one warp's task: each lane loads its slots' topology words and
+// emitted values in one round, and the slots whose delay matches deliver.
 //
 // `fresh_d1`: the previous step was frozen and its emit phase runs beside this
 // deliver, so its ring values are not written yet; a delay-1 event's value is
 // formed here from the same operands (activation x weight; no learning step
 // separates emission and delivery, so the weight is the one emit reads).
+constexpr uint32_t kDeliverUnroll = 4;  // slots per lane per round (S <= 128 in one round)
+
+__device__ __forceinline__ void deliver_trace(const LaneState& ln, const KernelConsts& kc, Trace* traces, uint2* const* lists,
+                                              uint32_t* counts, uint32_t cur, uint32_t slot, uint32_t s, float a) {
+    // activate_{recurrent,input}_trace (runtime.rs:719-735); one event per slot per tick
+    Trace t = load_trace(&traces[slot]);
+    advance_trace(kc.cfg, t, s);
+    t.branch_sens = t.branch_sens + a;
+    if ((t.tick_mark & 1u) == 0u) {
+        t.tick_mark |= 1u;
+        cg::coalesced_group g = cg::coalesced_threads();
+        uint32_t base = 0;
+        if (g.thread_rank() == 0) base = atomicAdd(&counts[cur], g.size());
+        base = g.shfl(base, 0);
+        lists[cur][base + g.thread_rank()] = make_uint2(slot, 0u);
+    }
+    store_trace(&traces[slot], t);
+}
+
 __device__ uint32_t phase_deliver(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t worker,
                                   uint32_t workers, bool learn, uint32_t symbol, bool fresh_d1) {
     const uint32_t S = kc.topo.s, F = kc.topo.f, maxa = kc.topo.max_active;
     LaneScalars* sc = ln.sc;
-    uint32_t prev = s >= 1 ? sc->ring_count[(s - 1) % LEO_RING] : 0u;
-    uint32_t a8 = s >= 8 ? sc->ring_count[(s - 8) % LEO_RING] : 0u;
-    uint32_t a4 = s >= 4 ? sc->ring_count[(s - 4) % LEO_RING] : 0u;
-    uint32_t a2 = s >= 2 ? sc->ring_count[(s - 2) % LEO_RING] : 0u;
-    uint32_t e8 = a8 * S, e4 = a4 * S, e2 = a2 * S, e1 = prev * S;
-    uint32_t events = e8 + e4 + e2 + e1;
-    uint32_t total = prev + events + F;
+    const uint32_t prev = s >= 1 ? sc->ring_count[(s - 1) % LEO_RING] : 0u;
+    const uint32_t a8 = s >= 8 ? sc->ring_count[(s - 8) % LEO_RING] : 0u;
+    const uint32_t a4 = s >= 4 ? sc->ring_count[(s - 4) % LEO_RING] : 0u;
+    const uint32_t a2 = s >= 2 ? sc->ring_count[(s - 2) % LEO_RING] : 0u;
+    const uint32_t e8 = a8 * S, e4 = a4 * S, e2 = a2 * S, e1 = prev * S;
+    const uint32_t events = e8 + e4 + e2 + e1;
     const uint32_t cur = sc->elig_cur;
     if (worker == 0) {
         sc->elig_count[cur ^ 1u] = 0;
         sc->in_elig_count[cur ^ 1u] = 0;
     }
     const uint32_t epoch = s + 1;
-    for (uint32_t i = worker; i < total; i += workers) {
-        if (i < prev) {
-            touch(ln, ln.ring_src[((s - 1) % LEO_RING) * maxa + i], epoch);
-            continue;
-        }
-        uint32_t q = i - prev;
-        if (q < events) {
-            uint32_t d, off;
-            if (q < e8) {
-                d = 8; off = q;
-            } else if (q < e8 + e4) {
-                d = 4; off = q - e8;
-            } else if (q < e8 + e4 + e2) {
-                d = 2; off = q - e8 - e4;
-            } else {
-                d = 1; off = q - e8 - e4 - e2;
-            }
-            uint32_t entry = (s - d) % LEO_RING;
-            uint32_t r = off / S, j = off - r * S;
-            uint32_t src = ln.ring_src[entry * maxa + r];
-            uint32_t slot = src * S + j;
-            uint32_t word = kc.topo.rec_word[slot];
-            if (LEO_WORD_DELAY(word) != d) continue;
-            uint32_t n = word & LEO_TARGET_MASK, b = LEO_WORD_BRANCH(word);
-            const float value = (fresh_d1 && d == 1) ? ln.ring_act[entry * maxa + r] * ln.p.rec_weight[slot]
-                                                     : ln.ring_val[((size_t)entry * maxa + r) * S + j];
-            touch(ln, n, epoch);
-            seg_push(ln, kc, n, (b << 30) | q, value);
-            if (learn) {  // activate_recurrent_trace (runtime.rs:719-726); one event per slot per tick
-                float a = ln.ring_act[entry * maxa + r];
-                Trace t = load_trace(&ln.traces[slot]);
-                advance_trace(kc.cfg, t, s);
-                t.branch_sens = t.branch_sens + a;
-                if ((t.tick_mark & 1u) == 0u) {
-                    t.tick_mark |= 1u;
-                    cg::coalesced_group g = cg::coalesced_threads();
-                    uint32_t base = 0;
-                    if (g.thread_rank() == 0) base = atomicAdd(&sc->elig_count[cur], g.size());
-                    base = g.shfl(base, 0);
-                    ln.elig[cur][base + g.thread_rank()] = make_uint2(slot, 0u);
-                }
-                store_trace(&ln.traces[slot], t);
-            }
+    const uint32_t lane = threadIdx.x & 31u, gwarp = worker >> 5, gwarps = workers >> 5;
+    __shared__ TouchBuffer tb;
+    if (threadIdx.x == 0) tb.count = 0u;
+    __syncthreads();
+    // previous actives are touched (start_tick, runtime.rs:537-561)
+    for (uint32_t i = worker; i < prev; i += workers)
+        touch_buffered(ln, ln.ring_src[((s - 1) % LEO_RING) * maxa + i], epoch, tb);
+    // due recurrent events, one warp per due source
+    const uint32_t tasks = a8 + a4 + a2 + prev;
+    for (uint32_t t = gwarp; t < tasks; t += gwarps) {
+        uint32_t d, r, qbase;
+        if (t < a8) {
+            d = 8; r = t; qbase = 0;
+        } else if (t < a8 + a4) {
+            d = 4; r = t - a8; qbase = e8;
+        } else if (t < a8 + a4 + a2) {
+            d = 2; r = t - a8 - a4; qbase = e8 + e4;
         } else {
-            uint32_t f = q - events;
-            uint32_t slot = symbol * F + f;
-            uint32_t word = kc.topo.in_word[slot];
-            uint32_t n = word & LEO_TARGET_MASK, b = LEO_WORD_BRANCH(word);
-            touch(ln, n, epoch);
-            seg_push(ln, kc, n, (b << 30) | q, ln.p.in_weight[slot]);
-            if (learn) {
-                Trace t = load_trace(&ln.in_traces[slot]);
-                advance_trace(kc.cfg, t, s);
-                t.branch_sens = t.branch_sens + 1.0f;
-                if ((t.tick_mark & 1u) == 0u) {
-                    t.tick_mark |= 1u;
-                    cg::coalesced_group g = cg::coalesced_threads();
-                    uint32_t base = 0;
-                    if (g.thread_rank() == 0) base = atomicAdd(&sc->in_elig_count[cur], g.size());
-                    base = g.shfl(base, 0);
-                    ln.in_elig[cur][base + g.thread_rank()] = make_uint2(slot, 0u);
+            d = 1; r = t - a8 - a4 - a2; qbase = e8 + e4 + e2;
+        }
+        const uint32_t entry = (s - d) % LEO_RING;
+        const uint32_t src = ln.ring_src[entry * maxa + r];
+        const float a = ln.ring_act[entry * maxa + r];
+        const bool fresh = fresh_d1 && d == 1u;
+        const float* vals = fresh ? ln.p.rec_weight + (size_t)src * S : ln.ring_val + ((size_t)entry * maxa + r) * S;
+        const uint32_t* words = kc.topo.rec_word + (size_t)src * S;
+        for (uint32_t j0 = 0; j0 < S; j0 += 32u * kDeliverUnroll) {
+            uint32_t w[kDeliverUnroll];
+            float v[kDeliverUnroll];
+#pragma unroll
+            for (uint32_t u = 0; u < kDeliverUnroll; ++u) {
+                const uint32_t j = j0 + 32u * u + lane;
+                w[u] = j < S ? words[j] : 0u;
+                v[u] = j < S ? vals[j] : 0.0f;
+            }
+#pragma unroll
+            for (uint32_t u = 0; u < kDeliverUnroll; ++u) {
+                const uint32_t j = j0 + 32u * u + lane;
+                if (j < S && LEO_WORD_DELAY(w[u]) == d) {
+                    const uint32_t n = w[u] & LEO_TARGET_MASK, b = LEO_WORD_BRANCH(w[u]);
+                    const float value = fresh ? a * v[u] : v[u];
+                    push_event(ln, kc, n, (b << 30) | (qbase + r * S + j), value, epoch, tb);
+                    if (learn) deliver_trace(ln, kc, ln.traces, ln.elig, sc->elig_count, cur, src * S + j, s, a);
                 }
-                store_trace(&ln.in_traces[slot], t);
             }
         }
     }
+    // the symbol's input slots (inject_symbol, runtime.rs:627-639)
+    for (uint32_t f = worker; f < F; f += workers) {
+        const uint32_t slot = symbol * F + f;
+        const uint32_t word = kc.topo.in_word[slot];
+        const uint32_t n = word & LEO_TARGET_MASK, b = LEO_WORD_BRANCH(word);
+        push_event(ln, kc, n, (b << 30) | (events + f), ln.p.in_weight[slot], epoch, tb);
+        if (learn) deliver_trace(ln, kc, ln.in_traces, ln.in_elig, sc->in_elig_count, cur, slot, s, 1.0f);
+    }
+    flush_touches(ln, tb);
     return events + F;
 }
 
@@ -619,20 +658,17 @@ __device__ __forceinline__ void bitonic_sort_keys(uint32_t* keys, uint32_t P, ui
 }
 
 // ---------------------------------------------------------------------------
-// Register-resident bitonic sort of P keys per thread in blocked layout
-// (thread t holds elements Pt .. Pt+P-1): strides below P exchange registers,
-// strides P..16P exchange with the partner lane by shuffle, and strides of
-// 32P and more (the CTA sort only) exchange through shared memory, one
-// barrier per such stage.  A warp sorts 256 keys (P = 8); a CTA sorts up to
-// 4096, with P = 2, 4 or 8 so that every warp takes part from 1024 keys up.
+// Register-resident bitonic sort of a warp's 256 keys, 8 per lane in blocked
+// layout (lane t holds elements 8t .. 8t+7): strides below 8 exchange
+// registers, strides 8..128 exchange with the partner lane by shuffle.
 constexpr uint32_t kSortPer = 8;
 constexpr uint32_t kWarpSortKeys = 32 * kSortPer;
-constexpr uint32_t kCtaSortKeys = kThreads * kSortPer;
+constexpr uint32_t kCtaSortKeys = kThreads * kSortPer;  // the CTA's radix sort: up to 8 keys per thread
 
-template <int P, int S>
-__device__ __forceinline__ void sort_regs(uint32_t (&v)[P], uint32_t e0, uint32_t w) {
+template <int S>
+__device__ __forceinline__ void sort_regs(uint32_t (&v)[kSortPer], uint32_t e0, uint32_t w) {
 #pragma unroll
-    for (int r = 0; r < P; ++r) {
+    for (int r = 0; r < (int)kSortPer; ++r) {
         if ((r & S) == 0) {
             const bool asc = ((e0 + (uint32_t)r) & w) == 0u;
             const uint32_t a = v[r], b = v[r | S];
@@ -643,86 +679,24 @@ __device__ __forceinline__ void sort_regs(uint32_t (&v)[P], uint32_t e0, uint32_
     }
 }
 
-template <int P>
-__device__ __forceinline__ void sort_shfl(uint32_t (&v)[P], uint32_t e0, uint32_t w, uint32_t stride) {
+__device__ __forceinline__ void sort_shfl(uint32_t (&v)[kSortPer], uint32_t e0, uint32_t w, uint32_t stride) {
     const bool keep_min = ((e0 & stride) == 0u) == ((e0 & w) == 0u);
-    const int lane_mask = (int)(stride / P);
+    const int lane_mask = (int)(stride / kSortPer);
 #pragma unroll
-    for (int r = 0; r < P; ++r) {
+    for (int r = 0; r < (int)kSortPer; ++r) {
         const uint32_t o = __shfl_xor_sync(0xffffffffu, v[r], lane_mask);
         v[r] = keep_min ? (v[r] < o ? v[r] : o) : (v[r] < o ? o : v[r]);
     }
 }
 
-// Thread t's P keys to / from words Pt .. Pt+P-1 of shared memory (16-byte aligned).
-template <int P>
-__device__ __forceinline__ void store_keys(uint32_t* buf, uint32_t t, const uint32_t (&v)[P]) {
-    if constexpr (P == 2) {
-        reinterpret_cast<uint2*>(buf)[t] = make_uint2(v[0], v[1]);
-    } else {
-#pragma unroll
-        for (int r = 0; r < P; r += 4) reinterpret_cast<uint4*>(buf)[(P / 4) * t + r / 4] = make_uint4(v[r], v[r + 1], v[r + 2], v[r + 3]);
-    }
-}
-template <int P>
-__device__ __forceinline__ void fetch_keys(const uint32_t* buf, uint32_t t, uint32_t (&v)[P]) {
-    if constexpr (P == 2) {
-        const uint2 x = reinterpret_cast<const uint2*>(buf)[t];
-        v[0] = x.x;
-        v[1] = x.y;
-    } else {
-#pragma unroll
-        for (int r = 0; r < P; r += 4) {
-            const uint4 x = reinterpret_cast<const uint4*>(buf)[(P / 4) * t + r / 4];
-            v[r] = x.x;
-            v[r + 1] = x.y;
-            v[r + 2] = x.z;
-            v[r + 3] = x.w;
-        }
-    }
-}
-
-template <int P>
-__device__ __forceinline__ void sort_smem(uint32_t (&v)[P], uint32_t* buf, uint32_t t, uint32_t w, uint32_t stride,
-                                          bool active) {
-    if (active) store_keys<P>(buf, t, v);
-    __syncthreads();
-    if (!active) return;
-    uint32_t o[P];
-    fetch_keys<P>(buf, t ^ (stride / P), o);
-    const uint32_t e0 = t * P;
-    const bool keep_min = ((e0 & stride) == 0u) == ((e0 & w) == 0u);
-#pragma unroll
-    for (int r = 0; r < P; ++r) v[r] = keep_min ? (v[r] < o[r] ? v[r] : o[r]) : (v[r] < o[r] ? o[r] : v[r]);
-}
-
-// Ascending sort of the n keys (a power of two, P per thread) held by threads
-// t < n / P: a warp (kCta false: n = 32 P, no shared memory), or some or all of
-// the CTA's threads (kCta true: `buf` holds 2 x n keys, 16-byte aligned, and
-// every thread of the CTA calls this, the others only meeting the barriers).
-template <bool kCta, int P>
-__device__ __forceinline__ void bitonic_sort_regs(uint32_t (&v)[P], uint32_t t, uint32_t n, uint32_t* buf) {
-    const uint32_t e0 = t * P;
-    const bool active = e0 < n;
-    uint32_t half = 0;
-    for (uint32_t w = 2; w <= n; w <<= 1) {
-        for (uint32_t stride = w >> 1; stride >= (uint32_t)P; stride >>= 1) {
-            if (kCta && stride >= (uint32_t)P * 32u) {
-                sort_smem<P>(v, buf + (half ? n : 0u), t, w, stride, active);
-                half ^= 1u;
-            } else if (active) {
-                sort_shfl<P>(v, e0, w, stride);
-            }
-        }
-        if (active) {
-            if constexpr (P >= 8) {
-                if (w >= 8) sort_regs<P, 4>(v, e0, w);
-            }
-            if constexpr (P >= 4) {
-                if (w >= 4) sort_regs<P, 2>(v, e0, w);
-            }
-            sort_regs<P, 1>(v, e0, w);
-        }
+// Ascending sort of the warp's kWarpSortKeys keys (lane index t).
+__device__ __forceinline__ void warp_sort_regs(uint32_t (&v)[kSortPer], uint32_t t) {
+    const uint32_t e0 = t * kSortPer;
+    for (uint32_t w = 2; w <= kWarpSortKeys; w <<= 1) {
+        for (uint32_t stride = w >> 1; stride >= kSortPer; stride >>= 1) sort_shfl(v, e0, w, stride);
+        if (w >= 8) sort_regs<4>(v, e0, w);
+        if (w >= 4) sort_regs<2>(v, e0, w);
+        sort_regs<1>(v, e0, w);
     }
 }
 
@@ -754,43 +728,15 @@ __device__ __forceinline__ float ordered_sum_pipelined(const float* vals, uint32
 }
 
 // Per-branch counts of the sorted keys e < k held in v (blocked layout).
-template <int P>
-__device__ __forceinline__ void branch_counts(const uint32_t (&v)[P], uint32_t e0, uint32_t k, uint32_t (&cnt)[4]) {
+__device__ __forceinline__ void branch_counts(const uint32_t (&v)[kSortPer], uint32_t e0, uint32_t k, uint32_t (&cnt)[4]) {
 #pragma unroll
     for (int b = 0; b < 4; ++b) cnt[b] = 0u;
 #pragma unroll
-    for (int r = 0; r < P; ++r) {
+    for (int r = 0; r < (int)kSortPer; ++r) {
         const uint32_t b = e0 + (uint32_t)r < k ? v[r] >> 30 : 4u;
 #pragma unroll
         for (int x = 0; x < 4; ++x) cnt[x] += b == (uint32_t)x ? 1u : 0u;
     }
-}
-
-// The CTA's sort of one target's n keys (loaded in smem[0, n)): threads
-// t < n / P sort them (exchange buffers after the first kCtaSortKeys words),
-// gather each key's event value, write the values back to smem[0, k) in
-// sorted order and add their per-branch counts to s_cnt.
-template <int P>
-__device__ __forceinline__ void cta_sort_values(const LaneState& ln, uint32_t* smem, uint32_t n, uint32_t k,
-                                                uint32_t* s_cnt) {
-    const uint32_t tid = threadIdx.x, e0 = tid * P;
-    const bool active = e0 < n;
-    uint32_t v[P];
-    if (active) fetch_keys<P>(smem, tid, v);
-    bitonic_sort_regs<true, P>(v, tid, n, smem + kCtaSortKeys);
-    if (!active) return;
-    uint32_t val[P];
-#pragma unroll
-    for (int r = 0; r < P; ++r)
-        val[r] = e0 + (uint32_t)r < k ? __float_as_uint(ln.ev_val[v[r] & kEventOrderMask]) : 0u;
-    uint32_t cnt[4];
-    branch_counts<P>(v, e0, k, cnt);
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-        const uint32_t c = __reduce_add_sync(0xffffffffu, cnt[b]);  // whole warps are active
-        if ((tid & 31u) == 0u && c) atomicAdd(&s_cnt[b], c);
-    }
-    store_keys<P>(smem, tid, val);
 }
 
 // Bitonic sorting network over the first N of 16 keys in registers (N a
@@ -828,12 +774,56 @@ __device__ __forceinline__ void add_branch(float4& acc, uint32_t branch, float v
         acc.w = acc.w + v;
 }
 
+// The CTA's radix sort of one target's k keys (k <= ITEMS x kThreads) by
+// (branch, event order) -- the key compacted to qbits + 2 bits, the branch
+// above the event order -- loaded striped (coalesced; the sort takes any
+// arrangement) and left blocked; each sorted key's event value is gathered
+// and written to smem[0, k) in order, and the per-branch counts added to s_cnt.
+// The sort's temporary storage follows the value area (kCtaSortKeys words).
+template <int ITEMS>
+__device__ __forceinline__ void cta_radix_values(const LaneState& ln, uint32_t* smem, const uint32_t* ev, uint32_t k,
+                                                 uint32_t qbits, uint32_t* s_cnt) {
+    using Sort = cub::BlockRadixSort<uint32_t, kThreads, ITEMS>;
+    static_assert(sizeof(typename Sort::TempStorage) + kCtaSortKeys * sizeof(uint32_t) <=
+                      (size_t)kWarps * kHubWarpEvents * sizeof(uint32_t), "radix sort storage fits the scratch");
+    typename Sort::TempStorage& temp = *reinterpret_cast<typename Sort::TempStorage*>(smem + kCtaSortKeys);
+    const uint32_t tid = threadIdx.x;
+    const uint32_t qmask = (1u << qbits) - 1u, pad = (1u << (qbits + 2u)) - 1u;
+    uint32_t key[ITEMS];
+#pragma unroll
+    for (int r = 0; r < ITEMS; ++r) {
+        const uint32_t e = (uint32_t)r * kThreads + tid;
+        const uint32_t raw = e < k ? ev[e] : 0u;
+        key[r] = e < k ? ((raw >> 30) << qbits) | (raw & qmask) : pad;
+    }
+    Sort(temp).Sort(key, 0, (int)qbits + 2);
+    const uint32_t e0 = tid * ITEMS;
+    float val[ITEMS];
+    uint32_t cnt[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int r = 0; r < ITEMS; ++r) {
+        const bool live = e0 + (uint32_t)r < k;
+        val[r] = live ? ln.ev_val[key[r] & qmask] : 0.0f;
+        const uint32_t b = live ? key[r] >> qbits : 4u;
+#pragma unroll
+        for (int x = 0; x < 4; ++x) cnt[x] += b == (uint32_t)x ? 1u : 0u;
+    }
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        const uint32_t c = __reduce_add_sync(0xffffffffu, cnt[b]);
+        if ((tid & 31u) == 0u && c) atomicAdd(&s_cnt[b], c);
+    }
+#pragma unroll
+    for (int r = 0; r < ITEMS; ++r)
+        if (e0 + (uint32_t)r < k) reinterpret_cast<float*>(smem)[e0 + r] = val[r];
+}
+
 // One target settled by the whole CTA (every thread calls it): its k keys
 // sorted (registers up to 4096, shared memory above), each key's event
 // value gathered, and each branch summed in ascending event order onto the
 // decayed branch value by one thread per branch; then integration.  Resets
 // the target's count.
-__device__ __noinline__ void settle_target_cta(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t n, uint32_t k,
+__device__ void settle_target_cta(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t n, uint32_t k,
                                   uint32_t offset, uint32_t* smem, float pop_inh, uint32_t rotation) {
     __shared__ float s_acc[4];
     __shared__ uint32_t s_cnt[4];
@@ -855,18 +845,17 @@ __device__ __noinline__ void settle_target_cta(const LaneState& ln, uint32_t s, 
     }
     if (tid < 4) s_cnt[tid] = 0u;
     if (k <= kCtaSortKeys) {
-        // The smallest power of two >= k (at least 256), P keys per thread
-        // with P as small as lets every warp take part.
-        uint32_t n = kWarpSortKeys;
-        while (n < k) n <<= 1;
-        load_keys(smem, ev, k, n, tid, kThreads);
-        __syncthreads();
-        if (n <= 2 * kThreads)
-            cta_sort_values<2>(ln, smem, n, k, s_cnt);
-        else if (n <= 4 * kThreads)
-            cta_sort_values<4>(ln, smem, n, k, s_cnt);
+        // Radix sort with 1, 2, 4 or 8 keys per thread.
+        const uint32_t qbits = kc.event_bits;
+        __syncthreads();  // s_cnt cleared
+        if (k <= kThreads)
+            cta_radix_values<1>(ln, smem, ev, k, qbits, s_cnt);
+        else if (k <= 2 * kThreads)
+            cta_radix_values<2>(ln, smem, ev, k, qbits, s_cnt);
+        else if (k <= 4 * kThreads)
+            cta_radix_values<4>(ln, smem, ev, k, qbits, s_cnt);
         else
-            cta_sort_values<8>(ln, smem, n, k, s_cnt);
+            cta_radix_values<8>(ln, smem, ev, k, qbits, s_cnt);
         __syncthreads();
         if (tid == 0) {
             s_bound[0] = 0u;
@@ -902,7 +891,7 @@ __device__ __noinline__ void settle_target_cta(const LaneState& ln, uint32_t s, 
 // One target settled by one warp (every lane calls it; k <= kHubWarpEvents):
 // registers up to 256 keys, the warp's shared-memory slice above.  Resets
 // the target's count.
-__device__ __noinline__ void settle_target_warp(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t n, uint32_t k,
+__device__ void settle_target_warp(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t n, uint32_t k,
                                    uint32_t offset, uint32_t* wkeys, float pop_inh, uint32_t rotation) {
     const uint32_t lane = threadIdx.x & 31u;
     const uint32_t* ev = ln.seg_events + offset;
@@ -922,12 +911,12 @@ __device__ __noinline__ void settle_target_warp(const LaneState& ln, uint32_t s,
         uint32_t v[kSortPer];
 #pragma unroll
         for (int r = 0; r < (int)kSortPer; ++r) v[r] = e0 + (uint32_t)r < k ? ev[e0 + r] : 0xffffffffu;
-        bitonic_sort_regs<false, kSortPer>(v, lane, kWarpSortKeys, nullptr);
+        warp_sort_regs(v, lane);
         float val[kSortPer];
 #pragma unroll
         for (int r = 0; r < (int)kSortPer; ++r) val[r] = e0 + (uint32_t)r < k ? ln.ev_val[v[r] & kEventOrderMask] : 0.0f;
         uint32_t cnt[4];
-        branch_counts<kSortPer>(v, e0, k, cnt);
+        branch_counts(v, e0, k, cnt);
         uint32_t acc_c = 0;
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
@@ -1003,7 +992,6 @@ __device__ __forceinline__ void settle_target_thread(const LaneState& ln, uint32
 constexpr uint32_t kCtaQueue = 32;
 // Listed targets classified per chunk of the CTA's share of the list.
 constexpr uint32_t kListedChunk = kThreads;
-
 // ---------------------------------------------------------------------------
 // settle (runtime.rs:576-603, 710-717, 541-548, 947-962): every touched
 // neuron adds its events per branch in ascending event order onto its decayed
@@ -1032,10 +1020,11 @@ __device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts
     const uint32_t epoch = s + 1;
     uint32_t* wkeys = smem + (size_t)warp * kHubWarpEvents;
     if (tid == 0) s_nqueue = 0u;
+    const unsigned long long t0 = clock64();
+    const uint32_t listed = kc.topo.cta_count;
     // Listed targets, one chunk of this CTA's share at a time: classified by
     // the step's event count into CTA / warp / thread work.
-    const unsigned long long t0 = clock64();
-    for (uint32_t round0 = 0; round0 * C < kc.topo.cta_count; round0 += kListedChunk) {
+    for (uint32_t round0 = 0; round0 * C < listed; round0 += kListedChunk) {
         if (tid < 3) s_nlist[tid] = 0u;
         __syncthreads();
         // Round r of the list goes to the CTAs in alternating directions, so
@@ -1043,7 +1032,7 @@ __device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts
         // the next.
         const uint32_t round = round0 + tid;
         const uint32_t i = round * C + ((round & 1u) ? C - 1u - rank : rank);
-        if (i < kc.topo.cta_count) {
+        if (i < listed) {
             const uint32_t n = kc.topo.cta_targets[i];
             const uint32_t k = ln.seg_count[n];
             const int tier = k > kc.topo.cta_events ? 0 : (k > kc.topo.thread_events ? 1 : 2);
@@ -1067,7 +1056,7 @@ __device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts
         __syncthreads();
     }
     // Listed share of settle (first CTA), reported as the last phase counter.
-    if (rank == 0 && tid == 0 && kc.topo.cta_count) sc->phase_cycles[LEO_PHASES - 1] += clock64() - t0;
+    if (rank == 0 && tid == 0 && listed) sc->phase_cycles[LEO_PHASES - 1] += clock64() - t0;
     __syncthreads();
     // The touched list, in warp-aligned ranges.
     for (uint32_t base = worker - lane; base < count; base += workers) {

@@ -1,7 +1,11 @@
 """Generate the golden story-batch fixtures from the CPU oracle.
 
-Usage: ``python tests/golden/make_golden.py`` (writes ``story_batches.json``
-beside this file).
+Usage: ``python tests/golden/make_golden.py [case ...]`` (writes
+``story_batches.json`` beside this file; with case names, only those cases are
+regenerated and the others kept).  The ``-full`` cases reach the regime the
+benchmark times (hundreds of actives and up to 10^6 eligible slots per step,
+whole-GPU replay segments, natural hub tiers) and take the oracle tens of
+minutes.
 
 The reference holds no value-level golden vectors for the story batch (its
 historical digests need a corpus that is not available), so these fixtures
@@ -34,6 +38,8 @@ CASES = [
     ("baseline1", "baseline1", 2, 4, 256, 1024, 0),
     ("baseline2-short", "baseline2", 2, 4, 48, 96, 5),
     ("baseline3-short", "baseline3", 1, 4, 24, 48, 9),
+    ("baseline2-full", "baseline2", 3, 32, 256, 1024, 11),
+    ("baseline3-full", "baseline3", 1, 8, 512, 2048, 13),
 ]
 
 
@@ -83,8 +89,21 @@ def main() -> None:
     from oracle import oracle_py
 
     oracle_py.build()
-    data = {"generator": "tests/golden/make_golden.py", "cases": [record_batches(*c) for c in CASES]}
-    (HERE / "story_batches.json").write_text(json.dumps(data, indent=1, sort_keys=True) + "\n")
+    path = HERE / "story_batches.json"
+    wanted = set(sys.argv[1:])
+    unknown = wanted - {c[0] for c in CASES}
+    if unknown:
+        raise SystemExit(f"unknown case(s): {sorted(unknown)}")
+    old = {c["name"]: c for c in json.loads(path.read_text())["cases"]} if wanted and path.exists() else {}
+    cases = []
+    for c in CASES:
+        if wanted and c[0] not in wanted and c[0] in old:
+            cases.append(old[c[0]])
+        else:
+            cases.append(record_batches(*c))
+            print(f"recorded {c[0]}", flush=True)
+    data = {"generator": "tests/golden/make_golden.py", "cases": cases}
+    path.write_text(json.dumps(data, indent=1, sort_keys=True) + "\n")
 
 
 if __name__ == "__main__":
