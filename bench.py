@@ -12,18 +12,23 @@ metric is input story bytes per second (``input_bytes`` of the reference's
 * ``e2e``: the same bytes / the max over ranks of the wall time of the public
   call ``training_story_batch`` with host buffers (story bytes in, per-target
   losses and summaries out).
-* ``roofline``: the dominant kernel's algorithmic bytes per launch (per-unit
-  figures in DESIGN.md) over its CUDA-event launch time, against the measured
-  HBM copy bandwidth.
-* ``cpu_baseline``: the CPU restatement of the reference backend (oracle/) on
-  a bounded sample of the same workload, timed on this box's host cores.
+* ``roofline``: the wavefront kernel's algorithmic bytes per launch (per-unit
+  figures below, units counted on the device) over its CUDA-event launch time,
+  against the measured HBM copy bandwidth.
+* ``cpu_baseline``: the CPU restatement of the reference backend (oracle/)
+  started from the GPU model's state at the first timed batch and run on that
+  batch's first stories, timed on this box's host cores.
+* ``config3`` (one GPU): the same measurement on the 262,144-unit Zipf
+  configuration (``baseline3``: 64 story workers of 512-2048 bytes) over a few
+  batches -- a full 25-batch run of it does not fit the driver's time limit.
 
-``--impl reference`` times that CPU implementation alone, one sample batch per
-step.  Under torchrun (N GPUs) one logical batch holds ``workers`` x N stories,
-sharded over the ranks with the exact batch-end merge exchanged over NCCL and
-the serial replay run on every rank (``leo_b200.parallel``; weak scaling: the
-lanes per GPU stay fixed); rank 0 prints one JSON line with the max-over-ranks
-batch time.
+``--impl reference`` times the CPU implementation alone on the same workload
+configuration, one bounded sample of stories per step, its model built by the
+oracle's own initializer.  Under torchrun (N GPUs) one logical batch holds
+``workers`` x N stories, sharded over the ranks with the exact batch-end merge
+exchanged over NCCL and the serial replay run on every rank
+(``leo_b200.parallel``; weak scaling: the lanes per GPU stay fixed); rank 0
+prints one JSON line with the max-over-ranks batch time.
 """
 
 from __future__ import annotations
@@ -36,6 +41,8 @@ import subprocess
 import sys
 import time
 from pathlib import Path
+
+import numpy as np
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
@@ -53,25 +60,28 @@ BYTES_PER_TOUCHED_HOMEOSTASIS = 12
 BYTES_PER_ELIGIBLE = 101
 BYTES_PER_DESTINATION = 1032
 BYTES_PER_PLASTIC = 20
+BYTES_PER_INHIBIT_SLOT = 16
+BYTES_PER_SELECTION_RECORD = 8
 
 
 def phase_algorithmic_bytes(p, cfg) -> dict[str, float]:
-    """Algorithmic bytes moved by each phase over the counters' window."""
+    """Algorithmic bytes moved by each phase over the counters' window (every
+    unit counted on the device)."""
     S, D, K = cfg.synapses_per_neuron, cfg.context_embedding_dim, cfg.context_max_order
     events = p.work_active * S  # every emitted event is delivered once
     steps = p.work_steps
     return {
         "deliver": events * BYTES_PER_EVENT + steps * cfg.input_fanout * BYTES_PER_INPUT_SLOT,
         "settle": p.work_touched * BYTES_PER_TOUCHED_SETTLE,
-        "blocks": p.work_active * 8.0,
-        "assemble": p.work_active * 8.0,
+        "blocks": p.work_winners * BYTES_PER_SELECTION_RECORD,
+        "assemble": p.work_winners * BYTES_PER_SELECTION_RECORD,
         "surrogate": p.work_touched * BYTES_PER_TOUCHED_SURROGATE,
         "eligible": p.work_eligible * BYTES_PER_ELIGIBLE,
         "emit_forward": p.work_active * (50 + 8 * S + 1028) + steps * (257 * D * 4 + K * D * 4),
         "learn": p.work_destinations * BYTES_PER_DESTINATION + p.work_active * 2056
         + p.work_touched * BYTES_PER_TOUCHED_HOMEOSTASIS,
         "plasticity": p.work_plastic * BYTES_PER_PLASTIC,
-        "inhibit": p.work_active * 0.2 * S * 16,
+        "inhibit": p.work_inhibit * BYTES_PER_INHIBIT_SLOT,
     }
 
 
@@ -138,49 +148,71 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def cpu_sample(workload, threads: int, stories_n: int, story_bytes: int, batches: int) -> dict:
-    """The CPU restatement of the reference backend on a bounded sample."""
-    from leo_b200.model import HostModel
-    from leo_b200.synthetic import story_stream
-    from oracle.oracle_py import OracleModel, OracleRuntime
-
+def workload_config(workload, world: int) -> dict:
+    """The ``config`` object of both arms' lines."""
     cfg = workload.config
-    model = HostModel.initialize(cfg, workload.topology)
-    canonical = OracleRuntime(OracleModel.from_arrays(cfg, model.arrays))
-    lo, hi = (story_bytes, story_bytes) if story_bytes else (workload.min_story_bytes, workload.max_story_bytes)
-    stories = story_stream(workload.story_seed + 7919, stories_n * batches, lo, hi)
-    times, nbytes = [], 0
-    for b in range(batches):
-        batch = stories[b * stories_n:(b + 1) * stories_n]
-        t0 = time.perf_counter()
-        canonical.train_story_batch(batch, 2, threads)
-        times.append(time.perf_counter() - t0)
-        nbytes += sum(len(s) for s in batch)
-    total = sum(times)
-    return {"value": nbytes / total, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{batches} batch(es) of {stories_n} stories ({nbytes} bytes, lengths {lo}-{hi}) of "
-                      f"{workload.name}, one thread per story, merge and replay included; {total:.1f} s of CPU work",
-            "seconds": total}
+    per_batch = workload.workers * world
+    return {"workload": workload.name, "neurons": cfg.neuron_count, "synapses_per_neuron": cfg.synapses_per_neuron,
+            "topology": "zipf(1.1) targets" if workload.topology == 2 else "uniform targets",
+            "workers": workload.workers, "story_bytes": [workload.min_story_bytes, workload.max_story_bytes],
+            "replay_fraction": cfg.replay_fraction,
+            "parallelism": f"dp{world}: one logical batch of {per_batch} stories sharded over {world} GPU(s)"
+                           f" ({workload.workers} lanes each), exact merge over NCCL, serial replay",
+            "global_batch": per_batch, "l2": "per-batch working set (lanes x 0.3-2.2 GB) exceeds L2"}
+
+
+def workload_batches(workload, per_batch: int, count: int) -> list[list[bytes]]:
+    """The story stream both arms read: batch i is stories [i * per_batch, (i + 1) * per_batch)."""
+    from leo_b200.synthetic import story_stream
+
+    stories = story_stream(workload.story_seed, per_batch * count, workload.min_story_bytes, workload.max_story_bytes)
+    return [stories[i * per_batch:(i + 1) * per_batch] for i in range(count)]
+
+
+def oracle_batch(cfg, runtime, stories: list[bytes], threads: int) -> tuple[float, int]:
+    """One story batch of the CPU restatement (one thread per story, merge and
+    replay included); returns (seconds, story bytes)."""
+    from leo_b200.ctypes_types import TRAINING
+
+    t0 = time.perf_counter()
+    runtime.train_story_batch(stories, TRAINING, threads)
+    return time.perf_counter() - t0, sum(len(x) for x in stories)
 
 
 def run_reference(args, workload) -> None:
+    """The reference arm: the CPU restatement of the reference backend
+    (oracle/, its own model initializer; no GPU library is loaded), each step a
+    bounded sample -- the first ``--cpu-stories`` stories of the GPU arm's batch
+    of the same index -- trained continuously like the GPU arm's batches."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    threads = min(args.cpu_stories, os.cpu_count() or 1)
-    for _ in range(args.warmup):
-        cpu_sample(workload, threads, args.cpu_stories, args.cpu_bytes, 1)
-    res = cpu_sample(workload, threads, args.cpu_stories, args.cpu_bytes, args.steps)
-    line = {"metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": res["seconds"] * 1000 / max(args.steps, 1),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded order-2 Markov printable-ASCII stories)",
-            "config": {"workload": workload.name, "stories_per_step": args.cpu_stories,
-                       "story_bytes": args.cpu_bytes, "replay_fraction": workload.config.replay_fraction},
-            "impl": "reference",
-            "cpu_baseline": {"value": res["value"], "unit": UNIT, "cores": res["cores"], "kind": "port",
-                             "sample": res["sample"]},
-            "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    from oracle.oracle_py import OracleModel, OracleRuntime
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    cfg = workload.config
+    n = min(args.cpu_stories, workload.workers * world)
+    threads = min(n, os.cpu_count() or 1)
+    runtime = OracleRuntime(OracleModel.initialize(cfg, workload.topology))
+    batches = workload_batches(workload, workload.workers * world, args.warmup + args.steps)
+    for b in range(args.warmup):
+        oracle_batch(cfg, runtime, batches[b][:n], threads)
+    seconds, nbytes = 0.0, 0
+    for b in range(args.warmup, args.warmup + args.steps):
+        dt, nb = oracle_batch(cfg, runtime, batches[b][:n], threads)
+        seconds += dt
+        nbytes += nb
+    value = nbytes / seconds
+    sample = (f"{args.steps} timed batch(es) after {args.warmup} warm-up, each the first {n} of the GPU arm's "
+              f"{workload.workers * world} stories of that batch ({nbytes} bytes timed), one thread per story, "
+              f"merge and replay included, trained continuously from the oracle's own initial model")
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": seconds * 1000 / max(args.steps, 1), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded order-2 Markov printable-ASCII stories), random-init model",
+            "config": workload_config(workload, world), "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -333,6 +365,77 @@ def measure_replay_off(backend, workload, args, device: int) -> dict:
             "batches": args.steps, "note": "same model, replay fraction 0, fresh stories"}
 
 
+def roofline_of(perf, cfg, workload_name: str) -> dict:
+    """The wavefront kernel's roofline over the counters' window."""
+    peak, peak_kind = measured_peaks()
+    alg = phase_algorithmic_bytes(perf, cfg)
+    launches = max(perf.wavefront_launches, 1)
+    per_launch_ms = perf.wavefront_ms / launches
+    per_launch_bytes = sum(alg.values()) / launches
+    achieved = per_launch_bytes / (per_launch_ms / 1000.0) / 1e9 if per_launch_ms > 0 else 0.0
+    cycles = np.array(list(perf.phase_cycles)[:10], dtype=np.float64)
+    from leo_b200.ctypes_types import PHASES
+
+    shares = {PHASES[i]: round(float(cycles[i] / max(cycles.sum(), 1.0)), 4) for i in range(10)}
+    traffic, traffic_source = dram_traffic(workload_name, per_launch_bytes)
+    return {"bound": "hbm", "kernel": "leo_wavefront_kernel", "achieved": round(achieved, 3), "peak": peak,
+            "unit": "GB/s", "frac": round(achieved / peak, 6), "peak_source": peak_kind, "traffic": traffic,
+            "traffic_source": traffic_source, "algorithmic_bytes_per_launch": round(per_launch_bytes, 1),
+            "algorithmic_bytes_by_phase": {k: round(v / launches, 1) for k, v in alg.items()},
+            "frac_of_nominal_8tbs": round(achieved / 8000.0, 6), "launch_ms": round(per_launch_ms, 4),
+            "launches": int(perf.wavefront_launches),
+            "share_of_step_time": round(perf.wavefront_ms / max(perf.batch_ms, 1e-9), 4),
+            "phase_cycle_shares": shares,
+            "clusters": {"story": perf.story_cluster, "replay": perf.replay_cluster}}
+
+
+def replay_step_us(perf) -> dict:
+    """Replay lane: wall microseconds per step by phase (first CTA's clock)."""
+    from leo_b200.ctypes_types import PHASES
+
+    steps = max(int(perf.replay_work_steps), 1)
+    mhz = 1965.0
+    return {PHASES[i]: round(perf.replay_phase_cycles[i] / mhz / steps, 2) for i in range(len(PHASES))}
+
+
+def measure_big(args, device: int) -> dict:
+    """The 262,144-unit configuration over a few batches on one GPU (a 25-batch
+    run of it does not fit the driver's limit): CUDA-event batch time after
+    one warm-up batch, its roofline and its replay step breakdown."""
+    from leo_b200.backend import GpuBackend
+    from leo_b200.configs import WORKLOADS
+    from leo_b200.ctypes_types import TRAINING
+    from leo_b200.model import HostModel
+
+    workload = WORKLOADS[args.big_workload]
+    cfg = workload.config
+    model = HostModel.initialize(cfg, workload.topology)
+    batches = workload_batches(workload, workload.workers, 1 + args.big_batches)
+    with GpuBackend(model, device=device, max_lanes=workload.workers) as big:
+        big.training_story_batch(batches[0], TRAINING)
+        big.reset_perf_stats()
+        wall, nbytes, batch_ms = 0.0, 0, []
+        for b in range(1, 1 + args.big_batches):
+            before = big.perf_stats().batch_ms
+            t0 = time.perf_counter()
+            big.training_story_batch(batches[b], TRAINING)
+            wall += time.perf_counter() - t0
+            batch_ms.append(round(big.perf_stats().batch_ms - before, 1))
+            nbytes += sum(len(x) for x in batches[b])
+        perf = big.perf_stats()
+        device_gb = round(big.device_bytes() / 1e9, 3)
+    device_s = perf.batch_ms / 1000.0
+    return {"config": workload_config(workload, 1), "value": round(nbytes / device_s, 3), "unit": UNIT,
+            "e2e_value": round(nbytes / wall, 3), "timed_batches": args.big_batches, "warmup_batches": 1,
+            "ms_per_step": round(device_s * 1000 / args.big_batches, 1), "batch_ms": batch_ms,
+            "story_pass_ms_per_step": round(perf.story_wavefront_ms / args.big_batches, 1),
+            "replay_ms_per_step": round(perf.replay_ms / args.big_batches, 1),
+            "replay_steps_per_batch": round(perf.replay_work_steps / args.big_batches, 1),
+            "replay_us_per_step_by_phase": replay_step_us(perf),
+            "roofline": roofline_of(perf, cfg, workload.name), "device_gb": device_gb,
+            "note": "not the headline: the driver's 25-batch run of this configuration would exceed its time limit"}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -340,11 +443,14 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", default="baseline2")
-    ap.add_argument("--cpu-stories", type=int, default=16)
-    ap.add_argument("--cpu-bytes", type=int, default=0, help="fixed CPU sample story length (0: workload's range)")
+    ap.add_argument("--cpu-stories", type=int, default=16,
+                    help="stories of the CPU samples (state-matched cpu_baseline, reference arm steps)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-replay-off", action="store_true",
                     help="skip the replay-off figure (same model, replay fraction 0) that follows the timed batches")
+    ap.add_argument("--big-workload", default="baseline3")
+    ap.add_argument("--big-batches", type=int, default=3,
+                    help="timed batches of the 262,144-unit configuration reported as `config3` (0: skip)")
     ap.add_argument("--micro", choices=["sparse-apply"], default=None,
                     help="run a microbenchmark instead of the training step (config 5)")
     ap.add_argument("--densities", default="0.001,0.01,0.1")
@@ -362,12 +468,9 @@ def main() -> None:
         run_reference(args, workload)
         return
 
-    import numpy as np
-
     from leo_b200.backend import GpuBackend
-    from leo_b200.ctypes_types import PHASES, TRAINING
+    from leo_b200.ctypes_types import TRAINING
     from leo_b200.model import HostModel
-    from leo_b200.synthetic import story_stream
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -396,9 +499,7 @@ def main() -> None:
     per_batch = workload.workers * world
     backend = GpuBackend(model, device=local, max_lanes=2 * workload.workers)
     total_batches = args.warmup + args.steps
-    stories = story_stream(workload.story_seed, per_batch * total_batches, workload.min_story_bytes,
-                           workload.max_story_bytes)
-    batches = [stories[i * per_batch:(i + 1) * per_batch] for i in range(total_batches)]
+    batches = workload_batches(workload, per_batch, total_batches)
 
     def run_batch(batch):
         if ex is None:
@@ -407,6 +508,11 @@ def main() -> None:
 
     for b in range(args.warmup):
         run_batch(batches[b])
+    # The state the first timed batch starts from, for the state-matched CPU baseline.
+    snapshot = None
+    if rank == 0 and not args.no_cpu_baseline:
+        trained = backend.synchronize_model().copy()
+        snapshot = (trained, backend.canonical_tick)
     backend.reset_perf_stats()
 
     if dist is not None:
@@ -434,66 +540,53 @@ def main() -> None:
     replay_off = None
     if world == 1 and cfg.replay_fraction > 0 and not args.no_replay_off:
         replay_off = measure_replay_off(backend, workload, args, local)
-    times = np.array([device_s, wall, float(nbytes)], dtype=np.float64)
+    backend.close()
+    times = np.array([device_s, wall], dtype=np.float64)
     if dist is not None:
         import torch
 
-        t = torch.tensor(times[:2], dtype=torch.float64, device=f"cuda:{local}")
+        t = torch.tensor(times, dtype=torch.float64, device=f"cuda:{local}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         device_s, wall = float(t[0]), float(t[1])
     total_bytes = float(nbytes)  # every rank passes the whole logical batch
 
     if rank == 0:
-        peak, peak_kind = measured_peaks()
-        alg = phase_algorithmic_bytes(perf, cfg)
-        launches = max(perf.wavefront_launches, 1)
-        per_launch_ms = perf.wavefront_ms / launches
-        per_launch_bytes = sum(alg.values()) / launches
-        achieved = per_launch_bytes / (per_launch_ms / 1000.0) / 1e9 if per_launch_ms > 0 else 0.0
-        cycles = np.array(list(perf.phase_cycles)[:10], dtype=np.float64)
-        shares = {PHASES[i]: round(float(cycles[i] / max(cycles.sum(), 1.0)), 4) for i in range(10)}
-        story_launches = max(perf.story_wavefront_launches, 1)
-        traffic, traffic_source = dram_traffic(workload.name, per_launch_bytes)
-        roofline = {"bound": "hbm", "kernel": "leo_wavefront_kernel", "achieved": round(achieved, 3),
-                    "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 6), "peak_source": peak_kind,
-                    "traffic": traffic, "traffic_source": traffic_source,
-                    "algorithmic_bytes_per_launch": round(per_launch_bytes, 1),
-                    "frac_of_nominal_8tbs": round(achieved / 8000.0, 6),
-                    "launch_ms": round(per_launch_ms, 4), "launches": int(perf.wavefront_launches),
-                    "share_of_step_time": round(perf.wavefront_ms / max(perf.batch_ms, 1e-9), 4),
-                    "story_pass_launch_ms": round(perf.story_wavefront_ms / story_launches, 3),
-                    "phase_cycle_shares": shares,
-                    "clusters": {"story": perf.story_cluster, "replay": perf.replay_cluster}}
         line = {
             "metric": METRIC, "value": round(total_bytes / device_s, 3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(device_s * 1000 / args.steps, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded order-2 Markov printable-ASCII stories), random-init model",
-            "config": {"workload": workload.name, "neurons": cfg.neuron_count,
-                       "synapses_per_neuron": cfg.synapses_per_neuron, "workers": workload.workers,
-                       "story_bytes": [workload.min_story_bytes, workload.max_story_bytes],
-                       "replay_fraction": cfg.replay_fraction,
-                       "parallelism": f"dp{world}: one logical batch of {per_batch} stories sharded over {world} GPU(s)"
-                                      f" ({workload.workers} lanes each), exact merge over NCCL, serial replay",
-                       "global_batch": per_batch,
-                       "l2": "per-batch working set (lanes x ~0.4 GB) exceeds L2"},
+            "config": workload_config(workload, world),
             "e2e": {"value": round(total_bytes / wall, 3), "unit": UNIT, "h2d_bytes_per_step": h2d // args.steps,
                     "d2h_bytes_per_step": d2h // args.steps},
-            "roofline": roofline, "clocks": clk, "gpu_launches": int(perf.launches),
+            "roofline": roofline_of(perf, cfg, workload.name), "clocks": clk, "gpu_launches": int(perf.launches),
             "steps_per_second": round(story_steps / device_s, 1),
             "execution_steps_per_second": round((story_steps + replay_steps) / device_s, 1),
             "replay_off": replay_off,
             "batch_end_ms_per_step": {k: round(getattr(perf, k) / args.steps, 2)
                                       for k in ("collect_ms", "merge_fixed_ms", "merge_context_ms", "replay_ms",
                                                 "replay_sync_ms")},
+            "replay_us_per_step_by_phase": replay_step_us(perf),
             "device_gb": device_gb,
         }
-        if not args.no_cpu_baseline:
-            res = cpu_sample(workload, min(args.cpu_stories, os.cpu_count() or 1), args.cpu_stories,
-                             args.cpu_bytes, 1)
-            line["cpu_baseline"] = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        if snapshot is not None:
+            from oracle.oracle_py import OracleModel, OracleRuntime
+
+            trained, tick = snapshot
+            gen, rev, stats = trained.generation, trained.parameter_revision, trained.statistics
+            n = min(args.cpu_stories, per_batch)
+            threads = min(n, os.cpu_count() or 1)
+            runtime = OracleRuntime(OracleModel.from_arrays(cfg, trained.arrays, gen, rev, stats))
+            runtime.tick = tick
+            seconds, sample_bytes = oracle_batch(cfg, runtime, batches[args.warmup][:n], threads)
+            line["cpu_baseline"] = {
+                "value": sample_bytes / seconds, "unit": UNIT, "cores": threads, "kind": "port",
+                "sample": f"the first {n} stories ({sample_bytes} bytes) of the first timed batch, started from the "
+                          f"GPU model's state at that batch (same weights, statistics and tick), one thread per "
+                          f"story, merge and replay included; {seconds:.1f} s of CPU work"}
+        if world == 1 and args.big_batches > 0:
+            line["config3"] = measure_big(args, local)
         print(json.dumps(line), flush=True)
-    backend.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

@@ -256,6 +256,8 @@ typedef struct LeoB200PerfStats {
     uint64_t replay_work_active;
     uint64_t replay_work_deliver;
     uint64_t replay_work_eligible;
+    uint64_t work_inhibit;  /* inhibitory-source slots visited by inhibitory homeostasis */
+    uint64_t work_winners;  /* block winners (selection records) assembled */
 } LeoB200PerfStats;
 
 #ifdef __cplusplus

@@ -140,6 +140,8 @@ struct LaneScalars {
     unsigned long long numerical_rejections, persistent_ticks, revision_increment, context_applied_steps;
     uint32_t error_flag;
     // work counters (units per phase, summed over steps; see LeoB200PerfStats)
+    unsigned long long work_inhibit;   // inhibitory-source slots visited by inhibitory homeostasis
+    unsigned long long work_winners;   // block winners (selection records) assembled
     unsigned long long work_deliver, work_touched, work_eligible, work_destinations, work_active, work_plastic,
         work_steps;
     unsigned long long phase_cycles[LEO_PHASES];  // SM clock cycles per phase (first CTA, first thread)

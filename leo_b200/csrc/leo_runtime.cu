@@ -707,6 +707,8 @@ void add_work(LeoB200Device& dev, const LaneScalars& sc, bool story) {
         dev.perf.replay_work_deliver += sc.work_deliver;
         dev.perf.replay_work_eligible += sc.work_eligible;
     }
+    dev.perf.work_inhibit += sc.work_inhibit;
+    dev.perf.work_winners += sc.work_winners;
 }
 
 void read_scalars(LeoB200Device& dev, Lane& lane, LaneScalars& out) {

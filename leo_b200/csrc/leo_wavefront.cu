@@ -58,6 +58,7 @@ namespace cg = cooperative_groups;
 
 
 
+
 // Most event keys one target's segment holds, all sorted in shared memory by
 // one CTA (128 KB; the host rejects larger segment capacities).
 constexpr uint32_t kHubSortShared = 32768;
@@ -209,6 +210,7 @@ struct TouchBuffer {
 __device__ __forceinline__ void touch_buffered(const LaneState& ln, uint32_t n, uint32_t epoch, TouchBuffer& tb) {
     if (*(volatile uint32_t*)&ln.touch_epoch[n] == epoch) return;
     if (atomicExch(&ln.touch_epoch[n], epoch) == epoch) return;
+
     const uint32_t pos = atomicAdd(&tb.count, 1u);
     if (pos < kTouchBuffer)
         tb.items[pos] = n;
@@ -229,8 +231,7 @@ __device__ __forceinline__ void flush_touches(const LaneState& ln, TouchBuffer& 
 // An event: its value is stored by event order, and its key (branch << 30 |
 // event order) appended to the target's segment, one atomic per group of
 // converged threads with the same target; settle restores the order by
-// sorting the keys.  The first event a target receives in the step also
-// touches it.  A segment holds every event the target can receive in one step
+// sorting the keys.  Every event group also touches its target.  A segment holds every event the target can receive in one step
 // (the bound is computed from the topology); an overrun is reported.
 constexpr uint32_t kEventOrderMask = 0x3fffffffu;
 __device__ __forceinline__ void push_event(const LaneState& ln, const KernelConsts& kc, uint32_t n, uint32_t key,
@@ -239,9 +240,13 @@ __device__ __forceinline__ void push_event(const LaneState& ln, const KernelCons
     cg::coalesced_group g = cg::coalesced_threads();
     cg::coalesced_group peers = cg::labeled_partition(g, n);
     uint32_t base = 0;
-    if (peers.thread_rank() == 0) base = atomicAdd(&ln.seg_count[n], peers.size());
+    if (peers.thread_rank() == 0) {
+        base = atomicAdd(&ln.seg_count[n], peers.size());
+        // One touch per group, issued while the count is in flight (its plain
+        // read skips the atomic for a target touched before).
+        touch_buffered(ln, n, epoch, tb);
+    }
     base = peers.shfl(base, 0);
-    if (base == 0u && peers.thread_rank() == 0) touch_buffered(ln, n, epoch, tb);
     const uint32_t pos = base + peers.thread_rank();
     ln.ev_val[key & kEventOrderMask] = value;
     if (pos < (seg.y & LEO_SEG_CAPACITY))
@@ -391,15 +396,14 @@ __device__ void context_resolve_warp(const LaneState& ln, uint32_t s, const Kern
 // deliver (runtime.rs:537-639).  Event order within a lane is the CPU's:
 // previous actives, then due events from emission ticks s-8, s-4, s-2, s-1
 // (rank, then slot), then the symbol's input slots; the event index q (the
-// position among all scanned slots, then the input slots) encodes it.  A due
-// source is one warp's task: each lane loads its slots' topology words and
-// emitted values in one round, and the slots whose delay matches deliver.
+// position among all scanned slots, then the input slots) encodes it.  The
+// scanned slots are spread over all threads; the slots whose delay matches
+// deliver.
 //
 // `fresh_d1`: the previous step was frozen and its emit phase runs beside this
 // deliver, so its ring values are not written yet; a delay-1 event's value is
 // formed here from the same operands (activation x weight; no learning step
 // separates emission and delivery, so the weight is the one emit reads).
-constexpr uint32_t kDeliverUnroll = 4;  // slots per lane per round (S <= 128 in one round)
 
 __device__ __forceinline__ void deliver_trace(const LaneState& ln, const KernelConsts& kc, Trace* traces, uint2* const* lists,
                                               uint32_t* counts, uint32_t cur, uint32_t slot, uint32_t s, float a) {
@@ -441,45 +445,29 @@ __device__ uint32_t phase_deliver(const LaneState& ln, uint32_t s, const KernelC
     // previous actives are touched (start_tick, runtime.rs:537-561)
     for (uint32_t i = worker; i < prev; i += workers)
         touch_buffered(ln, ln.ring_src[((s - 1) % LEO_RING) * maxa + i], epoch, tb);
-    // due recurrent events, one warp per due source
-    const uint32_t tasks = a8 + a4 + a2 + prev;
-    for (uint32_t t = gwarp; t < tasks; t += gwarps) {
-        uint32_t d, r, qbase;
-        if (t < a8) {
-            d = 8; r = t; qbase = 0;
-        } else if (t < a8 + a4) {
-            d = 4; r = t - a8; qbase = e8;
-        } else if (t < a8 + a4 + a2) {
-            d = 2; r = t - a8 - a4; qbase = e8 + e4;
+    // due recurrent events (ring entry of their delay class, rank, slot)
+    for (uint32_t q = worker; q < events; q += workers) {
+        uint32_t d, off;
+        if (q < e8) {
+            d = 8; off = q;
+        } else if (q < e8 + e4) {
+            d = 4; off = q - e8;
+        } else if (q < e8 + e4 + e2) {
+            d = 2; off = q - e8 - e4;
         } else {
-            d = 1; r = t - a8 - a4 - a2; qbase = e8 + e4 + e2;
+            d = 1; off = q - e8 - e4 - e2;
         }
         const uint32_t entry = (s - d) % LEO_RING;
+        const uint32_t r = off / S, j = off - r * S;
         const uint32_t src = ln.ring_src[entry * maxa + r];
+        const uint32_t slot = src * S + j;
+        const uint32_t word = kc.topo.rec_word[slot];
+        if (LEO_WORD_DELAY(word) != d) continue;
+        const uint32_t n = word & LEO_TARGET_MASK, b = LEO_WORD_BRANCH(word);
         const float a = ln.ring_act[entry * maxa + r];
-        const bool fresh = fresh_d1 && d == 1u;
-        const float* vals = fresh ? ln.p.rec_weight + (size_t)src * S : ln.ring_val + ((size_t)entry * maxa + r) * S;
-        const uint32_t* words = kc.topo.rec_word + (size_t)src * S;
-        for (uint32_t j0 = 0; j0 < S; j0 += 32u * kDeliverUnroll) {
-            uint32_t w[kDeliverUnroll];
-            float v[kDeliverUnroll];
-#pragma unroll
-            for (uint32_t u = 0; u < kDeliverUnroll; ++u) {
-                const uint32_t j = j0 + 32u * u + lane;
-                w[u] = j < S ? words[j] : 0u;
-                v[u] = j < S ? vals[j] : 0.0f;
-            }
-#pragma unroll
-            for (uint32_t u = 0; u < kDeliverUnroll; ++u) {
-                const uint32_t j = j0 + 32u * u + lane;
-                if (j < S && LEO_WORD_DELAY(w[u]) == d) {
-                    const uint32_t n = w[u] & LEO_TARGET_MASK, b = LEO_WORD_BRANCH(w[u]);
-                    const float value = fresh ? a * v[u] : v[u];
-                    push_event(ln, kc, n, (b << 30) | (qbase + r * S + j), value, epoch, tb);
-                    if (learn) deliver_trace(ln, kc, ln.traces, ln.elig, sc->elig_count, cur, src * S + j, s, a);
-                }
-            }
-        }
+        const float value = (fresh_d1 && d == 1) ? a * ln.p.rec_weight[slot] : ln.ring_val[((size_t)entry * maxa + r) * S + j];
+        push_event(ln, kc, n, (b << 30) | q, value, epoch, tb);
+        if (learn) deliver_trace(ln, kc, ln.traces, ln.elig, sc->elig_count, cur, slot, s, a);
     }
     // the symbol's input slots (inject_symbol, runtime.rs:627-639)
     for (uint32_t f = worker; f < F; f += workers) {
@@ -822,9 +810,10 @@ __device__ __forceinline__ void cta_radix_values(const LaneState& ln, uint32_t* 
 // sorted (registers up to 4096, shared memory above), each key's event
 // value gathered, and each branch summed in ascending event order onto the
 // decayed branch value by one thread per branch; then integration.  Resets
-// the target's count.
+// the target's count unless `keep_count` (the blocks phase resets it then).
 __device__ void settle_target_cta(const LaneState& ln, uint32_t s, const KernelConsts& kc, uint32_t n, uint32_t k,
-                                  uint32_t offset, uint32_t* smem, float pop_inh, uint32_t rotation) {
+                                  uint32_t offset, uint32_t* smem, float pop_inh, uint32_t rotation,
+                                  bool keep_count = false) {
     __shared__ float s_acc[4];
     __shared__ uint32_t s_cnt[4];
     __shared__ uint32_t s_bound[5];
@@ -883,7 +872,7 @@ __device__ void settle_target_cta(const LaneState& ln, uint32_t s, const KernelC
     if (tid == 0) {
         settle_integrate(ln, kc, n, s, s_cold, make_float4(s_acc[0], s_acc[1], s_acc[2], s_acc[3]), pop_inh, rotation,
                          s_pre);
-        ln.seg_count[n] = 0u;
+        if (!keep_count) ln.seg_count[n] = 0u;
     }
     __syncthreads();
 }
@@ -1022,8 +1011,40 @@ __device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts
     if (tid == 0) s_nqueue = 0u;
     const unsigned long long t0 = clock64();
     const uint32_t listed = kc.topo.cta_count;
-    // Listed targets, one chunk of this CTA's share at a time: classified by
-    // the step's event count into CTA / warp / thread work.
+    // The first kThreads listed targets (the largest capacities, where the
+    // busy ones are): every CTA reads their counts, numbers the ones with
+    // more than cta_events events in list order, and sorts those whose number
+    // is its rank modulo C -- one CTA sort per CTA while at most C are busy,
+    // whichever targets they are this step.  Their counts stay until the
+    // blocks phase, since every CTA classifies them by their counts here.
+    const uint32_t top = listed < kThreads ? listed : kThreads;
+    if (top > 0u) {
+        __shared__ uint32_t s_warp_busy[kWarps];
+        uint32_t n = 0, k = 0;
+        if (tid < top) {
+            n = kc.topo.cta_targets[tid];
+            k = ln.seg_count[n];
+        }
+        const bool busy = tid < top && k > kc.topo.cta_events;
+        const unsigned int ballot = __ballot_sync(0xffffffffu, busy);
+        if (lane == 0) s_warp_busy[warp] = (uint32_t)__popc(ballot);
+        if (tid == 0) s_nlist[0] = 0u;
+        __syncthreads();
+        uint32_t before = (uint32_t)__popc(ballot & ((1u << lane) - 1u));
+        for (uint32_t w = 0; w < warp; ++w) before += s_warp_busy[w];
+        if (busy && before % C == rank) {
+            const uint32_t pos = atomicAdd(&s_nlist[0], 1u);
+            s_list[0][pos] = n;
+            s_list_k[0][pos] = k;
+        }
+        __syncthreads();
+        const uint32_t nbig = s_nlist[0];
+        for (uint32_t j = 0; j < nbig; ++j)
+            settle_target_cta(ln, s, kc, s_list[0][j], s_list_k[0][j], kc.topo.seg[s_list[0][j]].x, smem, pop_inh,
+                              rotation, true);
+    }
+    // Every listed target not sorted above, one chunk of this CTA's share at a
+    // time: classified by the step's event count into CTA / warp / thread work.
     for (uint32_t round0 = 0; round0 * C < listed; round0 += kListedChunk) {
         if (tid < 3) s_nlist[tid] = 0u;
         __syncthreads();
@@ -1036,7 +1057,7 @@ __device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts
             const uint32_t n = kc.topo.cta_targets[i];
             const uint32_t k = ln.seg_count[n];
             const int tier = k > kc.topo.cta_events ? 0 : (k > kc.topo.thread_events ? 1 : 2);
-            if (tier < 2 || k > 0u || ln.touch_epoch[n] == epoch) {
+            if ((tier > 0 || i >= top) && (tier < 2 || k > 0u || ln.touch_epoch[n] == epoch)) {
                 const uint32_t pos = atomicAdd(&s_nlist[tier], 1u);
                 s_list[tier][pos] = n;
                 s_list_k[tier][pos] = k;
@@ -1113,18 +1134,21 @@ __device__ void phase_blocks(const LaneState& ln, const KernelConsts& kc, uint32
     for (uint32_t b = gwarp; b < B; b += gwarps) {
         uint32_t count = ln.block_cand_count[b];
         const unsigned long long* cand = ln.block_cand + (size_t)b * npb;
+        // The first 256 candidates in registers (static indices; a key of a
+        // candidate is never 0), the rest re-read from global memory per round.
         constexpr uint32_t kLocal = 8;
         unsigned long long mine[kLocal];
-        uint32_t held = 0;
-        for (uint32_t idx = lane; idx < count && held < kLocal; idx += 32) mine[held++] = cand[idx];
+#pragma unroll
+        for (uint32_t x = 0; x < kLocal; ++x) mine[x] = lane + 32u * x < count ? cand[lane + 32u * x] : 0ull;
         bool spill = count > 32 * kLocal;
         unsigned long long prev = ~0ull;
         uint32_t rounds = count < keep + 1 ? count : keep + 1;
         float cutoff = 0.0f;
         for (uint32_t k = 0; k < rounds; ++k) {
             unsigned long long best = 0ull;
-            for (uint32_t h = 0; h < held; ++h)
-                if (mine[h] < prev && mine[h] > best) best = mine[h];
+#pragma unroll
+            for (uint32_t x = 0; x < kLocal; ++x)
+                if (mine[x] < prev && mine[x] > best) best = mine[x];
             if (spill)
                 for (uint32_t idx = lane + 32 * kLocal; idx < count; idx += 32) {
                     unsigned long long key = cand[idx];
@@ -1764,10 +1788,12 @@ __device__ void phase_inhibit(const LaneState& ln, uint32_t s, const KernelConst
     float strength = sc->step_strength;
     uint32_t entry = s % LEO_RING;
     uint32_t total = sc->ring_count[entry] * S;
+    uint32_t visited = 0;
     for (uint32_t i = worker; i < total; i += workers) {
         uint32_t r = i / S, j = i - r * S;
         uint32_t src = ln.ring_src[entry * maxa + r];
         if (kc.topo.neuron_type[src] == 0) continue;
+        ++visited;
         float sa = ln.ring_act[entry * maxa + r];
         uint32_t slot = src * S + j;
         uint32_t target = kc.topo.rec_word[slot] & LEO_TARGET_MASK;
@@ -1780,12 +1806,15 @@ __device__ void phase_inhibit(const LaneState& ln, uint32_t s, const KernelConst
         if (nw != old_w && kc.track_changes) mark_and_append(ln.rec_mark, ln.rec_list, &sc->rec_changed, slot);
         ln.p.rec_weight[slot] = nw;
     }
+    // Work counter: one add per warp per step.
+    visited = __reduce_add_sync(0xffffffffu, visited);
+    if ((threadIdx.x & 31u) == 0u && visited) atomicAdd(&sc->work_inhibit, (unsigned long long)visited);
 }
 
 // Work counters of one launch, held by the launch's first thread and added to
 // the lane's scalars when the launch ends.
 struct WorkTally {
-    unsigned long long deliver, touched, active, steps, eligible, destinations;
+    unsigned long long deliver, touched, active, steps, eligible, destinations, winners;
 };
 
 // Step epilogue (one thread): work counters, per-tick counter reset, and the
@@ -1801,6 +1830,7 @@ __device__ void step_epilogue(const LaneState& ln, uint32_t s, bool frozen, Work
     const uint32_t e0 = sc->elig_count[0] + sc->in_elig_count[0], e1 = sc->elig_count[1] + sc->in_elig_count[1];
     tally.touched += touched;
     tally.active += active;
+    tally.winners += sc->last_block_selected;
     tally.steps += 1;
     if (!frozen) tally.eligible += cur ? e1 : e0;
     if ((flags & 3u) == 3u) tally.destinations += dsts;
@@ -1824,6 +1854,7 @@ __device__ void flush_tally(const LaneState& ln, const WorkTally& tally) {
     sc->work_steps += tally.steps;
     sc->work_eligible += tally.eligible;
     sc->work_destinations += tally.destinations;
+    sc->work_winners += tally.winners;
 }
 
 __device__ __forceinline__ unsigned long long clock_now() { return clock64(); }
@@ -1869,7 +1900,7 @@ __device__ __forceinline__ void wavefront_steps(const LaneState* __restrict__ la
     };
     if (timer) {
         for (int p = 0; p < LEO_PHASES; ++p) acc[p] = 0;
-        tally = WorkTally{0, 0, 0, 0, 0, 0};
+        tally = WorkTally{0, 0, 0, 0, 0, 0, 0};
         t0 = clock_now();
     }
     // `joined`: the previous step was frozen without a forward pass and its
@@ -1891,6 +1922,11 @@ __device__ __forceinline__ void wavefront_steps(const LaneState* __restrict__ la
         phase_settle(ln, s, kc, worker, workers, rank, C, reinterpret_cast<uint32_t*>(smem_sorted));
         sync();
         mark(1);
+        {
+            // counts the settle phase kept for its busy listed targets
+            const uint32_t top = kc.topo.cta_count < kThreads ? kc.topo.cta_count : kThreads;
+            for (uint32_t i = worker; i < top; i += workers) ln.seg_count[kc.topo.cta_targets[i]] = 0u;
+        }
         phase_blocks(ln, kc, gwarp, gwarps, win_write, nwin_write);
         if (frozen && worker == 0) release_touched(ln, tally);
         sync();

@@ -192,4 +192,6 @@ class LeoB200PerfStats(C.Structure):
         ("replay_work_active", C.c_uint64),
         ("replay_work_deliver", C.c_uint64),
         ("replay_work_eligible", C.c_uint64),
+        ("work_inhibit", C.c_uint64),
+        ("work_winners", C.c_uint64),
     ]

@@ -22,8 +22,7 @@ def _line(args):
 
 
 def test_reference_arm_prints_the_contract_line(oracle_lib):
-    d = _line(["--impl", "reference", "--workload", "test", "--steps", "1", "--warmup", "1", "--cpu-stories", "2",
-               "--cpu-bytes", "24"])
+    d = _line(["--impl", "reference", "--workload", "test", "--steps", "1", "--warmup", "1", "--cpu-stories", "2"])
     assert BASE_KEYS <= set(d)
     assert d["impl"] == "reference"
     assert d["value"] > 0 and d["higher_is_better"] is True
@@ -31,11 +30,13 @@ def test_reference_arm_prints_the_contract_line(oracle_lib):
     assert d["cpu_baseline"]["kind"] == "port"
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     assert "workload" in d["config"]
+    assert "oracle" not in d["config"]["workload"]
 
 
 @pytest.mark.gpu
 def test_gpu_arm_prints_the_contract_line(native_lib, oracle_lib):
-    d = _line(["--workload", "test", "--steps", "1", "--warmup", "3", "--cpu-stories", "2", "--cpu-bytes", "24"])
+    d = _line(["--workload", "test", "--steps", "1", "--warmup", "3", "--cpu-stories", "2", "--big-workload", "test",
+               "--big-batches", "1"])
     assert BASE_KEYS <= set(d)
     assert d["n_gpus"] == 1 and d["value"] > 0
     r = d["roofline"]
@@ -49,3 +50,6 @@ def test_gpu_arm_prints_the_contract_line(native_lib, oracle_lib):
     assert set(d["cpu_baseline"]) >= {"value", "unit", "cores", "kind", "sample"}
     assert d["replay_off"]["value"] > 0 and d["replay_off"]["unit"] == d["unit"]
     assert d["execution_steps_per_second"] >= d["steps_per_second"] > 0
+    big = d["config3"]
+    assert big["value"] > 0 and big["unit"] == d["unit"] and big["timed_batches"] == 1
+    assert big["roofline"]["frac"] > 0
