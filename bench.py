@@ -10,7 +10,7 @@ metric is input story bytes per second (``input_bytes`` of the reference's
 * ``value``: story bytes of the K timed batches (all ranks) / the max over
   ranks of the batch time measured with CUDA events on the backend's stream.
 * ``e2e``: the same bytes / the max over ranks of the wall time of the public
-  call ``training_story_batch`` with host buffers (story bytes in, per-target
+  call ``train_story_batch`` with host buffers (story bytes in, per-target
   losses and summaries out).
 * ``roofline``: the wavefront kernel's algorithmic bytes per launch (per-unit
   figures below, units counted on the device) over its CUDA-event launch time,
@@ -353,12 +353,12 @@ def measure_replay_off(backend, workload, args, device: int) -> dict:
     stories = story_stream(workload.story_seed + 1, n * (args.steps + 1), workload.min_story_bytes,
                            workload.max_story_bytes)
     with GpuBackend(model, device=device, max_lanes=2 * n) as off:
-        off.training_story_batch(stories[:n], TRAINING)
+        off.train_story_batch(stories[:n], TRAINING)
         off.reset_perf_stats()
         nbytes = 0
         for b in range(1, args.steps + 1):
             batch = stories[b * n:(b + 1) * n]
-            off.training_story_batch(batch, TRAINING)
+            off.train_story_batch(batch, TRAINING)
             nbytes += sum(len(s) for s in batch)
         ms = off.perf_stats().batch_ms
     return {"value": round(nbytes / (ms / 1000.0), 3), "unit": UNIT, "ms_per_step": round(ms / args.steps, 3),
@@ -412,13 +412,13 @@ def measure_big(args, device: int) -> dict:
     model = HostModel.initialize(cfg, workload.topology)
     batches = workload_batches(workload, workload.workers, 1 + args.big_batches)
     with GpuBackend(model, device=device, max_lanes=workload.workers) as big:
-        big.training_story_batch(batches[0], TRAINING)
+        big.train_story_batch(batches[0], TRAINING)
         big.reset_perf_stats()
         wall, nbytes, batch_ms = 0.0, 0, []
         for b in range(1, 1 + args.big_batches):
             before = big.perf_stats().batch_ms
             t0 = time.perf_counter()
-            big.training_story_batch(batches[b], TRAINING)
+            big.train_story_batch(batches[b], TRAINING)
             wall += time.perf_counter() - t0
             batch_ms.append(round(big.perf_stats().batch_ms - before, 1))
             nbytes += sum(len(x) for x in batches[b])
@@ -503,7 +503,7 @@ def main() -> None:
 
     def run_batch(batch):
         if ex is None:
-            return backend.training_story_batch(batch, TRAINING)
+            return backend.train_story_batch(batch, TRAINING)
         return sharded_story_batch(backend, ex, batch, TRAINING)
 
     for b in range(args.warmup):

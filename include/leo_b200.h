@@ -119,6 +119,84 @@ int leo_b200_shard_finish(LeoB200Device* device, const LeoB200ShardStory* storie
                           const uint8_t* context, const uint64_t* context_offsets, uint64_t fixed_updates,
                           LeoB200BatchReport* report, LeoB200StorySummary* summaries, float* losses_out);
 
+/* ---- RuntimeBackend, trait-shaped (crates/leo-core/src/backend.rs:351-475) ----
+   The entry points below let a caller drive the reference trainer's own loop
+   (crates/leo-cli/src/training.rs:1584-1660, 1833-1945) step by step: a
+   device story batch without replay, then the serial replay through the
+   canonical runtime's document calls with parameter tracking, then the
+   packed sparse sync.  Driven that way they reproduce the fused
+   leo_b200_train_story_batch bit for bit. */
+
+/* RuntimeBackend::training_story_batch (backend.rs:457-463, GpuRuntime
+   backend.rs:739-764): every story on its own lane, the device-local mean
+   merge into the canonical model and every lane; no replay.  Returns
+   LEO_B200_UNSUPPORTED for fewer than two stories (backend.rs:587-589).
+   `summaries` and `losses` as for leo_b200_train_story_batch; `range_counts`
+   (optional, one per story) and `ranges` (optional, 2 x total ranges: start,
+   end) receive each story's replay ranges (DeviceStoryBatchReport::
+   replay_ranges, select_replay_ranges training.rs:1782-1830). */
+int leo_b200_training_story_batch(LeoB200Device* device, const uint8_t* bytes, const uint64_t* offsets,
+                                  uint32_t stories, int permission, LeoB200BatchReport* report,
+                                  LeoB200StorySummary* summaries, float* losses, uint64_t* ranges,
+                                  uint32_t* range_counts);
+
+/* RuntimeBackend::training_story_batch_deltas (backend.rs:468-474,
+   backend.rs:766-795): every story on its own lane (one story too); each
+   story's private delta against the canonical model is kept for
+   leo_b200_story_deltas (SparseModelDelta, from_tracked_values
+   parallel.rs:461-674: changed indices with a nonzero difference, sorted; the
+   output weights indexed output * neuron_count + neuron) and the lanes return
+   to the canonical model, which this call does not change.  `sizes` receives
+   the entry counts the caller allocates for. */
+int leo_b200_training_story_batch_deltas(LeoB200Device* device, const uint8_t* bytes, const uint64_t* offsets,
+                                         uint32_t stories, int permission, LeoB200BatchReport* report,
+                                         LeoB200StorySummary* summaries, float* losses, uint64_t* ranges,
+                                         uint32_t* range_counts, LeoB200StoryDeltaSizes* sizes);
+/* The deltas of the last leo_b200_training_story_batch_deltas, into caller
+   buffers sized from its LeoB200StoryDeltaSizes (NULL members are skipped). */
+int leo_b200_story_deltas(LeoB200Device* device, const LeoB200StoryDeltas* out);
+
+/* The canonical runtime's document (Runtime::begin_document /
+   reset_transient_state, runtime.rs:353-435; backend.rs:391-402): the
+   transient state is reset at the canonical tick; parameters, tracking and
+   statistics are kept.  A story batch ends an open document. */
+int leo_b200_begin_document(LeoB200Device* device);
+int leo_b200_reset_transient_state(LeoB200Device* device);
+
+/* RuntimeBackend::training_step_batch (backend.rs:413-421): `count` serial
+   steps of the open document on the canonical model, step i reading input
+   symbol symbols[i] (0..257) with target targets[i] (0..255 or 257;
+   -1: none) at `permission`, in one device launch.  `losses` (optional)
+   receives each step's loss (0 without a target), `active_neurons`
+   (optional) its active-neuron count.  Advances the canonical tick,
+   statistics and revision as Runtime::step does. */
+int leo_b200_training_step_batch(LeoB200Device* device, const uint32_t* symbols, const int32_t* targets,
+                                 uint32_t count, int permission, float* losses, uint32_t* active_neurons);
+
+/* RuntimeBackend::advance_frozen_batch (backend.rs:428-431): the same steps
+   at Permission::Frozen, metrics discarded. */
+int leo_b200_advance_frozen_batch(LeoB200Device* device, const uint32_t* symbols, const int32_t* targets,
+                                  uint32_t count);
+
+/* Parameter tracking of the canonical runtime (RuntimeBackend::
+   enable_parameter_tracking / parameter_changes, backend.rs:358-359; the
+   CUDA backend's window semantics, cuda.rs:2827-2842): enabling starts an
+   empty window; the window collects every index the canonical runtime's
+   steps change (leo_b200_training_step_batch, leo_b200_advance_frozen_batch)
+   and closes at the next story batch or packed sync, which write those rows
+   into every lane.  leo_b200_parameter_changes stores the sizes and, when
+   `changes` is not NULL, the sorted indices into its caller buffers. */
+int leo_b200_enable_parameter_tracking(LeoB200Device* device);
+int leo_b200_parameter_changes(LeoB200Device* device, LeoB200ParameterChangeSizes* sizes,
+                               const LeoB200ParameterChanges* changes);
+
+/* RuntimeBackend::synchronize_packed_model (backend.rs:374-376;
+   PackedSparseModelUpdate::apply_to_model parallel.rs:196-300, the CUDA
+   backend's device scatter cuda.rs:2869-3080): the packet's values written
+   over the canonical model and every resident lane; generation, revision and
+   statistics replaced.  Indices are validated before anything is written. */
+int leo_b200_synchronize_packed_model(LeoB200Device* device, const LeoB200PackedUpdate* update);
+
 /* training_state_hash of the canonical device model. */
 int leo_b200_state_digest(LeoB200Device* device, uint8_t out[32]);
 

@@ -35,6 +35,11 @@ extern "C" {
 #define LEO_B200_OUTPUT_CLASSES 257u   /* crates/leo-core/src/symbols.rs:7 */
 #define LEO_B200_END_OUTPUT_INDEX 256u /* crates/leo-core/src/symbols.rs:8 */
 
+/* Return value of an optional device path that does not take the given input
+   (the trait's Ok(None), crates/leo-core/src/backend.rs:457-474): the caller
+   runs the step-level path instead.  Errors are -1. */
+#define LEO_B200_UNSUPPORTED 1
+
 /* Permission, crates/leo-core/src/permission.rs:5-11. */
 enum LeoB200Permission {
     LEO_B200_FROZEN = 0,
@@ -190,6 +195,79 @@ typedef struct LeoB200ShardStory {
 
 /* Fixed tensors merged at the batch end, in merge order. */
 #define LEO_B200_FIXED_TENSORS 6
+
+/* Per-story sparse deltas (SparseModelDelta, crates/leo-core/src/parallel.rs:
+   41-55): the fixed tensors in this order -- threshold, recurrent weight,
+   input weight, output weight (reference index output * N + neuron), output
+   bias, context output weight -- each a list of (index, delta) sorted by index
+   with every delta nonzero, then the keyed context deltas sorted by (order,
+   key), the statistics delta and the revision increment of every story. */
+#define LEO_B200_DELTA_TENSORS 6
+
+typedef struct LeoB200StoryDeltaSizes {
+    uint64_t entries[LEO_B200_DELTA_TENSORS]; /* (index, delta) pairs of all stories, per tensor */
+    uint64_t context_entries;                 /* keyed context deltas of all stories */
+    uint32_t embedding_dim;                   /* floats per context embedding delta */
+    uint32_t stories;
+} LeoB200StoryDeltaSizes;
+
+/* Caller-owned buffers for the deltas of `stories` stories; story s owns
+   entries offsets[t][s] .. offsets[t][s + 1] of tensor t and context entries
+   context_offsets[s] .. context_offsets[s + 1]. */
+typedef struct LeoB200StoryDeltas {
+    uint64_t* offsets[LEO_B200_DELTA_TENSORS];  /* stories + 1 each */
+    uint32_t* indices[LEO_B200_DELTA_TENSORS];  /* entries[t] each */
+    float* deltas[LEO_B200_DELTA_TENSORS];      /* entries[t] each */
+    uint64_t* context_offsets;                  /* stories + 1 */
+    uint32_t* context_orders;                   /* context_entries */
+    uint64_t* context_keys;                     /* context_entries */
+    uint32_t* context_observation_increments;   /* context_entries */
+    float* context_embedding_deltas;            /* context_entries x embedding_dim */
+    LeoB200Statistics* statistics;              /* stories: statistics delta (parallel.rs statistics_delta) */
+    uint64_t* revision_increments;              /* stories */
+} LeoB200StoryDeltas;
+
+/* Changed-parameter indices of the canonical runtime since tracking was
+   enabled (ParameterChanges, crates/leo-core/src/runtime.rs:38-46). */
+typedef struct LeoB200ParameterChangeSizes {
+    uint64_t threshold, recurrent_weight, input_weight, output_neurons, context_slots;
+    uint32_t output_bias_dirty, context_output_dirty;
+} LeoB200ParameterChangeSizes;
+
+typedef struct LeoB200ParameterChanges {
+    uint32_t* threshold;         /* sorted indices */
+    uint32_t* recurrent_weight;
+    uint32_t* input_weight;
+    uint32_t* output_neurons;
+    uint32_t* context_slots;
+} LeoB200ParameterChanges;
+
+/* PackedSparseModelUpdate (crates/leo-core/src/parallel.rs:78-97): host values
+   written over the canonical model and every resident lane. */
+typedef struct LeoB200PackedUpdate {
+    const uint32_t* threshold_indices;
+    const float* threshold_values;
+    uint64_t threshold_count;
+    const uint32_t* recurrent_indices;
+    const float* recurrent_values;
+    uint64_t recurrent_count;
+    const uint32_t* input_indices;
+    const float* input_values;
+    uint64_t input_count;
+    const uint32_t* output_neurons;
+    const float* output_values_by_neuron; /* 257 per neuron, output order */
+    uint64_t output_count;
+    const uint32_t* context_slots;
+    const uint64_t* context_keys;
+    const uint32_t* context_observations;
+    const float* context_embeddings; /* embedding_dim per slot */
+    uint64_t context_count;
+    const float* output_bias;            /* 257 values, or NULL: unchanged */
+    const float* context_output_weights; /* 257 x embedding_dim, or NULL */
+    uint64_t generation;
+    uint64_t parameter_revision;
+    LeoB200Statistics statistics;
+} LeoB200PackedUpdate;
 
 /* Phases of one step of the persistent wavefront, in execution order. */
 #define LEO_B200_PHASES 11

@@ -180,6 +180,7 @@ struct LaneState {
     LaneScalars* sc;
     const uint32_t* schedule;   // [steps]
     float* step_loss;           // [steps] loss per step (0 when untargeted)
+    uint32_t* step_active;      // [steps] active neurons per step
     NeuronHot* hot;             // [N]
     NeuronCold* cold;           // [N]
     float4* branches;           // [N] (E, I, T, G)

@@ -74,6 +74,7 @@ struct Lane {
     size_t schedule_capacity = 0;
     uint32_t* schedule = nullptr;
     float* step_loss = nullptr;
+    uint32_t* step_active = nullptr;
 };
 
 struct ContextRow {
@@ -118,6 +119,22 @@ struct LeoB200Device {
     uint8_t** d_lane_marks = nullptr;    // [max_lanes]
     // in-flight batch
     bool batch_open = false;
+    // Trait-level entry points: a single story still runs on a lane (its delta
+    // against the canonical model is exported), the exported story deltas, and
+    // the canonical runtime's open document.
+    bool force_lanes = false;
+    struct StoryDelta {
+        std::vector<uint32_t> index[LEO_B200_DELTA_TENSORS];
+        std::vector<float> delta[LEO_B200_DELTA_TENSORS];
+        std::vector<uint32_t> ctx_order, ctx_obs_inc;
+        std::vector<unsigned long long> ctx_key;
+        std::vector<float> ctx_emb;
+        LeoB200Statistics stats{};
+        uint64_t revision = 0;
+    };
+    std::vector<StoryDelta> story_deltas;
+    bool doc_open = false;
+    uint32_t doc_steps = 0;
     uint32_t batch_lanes = 0;
     uint32_t batch_steps = 0;
     uint32_t steps_done = 0;
@@ -322,9 +339,11 @@ void ensure_schedule(Lane& lane, size_t steps) {
     size_t cap = std::max<size_t>(steps, 4096);
     lane.schedule = lane.mem.alloc<uint32_t>(cap);
     lane.step_loss = lane.mem.alloc<float>(cap);
+    lane.step_active = lane.mem.alloc<uint32_t>(cap);
     lane.schedule_capacity = cap;
     lane.st.schedule = lane.schedule;
     lane.st.step_loss = lane.step_loss;
+    lane.st.step_active = lane.step_active;
 }
 
 void ensure_lanes(LeoB200Device& dev, uint32_t count) {
@@ -1231,6 +1250,24 @@ void sync_replay_changes(LeoB200Device& dev, const LaneScalars& rs) {
             std::copy_n(emb.begin() + (size_t)i * d, d, dev.ctx_emb.begin() + (size_t)slot * d);
         }
     }
+    // Every mark is clear again: the replay lane's lists restart empty.
+    LaneScalars cur;
+    read_scalars(dev, rl, cur);
+    cur.thr_changed = cur.rec_changed = cur.in_changed = cur.out_changed = cur.ctx_changed = 0;
+    cur.bias_dirty = cur.ctx_out_dirty = 0;
+    CUDA_CHECK(cudaMemcpyAsync(rl.st.sc, &cur, sizeof(cur), cudaMemcpyHostToDevice, dev.stream));
+    CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+}
+
+// Canonical rows that steps on the replay lane changed outside a story batch
+// (begin_document / training_step_batch) written into every story lane, so
+// that the next batch starts every lane from the canonical model.
+void refresh_lanes_from_replay(LeoB200Device& dev) {
+    LaneScalars rs;
+    read_scalars(dev, *dev.replay, rs);
+    if (rs.thr_changed | rs.rec_changed | rs.in_changed | rs.out_changed | rs.ctx_changed | rs.bias_dirty |
+        rs.ctx_out_dirty)
+        sync_replay_changes(dev, rs);
 }
 
 // ---------------------------------------------------------------- replay (training.rs:1782-1955)
@@ -1370,16 +1407,194 @@ void build_schedules(LeoB200Device& dev, uint32_t first, uint32_t count, int per
     dev.perf.launches += 1;
 }
 
+// ---------------------------------------------------------------- trait-level exports
+// Lane and canonical values of `count` rows of `row_len` floats (row stride
+// `row`) at list[i].
+__global__ void gather_value_pairs_kernel(const uint32_t* __restrict__ list, uint32_t count, uint32_t row,
+                                          uint32_t row_len, const float* __restrict__ lane,
+                                          const float* __restrict__ canon, float* out_lane, float* out_canon) {
+    const uint64_t total = (uint64_t)count * row_len;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = i / row_len, k = i - r * row_len;
+        const size_t at = (size_t)list[r] * row + k;
+        out_lane[i] = lane[at];
+        out_canon[i] = canon[at];
+    }
+}
+
+// values (count rows of row_len floats) written to base at list[i] * row.
+__global__ void write_rows_kernel(float* base, const uint32_t* __restrict__ list, uint32_t count, uint32_t row,
+                                  uint32_t row_len, const float* __restrict__ values) {
+    const uint64_t total = (uint64_t)count * row_len;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = i / row_len, k = i - r * row_len;
+        base[(size_t)list[r] * row + k] = values[i];
+    }
+}
+
+uint32_t grid_for(uint64_t work) { return (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(work / 256 + 1, 4096)); }
+
+// A temporary device buffer for one trait-level call.
+struct Scratch {
+    void* p = nullptr;
+    explicit Scratch(size_t bytes) { CUDA_CHECK(cudaMalloc(&p, std::max<size_t>(bytes, 16))); }
+    ~Scratch() { if (p) cudaFree(p); }
+    template <typename T> T* as() const { return static_cast<T*>(p); }
+};
+
+// One fixed tensor of a lane: its changed-index list and the row layout.
+struct LaneTensor {
+    const uint32_t* list;
+    uint8_t* marks;
+    uint32_t count;
+    uint32_t row, row_len;
+    float* lane;
+    const float* canon;
+};
+
+// Story deltas of lane `l` (SparseModelDelta::from_tracked_values,
+// parallel.rs:461-674): every changed index with a nonzero lane - canonical
+// difference, in reference indexing, sorted; keyed context deltas; the
+// statistics delta relative to the canonical statistics.
+void export_story_delta(LeoB200Device& dev, uint32_t l, const LaneScalars& sc, double canon_loss,
+                        LeoB200Device::StoryDelta& out) {
+    Lane& lane = *dev.lanes[l];
+    const ModelSizes& z = dev.z;
+    const uint32_t N = (uint32_t)z.n;
+    const LaneTensor fixed[4] = {
+        {lane.st.thr_list, lane.st.thr_mark, sc.thr_changed, 1, 1, lane.st.p.threshold, dev.canon.threshold},
+        {lane.st.rec_list, lane.st.rec_mark, sc.rec_changed, 1, 1, lane.st.p.rec_weight, dev.canon.rec_weight},
+        {lane.st.in_list, lane.st.in_mark, sc.in_changed, 1, 1, lane.st.p.in_weight, dev.canon.in_weight},
+        {lane.st.out_list, lane.st.out_mark, sc.out_changed, LEO_OUTPUT_STRIDE, LEO_OUTPUT_CLASSES,
+         lane.st.p.out_weight, dev.canon.out_weight},
+    };
+    for (int t = 0; t < 4; ++t) {
+        const LaneTensor& lt = fixed[t];
+        if (lt.count == 0) continue;
+        const size_t n = (size_t)lt.count * lt.row_len;
+        Scratch buf(2 * n * sizeof(float));
+        gather_value_pairs_kernel<<<grid_for(n), 256, 0, dev.stream>>>(lt.list, lt.count, lt.row, lt.row_len, lt.lane,
+                                                                      lt.canon, buf.as<float>(), buf.as<float>() + n);
+        CUDA_CHECK(cudaGetLastError());
+        std::vector<uint32_t> list(lt.count);
+        std::vector<float> vals(2 * n);
+        CUDA_CHECK(cudaMemcpyAsync(list.data(), lt.list, lt.count * 4, cudaMemcpyDeviceToHost, dev.stream));
+        CUDA_CHECK(cudaMemcpyAsync(vals.data(), buf.p, 2 * n * sizeof(float), cudaMemcpyDeviceToHost, dev.stream));
+        CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+        std::vector<std::pair<uint32_t, float>> pairs;
+        for (size_t r = 0; r < lt.count; ++r)
+            for (uint32_t k = 0; k < lt.row_len; ++k) {
+                const float d = vals[r * lt.row_len + k] - vals[n + r * lt.row_len + k];
+                if (d != 0.0f) pairs.push_back({lt.row_len == 1 ? list[r] : k * N + list[r], d});
+            }
+        std::sort(pairs.begin(), pairs.end(), [](const auto& a, const auto& b) { return a.first < b.first; });
+        for (const auto& [i, d] : pairs) {
+            out.index[t].push_back(i);
+            out.delta[t].push_back(d);
+        }
+    }
+    // Dense tensors when the lane changed them: output bias, context output weights.
+    const struct {
+        uint32_t dirty;
+        size_t count;
+        const float* lane;
+        const float* canon;
+        int tensor;
+    } dense[2] = {{sc.bias_dirty, LEO_OUTPUT_CLASSES, lane.st.p.out_bias, dev.canon.out_bias, 4},
+                  {sc.ctx_out_dirty, z.ctx_out, lane.st.p.ctx_out, dev.canon.ctx_out, 5}};
+    for (const auto& dt : dense) {
+        if (!dt.dirty) continue;
+        std::vector<float> a(dt.count), b(dt.count);
+        CUDA_CHECK(cudaMemcpyAsync(a.data(), dt.lane, dt.count * 4, cudaMemcpyDeviceToHost, dev.stream));
+        CUDA_CHECK(cudaMemcpyAsync(b.data(), dt.canon, dt.count * 4, cudaMemcpyDeviceToHost, dev.stream));
+        CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+        for (size_t i = 0; i < dt.count; ++i) {
+            const float d = a[i] - b[i];
+            if (d != 0.0f) {
+                out.index[dt.tensor].push_back((uint32_t)i);
+                out.delta[dt.tensor].push_back(d);
+            }
+        }
+    }
+    std::vector<uint32_t> slots;
+    std::vector<CtxDelta> ctx = collect_lane_context(dev, lane, sc.ctx_changed, slots);
+    // canonicalize_order (parallel.rs:676-691): by order, then key.
+    std::sort(ctx.begin(), ctx.end(), [](const CtxDelta& a, const CtxDelta& b) {
+        return a.order != b.order ? a.order < b.order : a.key < b.key;
+    });
+    for (const CtxDelta& cd : ctx) {
+        out.ctx_order.push_back(cd.order);
+        out.ctx_key.push_back(cd.key);
+        out.ctx_obs_inc.push_back(cd.obs_inc);
+        out.ctx_emb.insert(out.ctx_emb.end(), cd.emb_delta.begin(), cd.emb_delta.end());
+    }
+    const auto& story = dev.batch_stories[l];
+    LeoB200Statistics& st = out.stats;
+    st.processed_bytes = sc.processed_bytes;
+    st.processed_stories = (story.empty() || dev.batch_permission == LEO_B200_FROZEN) ? 0 : 1;
+    st.training_loss_sum = sc.loss_sum - canon_loss;
+    st.training_targets = sc.targets;
+    st.active_neurons_sum = sc.active_sum;
+    st.active_neurons_peak = sc.active_peak;
+    st.synaptic_events = sc.synaptic_events;
+    st.numerical_rejections = sc.numerical_rejections;
+    st.persistent_ticks = sc.persistent_ticks;
+    out.revision = sc.revision_increment;
+}
+
+// Lane `l` back to the canonical values at every index it changed, its marks
+// cleared (the canonical model is unchanged by an exported batch).
+void restore_lane(LeoB200Device& dev, uint32_t l, const LaneScalars& sc) {
+    Lane& lane = *dev.lanes[l];
+    const ModelSizes& z = dev.z;
+    struct Item {
+        float* LaneParams::*member;
+        uint32_t* list;
+        uint8_t* marks;
+        uint32_t count, row, row_len;
+    };
+    const Item items[] = {
+        {&LaneParams::threshold, lane.st.thr_list, lane.st.thr_mark, sc.thr_changed, 1, 1},
+        {&LaneParams::rec_weight, lane.st.rec_list, lane.st.rec_mark, sc.rec_changed, 1, 1},
+        {&LaneParams::in_weight, lane.st.in_list, lane.st.in_mark, sc.in_changed, 1, 1},
+        {&LaneParams::out_weight, lane.st.out_list, lane.st.out_mark, sc.out_changed, LEO_OUTPUT_STRIDE, LEO_OUTPUT_CLASSES},
+    };
+    for (const Item& it : items) {
+        if (it.count == 0) continue;
+        float* ptr = lane.st.p.*it.member;
+        CUDA_CHECK(cudaMemcpyAsync(dev.d_lane_ptrs, &ptr, sizeof(float*), cudaMemcpyHostToDevice, dev.stream));
+        leo_launch_scatter_rows(dev.d_lane_ptrs, 1, dev.canon.*it.member, it.list, it.count, it.row, it.row_len,
+                                dev.grid, dev.stream);
+        clear_marks_kernel<<<grid_for(it.count), 256, 0, dev.stream>>>(it.list, it.count, it.marks);
+        CUDA_CHECK(cudaGetLastError());
+        CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+    }
+    if (sc.bias_dirty)
+        CUDA_CHECK(cudaMemcpyAsync(lane.st.p.out_bias, dev.canon.out_bias, LEO_OUTPUT_STRIDE * 4, cudaMemcpyDeviceToDevice,
+                                   dev.stream));
+    if (sc.ctx_out_dirty)
+        CUDA_CHECK(cudaMemcpyAsync(lane.st.p.ctx_out, dev.canon.ctx_out, z.ctx_out * 4, cudaMemcpyDeviceToDevice,
+                                   dev.stream));
+    if (sc.ctx_changed) {
+        broadcast_context_rows_kernel<<<grid_for((uint64_t)sc.ctx_changed * (z.d + 1)), 256, 0, dev.stream>>>(
+            lane.st.ctx_list, sc.ctx_changed, dev.canon, (uint32_t)z.d, dev.d_lanes + l, 1);
+        CUDA_CHECK(cudaGetLastError());
+    }
+    CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+}
+
 // ---------------------------------------------------------------- batch
 void batch_begin(LeoB200Device& dev, const uint8_t* bytes, const uint64_t* offsets, uint32_t stories, int permission) {
     if (dev.batch_open) throw LeoFailure("a story batch is already in progress");
     if (stories == 0) throw LeoFailure("training batch cannot be empty");
     if (permission < 0 || permission > 3) throw LeoFailure("invalid permission");
+    refresh_lanes_from_replay(dev);
+    dev.doc_open = false;
     dev.batch_stories.assign(stories, {});
     for (uint32_t i = 0; i < stories; ++i)
         dev.batch_stories[i].assign(bytes + offsets[i], bytes + offsets[i + 1]);
     dev.batch_permission = permission;
-    dev.single_story = stories == 1;
+    dev.single_story = stories == 1 && !dev.force_lanes;
     dev.steps_done = 0;
     dev.batch_steps = 0;
     if (dev.single_story) {
@@ -1426,7 +1641,31 @@ void batch_steps(LeoB200Device& dev, uint32_t count) {
     dev.steps_done = end;
 }
 
-void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySummary* summaries, float* losses_out) {
+// How a batch ends: the fused path (merge, serial replay, replay sync), the
+// trait's training_story_batch (merge and lane sync; the caller replays), or
+// its training_story_batch_deltas (per-story deltas exported, nothing merged).
+enum class FinishMode { kFused, kNoReplay, kDeltas };
+
+// Every story's replay ranges (training.rs:1782-1830) as (start, end) pairs in
+// story order.
+void write_replay_ranges(const LeoB200Device& dev, const std::vector<std::vector<float>>& losses, uint64_t* ranges,
+                         uint32_t* range_counts) {
+    size_t k = 0;
+    for (size_t i = 0; i < losses.size(); ++i) {
+        const auto rr = select_replay_ranges(losses[i], dev.cfg.host.replay_fraction, dev.cfg.host.replay_segment_bytes);
+        if (range_counts) range_counts[i] = (uint32_t)rr.size();
+        for (const ReplayRange& r : rr) {
+            if (ranges) {
+                ranges[2 * k] = r.start;
+                ranges[2 * k + 1] = r.end;
+            }
+            ++k;
+        }
+    }
+}
+
+void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySummary* summaries, float* losses_out,
+                  FinishMode mode = FinishMode::kFused, uint64_t* ranges = nullptr, uint32_t* range_counts = nullptr) {
     if (!dev.batch_open) throw LeoFailure("no story batch in progress");
     batch_steps(dev, dev.batch_steps);
     CUDA_CHECK(cudaStreamSynchronize(dev.stream));
@@ -1476,7 +1715,7 @@ void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySu
         double sum = 0.0;
         for (float v : losses[0]) sum += (double)v;
         rep.mean_loss = sum / (double)std::max<size_t>(losses[0].size(), 1);
-        replay_story(dev, story, losses[0], dev.batch_permission, replay_changes, &rep);
+        if (mode == FinishMode::kFused) replay_story(dev, story, losses[0], dev.batch_permission, replay_changes, &rep);
         sync_replay_changes(dev, replay_changes);
     } else {
         uint32_t L = dev.batch_lanes;
@@ -1497,6 +1736,28 @@ void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySu
         // keyed context on the host mirror, statistics and revision here.
         double canon_loss = dev.stats.training_loss_sum;
         dev.perf.collect_ms += ms_since(t0);
+        if (mode == FinishMode::kDeltas) {
+            // Each story's delta leaves with the caller; the lanes return to
+            // the (unchanged) canonical model.
+            upload_lane_table(dev);
+            dev.story_deltas.assign(L, {});
+            for (uint32_t l = 0; l < L; ++l) {
+                export_story_delta(dev, l, scal[l], canon_loss, dev.story_deltas[l]);
+                restore_lane(dev, l, scal[l]);
+            }
+            for (uint32_t l = 0; l < L; ++l) {
+                const LaneScalars& sc = scal[l];
+                if (summaries) {
+                    summaries[l].training_loss_sum = 0.0;
+                    for (float v : losses[l]) summaries[l].training_loss_sum += (double)v;
+                    summaries[l].training_targets = sc.targets;
+                    summaries[l].active_neurons_sum = sc.active_sum;
+                    summaries[l].active_neurons_peak = sc.active_peak;
+                    summaries[l].synaptic_events = sc.synaptic_events;
+                    summaries[l].context_applied_steps = sc.context_applied_steps;
+                }
+            }
+        } else {
         t0 = std::chrono::steady_clock::now();
         rep.fixed_parameter_updates = merge_fixed(dev, L, scal);
         dev.perf.merge_fixed_ms += ms_since(t0);
@@ -1526,6 +1787,7 @@ void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySu
                 summaries[l].context_applied_steps = sc.context_applied_steps;
             }
         }
+        }
         rep.workers = L;
         double weighted = 0.0;
         size_t targets = 0;
@@ -1541,7 +1803,7 @@ void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySu
         // Serial canonical replay (training.rs:1709-1711), then one sync of the
         // replay's changed rows into every lane (training.rs:1644-1649).
         t0 = std::chrono::steady_clock::now();
-        for (uint32_t l = 0; l < L; ++l)
+        for (uint32_t l = 0; l < L && mode == FinishMode::kFused; ++l)
             replay_story(dev, dev.batch_stories[l], losses[l], dev.batch_permission, replay_changes, &rep);
         CUDA_CHECK(cudaStreamSynchronize(dev.stream));
         dev.perf.replay_ms += ms_since(t0);
@@ -1561,9 +1823,295 @@ void batch_finish(LeoB200Device& dev, LeoB200BatchReport* report, LeoB200StorySu
         for (auto& l : losses)
             for (float v : l) losses_out[k++] = v;
     }
+    if (ranges || range_counts) write_replay_ranges(dev, losses, ranges, range_counts);
     if (report) *report = rep;
 }
 
+
+// ---------------------------------------------------------------- canonical runtime, step by step
+// The replay lane holds the canonical runtime's transient state (its
+// parameters are the canonical model).  A document is begun at the canonical
+// tick and grows by the steps of each call; tracking of changed parameters
+// persists across documents until enabled afresh.
+
+void replay_scalars_write(LeoB200Device& dev, const LaneScalars& sc) {
+    CUDA_CHECK(cudaMemcpyAsync(dev.replay->st.sc, &sc, sizeof(sc), cudaMemcpyHostToDevice, dev.stream));
+    CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+}
+
+void doc_begin(LeoB200Device& dev) {
+    if (dev.batch_open) throw LeoFailure("a story batch is in progress");
+    Lane& rl = *dev.replay;
+    ensure_schedule(rl, 4096);
+    LaneScalars before;
+    read_scalars(dev, rl, before);
+    reset_lane(dev, rl, dev.canonical_tick, 0);
+    LaneScalars sc;
+    read_scalars(dev, rl, sc);
+    sc.thr_changed = before.thr_changed;
+    sc.rec_changed = before.rec_changed;
+    sc.in_changed = before.in_changed;
+    sc.out_changed = before.out_changed;
+    sc.ctx_changed = before.ctx_changed;
+    sc.bias_dirty = before.bias_dirty;
+    sc.ctx_out_dirty = before.ctx_out_dirty;
+    replay_scalars_write(dev, sc);
+    dev.doc_open = true;
+    dev.doc_steps = 0;
+}
+
+void doc_steps(LeoB200Device& dev, const uint32_t* symbols, const int32_t* targets, uint32_t count, int permission,
+               float* losses, uint32_t* actives) {
+    if (!dev.doc_open) throw LeoFailure("no document begun (leo_b200_begin_document)");
+    if (permission < 0 || permission > 3) throw LeoFailure("invalid permission");
+    if (count == 0) return;
+    if (!symbols || !targets) throw LeoFailure("steps are null");
+    std::vector<uint32_t> words(count);
+    for (uint32_t i = 0; i < count; ++i) {
+        if (symbols[i] >= LEO_B200_SYMBOL_COUNT) throw LeoFailure("input symbol out of range");
+        const int32_t t = targets[i];
+        if (t < -1 || t > (int32_t)LEO_B200_END_DOCUMENT || t == (int32_t)LEO_B200_BEGIN_DOCUMENT)
+            throw LeoFailure("target symbol out of range");
+        words[i] = schedule_word(symbols[i], t, permission);
+    }
+    Lane& rl = *dev.replay;
+    const uint32_t begin = dev.doc_steps, end = begin + count;
+    if (rl.schedule_capacity < end) {
+        // A longer document: new buffers (steps before `begin` are not read again).
+        rl.schedule_capacity = 0;
+        ensure_schedule(rl, std::max<size_t>(end, 2 * (size_t)end));
+    }
+    CUDA_CHECK(cudaMemcpyAsync(rl.schedule + begin, words.data(), count * 4, cudaMemcpyHostToDevice, dev.stream));
+    LaneScalars before;
+    read_scalars(dev, rl, before);
+    LaneScalars sc = before;
+    sc.steps = end;
+    replay_scalars_write(dev, sc);
+    CUDA_CHECK(cudaMemcpyAsync(dev.d_replay, &rl.st, sizeof(LaneState), cudaMemcpyHostToDevice, dev.stream));
+    run_steps(dev, dev.d_replay, 1, begin, end, false);
+    LaneScalars after;
+    read_scalars(dev, rl, after);
+    check_error_flag(after);
+    // Statistics, revision and tick advance with the steps (runtime.rs:1595-1622).
+    dev.canonical_tick += count;
+    dev.revision += after.revision_increment - before.revision_increment;
+    dev.stats.processed_bytes += after.processed_bytes - before.processed_bytes;
+    dev.stats.training_loss_sum = after.loss_sum;
+    dev.stats.training_targets += after.targets - before.targets;
+    dev.stats.active_neurons_sum += after.active_sum - before.active_sum;
+    dev.stats.active_neurons_peak = std::max<uint64_t>(dev.stats.active_neurons_peak, after.active_peak);
+    dev.stats.synaptic_events += after.synaptic_events - before.synaptic_events;
+    dev.stats.numerical_rejections += after.numerical_rejections - before.numerical_rejections;
+    dev.stats.persistent_ticks += after.persistent_ticks - before.persistent_ticks;
+    if (losses) CUDA_CHECK(cudaMemcpy(losses, rl.step_loss + begin, count * 4, cudaMemcpyDeviceToHost));
+    if (actives) CUDA_CHECK(cudaMemcpy(actives, rl.step_active + begin, count * 4, cudaMemcpyDeviceToHost));
+    dev.doc_steps = end;
+}
+
+// The replay lane's changed-index lists (one per tracked tensor).
+struct TrackedList {
+    uint32_t* list;
+    uint8_t* marks;
+    uint32_t count;
+};
+
+void tracking_enable(LeoB200Device& dev) {
+    if (dev.batch_open) throw LeoFailure("a story batch is in progress");
+    Lane& rl = *dev.replay;
+    LaneScalars sc;
+    read_scalars(dev, rl, sc);
+    const TrackedList lists[] = {{rl.st.thr_list, rl.st.thr_mark, sc.thr_changed},
+                                 {rl.st.rec_list, rl.st.rec_mark, sc.rec_changed},
+                                 {rl.st.in_list, rl.st.in_mark, sc.in_changed},
+                                 {rl.st.out_list, rl.st.out_mark, sc.out_changed},
+                                 {rl.st.ctx_list, rl.st.ctx_mark, sc.ctx_changed}};
+    for (const TrackedList& tl : lists) {
+        if (tl.count == 0) continue;
+        clear_marks_kernel<<<grid_for(tl.count), 256, 0, dev.stream>>>(tl.list, tl.count, tl.marks);
+        CUDA_CHECK(cudaGetLastError());
+    }
+    sc.thr_changed = sc.rec_changed = sc.in_changed = sc.out_changed = sc.ctx_changed = 0;
+    sc.bias_dirty = sc.ctx_out_dirty = 0;
+    replay_scalars_write(dev, sc);
+}
+
+void tracking_changes(LeoB200Device& dev, LeoB200ParameterChangeSizes* sizes, const LeoB200ParameterChanges* out) {
+    Lane& rl = *dev.replay;
+    LaneScalars sc;
+    read_scalars(dev, rl, sc);
+    const TrackedList lists[] = {{rl.st.thr_list, nullptr, sc.thr_changed},
+                                 {rl.st.rec_list, nullptr, sc.rec_changed},
+                                 {rl.st.in_list, nullptr, sc.in_changed},
+                                 {rl.st.out_list, nullptr, sc.out_changed},
+                                 {rl.st.ctx_list, nullptr, sc.ctx_changed}};
+    uint32_t* dst[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+    if (out) {
+        dst[0] = out->threshold;
+        dst[1] = out->recurrent_weight;
+        dst[2] = out->input_weight;
+        dst[3] = out->output_neurons;
+        dst[4] = out->context_slots;
+    }
+    if (sizes) {
+        sizes->threshold = sc.thr_changed;
+        sizes->recurrent_weight = sc.rec_changed;
+        sizes->input_weight = sc.in_changed;
+        sizes->output_neurons = sc.out_changed;
+        sizes->context_slots = sc.ctx_changed;
+        sizes->output_bias_dirty = sc.bias_dirty;
+        sizes->context_output_dirty = sc.ctx_out_dirty;
+    }
+    for (int i = 0; i < 5; ++i) {
+        if (!dst[i] || lists[i].count == 0) continue;
+        CUDA_CHECK(cudaMemcpy(dst[i], lists[i].list, lists[i].count * 4, cudaMemcpyDeviceToHost));
+        std::sort(dst[i], dst[i] + lists[i].count);
+    }
+}
+
+// PackedSparseModelUpdate::apply_to_model (parallel.rs:196-300) on the
+// canonical model, then the same values into every resident lane.
+void packed_update(LeoB200Device& dev, const LeoB200PackedUpdate& u) {
+    if (dev.batch_open) throw LeoFailure("a story batch is in progress");
+    const ModelSizes& z = dev.z;
+    refresh_lanes_from_replay(dev);
+    upload_lane_table(dev);
+    const uint32_t lane_count = (uint32_t)dev.lanes.size();
+    struct Item {
+        const uint32_t* idx;
+        const float* vals;
+        uint64_t count;
+        float* LaneParams::*member;
+        size_t length;
+        uint32_t row, row_len;
+        const char* label;
+    };
+    const Item items[] = {
+        {u.threshold_indices, u.threshold_values, u.threshold_count, &LaneParams::threshold, z.n, 1, 1, "threshold"},
+        {u.recurrent_indices, u.recurrent_values, u.recurrent_count, &LaneParams::rec_weight, z.synapses, 1, 1,
+         "recurrent"},
+        {u.input_indices, u.input_values, u.input_count, &LaneParams::in_weight, z.inputs, 1, 1, "input"},
+        {u.output_neurons, u.output_values_by_neuron, u.output_count, &LaneParams::out_weight, z.n, LEO_OUTPUT_STRIDE,
+         LEO_OUTPUT_CLASSES, "output"},
+    };
+    for (const Item& it : items) {
+        if (it.count == 0) continue;
+        if (!it.idx || !it.vals) throw LeoFailure(std::string(it.label) + " packed sparse arrays are null");
+        for (uint64_t i = 0; i < it.count; ++i)
+            if (it.idx[i] >= it.length) throw LeoFailure(std::string(it.label) + " packed sparse index is outside model");
+    }
+    if (u.context_count && (!u.context_slots || !u.context_keys || !u.context_observations || !u.context_embeddings))
+        throw LeoFailure("packed context rows are null");
+    for (uint64_t i = 0; i < u.context_count; ++i)
+        if (u.context_slots[i] >= z.ctx) throw LeoFailure("packed context slot is outside the model");
+    for (const Item& it : items) {
+        if (it.count == 0) continue;
+        const size_t n = (size_t)it.count * it.row_len;
+        Scratch buf(it.count * 4 + n * 4);
+        uint32_t* d_idx = buf.as<uint32_t>();
+        float* d_val = reinterpret_cast<float*>(d_idx + it.count);
+        CUDA_CHECK(cudaMemcpyAsync(d_idx, it.idx, it.count * 4, cudaMemcpyHostToDevice, dev.stream));
+        CUDA_CHECK(cudaMemcpyAsync(d_val, it.vals, n * 4, cudaMemcpyHostToDevice, dev.stream));
+        write_rows_kernel<<<grid_for(n), 256, 0, dev.stream>>>(dev.canon.*it.member, d_idx, (uint32_t)it.count, it.row,
+                                                              it.row_len, d_val);
+        CUDA_CHECK(cudaGetLastError());
+        if (lane_count) {
+            std::vector<float*> ptrs(lane_count);
+            for (uint32_t l = 0; l < lane_count; ++l) ptrs[l] = dev.lanes[l]->st.p.*it.member;
+            CUDA_CHECK(cudaMemcpyAsync(dev.d_lane_ptrs, ptrs.data(), lane_count * sizeof(float*), cudaMemcpyHostToDevice,
+                                       dev.stream));
+            leo_launch_scatter_rows(dev.d_lane_ptrs, (int)lane_count, dev.canon.*it.member, d_idx, (uint32_t)it.count,
+                                    it.row, it.row_len, dev.grid, dev.stream);
+        }
+        CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+    }
+    if (u.context_count) {
+        const uint32_t n = (uint32_t)u.context_count, d = (uint32_t)z.d;
+        std::vector<ContextRow> rows(n);
+        for (uint32_t i = 0; i < n; ++i) {
+            rows[i].key = u.context_keys[i];
+            rows[i].obs = u.context_observations[i];
+        }
+        const size_t head = ((size_t)n * 4 + 15) & ~(size_t)15;
+        Scratch buf(head + n * sizeof(ContextRow) + (size_t)n * d * 4);
+        uint32_t* d_slots = buf.as<uint32_t>();
+        ContextRow* d_rows = reinterpret_cast<ContextRow*>(buf.as<char>() + head);
+        float* d_emb = reinterpret_cast<float*>(d_rows + n);
+        CUDA_CHECK(cudaMemcpyAsync(d_slots, u.context_slots, n * 4, cudaMemcpyHostToDevice, dev.stream));
+        CUDA_CHECK(cudaMemcpyAsync(d_rows, rows.data(), n * sizeof(ContextRow), cudaMemcpyHostToDevice, dev.stream));
+        CUDA_CHECK(cudaMemcpyAsync(d_emb, u.context_embeddings, (size_t)n * d * 4, cudaMemcpyHostToDevice, dev.stream));
+        scatter_context_rows_kernel<<<grid_for((uint64_t)n * (d + 1)), 256, 0, dev.stream>>>(
+            d_slots, n, d_rows, d_emb, d, dev.canon, dev.d_lanes, (int)lane_count);
+        CUDA_CHECK(cudaGetLastError());
+        CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+        for (uint32_t i = 0; i < n; ++i) {
+            const uint32_t slot = u.context_slots[i];
+            dev.ctx_keys[slot] = u.context_keys[i];
+            dev.ctx_obs[slot] = u.context_observations[i];
+            std::copy_n(u.context_embeddings + (size_t)i * d, d, dev.ctx_emb.begin() + (size_t)slot * d);
+        }
+    }
+    std::vector<float*> bias_targets{dev.canon.out_bias}, ctx_targets{dev.canon.ctx_out};
+    for (auto& l : dev.lanes) {
+        bias_targets.push_back(l->st.p.out_bias);
+        ctx_targets.push_back(l->st.p.ctx_out);
+    }
+    if (u.output_bias)
+        for (float* t : bias_targets)
+            CUDA_CHECK(cudaMemcpyAsync(t, u.output_bias, LEO_OUTPUT_CLASSES * 4, cudaMemcpyHostToDevice, dev.stream));
+    if (u.context_output_weights)
+        for (float* t : ctx_targets)
+            CUDA_CHECK(cudaMemcpyAsync(t, u.context_output_weights, z.ctx_out * 4, cudaMemcpyHostToDevice, dev.stream));
+    CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+    dev.generation = u.generation;
+    dev.revision = u.parameter_revision;
+    dev.stats = u.statistics;
+}
+
+// Sizes of the exported story deltas, then the copy into caller buffers.
+void story_delta_sizes(const LeoB200Device& dev, LeoB200StoryDeltaSizes* sizes) {
+    if (!sizes) return;
+    *sizes = LeoB200StoryDeltaSizes{};
+    sizes->stories = (uint32_t)dev.story_deltas.size();
+    sizes->embedding_dim = (uint32_t)dev.z.d;
+    for (const auto& sd : dev.story_deltas) {
+        for (int t = 0; t < LEO_B200_DELTA_TENSORS; ++t) sizes->entries[t] += sd.index[t].size();
+        sizes->context_entries += sd.ctx_key.size();
+    }
+}
+
+void story_deltas_copy(const LeoB200Device& dev, const LeoB200StoryDeltas& out) {
+    const size_t d = dev.z.d;
+    for (int t = 0; t < LEO_B200_DELTA_TENSORS; ++t) {
+        uint64_t at = 0;
+        for (size_t s = 0; s < dev.story_deltas.size(); ++s) {
+            const auto& sd = dev.story_deltas[s];
+            if (out.offsets[t]) out.offsets[t][s] = at;
+            const size_t n = sd.index[t].size();
+            if (n && out.indices[t]) std::copy_n(sd.index[t].data(), n, out.indices[t] + at);
+            if (n && out.deltas[t]) std::copy_n(sd.delta[t].data(), n, out.deltas[t] + at);
+            at += n;
+        }
+        if (out.offsets[t]) out.offsets[t][dev.story_deltas.size()] = at;
+    }
+    uint64_t at = 0;
+    for (size_t s = 0; s < dev.story_deltas.size(); ++s) {
+        const auto& sd = dev.story_deltas[s];
+        if (out.context_offsets) out.context_offsets[s] = at;
+        const size_t n = sd.ctx_key.size();
+        if (n) {
+            if (out.context_orders) std::copy_n(sd.ctx_order.data(), n, out.context_orders + at);
+            if (out.context_keys)
+                for (size_t i = 0; i < n; ++i) out.context_keys[at + i] = sd.ctx_key[i];
+            if (out.context_observation_increments)
+                std::copy_n(sd.ctx_obs_inc.data(), n, out.context_observation_increments + at);
+            if (out.context_embedding_deltas) std::copy_n(sd.ctx_emb.data(), n * d, out.context_embedding_deltas + at * d);
+        }
+        if (out.statistics) out.statistics[s] = sd.stats;
+        if (out.revision_increments) out.revision_increments[s] = sd.revision;
+        at += n;
+    }
+    if (out.context_offsets) out.context_offsets[dev.story_deltas.size()] = at;
+}
 
 // ---------------------------------------------------------------- sharded batch (multi-GPU)
 // The logical batch's stories are split into contiguous ranges, one per rank
@@ -1582,6 +2130,8 @@ void shard_begin(LeoB200Device& dev, const uint8_t* bytes, const uint64_t* offse
     if (stories < 2) throw LeoFailure("a sharded batch needs at least two stories (one story trains the canonical model)");
     if (first > stories || count > stories - first) throw LeoFailure("shard range exceeds the batch");
     if (permission < 0 || permission > 3) throw LeoFailure("invalid permission");
+    refresh_lanes_from_replay(dev);
+    dev.doc_open = false;
     dev.batch_stories.assign(stories, {});
     for (uint32_t i = 0; i < stories; ++i) dev.batch_stories[i].assign(bytes + offsets[i], bytes + offsets[i + 1]);
     dev.batch_permission = permission;
@@ -2105,6 +2655,138 @@ int leo_b200_train_story_batch(LeoB200Device* dev, const uint8_t* bytes, const u
         return 0;
     } catch (const std::exception& e) {
         dev->batch_open = false;
+        return fail(e);
+    }
+}
+
+// Runs one batch on story lanes (a single story too) and ends it in `mode`.
+int trait_batch(LeoB200Device* dev, const uint8_t* bytes, const uint64_t* offsets, uint32_t stories, int permission,
+                LeoB200BatchReport* report, LeoB200StorySummary* summaries, float* losses, uint64_t* ranges,
+                uint32_t* range_counts, FinishMode mode) {
+    CUDA_CHECK(cudaSetDevice(dev->device));
+    dev->force_lanes = true;
+    try {
+        batch_begin(*dev, bytes, offsets, stories, permission);
+    } catch (...) {
+        dev->force_lanes = false;
+        throw;
+    }
+    dev->force_lanes = false;
+    batch_finish(*dev, report, summaries, losses, mode, ranges, range_counts);
+    return 0;
+}
+
+int leo_b200_training_story_batch(LeoB200Device* dev, const uint8_t* bytes, const uint64_t* offsets, uint32_t stories,
+                                  int permission, LeoB200BatchReport* report, LeoB200StorySummary* summaries,
+                                  float* losses, uint64_t* ranges, uint32_t* range_counts) {
+    try {
+        // backend.rs:587-589: fewer than two stories are not a device batch.
+        if (stories < 2) return LEO_B200_UNSUPPORTED;
+        return trait_batch(dev, bytes, offsets, stories, permission, report, summaries, losses, ranges, range_counts,
+                           FinishMode::kNoReplay);
+    } catch (const std::exception& e) {
+        dev->batch_open = false;
+        return fail(e);
+    }
+}
+
+int leo_b200_training_story_batch_deltas(LeoB200Device* dev, const uint8_t* bytes, const uint64_t* offsets,
+                                         uint32_t stories, int permission, LeoB200BatchReport* report,
+                                         LeoB200StorySummary* summaries, float* losses, uint64_t* ranges,
+                                         uint32_t* range_counts, LeoB200StoryDeltaSizes* sizes) {
+    try {
+        if (stories == 0) return LEO_B200_UNSUPPORTED;
+        dev->story_deltas.clear();
+        trait_batch(dev, bytes, offsets, stories, permission, report, summaries, losses, ranges, range_counts,
+                    FinishMode::kDeltas);
+        story_delta_sizes(*dev, sizes);
+        return 0;
+    } catch (const std::exception& e) {
+        dev->batch_open = false;
+        return fail(e);
+    }
+}
+
+int leo_b200_story_deltas(LeoB200Device* dev, const LeoB200StoryDeltas* out) {
+    try {
+        if (!out) throw LeoFailure("story delta buffers are null");
+        story_deltas_copy(*dev, *out);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_begin_document(LeoB200Device* dev) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        doc_begin(*dev);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_reset_transient_state(LeoB200Device* dev) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        doc_begin(*dev);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_training_step_batch(LeoB200Device* dev, const uint32_t* symbols, const int32_t* targets, uint32_t count,
+                                 int permission, float* losses, uint32_t* active_neurons) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        doc_steps(*dev, symbols, targets, count, permission, losses, active_neurons);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_advance_frozen_batch(LeoB200Device* dev, const uint32_t* symbols, const int32_t* targets,
+                                  uint32_t count) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        doc_steps(*dev, symbols, targets, count, LEO_B200_FROZEN, nullptr, nullptr);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_enable_parameter_tracking(LeoB200Device* dev) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        tracking_enable(*dev);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_parameter_changes(LeoB200Device* dev, LeoB200ParameterChangeSizes* sizes,
+                               const LeoB200ParameterChanges* changes) {
+    try {
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        tracking_changes(*dev, sizes, changes);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_synchronize_packed_model(LeoB200Device* dev, const LeoB200PackedUpdate* update) {
+    try {
+        if (!update) throw LeoFailure("packed update is null");
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        packed_update(*dev, *update);
+        return 0;
+    } catch (const std::exception& e) {
         return fail(e);
     }
 }

@@ -1282,6 +1282,7 @@ __device__ void phase_assemble(const LaneState& ln, uint32_t s, const KernelCons
     }
     if (tid == 0) {
         if (active_out) *active_out = active;
+        ln.step_active[s] = active;
         sc->ring_count[entry] = active;
         float activity = (float)active / (float)(n_count > 0 ? n_count : 1);
         float error = activity - c.target_activity;

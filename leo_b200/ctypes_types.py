@@ -148,6 +148,83 @@ class LeoB200BatchReport(C.Structure):
     ]
 
 
+DELTA_TENSORS = 6  # threshold, recurrent weight, input weight, output weight, output bias, context output
+UNSUPPORTED = 1    # an optional device path that does not take the input (the trait's Ok(None))
+
+
+class LeoB200StoryDeltaSizes(C.Structure):
+    _fields_ = [
+        ("entries", C.c_uint64 * DELTA_TENSORS),
+        ("context_entries", C.c_uint64),
+        ("embedding_dim", C.c_uint32),
+        ("stories", C.c_uint32),
+    ]
+
+
+class LeoB200StoryDeltas(C.Structure):
+    _fields_ = [
+        ("offsets", C.c_void_p * DELTA_TENSORS),
+        ("indices", C.c_void_p * DELTA_TENSORS),
+        ("deltas", C.c_void_p * DELTA_TENSORS),
+        ("context_offsets", C.c_void_p),
+        ("context_orders", C.c_void_p),
+        ("context_keys", C.c_void_p),
+        ("context_observation_increments", C.c_void_p),
+        ("context_embedding_deltas", C.c_void_p),
+        ("statistics", C.c_void_p),
+        ("revision_increments", C.c_void_p),
+    ]
+
+
+class LeoB200ParameterChangeSizes(C.Structure):
+    _fields_ = [
+        ("threshold", C.c_uint64),
+        ("recurrent_weight", C.c_uint64),
+        ("input_weight", C.c_uint64),
+        ("output_neurons", C.c_uint64),
+        ("context_slots", C.c_uint64),
+        ("output_bias_dirty", C.c_uint32),
+        ("context_output_dirty", C.c_uint32),
+    ]
+
+
+class LeoB200ParameterChanges(C.Structure):
+    _fields_ = [
+        ("threshold", C.c_void_p),
+        ("recurrent_weight", C.c_void_p),
+        ("input_weight", C.c_void_p),
+        ("output_neurons", C.c_void_p),
+        ("context_slots", C.c_void_p),
+    ]
+
+
+class LeoB200PackedUpdate(C.Structure):
+    _fields_ = [
+        ("threshold_indices", C.c_void_p),
+        ("threshold_values", C.c_void_p),
+        ("threshold_count", C.c_uint64),
+        ("recurrent_indices", C.c_void_p),
+        ("recurrent_values", C.c_void_p),
+        ("recurrent_count", C.c_uint64),
+        ("input_indices", C.c_void_p),
+        ("input_values", C.c_void_p),
+        ("input_count", C.c_uint64),
+        ("output_neurons", C.c_void_p),
+        ("output_values_by_neuron", C.c_void_p),
+        ("output_count", C.c_uint64),
+        ("context_slots", C.c_void_p),
+        ("context_keys", C.c_void_p),
+        ("context_observations", C.c_void_p),
+        ("context_embeddings", C.c_void_p),
+        ("context_count", C.c_uint64),
+        ("output_bias", C.c_void_p),
+        ("context_output_weights", C.c_void_p),
+        ("generation", C.c_uint64),
+        ("parameter_revision", C.c_uint64),
+        ("statistics", LeoB200Statistics),
+    ]
+
+
 FROZEN, PROVISIONAL, TRAINING, VERIFIED = 0, 1, 2, 3
 TOPOLOGY_REFERENCE, TOPOLOGY_UNIFORM, TOPOLOGY_ZIPF = 0, 1, 2
 BEGIN_DOCUMENT, END_DOCUMENT, SYMBOL_COUNT, OUTPUT_CLASSES = 256, 257, 258, 257

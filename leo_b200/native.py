@@ -10,10 +10,15 @@ from pathlib import Path
 
 from .ctypes_types import (
     LeoB200BatchReport,
-    LeoB200ShardStory,
     LeoB200Config,
     LeoB200HostModel,
+    LeoB200PackedUpdate,
+    LeoB200ParameterChanges,
+    LeoB200ParameterChangeSizes,
     LeoB200PerfStats,
+    LeoB200ShardStory,
+    LeoB200StoryDeltas,
+    LeoB200StoryDeltaSizes,
     LeoB200StorySummary,
 )
 
@@ -88,6 +93,18 @@ def lib() -> C.CDLL:
     L.leo_b200_reset_perf_stats.argtypes = [vp]
     L.leo_b200_device_bytes.argtypes = [vp]
     L.leo_b200_device_bytes.restype = sz
+    L.leo_b200_training_story_batch.argtypes = [vp, vp, vp, u32, C.c_int, P(LeoB200BatchReport),
+                                                P(LeoB200StorySummary), vp, vp, vp]
+    L.leo_b200_training_story_batch_deltas.argtypes = [vp, vp, vp, u32, C.c_int, P(LeoB200BatchReport),
+                                                       P(LeoB200StorySummary), vp, vp, vp, P(LeoB200StoryDeltaSizes)]
+    L.leo_b200_story_deltas.argtypes = [vp, P(LeoB200StoryDeltas)]
+    L.leo_b200_begin_document.argtypes = [vp]
+    L.leo_b200_reset_transient_state.argtypes = [vp]
+    L.leo_b200_training_step_batch.argtypes = [vp, vp, vp, u32, C.c_int, vp, vp]
+    L.leo_b200_advance_frozen_batch.argtypes = [vp, vp, vp, u32]
+    L.leo_b200_enable_parameter_tracking.argtypes = [vp]
+    L.leo_b200_parameter_changes.argtypes = [vp, P(LeoB200ParameterChangeSizes), P(LeoB200ParameterChanges)]
+    L.leo_b200_synchronize_packed_model.argtypes = [vp, P(LeoB200PackedUpdate)]
     _lib = L
     return L
 

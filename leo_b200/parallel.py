@@ -275,7 +275,7 @@ def sharded_story_batch(gpu, ex: Exchange, stories: list[bytes], permission: int
 
     L = native.lib()
     if len(stories) < 2:
-        result = gpu.training_story_batch(stories, permission)
+        result = gpu.train_story_batch(stories, permission)
         return ShardResult(result.report, result.summaries, result.losses)
     ranges = work_balanced_story_ranges(stories, ex.world)
     first, end = ranges[ex.rank] if ex.rank < len(ranges) else (len(stories), len(stories))

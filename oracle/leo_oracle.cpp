@@ -1940,26 +1940,11 @@ ReplayReport apply_replay_policy(Runtime& rt, const uint8_t* story, size_t len, 
 }
 
 // training.rs:1539-1727 (CPU backend)
-BatchReport train_story_batch(Runtime& canonical, const std::vector<std::vector<uint8_t>>& stories, Permission p,
-                              size_t max_threads) {
-    if (stories.empty()) throw LeoError(LeoError::Internal, "training batch cannot be empty");
-    BatchReport report;
-    report.stories = stories.size();
-    if (stories.size() == 1) {
-        DocumentPass pass = train_document_pass(canonical, stories[0].data(), stories[0].size(), p);
-        report.replay = apply_replay_policy(canonical, stories[0].data(), stories[0].size(), pass.losses, p);
-        report.mean_loss = pass.mean_loss;
-        report.targets = pass.losses.size();
-        report.merge.workers = 1;
-        report.losses_by_story.push_back(pass.losses);
-        report.replay_ranges.push_back(select_replay_ranges(pass.losses, canonical.model.config.replay_fraction,
-                                                            canonical.model.config.segment_bytes));
-        return report;
-    }
-    const Model base = canonical.model;
+std::vector<SparseModelDelta> worker_story_deltas(const Model& base, const std::vector<std::vector<uint8_t>>& stories,
+                                                  Permission p, size_t max_threads, std::vector<DocumentPass>& passes) {
     size_t count = stories.size();
     std::vector<SparseModelDelta> deltas(count);
-    std::vector<DocumentPass> passes(count);
+    passes.assign(count, DocumentPass{});
     std::vector<std::string> errors(count);
     std::atomic<size_t> next{0};
     size_t threads = max_threads == 0 ? count : std::min(max_threads, count);
@@ -1982,6 +1967,28 @@ BatchReport train_story_batch(Runtime& canonical, const std::vector<std::vector<
     for (auto& t : pool) t.join();
     for (auto& e : errors)
         if (!e.empty()) throw LeoError(LeoError::Internal, e);
+    return deltas;
+}
+
+BatchReport train_story_batch(Runtime& canonical, const std::vector<std::vector<uint8_t>>& stories, Permission p,
+                              size_t max_threads) {
+    if (stories.empty()) throw LeoError(LeoError::Internal, "training batch cannot be empty");
+    BatchReport report;
+    report.stories = stories.size();
+    if (stories.size() == 1) {
+        DocumentPass pass = train_document_pass(canonical, stories[0].data(), stories[0].size(), p);
+        report.replay = apply_replay_policy(canonical, stories[0].data(), stories[0].size(), pass.losses, p);
+        report.mean_loss = pass.mean_loss;
+        report.targets = pass.losses.size();
+        report.merge.workers = 1;
+        report.losses_by_story.push_back(pass.losses);
+        report.replay_ranges.push_back(select_replay_ranges(pass.losses, canonical.model.config.replay_fraction,
+                                                            canonical.model.config.segment_bytes));
+        return report;
+    }
+    size_t count = stories.size();
+    std::vector<DocumentPass> passes;
+    std::vector<SparseModelDelta> deltas = worker_story_deltas(canonical.model, stories, p, max_threads, passes);
     report.merge = apply_mean_deltas(canonical.model, deltas);
     canonical.model_changed();
     canonical.reset_transient_state();

@@ -429,6 +429,193 @@ int leo_oracle_sparse_mean_apply(float* target, size_t length, const uint32_t* i
     }
 }
 
+// ---- story deltas (SparseModelDelta, parallel.rs:411-691) in the CSR layout
+// of LeoB200StoryDeltas: tensors threshold, recurrent weight, input weight,
+// output weight, output bias, context output weight.
+void* leo_oracle_story_deltas(void* rtp, const uint8_t* bytes, const uint64_t* offsets, size_t stories, int permission,
+                              size_t threads) {
+    try {
+        Runtime& rt = *(Runtime*)rtp;
+        std::vector<std::vector<uint8_t>> batch(stories);
+        for (size_t i = 0; i < stories; ++i) batch[i].assign(bytes + offsets[i], bytes + offsets[i + 1]);
+        std::vector<DocumentPass> passes;
+        auto* out = new std::vector<SparseModelDelta>(
+            worker_story_deltas(rt.model, batch, (Permission)permission, threads, passes));
+        return out;
+    } catch (const std::exception& e) {
+        fail(e);
+        return nullptr;
+    }
+}
+
+// One delta of the runtime's model against `base`: between_tracked with the
+// runtime's parameter changes (tracked != 0) or the full between.
+void* leo_oracle_runtime_delta(void* base, void* rtp, int tracked) {
+    try {
+        Runtime& rt = *(Runtime*)rtp;
+        const Model& b = *(Model*)base;
+        auto* out = new std::vector<SparseModelDelta>();
+        out->push_back(tracked ? SparseModelDelta::between_tracked(b, rt.model, rt.parameter_changes())
+                               : SparseModelDelta::between(b, rt.model));
+        return out;
+    } catch (const std::exception& e) {
+        fail(e);
+        return nullptr;
+    }
+}
+
+void leo_oracle_deltas_free(void* h) { delete (std::vector<SparseModelDelta>*)h; }
+
+namespace {
+const std::vector<SparseF32Delta>& delta_tensor(const SparseModelDelta& d, int t) {
+    switch (t) {
+        case 0: return d.threshold;
+        case 1: return d.recurrent_weight;
+        case 2: return d.input_weight;
+        case 3: return d.output_weight;
+        case 4: return d.output_bias;
+        default: return d.context_output_weight;
+    }
+}
+}  // namespace
+
+int leo_oracle_deltas_sizes(void* h, size_t embedding_dim, LeoB200StoryDeltaSizes* sizes) {
+    const auto& v = *(std::vector<SparseModelDelta>*)h;
+    std::memset(sizes, 0, sizeof(*sizes));
+    sizes->stories = (uint32_t)v.size();
+    sizes->embedding_dim = (uint32_t)embedding_dim;
+    for (const auto& d : v) {
+        if (!d.excitability.empty()) {
+            g_error = "excitability deltas have no slot in the story delta layout";
+            return -1;
+        }
+        for (int t = 0; t < LEO_B200_DELTA_TENSORS; ++t) sizes->entries[t] += delta_tensor(d, t).size();
+        sizes->context_entries += d.context.size();
+    }
+    return 0;
+}
+
+int leo_oracle_deltas_copy(void* h, size_t embedding_dim, const LeoB200StoryDeltas* out) {
+    const auto& v = *(std::vector<SparseModelDelta>*)h;
+    for (int t = 0; t < LEO_B200_DELTA_TENSORS; ++t) {
+        uint64_t at = 0;
+        for (size_t s = 0; s < v.size(); ++s) {
+            out->offsets[t][s] = at;
+            for (const auto& e : delta_tensor(v[s], t)) {
+                out->indices[t][at] = (uint32_t)e.index;
+                out->deltas[t][at] = e.delta;
+                ++at;
+            }
+        }
+        out->offsets[t][v.size()] = at;
+    }
+    uint64_t at = 0;
+    for (size_t s = 0; s < v.size(); ++s) {
+        out->context_offsets[s] = at;
+        for (const auto& c : v[s].context) {
+            if (c.embedding_delta.size() != embedding_dim) {
+                g_error = "context delta embedding has the wrong width";
+                return -1;
+            }
+            out->context_orders[at] = (uint32_t)c.order;
+            out->context_keys[at] = c.key;
+            out->context_observation_increments[at] = c.observation_increment;
+            std::copy(c.embedding_delta.begin(), c.embedding_delta.end(),
+                      out->context_embedding_deltas + at * embedding_dim);
+            ++at;
+        }
+        const StatisticsDelta& sd = v[s].statistics;
+        LeoB200Statistics& st = out->statistics[s];
+        std::memset(&st, 0, sizeof(st));
+        st.processed_bytes = sd.processed_bytes;
+        st.processed_stories = sd.processed_stories;
+        st.training_loss_sum = sd.training_loss_sum;
+        st.training_targets = sd.training_targets;
+        st.active_neurons_sum = sd.active_neurons_sum;
+        st.active_neurons_peak = sd.active_neurons_peak;
+        st.synaptic_events = sd.synaptic_events;
+        st.numerical_rejections = sd.numerical_rejections;
+        st.persistent_ticks = sd.persistent_ticks;
+        out->revision_increments[s] = v[s].revision_increment;
+    }
+    out->context_offsets[v.size()] = at;
+    return 0;
+}
+
+// apply_mean_deltas / apply_sum_deltas (parallel.rs:694-798) of story deltas
+// given in the CSR layout, produced from `model`'s current revision.
+int leo_oracle_apply_story_deltas(void* mp, const LeoB200StoryDeltaSizes* sizes, const LeoB200StoryDeltas* in,
+                                  int sum_instead, LeoB200BatchReport* merge) {
+    try {
+        Model& m = *(Model*)mp;
+        const size_t n = sizes->stories, d = sizes->embedding_dim;
+        std::vector<SparseModelDelta> deltas(n);
+        for (size_t s = 0; s < n; ++s) {
+            SparseModelDelta& sd = deltas[s];
+            sd.config_fingerprint = m.config.fingerprint();
+            sd.base_revision = m.parameter_revision;
+            sd.revision_increment = in->revision_increments[s];
+            for (int t = 0; t < LEO_B200_DELTA_TENSORS; ++t) {
+                auto& dst = const_cast<std::vector<SparseF32Delta>&>(delta_tensor(sd, t));
+                for (uint64_t j = in->offsets[t][s]; j < in->offsets[t][s + 1]; ++j)
+                    dst.push_back({in->indices[t][j], in->deltas[t][j]});
+            }
+            for (uint64_t j = in->context_offsets[s]; j < in->context_offsets[s + 1]; ++j) {
+                ContextKeyDelta c;
+                c.order = in->context_orders[j];
+                c.key = in->context_keys[j];
+                c.observation_increment = in->context_observation_increments[j];
+                c.embedding_delta.assign(in->context_embedding_deltas + j * d, in->context_embedding_deltas + (j + 1) * d);
+                sd.context.push_back(std::move(c));
+            }
+            const LeoB200Statistics& st = in->statistics[s];
+            sd.statistics.processed_bytes = st.processed_bytes;
+            sd.statistics.processed_stories = st.processed_stories;
+            sd.statistics.training_loss_sum = st.training_loss_sum;
+            sd.statistics.training_targets = st.training_targets;
+            sd.statistics.active_neurons_sum = st.active_neurons_sum;
+            sd.statistics.active_neurons_peak = st.active_neurons_peak;
+            sd.statistics.synaptic_events = st.synaptic_events;
+            sd.statistics.numerical_rejections = st.numerical_rejections;
+            sd.statistics.persistent_ticks = st.persistent_ticks;
+        }
+        MergeMetrics mm = sum_instead ? apply_sum_deltas(m, deltas) : apply_mean_deltas(m, deltas);
+        if (merge) {
+            std::memset(merge, 0, sizeof(*merge));
+            merge->workers = mm.workers;
+            merge->fixed_parameter_updates = mm.fixed_parameter_updates;
+            merge->context_keys = mm.context_keys;
+        }
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+// Runtime::parameter_changes (runtime.rs:322-333): sizes, then (when `out` is
+// not NULL) the indices in the order they were first changed.
+int leo_oracle_runtime_parameter_changes(void* rtp, LeoB200ParameterChangeSizes* sizes,
+                                         const LeoB200ParameterChanges* out) {
+    const ParameterChanges c = ((Runtime*)rtp)->parameter_changes();
+    sizes->threshold = c.threshold.size();
+    sizes->recurrent_weight = c.recurrent_weight.size();
+    sizes->input_weight = c.input_weight.size();
+    sizes->output_neurons = c.output_neurons.size();
+    sizes->context_slots = c.context_slots.size();
+    sizes->output_bias_dirty = c.output_bias_dirty;
+    sizes->context_output_dirty = c.context_output_dirty;
+    if (out) {
+        const std::vector<size_t>* src[5] = {&c.threshold, &c.recurrent_weight, &c.input_weight, &c.output_neurons,
+                                             &c.context_slots};
+        uint32_t* dst[5] = {out->threshold, out->recurrent_weight, out->input_weight, out->output_neurons,
+                            out->context_slots};
+        for (int i = 0; i < 5; ++i)
+            if (dst[i])
+                for (size_t j = 0; j < src[i]->size(); ++j) dst[i][j] = (uint32_t)(*src[i])[j];
+    }
+    return 0;
+}
+
 int leo_oracle_select_replay_ranges(const float* losses, size_t n, float fraction, size_t segment, uint64_t* out,
                                     size_t cap, size_t* count) {
     std::vector<float> l(losses, losses + n);

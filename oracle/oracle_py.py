@@ -72,6 +72,15 @@ def lib() -> C.CDLL:
         L.leo_oracle_mean_of_models.argtypes = [vp, vp, sz, C.c_int]
         L.leo_oracle_sparse_mean_apply.argtypes = [vp, sz, vp, vp, vp, sz, C.c_float, C.c_float, C.POINTER(sz)]
         L.leo_oracle_select_replay_ranges.argtypes = [C.c_void_p, sz, C.c_float, sz, vp, sz, C.POINTER(sz)]
+        L.leo_oracle_story_deltas.restype = vp
+        L.leo_oracle_story_deltas.argtypes = [vp, vp, vp, sz, C.c_int, sz]
+        L.leo_oracle_runtime_delta.restype = vp
+        L.leo_oracle_runtime_delta.argtypes = [vp, vp, C.c_int]
+        L.leo_oracle_deltas_free.argtypes = [vp]
+        L.leo_oracle_deltas_sizes.argtypes = [vp, sz, vp]
+        L.leo_oracle_deltas_copy.argtypes = [vp, sz, vp]
+        L.leo_oracle_apply_story_deltas.argtypes = [vp, vp, vp, C.c_int, vp]
+        L.leo_oracle_runtime_parameter_changes.argtypes = [vp, vp, vp]
         _lib = L
     return _lib
 
@@ -262,6 +271,65 @@ class OracleRuntime:
             split.append([(int(ranges[2 * (k + j)]), int(ranges[2 * (k + j) + 1])) for j in range(c)])
             k += c
         return report, losses[:total_targets], split
+
+
+    def story_deltas(self, stories: list[bytes], permission: int, threads: int = 0):
+        """Each story's tracked delta against this runtime's model (the CPU
+        branch's workers, training.rs:1667-1695); the model is unchanged."""
+        data = np.frombuffer(b"".join(stories), dtype=np.uint8).copy() if any(stories) else np.zeros(1, np.uint8)
+        offsets = np.zeros(len(stories) + 1, dtype=np.uint64)
+        offsets[1:] = np.cumsum([len(s) for s in stories])
+        h = lib().leo_oracle_story_deltas(self.handle, data.ctypes.data, offsets.ctypes.data, len(stories),
+                                          permission, threads)
+        return _take_deltas(h, self.config.context_embedding_dim)
+
+    def delta_against(self, base: OracleModel, tracked: bool):
+        """SparseModelDelta::between_tracked (with this runtime's parameter
+        changes) or ::between of this runtime's model against ``base``."""
+        h = lib().leo_oracle_runtime_delta(base.handle, self.handle, 1 if tracked else 0)
+        return _take_deltas(h, self.config.context_embedding_dim)[0]
+
+    def parameter_changes(self):
+        """Runtime::parameter_changes (runtime.rs:322-333), in first-change order."""
+        from leo_b200.backend import ParameterChanges
+        from leo_b200.ctypes_types import LeoB200ParameterChanges, LeoB200ParameterChangeSizes
+
+        sizes = LeoB200ParameterChangeSizes()
+        _check(lib().leo_oracle_runtime_parameter_changes(self.handle, C.byref(sizes), None))
+        names = ("threshold", "recurrent_weight", "input_weight", "output_neurons", "context_slots")
+        arrays = {k: np.zeros(max(int(getattr(sizes, k)), 1), np.uint32) for k in names}
+        out = LeoB200ParameterChanges(*(arrays[k].ctypes.data for k in names))
+        _check(lib().leo_oracle_runtime_parameter_changes(self.handle, C.byref(sizes), C.byref(out)))
+        return ParameterChanges(*(arrays[k][: int(getattr(sizes, k))].copy() for k in names),
+                                bool(sizes.output_bias_dirty), bool(sizes.context_output_dirty))
+
+
+def _take_deltas(h, embedding_dim: int):
+    from leo_b200.backend import StoryDeltaBuffers
+    from leo_b200.ctypes_types import LeoB200StoryDeltaSizes
+
+    if not h:
+        raise RuntimeError(lib().leo_oracle_last_error().decode())
+    try:
+        sizes = LeoB200StoryDeltaSizes()
+        _check(lib().leo_oracle_deltas_sizes(h, embedding_dim, C.byref(sizes)))
+        buffers = StoryDeltaBuffers(sizes)
+        _check(lib().leo_oracle_deltas_copy(h, embedding_dim, C.byref(buffers.c)))
+        return buffers.unpack()
+    finally:
+        lib().leo_oracle_deltas_free(h)
+
+
+def apply_story_deltas(model: OracleModel, deltas, sum_instead: bool = False) -> LeoB200BatchReport:
+    """apply_mean_deltas / apply_sum_deltas (parallel.rs:694-798) of story
+    deltas (``leo_b200.backend.StoryDelta``) produced from ``model``."""
+    from leo_b200.backend import StoryDeltaBuffers
+
+    buffers = StoryDeltaBuffers.pack(list(deltas), model.config.context_embedding_dim)
+    merge = LeoB200BatchReport()
+    _check(lib().leo_oracle_apply_story_deltas(model.handle, C.byref(buffers.sizes), C.byref(buffers.c),
+                                               1 if sum_instead else 0, C.byref(merge)))
+    return merge
 
 
 def select_replay_ranges(losses: np.ndarray, fraction: float, segment: int) -> list[tuple[int, int]]:

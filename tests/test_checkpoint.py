@@ -426,7 +426,7 @@ def test_gpu_model_checkpoint_and_resume_keep_golden_hashes(native_lib, tmp_path
     model = HostModel.initialize(w.config, w.topology)
     with GpuBackend(model, device=0, max_lanes=case["stories_per_batch"]) as gpu:
         for rec, batch in zip(case["batches"][:cut], batches[:cut]):
-            gpu.training_story_batch(batch, TRAINING)
+            gpu.train_story_batch(batch, TRAINING)
             assert gpu.state_digest().hex() == rec["state_hash"]
         ck.save_model_atomic(path, gpu.synchronize_model(), False)
         tick = gpu.canonical_tick
@@ -435,7 +435,7 @@ def test_gpu_model_checkpoint_and_resume_keep_golden_hashes(native_lib, tmp_path
     with GpuBackend(loaded, device=0, max_lanes=case["stories_per_batch"]) as gpu:
         gpu.canonical_tick = tick  # the run loop's own resume record carries the tick
         for rec, batch in zip(case["batches"][cut:], batches[cut:]):
-            gpu.training_story_batch(batch, TRAINING)
+            gpu.train_story_batch(batch, TRAINING)
             assert gpu.state_digest().hex() == rec["state_hash"]
             assert gpu.canonical_tick == rec["canonical_tick"]
         final = gpu.synchronize_model()

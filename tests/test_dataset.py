@@ -237,7 +237,7 @@ def test_golden_case_through_the_feed_on_the_gpu(native_lib, tmp_path):
     with GpuBackend(model, device=0, max_lanes=case["stories_per_batch"]) as gpu:
         fed = 0
         for rec, (stories, _) in zip(case["batches"], ds.story_batches(d, np.arange(n), case["stories_per_batch"])):
-            gpu.training_story_batch(stories, TRAINING)
+            gpu.train_story_batch(stories, TRAINING)
             assert gpu.state_digest().hex() == rec["state_hash"]
             fed += 1
         assert fed == len(case["batches"])

@@ -3,7 +3,7 @@
 
 The CPU test pins the oracle and the synthetic story generator against the
 committed records; the GPU test checks the product path through the public
-``GpuBackend.training_story_batch`` (the C-ABI ``leo_b200_train_story_batch``)
+``GpuBackend.train_story_batch`` (the C-ABI ``leo_b200_train_story_batch``)
 against the same records: bit-exact state hash, per-target losses, batch
 report counts, revision, statistics and canonical tick.
 """
@@ -77,7 +77,7 @@ def test_gpu_story_batch_matches_golden(native_lib, name):
     assert model.training_state_hash().hex() == case["initial_state_hash"]
     with GpuBackend(model, device=0, max_lanes=case["stories_per_batch"]) as backend:
         for i, (rec, batch) in enumerate(zip(case["batches"], batches)):
-            result = backend.training_story_batch(batch, TRAINING)
+            result = backend.train_story_batch(batch, TRAINING)
             assert backend.state_digest().hex() == rec["state_hash"], f"batch {i}"
             losses = np.concatenate(result.losses).astype("<f4")
             assert hashlib.sha256(losses.tobytes()).hexdigest() == rec["losses_sha256"], f"batch {i}"
@@ -112,7 +112,7 @@ def test_gpu_result_does_not_depend_on_geometry(native_lib, geometry, case_name)
         backend.set_cluster_sizes(story_c, replay_c)
         backend.set_story_chunk(chunk)
         for i, (rec, batch) in enumerate(zip(case["batches"], batches)):
-            backend.training_story_batch(batch, TRAINING)
+            backend.train_story_batch(batch, TRAINING)
             assert backend.state_digest().hex() == rec["state_hash"], f"batch {i}"
 
 
@@ -140,7 +140,7 @@ def test_gpu_hub_path_matches_golden(native_lib, case_name, min_in_degree, cta_e
         hubs, _ = backend.hub_plan()
         assert hubs > 0
         for i, (rec, batch) in enumerate(zip(case["batches"], batches)):
-            backend.training_story_batch(batch, TRAINING)
+            backend.train_story_batch(batch, TRAINING)
             assert backend.state_digest().hex() == rec["state_hash"], f"batch {i}"
 
 
@@ -161,6 +161,6 @@ def test_gpu_context_merge_site_matches_golden(native_lib, case_name, device_mer
     with GpuBackend(model, device=0, max_lanes=case["stories_per_batch"]) as backend:
         backend.set_device_context_merge(device_merge)
         for i, (rec, batch) in enumerate(zip(case["batches"], batches)):
-            result = backend.training_story_batch(batch, TRAINING)
+            result = backend.train_story_batch(batch, TRAINING)
             assert backend.state_digest().hex() == rec["state_hash"], f"batch {i}"
             assert int(result.report.context_keys) == rec["report"]["context_keys"], f"batch {i}"

@@ -61,7 +61,7 @@ def test_story_batch_matches_oracle_state_hash(name, count, lo, hi, native_lib, 
     backend = _backend(hm, count)
     canonical = oracle_lib.OracleRuntime(om)
     for batch in range(2):
-        result = backend.training_story_batch(stories, TRAINING)
+        result = backend.train_story_batch(stories, TRAINING)
         report, losses, ranges = canonical.train_story_batch(stories, TRAINING)
         got = np.concatenate(result.losses)
         assert np.array_equal(got.view(np.uint32), losses.view(np.uint32)), f"batch {batch}: losses differ"
@@ -84,7 +84,7 @@ def test_single_story_batch_trains_canonical_directly(native_lib, oracle_lib):
     backend = _backend(hm, 2)
     canonical = oracle_lib.OracleRuntime(om)
     for _ in range(2):
-        backend.training_story_batch(story, TRAINING)
+        backend.train_story_batch(story, TRAINING)
         canonical.train_story_batch(story, TRAINING)
         assert backend.state_digest() == canonical.model.training_state_hash()
         assert backend.canonical_tick == canonical.tick
@@ -101,7 +101,7 @@ def test_story_batch_permissions_match_oracle(permission, native_lib, oracle_lib
     backend = _backend(hm, 4)
     canonical = oracle_lib.OracleRuntime(om)
     for batch in range(2):
-        result = backend.training_story_batch(stories, permission)
+        result = backend.train_story_batch(stories, permission)
         report, losses, ranges = canonical.train_story_batch(stories, permission)
         got = np.concatenate(result.losses)
         assert np.array_equal(got.view(np.uint32), losses.view(np.uint32)), f"batch {batch}: losses differ"
@@ -127,7 +127,7 @@ def test_edge_case_stories_match_oracle(native_lib, oracle_lib):
     backend = _backend(hm, 4)
     canonical = oracle_lib.OracleRuntime(om)
     for batch, permission in ((stories, TRAINING), ([stories[2]], FROZEN)):
-        result = backend.training_story_batch(batch, permission)
+        result = backend.train_story_batch(batch, permission)
         report, losses, ranges = canonical.train_story_batch(batch, permission)
         got = np.concatenate(result.losses) if result.losses else np.zeros(0, np.float32)
         assert np.array_equal(got.view(np.uint32), losses.view(np.uint32)), "losses differ"
@@ -152,14 +152,14 @@ def test_replace_model_restarts_from_the_given_model(native_lib, oracle_lib):
     wl, hm, om = _models("test", oracle_lib)
     stories = story_stream(9, 4, 8, 40)
     backend = _backend(hm, 4)
-    backend.training_story_batch(stories, TRAINING)
+    backend.train_story_batch(stories, TRAINING)
     first = backend.state_digest()
-    backend.training_story_batch(stories, TRAINING)  # moves the lanes and canonical model on
+    backend.train_story_batch(stories, TRAINING)  # moves the lanes and canonical model on
     assert backend.state_digest() != first
     backend.replace_model(hm)
     backend.canonical_tick = 0
-    backend.training_story_batch(stories, TRAINING)
+    backend.train_story_batch(stories, TRAINING)
     assert backend.state_digest() == first
     with pytest.raises(LeoError, match="lanes"):
-        backend.training_story_batch(stories + stories, TRAINING)
+        backend.train_story_batch(stories + stories, TRAINING)
     backend.close()
