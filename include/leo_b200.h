@@ -251,6 +251,14 @@ int leo_b200_set_hub_threshold(LeoB200Device* device, uint32_t min_in_degree, ui
                                uint32_t thread_events);
 int leo_b200_hub_count(LeoB200Device* device, uint32_t* hubs, uint64_t* events_per_lane);
 
+/* Diagnostic: caps every target's per-step event segment at `limit` entries
+   (0: the exact bound, min(in-degree, 4 x max_active_global x multiplicity)
+   plus the input fan-in, which no step can exceed).  A step whose events
+   overrun a capped segment drops the extra events without writing past it
+   and the batch fails with an error, as a device capacity overrun would.
+   Only before the first story batch. */
+int leo_b200_set_segment_capacity_limit(LeoB200Device* device, uint32_t limit);
+
 /* Device memory held by the backend, in bytes. */
 size_t leo_b200_device_bytes(LeoB200Device* device);
 

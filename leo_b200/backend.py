@@ -352,6 +352,10 @@ class GpuBackend:
         native.check(native.lib().leo_b200_hub_count(self.handle, C.byref(hubs), C.byref(events)))
         return hubs.value, events.value
 
+    def set_segment_capacity_limit(self, limit: int) -> None:
+        """Diagnostic cap on every target's event segment (0: the exact bound)."""
+        native.check(native.lib().leo_b200_set_segment_capacity_limit(self.handle, limit))
+
     def set_story_chunk(self, steps: int) -> None:
         native.check(native.lib().leo_b200_set_story_chunk(self.handle, steps))
 

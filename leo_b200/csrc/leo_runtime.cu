@@ -186,6 +186,7 @@ struct LeoB200Device {
     uint32_t cta_events = 256;        // a listed target with more events than this per step is sorted by a CTA
     uint32_t thread_events = 16;      // at most this many: one thread; otherwise one warp
     uint64_t seg_events_total = 0;    // sum of segment capacities (entries per lane)
+    uint32_t seg_capacity_limit = 0;  // diagnostic cap on every segment (0: the exact bound)
     std::vector<uint2> seg_host;      // the plan, to detect a changed topology
     cudaStream_t aux[4] = {nullptr, nullptr, nullptr, nullptr};
     cudaEvent_t fork = nullptr, join[4] = {nullptr, nullptr, nullptr, nullptr};
@@ -418,7 +419,8 @@ std::vector<uint2> plan_segments(LeoB200Device& dev, const uint32_t* recurrent_t
     std::vector<std::pair<uint64_t, uint32_t>> listed;
     uint64_t total = 0;
     for (uint32_t n = 0; n < N; ++n) {
-        const uint64_t cap = std::min<uint64_t>(degree[n], 4ull * maxa * mult[n]) + in_max[n];
+        uint64_t cap = std::min<uint64_t>(degree[n], 4ull * maxa * mult[n]) + in_max[n];
+        if (dev.seg_capacity_limit) cap = std::min<uint64_t>(cap, dev.seg_capacity_limit);
         // Every segment sorts in shared memory (32,768 keys): the device limits
         // (max_active_global <= 1024, four branches) keep capacities below that.
         if (cap > 32768) throw LeoFailure("a target's events per step exceed the settle sort (32768)");
@@ -741,6 +743,7 @@ void check_error_flag(const LaneScalars& sc) {
     if (sc.error_flag & LEO_ERR_NONFINITE_INHIBITORY) throw LeoFailure("non-finite inhibitory update rejected");
     if (sc.error_flag & LEO_ERR_NONFINITE_BIAS) throw LeoFailure("output bias became non-finite");
     if (sc.error_flag & LEO_ERR_NONFINITE_CONTEXT) throw LeoFailure("non-finite context update rejected");
+    if (sc.error_flag & LEO_ERR_CAPACITY) throw LeoFailure("a step's events exceeded a device event capacity");
     if (sc.error_flag) throw LeoFailure("device step reported an error");
 }
 
@@ -3151,6 +3154,27 @@ int leo_b200_set_hub_threshold(LeoB200Device* dev, uint32_t min_in_degree, uint3
         dev->cta_events = cta_events ? cta_events : 256;
         dev->thread_events = thread_events ? thread_events : 16;
         plan_segments(*dev, rec.data(), in.data(), true);  // capacities are unchanged: lane buffers stay valid
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_set_segment_capacity_limit(LeoB200Device* dev, uint32_t limit) {
+    try {
+        if (!dev->lanes.empty() || dev->batch_open)
+            throw LeoFailure("the segment capacity limit must be set before the first story batch");
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        const ModelSizes& z = dev->z;
+        std::vector<uint32_t> rec(z.synapses), in(z.inputs);
+        CUDA_CHECK(cudaMemcpy(rec.data(), dev->kc.topo.rec_word, z.synapses * 4, cudaMemcpyDeviceToHost));
+        CUDA_CHECK(cudaMemcpy(in.data(), dev->kc.topo.in_word, z.inputs * 4, cudaMemcpyDeviceToHost));
+        for (auto& w : rec) w &= LEO_TARGET_MASK;
+        for (auto& w : in) w &= LEO_TARGET_MASK;
+        // Capacities only shrink below the ones the replay lane was sized
+        // for at open, and story lanes are sized at their first batch.
+        dev->seg_capacity_limit = limit;
+        plan_segments(*dev, rec.data(), in.data(), true);
         return 0;
     } catch (const std::exception& e) {
         return fail(e);

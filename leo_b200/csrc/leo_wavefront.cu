@@ -1023,7 +1023,7 @@ __device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts
         uint32_t n = 0, k = 0;
         if (tid < top) {
             n = kc.topo.cta_targets[tid];
-            k = ln.seg_count[n];
+            k = min(ln.seg_count[n], kc.topo.seg[n].y & LEO_SEG_CAPACITY);
         }
         const bool busy = tid < top && k > kc.topo.cta_events;
         const unsigned int ballot = __ballot_sync(0xffffffffu, busy);
@@ -1055,7 +1055,7 @@ __device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts
         const uint32_t i = round * C + ((round & 1u) ? C - 1u - rank : rank);
         if (i < listed) {
             const uint32_t n = kc.topo.cta_targets[i];
-            const uint32_t k = ln.seg_count[n];
+            const uint32_t k = min(ln.seg_count[n], kc.topo.seg[n].y & LEO_SEG_CAPACITY);
             const int tier = k > kc.topo.cta_events ? 0 : (k > kc.topo.thread_events ? 1 : 2);
             if ((tier > 0 || i >= top) && (tier < 2 || k > 0u || ln.touch_epoch[n] == epoch)) {
                 const uint32_t pos = atomicAdd(&s_nlist[tier], 1u);
@@ -1088,7 +1088,9 @@ __device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts
         uint32_t k = 0;
         if (valid) {
             seg = kc.topo.seg[n];
-            k = ln.seg_count[n];
+            // An overrun count (events past the capacity were dropped and
+            // flagged) never reads past the segment.
+            k = min(ln.seg_count[n], seg.y & LEO_SEG_CAPACITY);
         }
         const bool listed = (seg.y & LEO_SEG_LISTED) != 0u;
         const bool alone = !listed && k <= kc.topo.thread_events;

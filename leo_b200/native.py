@@ -77,6 +77,7 @@ def lib() -> C.CDLL:
                                         P(LeoB200StorySummary), vp]
     L.leo_b200_set_hub_threshold.argtypes = [vp, u32, u32, u32]
     L.leo_b200_hub_count.argtypes = [vp, P(u32), P(u64)]
+    L.leo_b200_set_segment_capacity_limit.argtypes = [vp, u32]
     L.leo_b200_sparse_mean_apply.argtypes = [C.c_int, vp, u32, vp, vp, vp, u32, C.c_float, C.c_float, vp, u32, vp,
                                              P(u32)]
     L.leo_b200_sparse_mean_apply_static.argtypes = L.leo_b200_sparse_mean_apply.argtypes

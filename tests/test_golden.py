@@ -164,3 +164,27 @@ def test_gpu_context_merge_site_matches_golden(native_lib, case_name, device_mer
             result = backend.train_story_batch(batch, TRAINING)
             assert backend.state_digest().hex() == rec["state_hash"], f"batch {i}"
             assert int(result.report.context_keys) == rec["report"]["context_keys"], f"batch {i}"
+
+
+@pytest.mark.gpu
+def test_gpu_event_capacity_overrun_is_an_error(native_lib):
+    """A step whose events overrun a target's event segment fails the batch
+    with LeoError: the extra events are dropped without a write past the
+    segment and the kernel's capacity flag becomes the error.  (The planned
+    capacities are exact bounds; the diagnostic limit forces the overrun.)"""
+    from leo_b200.backend import GpuBackend
+    from leo_b200.ctypes_types import TRAINING
+    from leo_b200.model import HostModel
+    from leo_b200.native import LeoError
+
+    case = CASES["baseline1"]
+    w, batches = _stories(case)
+    model = HostModel.initialize(w.config, w.topology)
+    with GpuBackend(model, device=0, max_lanes=case["stories_per_batch"]) as backend:
+        backend.set_segment_capacity_limit(1)
+        with pytest.raises(LeoError, match="event capacity"):
+            backend.train_story_batch(batches[0], TRAINING)
+    with GpuBackend(model, device=0, max_lanes=case["stories_per_batch"]) as backend:
+        backend.set_segment_capacity_limit(1 << 20)  # above every exact bound: no effect
+        backend.train_story_batch(batches[0], TRAINING)
+        assert backend.state_digest().hex() == case["batches"][0]["state_hash"]
