@@ -87,8 +87,11 @@ def phase_algorithmic_bytes(p, cfg) -> dict[str, float]:
 
 def dram_traffic(workload: str, algorithmic_bytes_per_launch: float):
     """DRAM bytes per launch of the wavefront kernel: the ratio of DRAM traffic to
-    algorithmic bytes from the committed ncu capture of this workload, applied to
-    this run's algorithmic bytes per launch (None without a capture)."""
+    algorithmic bytes measured by the committed one-pass ncu capture that stands
+    in for this workload (a small case of the same model: its timed launches'
+    dram__bytes_read.sum + dram__bytes_write.sum over the algorithmic bytes the
+    same run counted), applied to this run's algorithmic bytes per launch; None
+    without a capture."""
     path = ROOT / "profiles" / f"leo_wavefront_kernel-dram-{workload}.json"
     if not path.exists():
         return None, None

@@ -350,6 +350,8 @@ WORKLOADS = {
     "baseline3": Workload("baseline3", BASELINE3, TOPOLOGY_ZIPF, 64, 50_000, 512, 2048),
     # Small case of the baseline3 model: 4 lanes of short stories.
     "baseline3-small": Workload("baseline3-small", BASELINE3, TOPOLOGY_ZIPF, 4, 64, 64, 128),
+    # Small case of the baseline3 model for kernel captures: 2 lanes of short stories.
+    "baseline3-profile": Workload("baseline3-profile", BASELINE3, TOPOLOGY_ZIPF, 2, 64, 80, 96),
     "baseline4": Workload("baseline4", BASELINE3, TOPOLOGY_ZIPF, 128, 50_000, 512, 2048),
 }
 
