@@ -1057,6 +1057,29 @@ void Runtime::apply_post_activation_dynamics() {
 }
 
 // runtime.rs:940-1074
+// runtime.rs:984-997: total order of positive candidates (activation
+// descending, then rotated neuron key ascending).
+bool selection_better(const std::pair<size_t, float>& l, const std::pair<size_t, float>& r, size_t rotation,
+                      size_t n_count) {
+    if (l.second != r.second) return l.second > r.second;
+    return rotated_tie_key(l.first, rotation, n_count) < rotated_tie_key(r.first, rotation, n_count);
+}
+
+// runtime.rs:964-997: a block's top `limit` candidates in rank order; when
+// more are positive, *cutoff becomes the (limit + 1)-th best value.
+void select_block(std::vector<std::pair<size_t, float>>& block, size_t limit, size_t rotation, size_t n_count,
+                  float* cutoff) {
+    auto better = [&](const std::pair<size_t, float>& l, const std::pair<size_t, float>& r) {
+        return selection_better(l, r, rotation, n_count);
+    };
+    if (block.size() > limit) {
+        std::nth_element(block.begin(), block.begin() + (long)limit, block.end(), better);
+        *cutoff = block[limit].second;
+        block.resize(limit);
+    }
+    std::sort(block.begin(), block.end(), better);
+}
+
 Runtime::SelectionMetrics Runtime::select_active_neurons() {
     const Config& c = model.config;
     size_t block_size = c.neurons_per_block;
@@ -1078,20 +1101,12 @@ Runtime::SelectionMetrics Runtime::select_active_neurons() {
     SelectionMetrics sm;
     for (auto& b : block_candidates) sm.suprathreshold += b.size();
 
-    auto better = [&](const std::pair<size_t, float>& l, const std::pair<size_t, float>& r) {
-        // right.1.total_cmp(&left.1) then rotated keys ascending (positive values only)
-        if (l.second != r.second) return l.second > r.second;
-        return rotated_tie_key(l.first, rotation, n_count) < rotated_tie_key(r.first, rotation, n_count);
-    };
     size_t limit = c.max_active_per_block;
     for (size_t bi = 0; bi < block_candidates.size(); ++bi) {
         auto& block = block_candidates[bi];
-        if (block.size() > limit) {
-            std::nth_element(block.begin(), block.begin() + (long)limit, block.end(), better);
-            block_selection_cutoff[bi] = block[limit].second;
-            block.resize(limit);
-        }
-        std::sort(block.begin(), block.end(), better);
+        float cutoff = block_selection_cutoff[bi];
+        select_block(block, limit, rotation, n_count, &cutoff);
+        block_selection_cutoff[bi] = cutoff;
         for (auto& p : block) active.push_back(p.first);
     }
     sm.block_selected = active.size();

@@ -286,6 +286,12 @@ struct Runtime {
     static void mark_changed(size_t index, std::vector<uint8_t>& marks, std::vector<size_t>& list);
 };
 
+// ---- selection order, crates/leo-core/src/runtime.rs:964-1030 ---------------
+bool selection_better(const std::pair<size_t, float>& l, const std::pair<size_t, float>& r, size_t rotation,
+                      size_t n_count);
+void select_block(std::vector<std::pair<size_t, float>>& block, size_t limit, size_t rotation, size_t n_count,
+                  float* cutoff);
+
 // ---- delta algebra, crates/leo-core/src/parallel.rs -------------------------
 struct SparseF32Delta { size_t index; float delta; };
 struct ContextKeyDelta {

@@ -1,6 +1,7 @@
 // TEST INFRASTRUCTURE ONLY -- C entry points over the parity oracle, for the
 // pytest suite (ctypes) and bench.py's cpu_baseline leg.  Never linked into or
 // called by the product library.
+#include <algorithm>
 #include <cstring>
 #include <string>
 
@@ -614,6 +615,37 @@ int leo_oracle_runtime_parameter_changes(void* rtp, LeoB200ParameterChangeSizes*
                 for (size_t j = 0; j < src[i]->size(); ++j) dst[i][j] = (uint32_t)(*src[i])[j];
     }
     return 0;
+}
+
+// One block's selection (select_block): candidates (value > 0 only, as the
+// runtime pushes them) in, winners in rank order and the cutoff out (0 when
+// at most `keep` are positive).
+void leo_oracle_select_block(const float* values, const uint32_t* neurons, size_t count, size_t keep, size_t rotation,
+                             size_t neuron_count, uint32_t* winners, float* winner_values, size_t* winner_count,
+                             float* cutoff) {
+    std::vector<std::pair<size_t, float>> block;
+    for (size_t i = 0; i < count; ++i)
+        if (values[i] > 0.0f) block.push_back({neurons[i], values[i]});
+    float c = 0.0f;
+    select_block(block, keep, rotation, neuron_count, &c);
+    for (size_t i = 0; i < block.size(); ++i) {
+        winners[i] = (uint32_t)block[i].first;
+        winner_values[i] = block[i].second;
+    }
+    *winner_count = block.size();
+    *cutoff = c;
+}
+
+// The global rank order of the cap (runtime.rs:1014-1030): indices of the
+// candidates sorted by selection_better.
+void leo_oracle_global_order(const float* values, const uint32_t* neurons, size_t count, size_t rotation,
+                             size_t neuron_count, uint32_t* order) {
+    std::vector<size_t> idx(count);
+    for (size_t i = 0; i < count; ++i) idx[i] = i;
+    std::sort(idx.begin(), idx.end(), [&](size_t a, size_t b) {
+        return selection_better({neurons[a], values[a]}, {neurons[b], values[b]}, rotation, neuron_count);
+    });
+    for (size_t i = 0; i < count; ++i) order[i] = (uint32_t)idx[i];
 }
 
 int leo_oracle_select_replay_ranges(const float* losses, size_t n, float fraction, size_t segment, uint64_t* out,

@@ -72,6 +72,8 @@ def lib() -> C.CDLL:
         L.leo_oracle_mean_of_models.argtypes = [vp, vp, sz, C.c_int]
         L.leo_oracle_sparse_mean_apply.argtypes = [vp, sz, vp, vp, vp, sz, C.c_float, C.c_float, C.POINTER(sz)]
         L.leo_oracle_select_replay_ranges.argtypes = [C.c_void_p, sz, C.c_float, sz, vp, sz, C.POINTER(sz)]
+        L.leo_oracle_select_block.argtypes = [vp, vp, sz, sz, sz, sz, vp, vp, C.POINTER(sz), C.POINTER(C.c_float)]
+        L.leo_oracle_global_order.argtypes = [vp, vp, sz, sz, sz, vp]
         L.leo_oracle_story_deltas.restype = vp
         L.leo_oracle_story_deltas.argtypes = [vp, vp, vp, sz, C.c_int, sz]
         L.leo_oracle_runtime_delta.restype = vp
@@ -330,6 +332,30 @@ def apply_story_deltas(model: OracleModel, deltas, sum_instead: bool = False) ->
     _check(lib().leo_oracle_apply_story_deltas(model.handle, C.byref(buffers.sizes), C.byref(buffers.c),
                                                1 if sum_instead else 0, C.byref(merge)))
     return merge
+
+
+def select_block(candidates, keep: int, rotation: int, neuron_count: int):
+    """A block's winners [(value, neuron)] in rank order and its cutoff
+    (runtime.rs:964-997) from candidates [(value, neuron)]."""
+    values = np.asarray([v for v, _ in candidates] or [0.0], dtype=np.float32)
+    neurons = np.asarray([n for _, n in candidates] or [0], dtype=np.uint32)
+    winners = np.zeros(max(len(candidates), 1), np.uint32)
+    wvals = np.zeros(max(len(candidates), 1), np.float32)
+    count, cutoff = C.c_size_t(), C.c_float()
+    lib().leo_oracle_select_block(values.ctypes.data, neurons.ctypes.data, len(candidates), keep, rotation,
+                                  neuron_count, winners.ctypes.data, wvals.ctypes.data, C.byref(count),
+                                  C.byref(cutoff))
+    return [(float(wvals[i]), int(winners[i])) for i in range(count.value)], float(cutoff.value)
+
+
+def global_order(candidates, rotation: int, neuron_count: int) -> list:
+    """Candidates [(value, neuron)] in the global cap's rank order (runtime.rs:1014-1030)."""
+    values = np.asarray([v for v, _ in candidates] or [0.0], dtype=np.float32)
+    neurons = np.asarray([n for _, n in candidates] or [0], dtype=np.uint32)
+    order = np.zeros(max(len(candidates), 1), np.uint32)
+    lib().leo_oracle_global_order(values.ctypes.data, neurons.ctypes.data, len(candidates), rotation, neuron_count,
+                                  order.ctypes.data)
+    return [candidates[int(i)] for i in order[: len(candidates)]]
 
 
 def select_replay_ranges(losses: np.ndarray, fraction: float, segment: int) -> list[tuple[int, int]]:
