@@ -336,6 +336,92 @@ def run_sparse_apply_micro(args) -> None:
         dist.destroy_process_group()
 
 
+def run_sparse_apply_reference(args) -> None:
+    """Config 5's reference arm: the reference's own CUDA path for the same job,
+    built from its unmodified cuda_kernels.cu (oracle/ref_cuda/Makefile ->
+    oracle/_ref/libleo_ref_kernels.so).  The same 32 stories' lists are merged
+    (FP64 sum in story order over the union, divided by the stories: what the
+    reference's host merge packs) outside the timed region; timed are the
+    reference's apply kernel over the dense delta + index list
+    (leo_apply_shared_wavefront_deltas) and the replica sync, one
+    leo_scatter_f32 launch per replica.  One JSON line per density on rank 0;
+    other ranks exit without work."""
+    import ctypes as C
+
+    import numpy as np
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    lib_path = ROOT / "oracle" / "_ref" / "libleo_ref_kernels.so"
+    if not lib_path.exists():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libleo_ref_kernels.so was not built "
+                          "(needs the reference checkout at build time)"}), flush=True)
+        return
+    lib = C.CDLL(str(lib_path))
+    lib.leo_ref_last_error.restype = C.c_char_p
+    vp, u32 = C.c_void_p, C.c_uint32
+    lib.leo_ref_apply_sync.argtypes = [C.c_int, vp, vp, u32, u32, vp, vp, vp, u32, vp, u32, C.c_float, C.c_float,
+                                       u32, C.POINTER(C.c_float), C.POINTER(C.c_float)]
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    n, S = 1 << 24, 64
+    stories, replicas = args.micro_stories, args.micro_replicas
+    peak, peak_kind = measured_peaks()
+    g = torch.Generator(device=dev)
+    g.manual_seed(99)
+    neuron_type = (torch.rand(n // S, generator=g, device=dev) < 0.2).to(torch.uint8)
+    for density in [float(x) for x in args.densities.split(",")]:
+        sums = torch.zeros(n, dtype=torch.float64, device=dev)
+        touched = torch.zeros(n, dtype=torch.bool, device=dev)
+        entries = 0
+        for sid in range(stories):
+            gs = torch.Generator(device=dev)
+            gs.manual_seed(7000 + sid)
+            idx = torch.nonzero(torch.rand(n, generator=gs, device=dev) < density).flatten()
+            val = torch.randn(idx.numel(), generator=gs, device=dev) * 1e-3
+            sums[idx] += val.to(torch.float64)
+            touched[idx] = True
+            entries += idx.numel()
+        union = torch.nonzero(touched).flatten().to(torch.int32)
+        merged = (sums[union.long()] / stories).to(torch.float32)
+        gb = torch.Generator(device=dev)
+        gb.manual_seed(4242)
+        base = torch.rand(n, generator=gb, device=dev) * 2.0 - 1.0
+        target = torch.empty_like(base)
+        reps = [base.clone() for _ in range(replicas)]
+        ptrs = (C.c_void_p * max(replicas, 1))(*[r.data_ptr() for r in reps])
+        apply_ms, sync_ms = C.c_float(), C.c_float()
+        torch.cuda.synchronize()
+
+        def run(iters):
+            rc = lib.leo_ref_apply_sync(0, base.data_ptr(), target.data_ptr(), n, S, neuron_type.data_ptr(),
+                                        union.data_ptr(), merged.data_ptr(), union.numel(), ptrs, replicas, -1.0, 1.0,
+                                        iters, C.byref(apply_ms), C.byref(sync_ms))
+            if rc != 0:
+                raise RuntimeError(lib.leo_ref_last_error().decode())
+
+        run(args.warmup)
+        run(args.steps)
+        a_ms, s_ms = apply_ms.value / args.steps, sync_ms.value / args.steps
+        m = union.numel()
+        # apply: list, dense delta, weight read + write, dense + mark clears, changed mark and list;
+        # sync: per replica index + value read and the weight write.
+        alg = 32.0 * m + 12.0 * m * replicas
+        ms = a_ms + s_ms
+        hbm = alg / (ms / 1000.0) / 1e9
+        print(json.dumps({
+            "impl": "reference", "metric": "sparse delta apply + replica sync (config 5)", "density": density,
+            "n_gpus": 1, "stories": stories, "replicas": replicas, "elements": n, "entries": entries, "merged": m,
+            "apply_ms": round(a_ms, 4), "sync_ms": round(s_ms, 4), "ms": round(ms, 4), "steps": args.steps,
+            "warmup": args.warmup,
+            "roofline": {"bound": "hbm", "achieved": round(hbm, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(hbm / peak, 4), "peak_source": peak_kind, "algorithmic_bytes": alg},
+            "path": "reference cuda_kernels.cu: leo_apply_shared_wavefront_deltas + leo_scatter_f32 per replica; "
+                    "the 32-story merge itself is host work in the reference and is not timed"}), flush=True)
+
+
 def measure_replay_off(backend, workload, args, device: int) -> dict:
     """The same model with replay fraction 0 (the reference's replay-off
     figure): one warm-up and `--steps` timed batches of fresh stories, CUDA-event
@@ -461,7 +547,10 @@ def main() -> None:
     ap.add_argument("--micro-replicas", type=int, default=8)
     args = ap.parse_args()
     if args.micro == "sparse-apply":
-        run_sparse_apply_micro(args)
+        if args.impl == "reference":
+            run_sparse_apply_reference(args)
+        else:
+            run_sparse_apply_micro(args)
         return
 
     from leo_b200.configs import WORKLOADS
