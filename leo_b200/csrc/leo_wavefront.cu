@@ -234,6 +234,11 @@ __device__ __forceinline__ void flush_touches(const LaneState& ln, TouchBuffer& 
 // sorting the keys.  Every event group also touches its target.  A segment holds every event the target can receive in one step
 // (the bound is computed from the topology); an overrun is reported.
 constexpr uint32_t kEventOrderMask = 0x3fffffffu;
+// Due slots a deliver thread loads together (see phase_deliver).
+#ifndef LEO_DELIVER_BATCH
+#define LEO_DELIVER_BATCH 4
+#endif
+constexpr uint32_t kDeliverBatch = LEO_DELIVER_BATCH;
 __device__ __forceinline__ void push_event(const LaneState& ln, const KernelConsts& kc, uint32_t n, uint32_t key,
                                            float value, uint32_t epoch, TouchBuffer& tb) {
     const uint2 seg = kc.topo.seg[n];
@@ -445,29 +450,55 @@ __device__ uint32_t phase_deliver(const LaneState& ln, uint32_t s, const KernelC
     // previous actives are touched (start_tick, runtime.rs:537-561)
     for (uint32_t i = worker; i < prev; i += workers)
         touch_buffered(ln, ln.ring_src[((s - 1) % LEO_RING) * maxa + i], epoch, tb);
-    // due recurrent events (ring entry of their delay class, rank, slot)
-    for (uint32_t q = worker; q < events; q += workers) {
-        uint32_t d, off;
-        if (q < e8) {
-            d = 8; off = q;
-        } else if (q < e8 + e4) {
-            d = 4; off = q - e8;
-        } else if (q < e8 + e4 + e2) {
-            d = 2; off = q - e8 - e4;
-        } else {
-            d = 1; off = q - e8 - e4 - e2;
+    // due recurrent events (ring entry of their delay class, rank, slot), kDeliverBatch
+    // slots per thread at a time: each stage's loads for all of them are in
+    // flight together (source, topology word, then the due ones' values), so a
+    // thread pays the dependent round trips once per batch, not once per slot.
+    for (uint32_t q0 = worker; q0 < events; q0 += workers * kDeliverBatch) {
+        uint32_t dl[kDeliverBatch], ent[kDeliverBatch], rr[kDeliverBatch], jj[kDeliverBatch], src[kDeliverBatch];
+#pragma unroll
+        for (uint32_t k = 0; k < kDeliverBatch; ++k) {
+            const uint32_t q = q0 + k * workers;
+            uint32_t d = 1, off = 0;
+            if (q < e8) {
+                d = 8; off = q;
+            } else if (q < e8 + e4) {
+                d = 4; off = q - e8;
+            } else if (q < e8 + e4 + e2) {
+                d = 2; off = q - e8 - e4;
+            } else if (q < events) {
+                d = 1; off = q - e8 - e4 - e2;
+            }
+            dl[k] = q < events ? d : 0u;  // 0: no slot (no word has delay 0)
+            ent[k] = (s - d) % LEO_RING;
+            rr[k] = off / S;
+            jj[k] = off - rr[k] * S;
+            src[k] = q < events ? ln.ring_src[ent[k] * maxa + rr[k]] : 0u;
         }
-        const uint32_t entry = (s - d) % LEO_RING;
-        const uint32_t r = off / S, j = off - r * S;
-        const uint32_t src = ln.ring_src[entry * maxa + r];
-        const uint32_t slot = src * S + j;
-        const uint32_t word = kc.topo.rec_word[slot];
-        if (LEO_WORD_DELAY(word) != d) continue;
-        const uint32_t n = word & LEO_TARGET_MASK, b = LEO_WORD_BRANCH(word);
-        const float a = ln.ring_act[entry * maxa + r];
-        const float value = (fresh_d1 && d == 1) ? a * ln.p.rec_weight[slot] : ln.ring_val[((size_t)entry * maxa + r) * S + j];
-        push_event(ln, kc, n, (b << 30) | q, value, epoch, tb);
-        if (learn) deliver_trace(ln, kc, ln.traces, ln.elig, sc->elig_count, cur, slot, s, a);
+        uint32_t word[kDeliverBatch];
+#pragma unroll
+        for (uint32_t k = 0; k < kDeliverBatch; ++k) word[k] = dl[k] ? kc.topo.rec_word[src[k] * S + jj[k]] : 0u;
+        float act[kDeliverBatch], val[kDeliverBatch];
+#pragma unroll
+        for (uint32_t k = 0; k < kDeliverBatch; ++k) {
+            act[k] = 0.0f;
+            val[k] = 0.0f;
+            if (dl[k] && LEO_WORD_DELAY(word[k]) == dl[k]) {
+                act[k] = ln.ring_act[ent[k] * maxa + rr[k]];
+                val[k] = (fresh_d1 && dl[k] == 1u) ? ln.p.rec_weight[src[k] * S + jj[k]]
+                                                  : ln.ring_val[((size_t)ent[k] * maxa + rr[k]) * S + jj[k]];
+            }
+        }
+#pragma unroll
+        for (uint32_t k = 0; k < kDeliverBatch; ++k) {
+            if (!dl[k] || LEO_WORD_DELAY(word[k]) != dl[k]) continue;
+            const uint32_t q = q0 + k * workers;
+            const uint32_t n = word[k] & LEO_TARGET_MASK, b = LEO_WORD_BRANCH(word[k]);
+            // a delay-1 event of a step whose emit is still open: activation x weight, as emit forms it
+            const float value = (fresh_d1 && dl[k] == 1u) ? act[k] * val[k] : val[k];
+            push_event(ln, kc, n, (b << 30) | q, value, epoch, tb);
+            if (learn) deliver_trace(ln, kc, ln.traces, ln.elig, sc->elig_count, cur, src[k] * S + jj[k], s, act[k]);
+        }
     }
     // the symbol's input slots (inject_symbol, runtime.rs:627-639)
     for (uint32_t f = worker; f < F; f += workers) {
