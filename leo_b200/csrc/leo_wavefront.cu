@@ -235,10 +235,7 @@ __device__ __forceinline__ void flush_touches(const LaneState& ln, TouchBuffer& 
 // (the bound is computed from the topology); an overrun is reported.
 constexpr uint32_t kEventOrderMask = 0x3fffffffu;
 // Due slots a deliver thread loads together (see phase_deliver).
-#ifndef LEO_DELIVER_BATCH
-#define LEO_DELIVER_BATCH 4
-#endif
-constexpr uint32_t kDeliverBatch = LEO_DELIVER_BATCH;
+constexpr uint32_t kDeliverBatch = 4;
 __device__ __forceinline__ void push_event(const LaneState& ln, const KernelConsts& kc, uint32_t n, uint32_t key,
                                            float value, uint32_t epoch, TouchBuffer& tb) {
     const uint2 seg = kc.topo.seg[n];
@@ -1007,6 +1004,53 @@ __device__ __forceinline__ void settle_target_thread(const LaneState& ln, uint32
     if (k) ln.seg_count[n] = 0u;
 }
 
+// Shares of the touched list when some CTAs sort busy targets first: every
+// CTA computes the same partition from the busy targets' key counts (busy
+// target i goes to CTA i mod C).  Modelled cost: one sorted key of a busy
+// target costs 1 / kBusyKeyShare of one touched neuron, so CTA r's share is
+// max(0, T - keys_r / kBusyKeyShare) with T chosen so the shares cover the list; the
+// partition only moves work between CTAs (every entry is settled once).
+// Writes [begin, end) of this CTA to range[0..1]; every thread calls it.
+// Touched neurons one busy-target key is worth in the share model below
+// (measured on config 3: shares from 1/2 to 1/5 of a neuron per key gave the
+// same settle time; results never depend on it).
+constexpr unsigned long long kBusyKeyShare = 5;
+__device__ void touched_shares(const uint32_t* busy_k, uint32_t nbusy, uint32_t count, uint32_t C, uint32_t rank,
+                               uint32_t* range) {
+    static_assert(kThreads >= 256, "C <= 256 CTAs share one scan");
+    __shared__ unsigned long long s_share[256];
+    __shared__ unsigned long long s_sum[kWarps];
+    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+    unsigned long long keys = 0;
+    for (uint32_t i = tid; i < nbusy; i += C) keys += busy_k[i];  // CTA tid's busy keys (tid < C)
+    // T = (count + all keys / 5) / C, so that the unclamped shares sum to count
+    unsigned long long all = 0;
+    for (uint32_t i = lane; i < nbusy; i += 32u) all += busy_k[i];
+    for (int o = 16; o > 0; o >>= 1) all += __shfl_xor_sync(0xffffffffu, all, o);
+    const unsigned long long T = ((unsigned long long)count + all / kBusyKeyShare) / C + 1u;
+    unsigned long long share = 0;
+    if (tid < C) share = T > keys / kBusyKeyShare ? T - keys / kBusyKeyShare : 0u;
+    // inclusive scan of the shares over the CTAs
+    unsigned long long incl = share;
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= (uint32_t)o) incl += y;
+    }
+    if (lane == 31) s_sum[warp] = incl;
+    __syncthreads();
+    unsigned long long before = 0;
+    for (uint32_t w = 0; w < warp; ++w) before += s_sum[w];
+    if (tid < 256u) s_share[tid] = before + incl;
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned long long total = s_share[C - 1];
+        const unsigned long long a = rank == 0 ? 0ull : s_share[rank - 1], b = s_share[rank];
+        range[0] = (uint32_t)(total ? (unsigned long long)count * a / total : 0ull);
+        range[1] = (uint32_t)(total ? (unsigned long long)count * b / total : (rank + 1 == C ? count : 0ull));
+    }
+    __syncthreads();
+}
+
 // Unlisted targets with more events than a warp sorts: queued per CTA during
 // the touched loop and settled by the CTA after it.
 constexpr uint32_t kCtaQueue = 32;
@@ -1049,8 +1093,13 @@ __device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts
     // whichever targets they are this step.  Their counts stay until the
     // blocks phase, since every CTA classifies them by their counts here.
     const uint32_t top = listed < kThreads ? listed : kThreads;
+    // The touched list's range of this CTA: equal shares, or (with busy
+    // targets this step) shares shrunk by each CTA's busy-target keys.
+    __shared__ uint32_t s_range[2];
+    bool weighted = false;
     if (top > 0u) {
         __shared__ uint32_t s_warp_busy[kWarps];
+        __shared__ uint32_t s_busy_k[kThreads];
         uint32_t n = 0, k = 0;
         if (tid < top) {
             n = kc.topo.cta_targets[tid];
@@ -1068,7 +1117,12 @@ __device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts
             s_list[0][pos] = n;
             s_list_k[0][pos] = k;
         }
+        if (busy) s_busy_k[before] = k;
+        uint32_t nbusy = 0;
+        for (uint32_t w = 0; w < kWarps; ++w) nbusy += s_warp_busy[w];
         __syncthreads();
+        weighted = nbusy > 0u && count > 0u;
+        if (weighted) touched_shares(s_busy_k, nbusy, count, C, rank, s_range);
         const uint32_t nbig = s_nlist[0];
         for (uint32_t j = 0; j < nbig; ++j)
             settle_target_cta(ln, s, kc, s_list[0][j], s_list_k[0][j], kc.topo.seg[s_list[0][j]].x, smem, pop_inh,
@@ -1110,10 +1164,13 @@ __device__ void phase_settle(const LaneState& ln, uint32_t s, const KernelConsts
     // Listed share of settle (first CTA), reported as the last phase counter.
     if (rank == 0 && tid == 0 && listed) sc->phase_cycles[LEO_PHASES - 1] += clock64() - t0;
     __syncthreads();
-    // The touched list, in warp-aligned ranges.
-    for (uint32_t base = worker - lane; base < count; base += workers) {
+    // The touched list, in warp-aligned ranges: strided over the whole group,
+    // or this CTA's own range when the shares are weighted.
+    const uint32_t lo = weighted ? s_range[0] : 0u, hi = weighted ? s_range[1] : count;
+    const uint32_t first = weighted ? lo + (tid - lane) : worker - lane, stride = weighted ? kThreads : workers;
+    for (uint32_t base = first; base < hi; base += stride) {
         const uint32_t i = base + lane;
-        const bool valid = i < count;
+        const bool valid = i < hi;
         const uint32_t n = valid ? ln.touched[i] : 0u;
         uint2 seg = make_uint2(0u, LEO_SEG_LISTED);
         uint32_t k = 0;
