@@ -309,6 +309,10 @@ int leo_b200_sparse_mean_apply_static(int device, float* target, uint32_t length
                                       float lo, float hi, float* const* replicas, uint32_t replica_count,
                                       void* stream, uint32_t* updates);
 
+/* Bytes of device scratch that leo_b200_sparse_mean_apply holds on `device`
+   (0 before its first call there; the static variant never adds to it). */
+size_t leo_b200_sparse_apply_scratch_bytes(int device);
+
 #ifdef __cplusplus
 }
 #endif

@@ -285,6 +285,13 @@ int leo_b200_sparse_mean_apply(int device, float* target, uint32_t length, const
     }
 }
 
+size_t leo_b200_sparse_apply_scratch_bytes(int device) {
+    if (device < 0 || device >= LEO_SPARSE_APPLY_MAX_DEVICES) return 0;
+    DeviceScratch& sc = g_scratch[device];
+    std::lock_guard<std::mutex> guard(sc.lock);
+    return sc.words * sizeof(uint32_t);
+}
+
 // The variant of leo_b200_sparse_mean_apply that allocates nothing: its
 // scratch is the fixed array above.  Every CUDA call it makes is a device
 // selection, an asynchronous memset / copy on the caller's stream, the two

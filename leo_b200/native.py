@@ -81,6 +81,8 @@ def lib() -> C.CDLL:
     L.leo_b200_sparse_mean_apply.argtypes = [C.c_int, vp, u32, vp, vp, vp, u32, C.c_float, C.c_float, vp, u32, vp,
                                              P(u32)]
     L.leo_b200_sparse_mean_apply_static.argtypes = L.leo_b200_sparse_mean_apply.argtypes
+    L.leo_b200_sparse_apply_scratch_bytes.argtypes = [C.c_int]
+    L.leo_b200_sparse_apply_scratch_bytes.restype = sz
     L.leo_b200_train_story_batch.argtypes = [vp, vp, vp, u32, C.c_int, P(LeoB200BatchReport),
                                              P(LeoB200StorySummary), vp]
     L.leo_b200_batch_begin.argtypes = [vp, vp, vp, u32, C.c_int]
