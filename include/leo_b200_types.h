@@ -204,11 +204,17 @@ typedef struct LeoB200ShardStory {
    key), the statistics delta and the revision increment of every story. */
 #define LEO_B200_DELTA_TENSORS 6
 
+/* Tracked-index lists of a story's ParameterChanges (runtime.rs:38-46), in
+   this order: threshold, recurrent weight, input weight, output neurons,
+   context slots. */
+#define LEO_B200_CHANGE_LISTS 5
+
 typedef struct LeoB200StoryDeltaSizes {
     uint64_t entries[LEO_B200_DELTA_TENSORS]; /* (index, delta) pairs of all stories, per tensor */
     uint64_t context_entries;                 /* keyed context deltas of all stories */
     uint32_t embedding_dim;                   /* floats per context embedding delta */
     uint32_t stories;
+    uint64_t changes[LEO_B200_CHANGE_LISTS];  /* changed indices of all stories, per list */
 } LeoB200StoryDeltaSizes;
 
 /* Caller-owned buffers for the deltas of `stories` stories; story s owns
@@ -225,6 +231,12 @@ typedef struct LeoB200StoryDeltas {
     float* context_embedding_deltas;            /* context_entries x embedding_dim */
     LeoB200Statistics* statistics;              /* stories: statistics delta (parallel.rs statistics_delta) */
     uint64_t* revision_increments;              /* stories */
+    /* Each story's ParameterChanges (DeviceStoryBatchDeltaReport::story_changes,
+       backend.rs:348): every index its lane changed, sorted, per list; and
+       per story bit 0 output_bias_dirty, bit 1 context_output_dirty. */
+    uint64_t* change_offsets[LEO_B200_CHANGE_LISTS]; /* stories + 1 each */
+    uint32_t* change_indices[LEO_B200_CHANGE_LISTS]; /* changes[l] each */
+    uint32_t* dirty_flags;                           /* stories */
 } LeoB200StoryDeltas;
 
 /* Changed-parameter indices of the canonical runtime since tracking was

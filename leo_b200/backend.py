@@ -30,6 +30,7 @@ import numpy as np
 from . import native
 from .configs import Config
 from .ctypes_types import (
+    CHANGE_LISTS,
     DELTA_TENSORS,
     FROZEN,
     OUTPUT_CLASSES,
@@ -85,6 +86,7 @@ class StoryDelta:
     context_embedding_deltas: np.ndarray  # [entries, embedding_dim]
     statistics: LeoB200Statistics
     revision_increment: int
+    changes: "ParameterChanges | None" = None  # the story's tracked indices (story_changes, backend.rs:348)
 
 
 class StoryDeltaBuffers:
@@ -103,6 +105,9 @@ class StoryDeltaBuffers:
         self.obs, self.emb = np.zeros(ce, np.uint32), np.zeros(ce * max(d, 1), np.float32)
         self.stats = (LeoB200Statistics * max(n, 1))()
         self.revisions = np.zeros(max(n, 1), np.uint64)
+        self.change_offsets = [np.zeros(n + 1, np.uint64) for _ in range(CHANGE_LISTS)]
+        self.change_indices = [np.zeros(max(int(sizes.changes[i]), 1), np.uint32) for i in range(CHANGE_LISTS)]
+        self.dirty = np.zeros(max(n, 1), np.uint32)
         c = LeoB200StoryDeltas()
         for t in range(DELTA_TENSORS):
             c.offsets[t] = self.offsets[t].ctypes.data
@@ -115,6 +120,10 @@ class StoryDeltaBuffers:
         c.context_embedding_deltas = self.emb.ctypes.data
         c.statistics = C.addressof(self.stats)
         c.revision_increments = self.revisions.ctypes.data
+        for i in range(CHANGE_LISTS):
+            c.change_offsets[i] = self.change_offsets[i].ctypes.data
+            c.change_indices[i] = self.change_indices[i].ctypes.data
+        c.dirty_flags = self.dirty.ctypes.data
         self.c = c
 
     @classmethod
@@ -161,9 +170,12 @@ class StoryDeltaBuffers:
             lo, hi = int(self.context_offsets[s]), int(self.context_offsets[s + 1])
             stats = LeoB200Statistics()
             C.memmove(C.byref(stats), C.byref(self.stats[s]), C.sizeof(stats))
+            lists = [self.change_indices[i][int(self.change_offsets[i][s]):int(self.change_offsets[i][s + 1])].copy()
+                     for i in range(CHANGE_LISTS)]
+            changes = ParameterChanges(*lists, bool(self.dirty[s] & 1), bool(self.dirty[s] & 2))
             out.append(StoryDelta(tensors, self.orders[lo:hi].copy(), self.keys[lo:hi].copy(), self.obs[lo:hi].copy(),
                                   self.emb[lo * d:hi * d].reshape(hi - lo, d).copy(), stats,
-                                  int(self.revisions[s])))
+                                  int(self.revisions[s]), changes))
         return out
 
 

@@ -131,6 +131,8 @@ struct LeoB200Device {
         std::vector<float> ctx_emb;
         LeoB200Statistics stats{};
         uint64_t revision = 0;
+        std::vector<uint32_t> changed[LEO_B200_CHANGE_LISTS];  // the lane's tracked indices, sorted
+        uint32_t dirty = 0;                                   // bit 0 output bias, bit 1 context output
     };
     std::vector<StoryDelta> story_deltas;
     bool doc_open = false;
@@ -1484,6 +1486,8 @@ void export_story_delta(LeoB200Device& dev, uint32_t l, const LaneScalars& sc, d
         CUDA_CHECK(cudaMemcpyAsync(list.data(), lt.list, lt.count * 4, cudaMemcpyDeviceToHost, dev.stream));
         CUDA_CHECK(cudaMemcpyAsync(vals.data(), buf.p, 2 * n * sizeof(float), cudaMemcpyDeviceToHost, dev.stream));
         CUDA_CHECK(cudaStreamSynchronize(dev.stream));
+        out.changed[t].assign(list.begin(), list.end());
+        std::sort(out.changed[t].begin(), out.changed[t].end());
         std::vector<std::pair<uint32_t, float>> pairs;
         for (size_t r = 0; r < lt.count; ++r)
             for (uint32_t k = 0; k < lt.row_len; ++k) {
@@ -1521,6 +1525,9 @@ void export_story_delta(LeoB200Device& dev, uint32_t l, const LaneScalars& sc, d
     }
     std::vector<uint32_t> slots;
     std::vector<CtxDelta> ctx = collect_lane_context(dev, lane, sc.ctx_changed, slots);
+    out.changed[4].assign(slots.begin(), slots.end());
+    std::sort(out.changed[4].begin(), out.changed[4].end());
+    out.dirty = (sc.bias_dirty ? 1u : 0u) | (sc.ctx_out_dirty ? 2u : 0u);
     // canonicalize_order (parallel.rs:676-691): by order, then key.
     std::sort(ctx.begin(), ctx.end(), [](const CtxDelta& a, const CtxDelta& b) {
         return a.order != b.order ? a.order < b.order : a.key < b.key;
@@ -2079,6 +2086,7 @@ void story_delta_sizes(const LeoB200Device& dev, LeoB200StoryDeltaSizes* sizes) 
     for (const auto& sd : dev.story_deltas) {
         for (int t = 0; t < LEO_B200_DELTA_TENSORS; ++t) sizes->entries[t] += sd.index[t].size();
         sizes->context_entries += sd.ctx_key.size();
+        for (int l = 0; l < LEO_B200_CHANGE_LISTS; ++l) sizes->changes[l] += sd.changed[l].size();
     }
 }
 
@@ -2114,6 +2122,18 @@ void story_deltas_copy(const LeoB200Device& dev, const LeoB200StoryDeltas& out) 
         at += n;
     }
     if (out.context_offsets) out.context_offsets[dev.story_deltas.size()] = at;
+    for (int l = 0; l < LEO_B200_CHANGE_LISTS; ++l) {
+        uint64_t pos = 0;
+        for (size_t s = 0; s < dev.story_deltas.size(); ++s) {
+            const auto& c = dev.story_deltas[s].changed[l];
+            if (out.change_offsets[l]) out.change_offsets[l][s] = pos;
+            if (out.change_indices[l] && !c.empty()) std::copy(c.begin(), c.end(), out.change_indices[l] + pos);
+            pos += c.size();
+        }
+        if (out.change_offsets[l]) out.change_offsets[l][dev.story_deltas.size()] = pos;
+    }
+    if (out.dirty_flags)
+        for (size_t s = 0; s < dev.story_deltas.size(); ++s) out.dirty_flags[s] = dev.story_deltas[s].dirty;
 }
 
 // ---------------------------------------------------------------- sharded batch (multi-GPU)

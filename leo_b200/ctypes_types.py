@@ -149,6 +149,7 @@ class LeoB200BatchReport(C.Structure):
 
 
 DELTA_TENSORS = 6  # threshold, recurrent weight, input weight, output weight, output bias, context output
+CHANGE_LISTS = 5   # threshold, recurrent weight, input weight, output neurons, context slots
 UNSUPPORTED = 1    # an optional device path that does not take the input (the trait's Ok(None))
 
 
@@ -158,6 +159,7 @@ class LeoB200StoryDeltaSizes(C.Structure):
         ("context_entries", C.c_uint64),
         ("embedding_dim", C.c_uint32),
         ("stories", C.c_uint32),
+        ("changes", C.c_uint64 * CHANGE_LISTS),
     ]
 
 
@@ -173,6 +175,9 @@ class LeoB200StoryDeltas(C.Structure):
         ("context_embedding_deltas", C.c_void_p),
         ("statistics", C.c_void_p),
         ("revision_increments", C.c_void_p),
+        ("change_offsets", C.c_void_p * CHANGE_LISTS),
+        ("change_indices", C.c_void_p * CHANGE_LISTS),
+        ("dirty_flags", C.c_void_p),
     ]
 
 

@@ -1956,9 +1956,11 @@ ReplayReport apply_replay_policy(Runtime& rt, const uint8_t* story, size_t len, 
 
 // training.rs:1539-1727 (CPU backend)
 std::vector<SparseModelDelta> worker_story_deltas(const Model& base, const std::vector<std::vector<uint8_t>>& stories,
-                                                  Permission p, size_t max_threads, std::vector<DocumentPass>& passes) {
+                                                  Permission p, size_t max_threads, std::vector<DocumentPass>& passes,
+                                                  std::vector<ParameterChanges>* changes) {
     size_t count = stories.size();
     std::vector<SparseModelDelta> deltas(count);
+    if (changes) changes->assign(count, ParameterChanges{});
     passes.assign(count, DocumentPass{});
     std::vector<std::string> errors(count);
     std::atomic<size_t> next{0};
@@ -1972,6 +1974,7 @@ std::vector<SparseModelDelta> worker_story_deltas(const Model& base, const std::
                 w.enable_parameter_tracking();
                 passes[i] = train_document_pass(w, stories[i].data(), stories[i].size(), p);
                 deltas[i] = SparseModelDelta::between_tracked(base, w.model, w.parameter_changes());
+                if (changes) (*changes)[i] = w.parameter_changes();
             } catch (const std::exception& e) {
                 errors[i] = e.what();
             }

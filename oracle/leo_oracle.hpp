@@ -356,7 +356,8 @@ struct BatchReport {
 // `base` with parameter tracking, one document pass, its between_tracked delta
 // (parallel.rs:385-454).  `passes` receives each story's pass.
 std::vector<SparseModelDelta> worker_story_deltas(const Model& base, const std::vector<std::vector<uint8_t>>& stories,
-                                                  Permission p, size_t max_threads, std::vector<DocumentPass>& passes);
+                                                  Permission p, size_t max_threads, std::vector<DocumentPass>& passes,
+                                                  std::vector<ParameterChanges>* changes = nullptr);
 // training.rs:1539-1727, CPU branch (stories.len() > 1) and the single-story branch.
 // `canonical` is the canonical CPU runtime (its tick persists across batches).
 BatchReport train_story_batch(Runtime& canonical, const std::vector<std::vector<uint8_t>>& stories,

@@ -12,6 +12,7 @@ using namespace leo_oracle;
 
 namespace {
 thread_local std::string g_error;
+thread_local std::vector<ParameterChanges> g_last_changes;
 
 int fail(const std::exception& e) {
     g_error = e.what();
@@ -441,7 +442,7 @@ void* leo_oracle_story_deltas(void* rtp, const uint8_t* bytes, const uint64_t* o
         for (size_t i = 0; i < stories; ++i) batch[i].assign(bytes + offsets[i], bytes + offsets[i + 1]);
         std::vector<DocumentPass> passes;
         auto* out = new std::vector<SparseModelDelta>(
-            worker_story_deltas(rt.model, batch, (Permission)permission, threads, passes));
+            worker_story_deltas(rt.model, batch, (Permission)permission, threads, passes, &g_last_changes));
         return out;
     } catch (const std::exception& e) {
         fail(e);
@@ -466,6 +467,35 @@ void* leo_oracle_runtime_delta(void* base, void* rtp, int tracked) {
 }
 
 void leo_oracle_deltas_free(void* h) { delete (std::vector<SparseModelDelta>*)h; }
+
+// The per-story ParameterChanges of the last leo_oracle_story_deltas call on
+// this thread: sizes (stories, then per story the five list lengths and the
+// dirty bits) and, with `out` not NULL, list l of story s at out[l] in story
+// order, each list sorted.
+int leo_oracle_last_story_changes(uint64_t* counts, uint32_t* dirty, uint32_t* const* out) {
+    const auto& v = g_last_changes;
+    for (size_t s = 0; s < v.size(); ++s) {
+        const std::vector<size_t>* lists[5] = {&v[s].threshold, &v[s].recurrent_weight, &v[s].input_weight,
+                                               &v[s].output_neurons, &v[s].context_slots};
+        for (int l = 0; l < 5; ++l) {
+            if (counts) counts[s * 5 + l] = lists[l]->size();
+        }
+        if (dirty) dirty[s] = (v[s].output_bias_dirty ? 1u : 0u) | (v[s].context_output_dirty ? 2u : 0u);
+    }
+    if (out) {
+        for (int l = 0; l < 5; ++l) {
+            size_t at = 0;
+            for (size_t s = 0; s < v.size(); ++s) {
+                const std::vector<size_t>* lists[5] = {&v[s].threshold, &v[s].recurrent_weight, &v[s].input_weight,
+                                                       &v[s].output_neurons, &v[s].context_slots};
+                std::vector<size_t> sorted(*lists[l]);
+                std::sort(sorted.begin(), sorted.end());
+                for (size_t x : sorted) out[l][at++] = (uint32_t)x;
+            }
+        }
+    }
+    return 0;
+}
 
 namespace {
 const std::vector<SparseF32Delta>& delta_tensor(const SparseModelDelta& d, int t) {

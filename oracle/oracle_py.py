@@ -83,6 +83,7 @@ def lib() -> C.CDLL:
         L.leo_oracle_deltas_copy.argtypes = [vp, sz, vp]
         L.leo_oracle_apply_story_deltas.argtypes = [vp, vp, vp, C.c_int, vp]
         L.leo_oracle_runtime_parameter_changes.argtypes = [vp, vp, vp]
+        L.leo_oracle_last_story_changes.argtypes = [vp, vp, vp]
         _lib = L
     return _lib
 
@@ -283,7 +284,26 @@ class OracleRuntime:
         offsets[1:] = np.cumsum([len(s) for s in stories])
         h = lib().leo_oracle_story_deltas(self.handle, data.ctypes.data, offsets.ctypes.data, len(stories),
                                           permission, threads)
-        return _take_deltas(h, self.config.context_embedding_dim)
+        deltas = _take_deltas(h, self.config.context_embedding_dim)
+        # each story's tracked ParameterChanges (lists sorted)
+        from leo_b200.backend import ParameterChanges
+
+        n = len(stories)
+        counts = np.zeros(max(n * 5, 1), np.uint64)
+        dirty = np.zeros(max(n, 1), np.uint32)
+        _check(lib().leo_oracle_last_story_changes(counts.ctypes.data, dirty.ctypes.data, None))
+        per_list = [np.zeros(max(int(counts[l::5][:n].sum()), 1), np.uint32) for l in range(5)]
+        table = (C.c_void_p * 5)(*[a.ctypes.data for a in per_list])
+        _check(lib().leo_oracle_last_story_changes(None, None, table))
+        at = [0] * 5
+        for s, d in enumerate(deltas):
+            lists = []
+            for l in range(5):
+                c = int(counts[s * 5 + l])
+                lists.append(per_list[l][at[l]:at[l] + c].copy())
+                at[l] += c
+            d.changes = ParameterChanges(*lists, bool(dirty[s] & 1), bool(dirty[s] & 2))
+        return deltas
 
     def delta_against(self, base: OracleModel, tracked: bool):
         """SparseModelDelta::between_tracked (with this runtime's parameter

@@ -224,7 +224,8 @@ def test_trait_entry_points_are_exported(native_lib):
 @pytest.mark.parametrize("name", ["test", "test-8", "baseline1"])
 def test_gpu_story_deltas_match_oracle(native_lib, oracle_lib, name):
     """Each story's exported delta (training_story_batch_deltas) equals the
-    oracle worker's between_tracked delta bit for bit; the canonical model is
+    oracle worker's between_tracked delta bit for bit, and its story_changes
+    the worker's tracked parameter_changes; the canonical model is
     unchanged by the call, and the oracle's apply_mean_deltas of the GPU's
     deltas reproduces the GPU's own merge (training_story_batch)."""
     from leo_b200.backend import GpuBackend
@@ -245,6 +246,11 @@ def test_gpu_story_deltas_match_oracle(native_lib, oracle_lib, name):
             for s, (got, want) in enumerate(zip(rep.story_deltas, expected)):
                 try:
                     _same_delta(got, want)
+                    # story_changes: the indices the story's lane tracked, as the worker's parameter_changes
+                    for field in ("threshold", "recurrent_weight", "input_weight", "output_neurons", "context_slots"):
+                        assert np.array_equal(getattr(got.changes, field), getattr(want.changes, field)), field
+                    assert got.changes.output_bias_dirty == want.changes.output_bias_dirty
+                    assert got.changes.context_output_dirty == want.changes.context_output_dirty
                 except AssertionError as e:
                     raise AssertionError(f"batch {i} story {s}: {e}") from e
             merged = gpu.training_story_batch(batch, TRAINING)
