@@ -1975,7 +1975,10 @@ __device__ __forceinline__ void wavefront_steps(const LaneState* __restrict__ la
     LaneScalars* sc = ln.sc;
     const uint32_t steps = sc->steps;
     const uint32_t worker = rank * kThreads + threadIdx.x, workers = C * kThreads;
-    const uint32_t gwarp = rank * kWarps + (threadIdx.x >> 5), gwarps = C * kWarps;
+    // Warp-sized tasks (a block's top-k, 32 learning destinations) are dealt
+    // over the CTAs first: task t runs on CTA t mod C, so a few hundred tasks
+    // spread over every SM instead of filling the first CTAs' warps.
+    const uint32_t gwarp = (threadIdx.x >> 5) * C + rank, gwarps = C * kWarps;
     const bool timer = rank == 0 && threadIdx.x == 0;
     // Phase clocks and work counters belong to the first thread alone; they
     // live in shared memory so they cost the other threads no registers.
