@@ -414,3 +414,40 @@ def test_gpu_training_story_batch_declines_one_story(native_lib):
         rep = gpu.training_story_batch_deltas([b"abc"], TRAINING)
         assert rep is not None and len(rep.story_deltas) == 1
         assert gpu.state_digest() == before
+
+
+def test_story_delta_buffers_round_trip(native_lib):
+    """The CSR layout a caller hands to leo_b200_story_deltas / the oracle's
+    apply: packing story deltas and unpacking them gives them back."""
+    from leo_b200.backend import DELTA_NAMES, StoryDelta, StoryDeltaBuffers
+    from leo_b200.ctypes_types import LeoB200Statistics
+
+    rng = np.random.default_rng(5)
+    d = 3
+    deltas = []
+    for s in range(4):
+        tensors = {}
+        for name in DELTA_NAMES:
+            k = int(rng.integers(0, 6))
+            idx = np.sort(rng.choice(1000, size=k, replace=False)).astype(np.uint32)
+            tensors[name] = (idx, rng.standard_normal(k).astype(np.float32))
+        m = int(rng.integers(0, 3))
+        stats = LeoB200Statistics()
+        stats.processed_bytes = 10 * s
+        stats.training_loss_sum = 0.5 * s
+        deltas.append(StoryDelta(tensors, rng.integers(1, 5, m).astype(np.uint32),
+                                 rng.integers(1, 2**63, m, dtype=np.uint64), rng.integers(0, 3, m).astype(np.uint32),
+                                 rng.standard_normal((m, d)).astype(np.float32), stats, s + 1))
+    back = StoryDeltaBuffers.pack(deltas, d).unpack()
+    assert len(back) == len(deltas)
+    for a, b in zip(deltas, back):
+        for name in DELTA_NAMES:
+            assert np.array_equal(a.tensors[name][0], b.tensors[name][0])
+            assert np.array_equal(a.tensors[name][1], b.tensors[name][1])
+        assert np.array_equal(a.context_keys, b.context_keys)
+        assert np.array_equal(a.context_orders, b.context_orders)
+        assert np.array_equal(a.context_observation_increments, b.context_observation_increments)
+        assert np.array_equal(a.context_embedding_deltas, b.context_embedding_deltas)
+        assert a.statistics.processed_bytes == b.statistics.processed_bytes
+        assert a.statistics.training_loss_sum == b.statistics.training_loss_sum
+        assert a.revision_increment == b.revision_increment
