@@ -237,16 +237,18 @@ int leo_b200_set_story_chunk(LeoB200Device* device, uint32_t steps);
    on the host (crates/leo-core/src/parallel.rs:1024-1113, cuda.rs:9230-9260). */
 int leo_b200_set_device_context_merge(LeoB200Device* device, int enable);
 
-/* Execution geometry only: neurons whose recurrent in-degree is at least
-   `min_in_degree` are hubs -- their events per step go to a contiguous buffer
-   sorted by event order instead of a per-target linked list, which keeps
-   power-law topologies (a few targets receiving thousands of events per step)
-   from serialising on one list.  0 restores the default,
-   max(4 x synapses_per_neuron, 8 x neuron_count / max_active_global).  A hub
-   with more than `cta_events` events in a step (1..2048; 0: 256) is sorted
-   and summed by a whole CTA, one with at most `thread_events` (1..16; 0: 16)
-   by a single thread, one in between by a warp.  Only before the first story
-   batch.  leo_b200_hub_count reports the plan. */
+/* Execution geometry only (results never depend on it).  Every target's
+   events of a step are keys in its own segment, sorted and summed in event
+   order by settle: by one thread when a step brings it at most
+   `thread_events` events (1..16; 0: 16), by a warp up to 256, by a whole CTA
+   above.  Targets whose recurrent in-degree is at least `min_in_degree` are
+   listed (0 restores the default, max(1, 16 x neuron_count /
+   (4 x max_active_global))): they are dealt over the CTAs in descending
+   segment capacity, and among the first 512 those with more than
+   `cta_events` events in the step (1..2048; 0: 256) are sorted one per CTA
+   while the other CTAs settle the touched list.  Only before the first story
+   batch.  leo_b200_hub_count reports the number of listed targets and the
+   event-segment entries per lane. */
 int leo_b200_set_hub_threshold(LeoB200Device* device, uint32_t min_in_degree, uint32_t cta_events,
                                uint32_t thread_events);
 int leo_b200_hub_count(LeoB200Device* device, uint32_t* hubs, uint64_t* events_per_lane);
