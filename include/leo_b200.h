@@ -181,10 +181,11 @@ int leo_b200_advance_frozen_batch(LeoB200Device* device, const uint32_t* symbols
 /* Parameter tracking of the canonical runtime (RuntimeBackend::
    enable_parameter_tracking / parameter_changes, backend.rs:358-359; the
    CUDA backend's window semantics, cuda.rs:2827-2842): enabling starts an
-   empty window; the window collects every index the canonical runtime's
-   steps change (leo_b200_training_step_batch, leo_b200_advance_frozen_batch)
-   and closes at the next story batch or packed sync, which write those rows
-   into every lane.  leo_b200_parameter_changes stores the sizes and, when
+   empty window (rows changed before it are first written into every lane);
+   the window collects every index the canonical runtime's steps change
+   (leo_b200_training_step_batch, leo_b200_advance_frozen_batch) and closes
+   at the next story batch or packed sync, which write those rows into every
+   lane.  leo_b200_parameter_changes stores the sizes and, when
    `changes` is not NULL, the sorted indices into its caller buffers. */
 int leo_b200_enable_parameter_tracking(LeoB200Device* device);
 int leo_b200_parameter_changes(LeoB200Device* device, LeoB200ParameterChangeSizes* sizes,

@@ -1925,24 +1925,12 @@ struct TrackedList {
     uint32_t count;
 };
 
+// A new window: changes the canonical runtime made before it are first written
+// into every lane and the host mirror (their lists then restart empty), so no
+// change is lost to the lanes when the lists are reset.
 void tracking_enable(LeoB200Device& dev) {
     if (dev.batch_open) throw LeoFailure("a story batch is in progress");
-    Lane& rl = *dev.replay;
-    LaneScalars sc;
-    read_scalars(dev, rl, sc);
-    const TrackedList lists[] = {{rl.st.thr_list, rl.st.thr_mark, sc.thr_changed},
-                                 {rl.st.rec_list, rl.st.rec_mark, sc.rec_changed},
-                                 {rl.st.in_list, rl.st.in_mark, sc.in_changed},
-                                 {rl.st.out_list, rl.st.out_mark, sc.out_changed},
-                                 {rl.st.ctx_list, rl.st.ctx_mark, sc.ctx_changed}};
-    for (const TrackedList& tl : lists) {
-        if (tl.count == 0) continue;
-        clear_marks_kernel<<<grid_for(tl.count), 256, 0, dev.stream>>>(tl.list, tl.count, tl.marks);
-        CUDA_CHECK(cudaGetLastError());
-    }
-    sc.thr_changed = sc.rec_changed = sc.in_changed = sc.out_changed = sc.ctx_changed = 0;
-    sc.bias_dirty = sc.ctx_out_dirty = 0;
-    replay_scalars_write(dev, sc);
+    refresh_lanes_from_replay(dev);
 }
 
 void tracking_changes(LeoB200Device& dev, LeoB200ParameterChangeSizes* sizes, const LeoB200ParameterChanges* out) {

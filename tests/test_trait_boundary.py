@@ -451,3 +451,32 @@ def test_story_delta_buffers_round_trip(native_lib):
         assert a.statistics.processed_bytes == b.statistics.processed_bytes
         assert a.statistics.training_loss_sum == b.statistics.training_loss_sum
         assert a.revision_increment == b.revision_increment
+
+
+@pytest.mark.gpu
+def test_gpu_tracking_window_keeps_earlier_changes_for_the_lanes(native_lib):
+    """Canonical steps before enable_parameter_tracking still reach the story
+    lanes: a batch after (steps, enable) matches a batch after the steps alone."""
+    from leo_b200.backend import GpuBackend
+    from leo_b200.configs import WORKLOADS
+    from leo_b200.ctypes_types import TRAINING
+    from leo_b200.model import HostModel
+
+    case = CASES["test"]
+    w, batches = _stories(case)
+    story = b"a story for the canonical runtime"
+    steps = [(BEGIN, story[0])] + [(story[p - 1], story[p] if p < len(story) else END)
+                                   for p in range(1, len(story) + 1)]
+    digests = []
+    for enable in (False, True):
+        model = HostModel.initialize(w.config, w.topology)
+        with GpuBackend(model, device=0, max_lanes=4) as gpu:
+            gpu.train_story_batch(batches[0], TRAINING)  # lanes resident
+            gpu.begin_document()
+            gpu.training_step_batch(steps, TRAINING)
+            if enable:
+                gpu.enable_parameter_tracking()
+                assert len(gpu.parameter_changes().threshold) == 0
+            gpu.train_story_batch(batches[1], TRAINING)
+            digests.append(gpu.state_digest())
+    assert digests[0] == digests[1]
