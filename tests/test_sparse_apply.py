@@ -155,3 +155,69 @@ def test_gpu_rejects_invalid_deltas_without_writing(native_lib, bad):
     _, good_idx, good_dl, good_off = make_case(12, 20_000, 3, 0.01)
     sparse_mean_apply(t, torch.from_numpy(good_idx.view(np.int32).copy()).to(dev),
                       torch.from_numpy(good_dl).to(dev), good_off, -1.0, 1.0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("density", [0.001, 0.01, 0.1])
+def test_reference_cuda_kernels_agree(native_lib, density):
+    """The reference's own kernels (leo_apply_shared_wavefront_deltas +
+    leo_scatter_f32, built unmodified by oracle/ref_cuda/Makefile) on the same
+    merged deltas give this build's values bit for bit, after the sign rule the
+    reference's apply adds for recurrent weights (excitatory sources >= 0,
+    inhibitory <= 0; and it leaves an index whose merged delta is exactly 0
+    alone), in the target and in every replica."""
+    import torch
+    from pathlib import Path
+
+    from leo_b200.sparse_apply import sparse_mean_apply
+
+    lib_path = Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "libleo_ref_kernels.so"
+    if not lib_path.exists():
+        pytest.skip("the reference kernels were not built (needs the reference checkout at build time)")
+    ref = C.CDLL(str(lib_path))
+    ref.leo_ref_last_error.restype = C.c_char_p
+    vp, u32 = C.c_void_p, C.c_uint32
+    ref.leo_ref_apply_sync.argtypes = [C.c_int, vp, vp, u32, u32, vp, vp, vp, u32, vp, u32, C.c_float, C.c_float,
+                                       u32, C.POINTER(C.c_float), C.POINTER(C.c_float)]
+    length, stories, S, n_rep = 1 << 20, 16, 64, 3
+    target, indices, deltas, offsets = make_case(41, length, stories, density)
+    dev = torch.device("cuda:0")
+    base = torch.from_numpy(target.copy()).to(dev)
+    ours = base.clone()
+    idx = torch.from_numpy(indices.view(np.int32).copy()).to(dev)
+    dl = torch.from_numpy(deltas.copy()).to(dev)
+    sparse_mean_apply(ours, idx, dl, offsets, -1.0, 1.0, [])
+    # the reference's input: the union and its merged deltas (FP64 sums in story order / stories)
+    sums = np.zeros(length, np.float64)
+    touched = np.zeros(length, bool)
+    for s in range(stories):
+        a, b = int(offsets[s]), int(offsets[s + 1])
+        sums[indices[a:b]] += deltas[a:b].astype(np.float64)
+        touched[indices[a:b]] = True
+    union = np.flatnonzero(touched).astype(np.uint32)
+    merged = (sums[union] / stories).astype(np.float32)
+    rng = np.random.default_rng(42)
+    types = (rng.random(length // S) < 0.2).astype(np.uint8)
+    d_types = torch.from_numpy(types).to(dev)
+    d_union = torch.from_numpy(union.view(np.int32).copy()).to(dev)
+    d_merged = torch.from_numpy(merged).to(dev)
+    theirs = torch.empty_like(base)
+    reps = [base.clone() for _ in range(n_rep)]
+    table = (C.c_void_p * n_rep)(*[r.data_ptr() for r in reps])
+    apply_ms, sync_ms = C.c_float(), C.c_float()
+    torch.cuda.synchronize()
+    rc = ref.leo_ref_apply_sync(0, base.data_ptr(), theirs.data_ptr(), length, S, d_types.data_ptr(),
+                                d_union.data_ptr(), d_merged.data_ptr(), union.size, table, n_rep, -1.0, 1.0, 1,
+                                C.byref(apply_ms), C.byref(sync_ms))
+    torch.cuda.synchronize()
+    assert rc == 0, ref.leo_ref_last_error()
+    got = ours.cpu().numpy()
+    source_type = np.repeat(types, S)
+    # The reference's apply skips an index whose merged delta is exactly 0 (no clamp, no sign rule).
+    moved = np.zeros(length, bool)
+    moved[union] = merged != 0.0
+    want = np.where(moved, np.where(source_type == 0, np.maximum(got, 0.0), np.minimum(got, 0.0)), target)
+    theirs_h = theirs.cpu().numpy()
+    assert np.array_equal(theirs_h, want)  # +0.0 and -0.0 compare equal
+    for r in reps:
+        assert np.array_equal(r.cpu().numpy()[touched], theirs_h[touched])
