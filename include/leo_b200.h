@@ -198,6 +198,11 @@ int leo_b200_parameter_changes(LeoB200Device* device, LeoB200ParameterChangeSize
    statistics replaced.  Indices are validated before anything is written. */
 int leo_b200_synchronize_packed_model(LeoB200Device* device, const LeoB200PackedUpdate* update);
 
+/* RuntimeBackend::commit_packed_host_model (backend.rs:385-387; cuda.rs:
+   2858-2867): the same writes, keeping the parameter-tracking window open
+   (its tracked rows are written into the lanes at the next story batch). */
+int leo_b200_commit_packed_host_model(LeoB200Device* device, const LeoB200PackedUpdate* update);
+
 /* training_state_hash of the canonical device model. */
 int leo_b200_state_digest(LeoB200Device* device, uint8_t out[32]);
 

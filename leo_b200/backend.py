@@ -518,6 +518,20 @@ class GpuBackend:
 
     def synchronize_packed_model(self, update: PackedSparseModelUpdate) -> None:
         """RuntimeBackend::synchronize_packed_model (backend.rs:374-376)."""
+        u, keep = self._packed(update)  # keep: the arrays u points at, alive through the call
+        native.check(native.lib().leo_b200_synchronize_packed_model(self.handle, C.byref(u)))
+        del keep
+
+    def commit_packed_host_model(self, update: PackedSparseModelUpdate) -> None:
+        """RuntimeBackend::commit_packed_host_model (backend.rs:385-387): the
+        same writes, the tracking window left open."""
+        u, keep = self._packed(update)
+        native.check(native.lib().leo_b200_commit_packed_host_model(self.handle, C.byref(u)))
+        del keep
+
+    @staticmethod
+    def _packed(update: PackedSparseModelUpdate):
+        """The C view of a packet and the arrays it points at (kept alive by the caller)."""
         keep = []
 
         def ptr(a, dtype):
@@ -550,7 +564,7 @@ class GpuBackend:
         u.generation = update.generation
         u.parameter_revision = update.parameter_revision
         u.statistics = update.statistics
-        native.check(native.lib().leo_b200_synchronize_packed_model(self.handle, C.byref(u)))
+        return u, keep
 
     # ---------------------------------------------------------------- inspection
     CANONICAL_LANE = 0xFFFFFFFF

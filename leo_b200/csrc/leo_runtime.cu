@@ -1968,10 +1968,13 @@ void tracking_changes(LeoB200Device& dev, LeoB200ParameterChangeSizes* sizes, co
 
 // PackedSparseModelUpdate::apply_to_model (parallel.rs:196-300) on the
 // canonical model, then the same values into every resident lane.
-void packed_update(LeoB200Device& dev, const LeoB200PackedUpdate& u) {
+// `close_window`: synchronize_packed_model first writes the canonical
+// runtime's tracked changes into the lanes (closing the tracking window);
+// commit_packed_host_model keeps the window open (cuda.rs:2861-2866).
+void packed_update(LeoB200Device& dev, const LeoB200PackedUpdate& u, bool close_window = true) {
     if (dev.batch_open) throw LeoFailure("a story batch is in progress");
     const ModelSizes& z = dev.z;
-    refresh_lanes_from_replay(dev);
+    if (close_window) refresh_lanes_from_replay(dev);
     upload_lane_table(dev);
     const uint32_t lane_count = (uint32_t)dev.lanes.size();
     struct Item {
@@ -2796,6 +2799,17 @@ int leo_b200_synchronize_packed_model(LeoB200Device* dev, const LeoB200PackedUpd
         if (!update) throw LeoFailure("packed update is null");
         CUDA_CHECK(cudaSetDevice(dev->device));
         packed_update(*dev, *update);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int leo_b200_commit_packed_host_model(LeoB200Device* dev, const LeoB200PackedUpdate* update) {
+    try {
+        if (!update) throw LeoFailure("packed update is null");
+        CUDA_CHECK(cudaSetDevice(dev->device));
+        packed_update(*dev, *update, false);
         return 0;
     } catch (const std::exception& e) {
         return fail(e);

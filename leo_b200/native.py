@@ -108,6 +108,7 @@ def lib() -> C.CDLL:
     L.leo_b200_enable_parameter_tracking.argtypes = [vp]
     L.leo_b200_parameter_changes.argtypes = [vp, P(LeoB200ParameterChangeSizes), P(LeoB200ParameterChanges)]
     L.leo_b200_synchronize_packed_model.argtypes = [vp, P(LeoB200PackedUpdate)]
+    L.leo_b200_commit_packed_host_model.argtypes = [vp, P(LeoB200PackedUpdate)]
     _lib = L
     return L
 

@@ -480,3 +480,37 @@ def test_gpu_tracking_window_keeps_earlier_changes_for_the_lanes(native_lib):
             gpu.train_story_batch(batches[1], TRAINING)
             digests.append(gpu.state_digest())
     assert digests[0] == digests[1]
+
+
+@pytest.mark.gpu
+def test_gpu_commit_packed_host_model_keeps_the_tracking_window(native_lib):
+    """commit_packed_host_model writes the packet like synchronize_packed_model
+    but leaves the tracked changes in the window; synchronize closes it."""
+    from leo_b200.backend import GpuBackend, ParameterChanges, PackedSparseModelUpdate
+    from leo_b200.configs import WORKLOADS
+    from leo_b200.ctypes_types import TRAINING
+    from leo_b200.model import HostModel
+
+    w = WORKLOADS["test"]
+    story = b"tracked steps before a commit"
+    steps = [(BEGIN, story[0])] + [(story[p - 1], story[p] if p < len(story) else END)
+                                   for p in range(1, len(story) + 1)]
+    model = HostModel.initialize(w.config, w.topology)
+    with GpuBackend(model, device=0, max_lanes=2) as gpu:
+        gpu.enable_parameter_tracking()
+        gpu.begin_document()
+        gpu.training_step_batch(steps, TRAINING)
+        before = gpu.parameter_changes()
+        assert len(before.threshold) > 0
+        target = gpu.synchronize_model().copy()
+        target.arrays["output_bias"][2] += np.float32(0.5)
+        none = np.zeros(0, np.uint32)
+        packet = PackedSparseModelUpdate.from_model(target, ParameterChanges(none, none, none, none, none, True,
+                                                                             False))
+        gpu.commit_packed_host_model(packet)
+        after = gpu.parameter_changes()
+        assert np.array_equal(after.threshold, before.threshold)
+        assert gpu.state_digest() == target.training_state_hash()
+        gpu.synchronize_packed_model(packet)
+        assert len(gpu.parameter_changes().threshold) == 0
+        assert gpu.state_digest() == target.training_state_hash()
